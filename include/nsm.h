@@ -1,0 +1,250 @@
+/*
+ * nsm.h -- C ABI of the B200-native blockwise-sparse NF4 decode MLP.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t,
+ * returns an int status (NSM_OK == 0, negative on error), never throws,
+ * never allocates device memory, and is ordered on the given stream.  Scratch
+ * memory is a caller-owned workspace whose size is returned by the matching
+ * *_workspace_bytes() query.  A workspace must be zero-filled once before
+ * its first use (nsm_workspace_init); every call leaves its counters zero
+ * again.  Calls that share one workspace must not overlap on the GPU.
+ *
+ * The reference (andott28/next_step_ai) has no native code: its hot path is
+ * Python + Triton.  Each declaration below names the reference interface it
+ * replaces (paths relative to the reference checkout).
+ *
+ * NF4 conventions (as in the reference): element e of a row-major weight lives
+ * in byte e/2, high nibble = even element; value = code[nibble] *
+ * absmax[e / quant_block_size].  This build's fast paths require
+ * block_size == 32 and quant_block_size == 64 (the configuration the
+ * reference's single-kernel path requires, triton_sparse_mlp.py:1401-1406).
+ */
+#ifndef NSM_H_
+#define NSM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* nsm_stream_t; /* == cudaStream_t */
+
+/* ---- status codes ---------------------------------------------------- */
+#define NSM_OK 0
+#define NSM_ERR_INVALID_ARG (-1)   /* bad pointer / size / layout         */
+#define NSM_ERR_UNSUPPORTED (-2)   /* shape outside the supported set     */
+#define NSM_ERR_CUDA (-3)          /* a CUDA runtime call failed          */
+#define NSM_ERR_TIMEOUT (-4)       /* a bounded device wait gave up       */
+#define NSM_ERR_WORKSPACE (-5)     /* workspace missing or too small      */
+#define NSM_ERR_DEVICE (-6)        /* device is not sm_100 / not present  */
+
+/* ---- element types --------------------------------------------------- */
+#define NSM_F32 0
+#define NSM_F16 1
+#define NSM_BF16 2
+
+int nsm_abi_version(void);
+const char* nsm_status_string(int status);
+/* Detail of the last failing call on the calling host thread. */
+const char* nsm_last_error(void);
+/* Zero-fills a workspace (stream-ordered). */
+int nsm_workspace_init(void* ws, size_t ws_bytes, nsm_stream_t stream);
+
+/* ---- router ------------------------------------------------------------
+ * Learned-basis router weights.  Replaces the per-layer routing dict the
+ * reference builds at streaming_llama_runtime.py:849-991 and consumes in
+ * _compute_sparse_basis_latent / _route_sparse_mlp (:4209-4238, :4311-4352).
+ *   enc_w   [rank, H]    enc_b [rank] (may be NULL)
+ *   score_w [NB, rank]   score_b [NB] (may be NULL)       -- learned head
+ *   legacy_abs_latent=1: scores = |latent| @ score_w^T with score_w = dec_norm_t^T
+ *   down_block_norm [NB] fp32 (may be NULL): scores *= down_block_norm
+ * weight_dtype applies to enc_w, enc_b, score_w, score_b.                 */
+typedef struct nsm_router_weights {
+  const void* enc_w;
+  const void* enc_b;
+  const void* score_w;
+  const void* score_b;
+  const float* down_block_norm;
+  int32_t weight_dtype;
+  int32_t rank;
+  int32_t num_blocks;
+  int32_t top_k;
+  int32_t basis_top_k;
+  int32_t legacy_abs_latent;
+} nsm_router_weights;
+
+/* ---- NF4 MLP weights ---------------------------------------------------
+ * Replaces the gathered / hot-pool tensors the reference passes to
+ * _sparse_mlp_forward_fast_triton (streaming_llama_runtime.py:5526-5547)
+ * and to triton_sparse_mlp_decode_4bit_single_kernel_sm75
+ * (triton_sparse_mlp.py:1378-1396).
+ *
+ * gate/up: one 32-row block per "pool row", bitsandbytes row-major inside a
+ *   block: byte (row i, col c) of pool row p at
+ *   gate_packed + p*gateup_block_stride + i*(H/2) + c/2; fp32 absmax at
+ *   gate_absmax + p*gateup_absmax_block_stride + i*(H/64) + c/64.
+ *   Strides 0 mean the dense values 16*H and H/2.
+ * down: the 16 packed bytes of row h of pool row p at
+ *   down_packed + p*down_block_stride + h*down_row_stride; its absmax at
+ *   down_absmax[p*down_absmax_block_stride + h*down_absmax_row_stride].
+ *   Block-major [P][H][16] + [P][H]: strides (16*H, 16, H, 1) (the default
+ *   when all four are 0).  The reference's gathered columns [H][U][16] +
+ *   [H][U]: (16, 16*U, 1, U).  A whole bitsandbytes down weight [H][I/2] +
+ *   [H][I/64] addressed by block id: (16, I/2, 1, I/64) with
+ *   down_absmax_pair=1.
+ * down_absmax_pair=1 means the absmax index of block b is b/2 (64-column
+ *   quant groups over 32-column blocks), as in the reference's column
+ *   gather abs_idx = (b*32)//64 (streaming_llama_runtime.py:4510).       */
+typedef struct nsm_mlp_weights {
+  const uint8_t* gate_packed;
+  const float* gate_absmax;
+  const uint8_t* up_packed;
+  const float* up_absmax;
+  const uint8_t* down_packed;
+  const float* down_absmax;
+  const float* gate_code; /* [16] fp32 */
+  const float* up_code;
+  const float* down_code;
+  const void* gate_bias;  /* [I] (indexed by block*32+row) or NULL */
+  const void* up_bias;
+  const void* down_bias;  /* [H] or NULL */
+  int32_t bias_dtype;
+  int32_t pool_rows;      /* number of valid pool rows                   */
+  int64_t gateup_block_stride;
+  int64_t gateup_absmax_block_stride;
+  int64_t down_block_stride;
+  int64_t down_row_stride;
+  int64_t down_absmax_block_stride;
+  int64_t down_absmax_row_stride;
+  int32_t down_absmax_pair;
+  int32_t reserved;
+} nsm_mlp_weights;
+
+/* Block -> pool-row mapping applied to the router's selection.
+ *   slot_of_block [NB] int32 (device): pool row, or <0 = not present here.
+ *   If NULL: pool row = block - block_begin for block_begin <= block < block_end,
+ *   other blocks are not present here (multi-GPU shards; [0,NB) = everything). */
+typedef struct nsm_block_map {
+  const int32_t* slot_of_block;
+  int32_t block_begin;
+  int32_t block_end;
+} nsm_block_map;
+
+/* Residual / RMSNorm prologue of a decoder layer (optional).
+ *   If residual != NULL: residual[H] (fp32, in/out) += y_prev[H] (if not NULL,
+ *   y_prev_dtype) and the MLP input is rmsnorm(residual) * norm_weight, as the
+ *   reference's post_attention_layernorm + residual add
+ *   (streaming_llama_runtime.py:7762-7775).  Otherwise x is the MLP input. */
+typedef struct nsm_layer_io {
+  float* residual;
+  const void* y_prev;
+  int32_t y_prev_dtype;
+  int32_t norm_weight_dtype;
+  const void* norm_weight; /* [H] or NULL (= ones) */
+  float eps;
+  int32_t reserved;
+} nsm_layer_io;
+
+size_t nsm_decode_workspace_bytes(int hidden, int intermediate, int top_k, int rank);
+
+/* Router only (latent GEMV + block scores + top-k), one token.
+ * Replaces StreamingLlamaRuntime._route_sparse_mlp for rows == 1
+ * (streaming_llama_runtime.py:4311-4352).  idx_out [top_k] int32 block ids in
+ * score-descending order (ties: lower block id first); score_out [top_k]
+ * fp32 (may be NULL); latent_out [rank] fp32 (may be NULL). */
+int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_weights* rw,
+              int32_t* idx_out, float* score_out, float* latent_out, void* ws, size_t ws_bytes,
+              nsm_stream_t stream);
+
+/* Whole decode MLP for one token: route, gather-GEMV gate/up, SiLU*up,
+ * gather-GEMV down.  Replaces _mlp_forward_dispatch's decode branch
+ * (streaming_llama_runtime.py:5906-5913) = _route_sparse_mlp +
+ * _sparse_mlp_forward_fast (:5104) with resident blocks.
+ *   x [H] (x_dtype) unless io.residual is set (then x is ignored).
+ *   idx_in: if not NULL, [k_in] int32 block ids replace the router (rw may
+ *   then be NULL).  y [H] in y_dtype: the MLP output (the partial over the
+ *   blocks present here when the map selects a shard).
+ *   idx_out/score_out (may be NULL): the router's selection. */
+int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_t intermediate,
+                          const nsm_layer_io* io, const nsm_router_weights* rw, const int32_t* idx_in,
+                          int32_t k_in, const nsm_block_map* map, const nsm_mlp_weights* w, void* y,
+                          int32_t y_dtype, int32_t* idx_out, float* score_out, void* ws, size_t ws_bytes,
+                          nsm_stream_t stream);
+
+/* Decode MLP on blocks the caller already gathered, in the reference
+ * runtime's layout: gate/up [U][32][H/2] + [U][32][H/64], down [H][U][16] +
+ * [H][U].  Replaces triton_sparse_mlp_decode_4bit_single_kernel_sm75
+ * (triton_sparse_mlp.py:1378-1516) and the rows == 1 use of
+ * _sparse_mlp_forward_fast_triton (streaming_llama_runtime.py:5579-5625);
+ * unlike the reference it is not restricted to sm_75.
+ *   act_out [U*32] fp32 (may be NULL): SiLU(gate)*up. */
+int nsm_decode_gathered(const void* x, int32_t x_dtype, int32_t hidden, int32_t num_blocks_gathered,
+                        const nsm_mlp_weights* w, void* y, int32_t y_dtype, float* act_out, void* ws,
+                        size_t ws_bytes, nsm_stream_t stream);
+
+/* Multi-row decode on gathered blocks with the reference's per-row mask:
+ * y[r] = down(silu(gate(x[r]) * flat_mask[r]) * (up(x[r]) * flat_mask[r])).
+ * Replaces the rows > 1 branch of _sparse_mlp_forward_fast
+ * (streaming_llama_runtime.py:5433-5492, layout from :4857-4908).
+ *   x [rows][H]; flat_mask [rows][U*32] (mask_dtype); y [rows][H]. */
+size_t nsm_decode_rows_workspace_bytes(int hidden, int num_blocks_gathered, int rows);
+int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32_t hidden,
+                             int32_t num_blocks_gathered, const void* flat_mask, int32_t mask_dtype,
+                             const nsm_mlp_weights* w, void* y, int32_t y_dtype, void* ws, size_t ws_bytes,
+                             nsm_stream_t stream);
+
+/* ---- layout helpers ----------------------------------------------------- */
+/* bitsandbytes down weight [H][I/2] + absmax [H][I/64] -> block-major
+ * [n][H][16] + [n][H] for the listed blocks (blocks == NULL: all I/32).
+ * Replaces the column extraction of _load_down_proj_cold_cols /
+ * _maybe_cache_down_proj_hot_columns (streaming_llama_runtime.py:4497-4513,
+ * :2664-2674). */
+int nsm_repack_down_block_major(const uint8_t* down_packed, const float* down_absmax, int32_t hidden,
+                                int32_t intermediate, const int32_t* blocks, int32_t n, uint8_t* out_packed,
+                                float* out_absmax, nsm_stream_t stream);
+
+/* ---- reference Triton API semantics --------------------------------------
+ * triton_sparse_input_linear_4bit (triton_sparse_mlp.py:1303-1337, kernels
+ * :437-575): out[r][n] = bias[n] + sum over slots of active_idx[r] >= 0 and
+ * i < block_size of W(e=(blk*bs+i)*out_features+n) * x[r][blk*bs+i].
+ * x, bias, out in act_dtype; accumulation fp32. */
+int nsm_sparse_input_linear_4bit(const void* x, int32_t act_dtype, int32_t rows, const int32_t* active_idx,
+                                 int32_t top_k, const uint8_t* packed, const float* absmax, const float* code,
+                                 int32_t out_features, int32_t in_features, int32_t quant_block_size,
+                                 const void* bias, int32_t block_size, void* out, nsm_stream_t stream);
+
+/* triton_sparse_output_linear_4bit (triton_sparse_mlp.py:1340-1375, kernel
+ * :578-651): out[r][blk*bs+o] = (bias[blk*bs+o] + sum_k W(e=k*bs+blk*bs+o) *
+ * x[r][k]) * flat_mask[r][blk*bs+o]; other columns 0.  out is [rows][width]. */
+int nsm_sparse_output_linear_4bit(const void* x, int32_t act_dtype, int32_t rows, const int32_t* active_idx,
+                                  int32_t top_k, const void* flat_mask, int32_t width, const uint8_t* packed,
+                                  const float* absmax, const float* code, int32_t input_dim,
+                                  int32_t quant_block_size, const void* bias, int32_t block_size, void* out,
+                                  nsm_stream_t stream);
+
+/* ---- VRAM hot-block cache ------------------------------------------------
+ * Device side of the reference's hot-block cache
+ * (streaming_llama_runtime.py:2619-2786, :2809-3018).  The policy
+ * (_plan_fixed_capacity_bank_update, :2577-2617) runs on the host; these
+ * move bytes and tables.
+ * nsm_cache_split: for idx[k] and slot_of_block[NB], writes hit_rows[] (pool
+ * rows of resident blocks, in idx order), miss_pos[] (positions in idx of
+ * the misses) and counts[2] = {hits, misses} (all device). */
+int nsm_cache_split(const int32_t* idx, int32_t k, const int32_t* slot_of_block, int32_t num_blocks,
+                    int32_t* hit_rows, int32_t* miss_pos, int32_t* counts, nsm_stream_t stream);
+
+/* Copies pool rows src_rows[i] -> dst_rows[i] (gate, up, down and absmax of
+ * each block) inside the same pools and sets slot_of_block[block_ids[i]] =
+ * dst_rows[i], slot_of_block[evicted_ids[i]] = -1 when evicted_ids[i] >= 0.
+ * Replaces the promotion copies of _promote_down_proj_hot_columns_from_gpu
+ * (:2995-3003) and _promote_sparse_param_hot_blocks_from_gpu (:2872-2877). */
+int nsm_cache_promote(const nsm_mlp_weights* w, int32_t hidden, const int32_t* src_rows, const int32_t* dst_rows,
+                      const int32_t* block_ids, const int32_t* evicted_ids, int32_t n, int32_t* slot_of_block,
+                      nsm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NSM_H_ */

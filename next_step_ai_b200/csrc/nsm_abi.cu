@@ -1,0 +1,135 @@
+// nsm_abi.cu -- status strings, per-thread error detail, device checks and the
+// decode workspace layout.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "nsm_internal.h"
+
+namespace nsm {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int status, const std::string& msg) {
+  g_last_error = msg;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return NSM_ERR_CUDA;
+}
+
+static std::mutex g_dev_mu;
+static DeviceInfo g_dev_cache[64];
+
+int current_device(DeviceInfo* info) {
+  int dev = -1;
+  NSM_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(NSM_ERR_DEVICE, "device index out of range");
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (g_dev_cache[dev].device == dev) {
+      *info = g_dev_cache[dev];
+      return NSM_OK;
+    }
+  }
+  DeviceInfo d;
+  d.device = dev;
+  NSM_CHECK_CUDA(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev));
+  NSM_CHECK_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
+  NSM_CHECK_CUDA(cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev));
+  NSM_CHECK_CUDA(cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  if (d.major != 10 || d.minor != 0) {
+    char buf[128];
+    snprintf(buf, sizeof(buf), "this library is built for sm_100a (B200); device %d is sm_%d%d", dev, d.major,
+             d.minor);
+    return fail(NSM_ERR_DEVICE, buf);
+  }
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  g_dev_cache[dev] = d;
+  *info = d;
+  return NSM_OK;
+}
+
+size_t decode_ws_counter_bytes(int hidden, int top_k) {
+  size_t off = 0;
+  off = align_up(off + 2 * sizeof(int), 256);
+  off = align_up(off + (size_t)top_k * sizeof(int), 256);
+  off = align_up(off + (size_t)(hidden / 32) * sizeof(int), 256);
+  return off;
+}
+
+DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank) {
+  DecodeWs w{};
+  char* b = reinterpret_cast<char*>(base);
+  size_t off = 0;
+  auto take = [&](size_t bytes) -> char* {
+    char* p = b ? b + off : nullptr;
+    off = align_up(off + bytes, 256);
+    return p;
+  };
+  const int nb = intermediate / 32;
+  char* tick = take(2 * sizeof(int));
+  w.ticket_router_a = reinterpret_cast<int*>(tick);
+  w.ticket_router_b = w.ticket_router_a ? w.ticket_router_a + 1 : nullptr;
+  w.ticket_slot = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
+  w.ticket_rowtile = reinterpret_cast<int*>(take((size_t)(hidden / 32) * sizeof(int)));
+  w.latent_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * rank * sizeof(float)));
+  w.sumsq_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * sizeof(float)));
+  w.latent = reinterpret_cast<float*>(take((size_t)rank * sizeof(float)));
+  w.norm_scale = reinterpret_cast<float*>(take(sizeof(float)));
+  w.scores = reinterpret_cast<float*>(take((size_t)nb * sizeof(float)));
+  w.x16 = reinterpret_cast<__half*>(take((size_t)hidden * sizeof(__half)));
+  w.xscale = reinterpret_cast<float*>(take((size_t)(hidden / 64) * sizeof(float)));
+  w.rows = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
+  w.count = reinterpret_cast<int*>(take(sizeof(int)));
+  w.sel_idx = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
+  w.row_block = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
+  w.gu_part = reinterpret_cast<float*>(take((size_t)top_k * kMaxUnitsPerSlot * 64 * sizeof(float)));
+  w.act16 = reinterpret_cast<__half*>(take((size_t)top_k * 32 * sizeof(__half)));
+  w.act_scale = reinterpret_cast<float*>(take((size_t)top_k * sizeof(float)));
+  w.ypart = reinterpret_cast<float*>(take((size_t)kMaxSlotGroups * hidden * sizeof(float)));
+  w.bytes = off;
+  return w;
+}
+
+}  // namespace nsm
+
+using namespace nsm;
+
+extern "C" {
+
+int nsm_abi_version(void) { return 1; }
+
+const char* nsm_status_string(int status) {
+  switch (status) {
+    case NSM_OK: return "ok";
+    case NSM_ERR_INVALID_ARG: return "invalid argument";
+    case NSM_ERR_UNSUPPORTED: return "unsupported shape";
+    case NSM_ERR_CUDA: return "CUDA error";
+    case NSM_ERR_TIMEOUT: return "device wait timed out";
+    case NSM_ERR_WORKSPACE: return "workspace missing or too small";
+    case NSM_ERR_DEVICE: return "unsupported device";
+    default: return "unknown status";
+  }
+}
+
+const char* nsm_last_error(void) { return g_last_error.c_str(); }
+
+int nsm_workspace_init(void* ws, size_t ws_bytes, nsm_stream_t stream) {
+  if (ws == nullptr || ws_bytes == 0) return fail(NSM_ERR_WORKSPACE, "nsm_workspace_init: empty workspace");
+  NSM_CHECK_CUDA(cudaMemsetAsync(ws, 0, ws_bytes, reinterpret_cast<cudaStream_t>(stream)));
+  return NSM_OK;
+}
+
+size_t nsm_decode_workspace_bytes(int hidden, int intermediate, int top_k, int rank) {
+  if (hidden <= 0 || intermediate <= 0 || top_k <= 0 || rank <= 0) return 0;
+  return decode_ws_layout(nullptr, hidden, intermediate, top_k, rank).bytes;
+}
+
+}  // extern "C"

@@ -1,0 +1,299 @@
+// nsm_aux.cu -- layout repack, the reference's generic 4-bit linear API
+// semantics, and the device side of the VRAM hot-block cache.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "nsm_common.cuh"
+#include "nsm_internal.h"
+
+namespace nsm {
+
+// ---------------------------------------------------------------------------
+// down weight [H][I/2] (+ absmax [H][I/64]) -> block-major [n][H][16] + [n][H]
+// ---------------------------------------------------------------------------
+__global__ void repack_down_kernel(const uint8_t* __restrict__ src, const float* __restrict__ src_am, int H, int I,
+                                   const int32_t* __restrict__ blocks, int n, uint8_t* __restrict__ dst,
+                                   float* __restrict__ dst_am) {
+  const int64_t total = (int64_t)n * H;
+  const int64_t bpr = I / 2, apr = I / 64;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int slot = (int)(i / H), h = (int)(i - (int64_t)slot * H);
+    const int b = blocks ? blocks[slot] : slot;
+    const uint4 v = *reinterpret_cast<const uint4*>(src + (int64_t)h * bpr + (int64_t)b * 16);
+    *reinterpret_cast<uint4*>(dst + ((int64_t)slot * H + h) * 16) = v;
+    dst_am[(int64_t)slot * H + h] = src_am[(int64_t)h * apr + (b >> 1)];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// triton_sparse_input_linear_4bit semantics (NF4 of weight.t(): element index
+// e = in_idx * out_features + out_idx).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float nf4_elem(const uint8_t* packed, const float* absmax, const float* code, int64_t e,
+                                          int qbs) {
+  const uint8_t byte = packed[e >> 1];
+  const int nib = (e & 1) ? (byte & 0x0f) : (byte >> 4);
+  return code[nib] * absmax[e / qbs];
+}
+
+__global__ void input_linear_4bit_kernel(const void* x, int dt, int rows, const int32_t* idx, int k,
+                                         const uint8_t* packed, const float* absmax, const float* code, int out_f,
+                                         int in_f, int qbs, const void* bias, int bs, void* out) {
+  __shared__ float scode[16];
+  if (threadIdx.x < 16) scode[threadIdx.x] = code[threadIdx.x];
+  __syncthreads();
+  const int r = blockIdx.y;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= out_f) return;
+  float acc = bias ? load_as_f32(bias, dt, n) : 0.f;
+  for (int s = 0; s < k; ++s) {
+    const int blk = idx[(int64_t)r * k + s];
+    if (blk < 0) continue;
+    for (int i = 0; i < bs; ++i) {
+      const int col = blk * bs + i;
+      if (col >= in_f) break;
+      const int64_t e = (int64_t)col * out_f + n;
+      acc = fmaf(nf4_elem(packed, absmax, scode, e, qbs), load_as_f32(x, dt, (int64_t)r * in_f + col), acc);
+    }
+  }
+  store_from_f32(out, dt, (int64_t)r * out_f + n, acc);
+}
+
+// triton_sparse_output_linear_4bit semantics: e = k*bs + blk*bs + o.
+__global__ void output_linear_4bit_kernel(const void* x, int dt, int rows, const int32_t* idx, int k,
+                                          const void* mask, int width, const uint8_t* packed, const float* absmax,
+                                          const float* code, int din, int qbs, const void* bias, int bs, void* out) {
+  __shared__ float scode[16];
+  if (threadIdx.x < 16) scode[threadIdx.x] = code[threadIdx.x];
+  __syncthreads();
+  const int r = blockIdx.y / k, s = blockIdx.y - (blockIdx.y / k) * k;
+  const int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= bs) return;
+  const int blk = idx[(int64_t)r * k + s];
+  if (blk < 0) return;
+  const int col = blk * bs + o;
+  if (col >= width) return;
+  float acc = bias ? load_as_f32(bias, dt, col) : 0.f;
+  for (int kk = 0; kk < din; ++kk) {
+    const int64_t e = (int64_t)kk * bs + col;
+    acc = fmaf(nf4_elem(packed, absmax, scode, e, qbs), load_as_f32(x, dt, (int64_t)r * din + kk), acc);
+  }
+  const float m = mask ? load_as_f32(mask, dt, (int64_t)r * width + col) : 1.f;
+  store_from_f32(out, dt, (int64_t)r * width + col, acc * m);
+}
+
+// ---------------------------------------------------------------------------
+// hot-block cache
+// ---------------------------------------------------------------------------
+__global__ void cache_split_kernel(const int32_t* idx, int k, const int32_t* slot_of_block, int nb, int32_t* hit_rows,
+                                   int32_t* miss_pos, int32_t* counts) {
+  __shared__ int wh[32], wm[32];
+  __shared__ int base_h, base_m;
+  if (threadIdx.x == 0) base_h = base_m = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int j0 = 0; j0 < k; j0 += blockDim.x) {
+    const int j = j0 + threadIdx.x;
+    int row = -1;
+    bool valid = false;
+    if (j < k) {
+      const int b = idx[j];
+      valid = b >= 0 && b < nb;
+      row = valid ? slot_of_block[b] : -1;
+    }
+    const bool hit = valid && row >= 0;
+    const bool miss = valid && row < 0;
+    const unsigned bh = __ballot_sync(0xffffffffu, hit), bm = __ballot_sync(0xffffffffu, miss);
+    if (lane == 0) {
+      wh[warp] = __popc(bh);
+      wm[warp] = __popc(bm);
+    }
+    __syncthreads();
+    int oh = 0, om = 0;
+    for (int w = 0; w < warp; ++w) {
+      oh += wh[w];
+      om += wm[w];
+    }
+    const unsigned lt = (1u << lane) - 1u;
+    if (hit) hit_rows[base_h + oh + __popc(bh & lt)] = row;
+    if (miss) miss_pos[base_m + om + __popc(bm & lt)] = j;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 0; w < nw; ++w) {
+        base_h += wh[w];
+        base_m += wm[w];
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    counts[0] = base_h;
+    counts[1] = base_m;
+  }
+}
+
+__device__ __forceinline__ void copy_bytes(uint8_t* dst, const uint8_t* src, int64_t n, int tid, int nthr) {
+  const int64_t n16 = n / 16;
+  for (int64_t i = tid; i < n16; i += nthr)
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  for (int64_t i = n16 * 16 + tid; i < n; i += nthr) dst[i] = src[i];
+}
+
+struct PromoteParams {
+  uint8_t* gate;
+  float* gate_am;
+  uint8_t* up;
+  float* up_am;
+  uint8_t* down;
+  float* down_am;
+  int64_t gstride, gastride, dbs, dabs;
+  int H;
+  const int32_t* src;
+  const int32_t* dst;
+};
+
+__global__ void cache_promote_copy_kernel(PromoteParams p) {
+  const int i = blockIdx.y;
+  const int s = p.src[i], d = p.dst[i];
+  const int nthr = gridDim.x * blockDim.x, tid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t gb = (int64_t)16 * p.H;          // 32 rows * H/2 bytes
+  const int64_t gab = (int64_t)(p.H / 2) * 4;    // 32 rows * H/64 floats
+  copy_bytes(p.gate + d * p.gstride, p.gate + s * p.gstride, gb, tid, nthr);
+  copy_bytes(p.up + d * p.gstride, p.up + s * p.gstride, gb, tid, nthr);
+  copy_bytes(reinterpret_cast<uint8_t*>(p.gate_am + d * p.gastride),
+             reinterpret_cast<const uint8_t*>(p.gate_am + s * p.gastride), gab, tid, nthr);
+  copy_bytes(reinterpret_cast<uint8_t*>(p.up_am + d * p.gastride),
+             reinterpret_cast<const uint8_t*>(p.up_am + s * p.gastride), gab, tid, nthr);
+  copy_bytes(p.down + d * p.dbs, p.down + s * p.dbs, (int64_t)16 * p.H, tid, nthr);
+  copy_bytes(reinterpret_cast<uint8_t*>(p.down_am + d * p.dabs),
+             reinterpret_cast<const uint8_t*>(p.down_am + s * p.dabs), (int64_t)4 * p.H, tid, nthr);
+}
+
+__global__ void cache_table_update_kernel(const int32_t* block_ids, const int32_t* evicted, const int32_t* dst, int n,
+                                          int32_t* slot_of_block) {
+  // evictions first, then installs (single thread keeps the order exact)
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  for (int i = 0; i < n; ++i)
+    if (evicted && evicted[i] >= 0) slot_of_block[evicted[i]] = -1;
+  for (int i = 0; i < n; ++i) slot_of_block[block_ids[i]] = dst[i];
+}
+
+static int dtype_ok(int d) { return d == NSM_F32 || d == NSM_F16 || d == NSM_BF16; }
+
+}  // namespace nsm
+
+using namespace nsm;
+
+extern "C" {
+
+int nsm_repack_down_block_major(const uint8_t* down_packed, const float* down_absmax, int32_t hidden,
+                                int32_t intermediate, const int32_t* blocks, int32_t n, uint8_t* out_packed,
+                                float* out_absmax, nsm_stream_t stream) {
+  NSM_REQUIRE(down_packed && down_absmax && out_packed && out_absmax, NSM_ERR_INVALID_ARG, "NULL pointer");
+  NSM_REQUIRE(hidden > 0 && intermediate > 0 && intermediate % 64 == 0, NSM_ERR_UNSUPPORTED,
+              "intermediate must be a positive multiple of 64");
+  NSM_REQUIRE(((uintptr_t)down_packed & 15) == 0 && ((uintptr_t)out_packed & 15) == 0, NSM_ERR_INVALID_ARG,
+              "packed pointers must be 16-byte aligned");
+  const int nb = intermediate / 32;
+  const int cnt = blocks ? n : nb;
+  NSM_REQUIRE(cnt > 0, NSM_ERR_INVALID_ARG, "nothing to repack");
+  const int64_t total = (int64_t)cnt * hidden;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+  repack_down_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(down_packed, down_absmax, hidden,
+                                                                                intermediate, blocks, cnt,
+                                                                                out_packed, out_absmax);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+int nsm_sparse_input_linear_4bit(const void* x, int32_t act_dtype, int32_t rows, const int32_t* active_idx,
+                                 int32_t top_k, const uint8_t* packed, const float* absmax, const float* code,
+                                 int32_t out_features, int32_t in_features, int32_t quant_block_size,
+                                 const void* bias, int32_t block_size, void* out, nsm_stream_t stream) {
+  NSM_REQUIRE(dtype_ok(act_dtype), NSM_ERR_INVALID_ARG, "bad activation dtype");
+  NSM_REQUIRE(block_size > 0, NSM_ERR_INVALID_ARG, "block_size must be > 0 for triton_sparse_input_linear_4bit");
+  NSM_REQUIRE(in_features % block_size == 0, NSM_ERR_INVALID_ARG, "in_features must be divisible by block_size");
+  NSM_REQUIRE(quant_block_size > 0, NSM_ERR_INVALID_ARG, "quant_block_size must be > 0");
+  NSM_REQUIRE(out != nullptr, NSM_ERR_INVALID_ARG, "out is NULL");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (rows <= 0 || out_features <= 0) return NSM_OK;
+  NSM_REQUIRE(x && packed && absmax && code, NSM_ERR_INVALID_ARG, "NULL pointer");
+  NSM_REQUIRE(top_k == 0 || active_idx != nullptr, NSM_ERR_INVALID_ARG, "active_idx is NULL");
+  dim3 grid((out_features + 255) / 256, rows);
+  input_linear_4bit_kernel<<<grid, 256, 0, s>>>(x, act_dtype, rows, active_idx, top_k, packed, absmax, code,
+                                                 out_features, in_features, quant_block_size, bias, block_size, out);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+int nsm_sparse_output_linear_4bit(const void* x, int32_t act_dtype, int32_t rows, const int32_t* active_idx,
+                                  int32_t top_k, const void* flat_mask, int32_t width, const uint8_t* packed,
+                                  const float* absmax, const float* code, int32_t input_dim,
+                                  int32_t quant_block_size, const void* bias, int32_t block_size, void* out,
+                                  nsm_stream_t stream) {
+  NSM_REQUIRE(dtype_ok(act_dtype), NSM_ERR_INVALID_ARG, "bad activation dtype");
+  NSM_REQUIRE(block_size > 0, NSM_ERR_INVALID_ARG, "block_size must be > 0 for triton_sparse_output_linear_4bit");
+  NSM_REQUIRE(input_dim % block_size == 0, NSM_ERR_INVALID_ARG, "input_dim must be divisible by block_size");
+  NSM_REQUIRE(quant_block_size > 0, NSM_ERR_INVALID_ARG, "quant_block_size must be > 0");
+  NSM_REQUIRE(out != nullptr && width >= 0, NSM_ERR_INVALID_ARG, "out is NULL");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int es = act_dtype == NSM_F32 ? 4 : 2;
+  if (rows <= 0 || width == 0) return NSM_OK;
+  NSM_CHECK_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * width * es, s));
+  if (top_k <= 0) return NSM_OK;
+  NSM_REQUIRE(x && packed && absmax && code && active_idx, NSM_ERR_INVALID_ARG, "NULL pointer");
+  dim3 grid((block_size + 127) / 128, rows * top_k);
+  output_linear_4bit_kernel<<<grid, 128, 0, s>>>(x, act_dtype, rows, active_idx, top_k, flat_mask, width, packed,
+                                                  absmax, code, input_dim, quant_block_size, bias, block_size, out);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+int nsm_cache_split(const int32_t* idx, int32_t k, const int32_t* slot_of_block, int32_t num_blocks, int32_t* hit_rows,
+                    int32_t* miss_pos, int32_t* counts, nsm_stream_t stream) {
+  NSM_REQUIRE(idx && slot_of_block && hit_rows && miss_pos && counts, NSM_ERR_INVALID_ARG, "NULL pointer");
+  NSM_REQUIRE(k > 0 && num_blocks > 0, NSM_ERR_INVALID_ARG, "k and num_blocks must be > 0");
+  cache_split_kernel<<<1, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(idx, k, slot_of_block, num_blocks,
+                                                                            hit_rows, miss_pos, counts);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+int nsm_cache_promote(const nsm_mlp_weights* w, int32_t hidden, const int32_t* src_rows, const int32_t* dst_rows,
+                      const int32_t* block_ids, const int32_t* evicted_ids, int32_t n, int32_t* slot_of_block,
+                      nsm_stream_t stream) {
+  NSM_REQUIRE(w != nullptr, NSM_ERR_INVALID_ARG, "weights descriptor is NULL");
+  NSM_REQUIRE(src_rows && dst_rows && block_ids && slot_of_block, NSM_ERR_INVALID_ARG, "NULL pointer");
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0, NSM_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  const bool block_major = (w->down_block_stride == 0 || w->down_block_stride == (int64_t)16 * hidden) &&
+                           (w->down_row_stride == 0 || w->down_row_stride == 16) &&
+                           (w->down_absmax_row_stride == 0 || w->down_absmax_row_stride == 1) &&
+                           w->down_absmax_pair == 0;
+  NSM_REQUIRE(block_major, NSM_ERR_UNSUPPORTED, "cache pools must use the block-major down layout");
+  if (n <= 0) return NSM_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  PromoteParams p{};
+  p.gate = const_cast<uint8_t*>(w->gate_packed);
+  p.gate_am = const_cast<float*>(w->gate_absmax);
+  p.up = const_cast<uint8_t*>(w->up_packed);
+  p.up_am = const_cast<float*>(w->up_absmax);
+  p.down = const_cast<uint8_t*>(w->down_packed);
+  p.down_am = const_cast<float*>(w->down_absmax);
+  p.gstride = w->gateup_block_stride ? w->gateup_block_stride : (int64_t)16 * hidden;
+  p.gastride = w->gateup_absmax_block_stride ? w->gateup_absmax_block_stride : (int64_t)hidden / 2;
+  p.dbs = (int64_t)16 * hidden;
+  p.dabs = w->down_absmax_block_stride ? w->down_absmax_block_stride : hidden;
+  p.H = hidden;
+  p.src = src_rows;
+  p.dst = dst_rows;
+  dim3 grid(16, n);
+  cache_promote_copy_kernel<<<grid, 256, 0, s>>>(p);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  cache_table_update_kernel<<<1, 32, 0, s>>>(block_ids, evicted_ids, dst_rows, n, slot_of_block);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+}  // extern "C"

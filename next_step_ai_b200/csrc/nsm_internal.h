@@ -1,0 +1,90 @@
+// nsm_internal.h -- host-side helpers shared by the ABI translation units:
+// error reporting, device checks, and the decode workspace layout.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/nsm.h"
+
+namespace nsm {
+
+// Thread-local detail for nsm_last_error().
+void set_error(const std::string& msg);
+int fail(int status, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define NSM_CHECK_CUDA(expr)                         \
+  do {                                               \
+    cudaError_t _e = (expr);                         \
+    if (_e != cudaSuccess) return cuda_fail(_e, #expr); \
+  } while (0)
+
+#define NSM_REQUIRE(cond, status, msg) \
+  do {                                 \
+    if (!(cond)) return fail((status), (msg)); \
+  } while (0)
+
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int major = 0, minor = 0;
+  int max_smem_optin = 0;
+};
+// Current device's properties (cached per device); status != 0 if not sm_100.
+int current_device(DeviceInfo* info);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Limits of the single-token decode path.
+constexpr int kMaxRank = 256;
+constexpr int kMaxTopK = 4096;
+constexpr int kMaxNumBlocks = 8192;     // top-k sort capacity of the router
+constexpr int kMaxUnitsPerSlot = 64;    // gate/up column splits per block
+constexpr int kMaxSlotGroups = 32;      // down split-K groups
+constexpr int kRouterMaxCtas = 256;
+
+// Decode workspace: one contiguous caller-owned buffer, 256-byte aligned parts.
+struct DecodeWs {
+  // counters (must be zero between calls)
+  int* ticket_router_a;          // [1]
+  int* ticket_router_b;          // [1]
+  int* ticket_slot;              // [top_k]
+  int* ticket_rowtile;           // [H/32]
+  // router
+  float* latent_part;            // [kRouterMaxCtas][rank]
+  float* sumsq_part;             // [kRouterMaxCtas]
+  float* latent;                 // [rank]
+  float* norm_scale;             // [1]
+  float* scores;                 // [NB]
+  // activations
+  __half* x16;                   // [H]
+  float* xscale;                 // [H/64]
+  int* rows;                     // [top_k]
+  int* count;                    // [1]
+  int* sel_idx;                  // [top_k] router selection (when no idx_out)
+  int* row_block;                // [top_k] block id of each compacted pool row
+  float* gu_part;                // [top_k][kMaxUnitsPerSlot][2][32]
+  __half* act16;                 // [top_k][32]
+  float* act_scale;              // [top_k]
+  float* ypart;                  // [kMaxSlotGroups][H]
+  size_t bytes;
+};
+
+// counters live first so a single memset of the head re-zeroes them
+DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank);
+size_t decode_ws_counter_bytes(int hidden, int top_k);
+
+// Cached occupancy-derived persistent grid sizes.
+struct LaunchShape {
+  int gateup_ctas = 0;
+  int down_ctas = 0;
+  int warps_per_cta = 8;
+};
+int launch_shape(LaunchShape* s);
+
+}  // namespace nsm

@@ -1,0 +1,455 @@
+"""GPU parity of the sm_100a decode path against the CPU oracle and the
+reference's golden vectors.  Everything calls through libnsm.so's C ABI.
+
+Tolerances (from the build's contract): selected block indices bit-exact
+(same blocks, same order, ties to the lower index); MLP outputs within
+max-abs-err <= 2e-2 and relative L2 <= 5e-3 of the fp32 oracle when the
+kernel writes fp32.  For bf16 output the bf16 rounding of the result itself
+is added to the absolute bound (half an ulp of the reference value).
+"""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+from oracle import layout as lay  # noqa: E402
+from oracle import linear4bit as l4  # noqa: E402
+from oracle import mlp as om  # noqa: E402
+from oracle import router as orr  # noqa: E402
+from oracle import synthetic as syn  # noqa: E402
+from oracle.nf4 import bf16_round  # noqa: E402
+
+MAX_ABS = 2e-2
+REL_L2 = 5e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from next_step_ai_b200 import _lib
+
+    _lib.load()
+    return torch.device("cuda", 0)
+
+
+def T(a, dev, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t.to(dtype) if dtype is not None else t
+
+
+def assert_close(got, ref, *, bf16_out=False):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rel = np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
+    bound = MAX_ABS + (np.abs(ref) * 2.0 ** -8 if bf16_out else 0.0)
+    err = np.abs(got - ref)
+    assert rel <= REL_L2, f"relative L2 {rel:.3e} > {REL_L2}"
+    assert np.all(err <= bound), f"max abs err {err.max():.3e} (bound {MAX_ABS})"
+    return rel, float(err.max())
+
+
+def router_for(shape, R, dev, dtype=torch.bfloat16, **kw):
+    from next_step_ai_b200 import RouterWeights
+
+    return RouterWeights(enc_w=T(R["enc_w"], dev, dtype), score_w=T(R["score_w"], dev, dtype),
+                         enc_b=T(R["enc_b"], dev, dtype), score_b=T(R["score_b"], dev, dtype),
+                         top_k=kw.pop("top_k", shape.top_k), basis_top_k=kw.pop("basis_top_k", shape.rank), **kw)
+
+
+def weights_for(shape, full, dev):
+    from next_step_ai_b200 import SparseMlpWeights
+
+    return SparseMlpWeights.from_bnb_rowmajor(
+        hidden=shape.hidden, intermediate=shape.intermediate, gate_packed=T(full["gate_packed"], dev),
+        gate_absmax=T(full["gate_absmax"], dev), up_packed=T(full["up_packed"], dev),
+        up_absmax=T(full["up_absmax"], dev), down_packed=T(full["down_packed"], dev),
+        down_absmax=T(full["down_absmax"], dev), code=T(full["code"], dev))
+
+
+_FULL_CACHE: dict = {}
+
+
+def full_layer(name, seed):
+    key = (name, seed)
+    if key not in _FULL_CACHE:
+        _FULL_CACHE[key] = syn.make_layer_full(syn.SHAPES[name], seed)
+    return _FULL_CACHE[key]
+
+
+# --------------------------------------------------------------------------- router
+@pytest.mark.parametrize("name,rows", [("tiny", 3), ("small", 2), ("cfg0", 4), ("cfg1", 4)])
+def test_router_bit_exact(dev, name, rows):
+    from next_step_ai_b200 import route_sparse_mlp
+
+    shape = syn.SHAPES[name]
+    for seed in (0, 1):
+        R = syn.make_router(shape, seed)
+        x = syn.make_x(shape, seed, rows)
+        ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)
+        got, scores = route_sparse_mlp(T(x, dev, torch.bfloat16), router_for(shape, R, dev), return_scores=True)
+        assert np.array_equal(got.cpu().numpy(), ref), (name, seed)
+        lat = orr.basis_latent(x, R["enc_w"], R["enc_b"], shape.rank)
+        s_ref = orr.block_scores(lat, R["score_w"], R["score_b"])
+        s_ref_sel = np.take_along_axis(s_ref, ref, axis=1)
+        assert np.allclose(scores.cpu().numpy(), s_ref_sel, rtol=1e-4, atol=1e-5)
+
+
+def test_router_golden_cfg1(dev, golden):
+    """Indices pinned by the reference's own _route_sparse_mlp (fp32)."""
+    from next_step_ai_b200 import route_sparse_mlp
+
+    cases = {c["name"]: c for c in json.loads(bytes(golden["router/cases.json"]).decode())}
+    for name in ("cfg0_r1", "cfg0_r8", "cfg1_r1", "cfg1_r4"):
+        c = cases[name]
+        shape = syn.SHAPES[c["shape"]]
+        R = syn.make_router(shape, c["seed"])
+        x = syn.make_x(shape, c["seed"], c["rows"])
+        got = route_sparse_mlp(T(x, dev, torch.bfloat16), router_for(shape, R, dev))
+        assert np.array_equal(got.cpu().numpy(), golden[f"router/{name}/idx"]), name
+
+
+def test_router_fp32_weights_and_variants(dev):
+    from next_step_ai_b200 import route_sparse_mlp
+
+    shape = syn.SHAPES["small"]
+    R = syn.make_router(shape, 4)
+    x = syn.make_x(shape, 4, 3)
+    xd = T(x, dev, torch.float32)
+    # fp32 router weights
+    got = route_sparse_mlp(xd, router_for(shape, R, dev, torch.float32))
+    ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)
+    assert np.array_equal(got.cpu().numpy(), ref)
+    # basis top-k < rank
+    got = route_sparse_mlp(xd, router_for(shape, R, dev, torch.float32, basis_top_k=7))
+    ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, 7)
+    assert np.array_equal(got.cpu().numpy(), ref)
+    # down_block_norm
+    dbn = np.random.default_rng(3).uniform(0.5, 1.5, shape.num_blocks).astype(np.float32)
+    got = route_sparse_mlp(xd, router_for(shape, R, dev, torch.float32, down_block_norm=T(dbn, dev)))
+    ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank,
+                               down_block_norm=dbn)
+    assert np.array_equal(got.cpu().numpy(), ref)
+    # prefill-style k override, and k clamped to NB
+    got = route_sparse_mlp(xd, router_for(shape, R, dev, torch.float32), top_k=5)
+    ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], 5, shape.rank)
+    assert np.array_equal(got.cpu().numpy(), ref)
+    got = route_sparse_mlp(xd, router_for(shape, R, dev, torch.float32), top_k=10 ** 6)
+    assert got.shape[1] == shape.num_blocks
+    ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.num_blocks, shape.rank)
+    assert np.array_equal(got.cpu().numpy(), ref)
+
+
+def test_router_legacy_abs_latent(dev):
+    from next_step_ai_b200 import RouterWeights, route_sparse_mlp
+
+    shape = syn.SHAPES["small"]
+    R = syn.make_router(shape, 6)
+    x = syn.make_x(shape, 6, 2)
+    dnt = np.abs(np.random.default_rng(7).standard_normal((shape.rank, shape.num_blocks))).astype(np.float32)
+    rw = RouterWeights(enc_w=T(R["enc_w"], dev), score_w=T(dnt.T, dev), enc_b=T(R["enc_b"], dev),
+                       top_k=shape.top_k, basis_top_k=shape.rank, legacy_abs_latent=True)
+    got = route_sparse_mlp(T(x, dev, torch.float32), rw)
+    ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], None, None, shape.top_k, shape.rank, dec_norm_t=dnt)
+    assert np.array_equal(got.cpu().numpy(), ref)
+
+
+def test_router_tie_break_lower_index(dev):
+    from next_step_ai_b200 import RouterWeights, route_sparse_mlp
+
+    # all-zero score head: every score is clamp0(bias); equal biases tie
+    H, r, NB = 128, 8, 40
+    enc = np.zeros((r, H), np.float32)
+    sw = np.zeros((NB, r), np.float32)
+    sb = np.zeros(NB, np.float32)
+    sb[[3, 7, 11, 30]] = 1.0
+    sb[[5, 9]] = 2.0
+    rw = RouterWeights(enc_w=T(enc, dev), score_w=T(sw, dev), score_b=T(sb, dev), top_k=8, basis_top_k=r)
+    got = route_sparse_mlp(torch.ones(1, H, device=dev), rw).cpu().numpy()[0]
+    assert got.tolist() == [5, 9, 3, 7, 11, 30, 0, 1]
+
+
+# --------------------------------------------------------------------------- decode, resident weights
+@pytest.mark.parametrize("name,seed", [("tiny", 11), ("small", 12), ("cfg0", 0)])
+def test_decode_resident_matches_oracle(dev, name, seed):
+    from next_step_ai_b200 import sparse_mlp_decode
+
+    shape = syn.SHAPES[name]
+    full = full_layer(name, seed)
+    R = syn.make_router(shape, seed)
+    w = weights_for(shape, full, dev)
+    rw = router_for(shape, R, dev)
+    for rowseed in range(2):
+        x = syn.make_x(shape, seed * 10 + rowseed, 1)[0]
+        idx = torch.empty(shape.top_k, dtype=torch.int32, device=dev)
+        y = sparse_mlp_decode(T(x, dev, torch.bfloat16), rw, w, out_dtype=torch.float32, idx_out=idx)
+        ref_idx = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k,
+                                       shape.rank)[0]
+        assert np.array_equal(idx.cpu().numpy(), ref_idx)
+        ref = om.sparse_mlp_full(x, ref_idx, full["gate_packed"], full["gate_absmax"], full["up_packed"],
+                                 full["up_absmax"], full["down_packed"], full["down_absmax"], full["code"],
+                                 hidden=shape.hidden, intermediate=shape.intermediate)[0]
+        assert_close(y.cpu().numpy(), ref)
+        yb = sparse_mlp_decode(T(x, dev, torch.bfloat16), rw, w, out_dtype=torch.bfloat16)
+        assert_close(yb.float().cpu().numpy(), ref, bf16_out=True)
+
+
+def test_decode_cfg1_device_generated(dev):
+    """Full 405B-shaped layer generated on the GPU; the oracle checks the
+    selected blocks copied back to the host."""
+    from next_step_ai_b200 import sparse_mlp_decode
+    from next_step_ai_b200 import synthetic as dsyn
+
+    shape = dsyn.SHAPES["cfg1"]
+    w, bnb = dsyn.make_layer_weights(shape, 0, 0, dev, keep_bnb=True)
+    rw = dsyn.make_router(shape, 0, 0, dev)
+    x = dsyn.make_x(shape, 0, 1, dev)[0]
+    idx = torch.empty(shape.top_k, dtype=torch.int32, device=dev)
+    y = sparse_mlp_decode(x, rw, w, out_dtype=torch.float32, idx_out=idx)
+    torch.cuda.synchronize()
+    sel = idx.cpu().numpy().astype(np.int64)
+    xn = x.float().cpu().numpy()
+    ref_idx = orr.route_sparse_mlp(xn, rw.enc_w.float().cpu().numpy(), rw.enc_b.float().cpu().numpy(),
+                                   rw.score_w.float().cpu().numpy(), rw.score_b.float().cpu().numpy(), shape.top_k,
+                                   shape.rank)[0]
+    assert np.array_equal(sel, ref_idx)
+    H, I = shape.hidden, shape.intermediate
+    gm = om.Nf4ParamMeta(I, H)
+    dmeta = om.Nf4ParamMeta(H, I)
+    s = torch.from_numpy(sel).to(dev)
+    gp = bnb["gate_packed"].view(-1, gm.bytes_per_block)[s].cpu().numpy()
+    ga = bnb["gate_absmax"].view(-1, gm.absmax_per_block)[s].cpu().numpy()
+    upk = bnb["up_packed"].view(-1, gm.bytes_per_block)[s].cpu().numpy()
+    ua = bnb["up_absmax"].view(-1, gm.absmax_per_block)[s].cpu().numpy()
+    dcols = w.down_packed[s].permute(1, 0, 2).contiguous().cpu().numpy()
+    dabs = w.down_absmax[s].t().contiguous().cpu().numpy()
+    code = bnb["code"].cpu().numpy()
+    ref = om.sparse_mlp_gathered(xn, gp, ga, code, upk, ua, code, dcols, dabs, code)[0]
+    assert_close(y.cpu().numpy(), ref)
+    # block-major down repack equals the reference column gather of the raw weight
+    raw_cols, raw_abs = om.gather_down_cols(bnb["down_packed"].cpu().numpy(), bnb["down_absmax"].cpu().numpy(),
+                                            dmeta, sel[:5])
+    assert np.array_equal(dcols[:, :5], raw_cols) and np.array_equal(dabs[:, :5], raw_abs)
+
+
+def test_decode_explicit_idx_and_shards_sum(dev):
+    from next_step_ai_b200 import sparse_mlp_decode
+
+    shape = syn.SHAPES["small"]
+    full = full_layer("small", 21)
+    w = weights_for(shape, full, dev)
+    x = syn.make_x(shape, 21, 1)[0]
+    sel = np.array([0, 127, 5, 64, 63, 17, 90], np.int64)
+    xd = T(x, dev, torch.bfloat16)
+    y = sparse_mlp_decode(xd, None, w, idx=T(sel, dev), out_dtype=torch.float32).cpu().numpy()
+    ref = om.sparse_mlp_full(x, sel, full["gate_packed"], full["gate_absmax"], full["up_packed"], full["up_absmax"],
+                             full["down_packed"], full["down_absmax"], full["code"], hidden=shape.hidden,
+                             intermediate=shape.intermediate)[0]
+    assert_close(y, ref)
+    # four shards over [0, NB): each pool holds its own blocks only
+    nb = shape.num_blocks
+    acc = np.zeros_like(ref)
+    for lo in range(0, nb, nb // 4):
+        hi = lo + nb // 4
+        from next_step_ai_b200 import SparseMlpWeights
+
+        ws = SparseMlpWeights(hidden=w.hidden, intermediate=w.intermediate, gate_packed=w.gate_packed[lo:hi].clone(),
+                              gate_absmax=w.gate_absmax[lo:hi].clone(), up_packed=w.up_packed[lo:hi].clone(),
+                              up_absmax=w.up_absmax[lo:hi].clone(), down_packed=w.down_packed[lo:hi].clone(),
+                              down_absmax=w.down_absmax[lo:hi].clone(), gate_code=w.gate_code, up_code=w.up_code,
+                              down_code=w.down_code)
+        acc += sparse_mlp_decode(xd, None, ws, idx=T(sel, dev), block_range=(lo, hi),
+                                 out_dtype=torch.float32).cpu().numpy()
+    assert_close(acc, ref)
+
+
+def test_decode_edge_cases(dev):
+    from next_step_ai_b200 import sparse_mlp_decode
+
+    shape = syn.SHAPES["tiny"]
+    full = full_layer("tiny", 3)
+    w = weights_for(shape, full, dev)
+    x = syn.make_x(shape, 3, 1)[0]
+    xd = T(x, dev, torch.bfloat16)
+    args = (full["gate_packed"], full["gate_absmax"], full["up_packed"], full["up_absmax"], full["down_packed"],
+            full["down_absmax"], full["code"])
+    kw = dict(hidden=shape.hidden, intermediate=shape.intermediate)
+    # k = 1 and k = all blocks
+    for sel in (np.array([9]), np.arange(shape.num_blocks)):
+        y = sparse_mlp_decode(xd, None, w, idx=T(sel, dev), out_dtype=torch.float32).cpu().numpy()
+        assert_close(y, om.sparse_mlp_full(x, sel, *args, **kw)[0])
+    # invalid ids are skipped (they are not present in the pool)
+    sel = np.array([-1, 4, 10 ** 6, 7], np.int64)
+    y = sparse_mlp_decode(xd, None, w, idx=T(sel, dev), out_dtype=torch.float32).cpu().numpy()
+    assert_close(y, om.sparse_mlp_full(x, np.array([4, 7]), *args, **kw)[0])
+    # a shard that holds none of the selected blocks returns zeros
+    y = sparse_mlp_decode(xd, None, w, idx=T(np.array([1, 2]), dev), block_range=(10, 20),
+                          out_dtype=torch.float32).cpu().numpy()
+    assert np.all(y == 0)
+    # bad shapes raise RuntimeError (no silent fallback)
+    with pytest.raises(RuntimeError):
+        sparse_mlp_decode(xd[:100], None, w, idx=T(np.array([1]), dev))
+
+
+def test_decode_deterministic(dev):
+    from next_step_ai_b200 import sparse_mlp_decode
+
+    shape = syn.SHAPES["cfg0"]
+    full = full_layer("cfg0", 0)
+    w = weights_for(shape, full, dev)
+    rw = router_for(shape, syn.make_router(shape, 0), dev)
+    xd = T(syn.make_x(shape, 0, 1)[0], dev, torch.bfloat16)
+    a = sparse_mlp_decode(xd, rw, w, out_dtype=torch.float32)
+    b = sparse_mlp_decode(xd, rw, w, out_dtype=torch.float32)
+    assert torch.equal(a, b)
+
+
+def test_decode_residual_rmsnorm(dev):
+    from next_step_ai_b200 import sparse_mlp_decode
+
+    shape = syn.SHAPES["small"]
+    full = full_layer("small", 12)
+    R = syn.make_router(shape, 12)
+    w = weights_for(shape, full, dev)
+    rw = router_for(shape, R, dev)
+    rng = np.random.default_rng(1)
+    resid = (rng.standard_normal(shape.hidden) * 3).astype(np.float32)
+    yprev = bf16_round((rng.standard_normal(shape.hidden)).astype(np.float32))
+    gamma = bf16_round(rng.uniform(0.5, 1.5, shape.hidden).astype(np.float32))
+    r_d = T(resid, dev)
+    idx = torch.empty(shape.top_k, dtype=torch.int32, device=dev)
+    y = sparse_mlp_decode(None, rw, w, residual=r_d, y_prev=T(yprev, dev, torch.bfloat16),
+                          norm_weight=T(gamma, dev, torch.bfloat16), eps=1e-5, out_dtype=torch.float32, idx_out=idx)
+    r_ref = resid + yprev
+    assert np.allclose(r_d.cpu().numpy(), r_ref, rtol=0, atol=0)
+    xn = om.rms_norm(r_ref, gamma, 1e-5)
+    ref_idx = orr.route_sparse_mlp(xn, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k,
+                                   shape.rank)[0]
+    assert np.array_equal(idx.cpu().numpy(), ref_idx)
+    ref = om.sparse_mlp_full(xn, ref_idx, full["gate_packed"], full["gate_absmax"], full["up_packed"],
+                             full["up_absmax"], full["down_packed"], full["down_absmax"], full["code"],
+                             hidden=shape.hidden, intermediate=shape.intermediate)[0]
+    assert_close(y.cpu().numpy(), ref)
+
+
+# --------------------------------------------------------------------------- reference-layout drop-ins
+@pytest.mark.parametrize("name", ["tiny_k4", "small_k16", "cfg0_k56"])
+def test_single_kernel_dropin_matches_reference_golden(dev, golden, name):
+    """The drop-in for triton_sparse_mlp_decode_4bit_single_kernel_sm75 against
+    the reference kernel's own output (Triton interpreter)."""
+    from next_step_ai_b200 import triton_sparse_mlp as tsm
+
+    case = {c["name"]: c for c in json.loads(bytes(golden["single/cases.json"]).decode())}[name]
+    shape = syn.SHAPES[case["shape"]]
+    blocks = golden[f"single/{name}/blocks"]
+    G = syn.selected_blocks_gathered(shape, case["seed"], 0, blocks)
+    x = syn.make_x(shape, case["seed"], 1)
+    H, k = shape.hidden, case["k"]
+    out = torch.empty((1, H), dtype=torch.float16, device=dev)
+    acc = torch.zeros(H, dtype=torch.float32, device=dev)
+    code = T(G["code"], dev)
+    res = tsm.triton_sparse_mlp_decode_4bit_single_kernel_sm75(
+        T(x, dev, torch.bfloat16), T(blocks, dev), T(G["gate_packed"], dev), T(G["gate_absmax"], dev), code,
+        T(G["up_packed"], dev), T(G["up_absmax"], dev), code, T(G["down_cols"], dev), T(G["down_absmax_cols"], dev),
+        code, out, acc, H, 32, 64, k)
+    ref = golden[f"single/{name}/y"]
+    assert_close(acc.cpu().numpy(), ref)
+    assert res.shape == (1, H) and res.dtype == torch.float16
+    with pytest.raises(RuntimeError, match="block_size=32"):
+        tsm.triton_sparse_mlp_decode_4bit_single_kernel_sm75(
+            T(x, dev, torch.bfloat16), T(blocks, dev), T(G["gate_packed"], dev), T(G["gate_absmax"], dev), code,
+            T(G["up_packed"], dev), T(G["up_absmax"], dev), code, T(G["down_cols"], dev),
+            T(G["down_absmax_cols"], dev), code, out, acc, H, 16, 64, k)
+
+
+def test_gathered_rows_with_flat_mask(dev):
+    from next_step_ai_b200 import decode_gathered_rows
+
+    shape = syn.SHAPES["small"]
+    rows = 5
+    X = syn.make_x(shape, 33, rows, shared=0.8)
+    R = syn.make_router(shape, 33)
+    ab = orr.route_sparse_mlp(X, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)
+    ordered, active_local, flat_mask, _ = lay.build_sparse_active_layout(ab, rows, 32, shape.num_blocks)
+    G = syn.selected_blocks_gathered(shape, 33, 0, ordered)
+    y = decode_gathered_rows(T(X, dev, torch.bfloat16), T(flat_mask, dev), gate_packed=T(G["gate_packed"], dev),
+                             gate_absmax=T(G["gate_absmax"], dev), gate_code=T(G["code"], dev),
+                             up_packed=T(G["up_packed"], dev), up_absmax=T(G["up_absmax"], dev),
+                             up_code=T(G["code"], dev), down_packed=T(G["down_cols"], dev),
+                             down_absmax=T(G["down_absmax_cols"], dev), down_code=T(G["code"], dev),
+                             out_dtype=torch.float32)
+    ref = om.sparse_mlp_gathered(X, G["gate_packed"], G["gate_absmax"], G["code"], G["up_packed"], G["up_absmax"],
+                                 G["code"], G["down_cols"], G["down_absmax_cols"], G["code"], flat_mask=flat_mask)
+    for r in range(rows):
+        assert_close(y[r].cpu().numpy(), ref[r])
+
+
+@pytest.mark.parametrize("name", ["in_a", "in_b", "in_c"])
+def test_input_linear_4bit_matches_reference_golden(dev, golden, name):
+    from next_step_ai_b200 import triton_sparse_mlp as tsm
+
+    c = {c["name"]: c for c in json.loads(bytes(golden["lin4/cases.json"]).decode())}[name]
+    p = f"lin4/{name}/"
+    bias = T(golden[p + "bias"], dev) if (p + "bias") in golden.files else None
+    out = tsm.triton_sparse_input_linear_4bit(
+        T(golden[p + "x"], dev), T(golden[p + "idx"], dev), packed_weight=T(golden[p + "packed"], dev),
+        absmax=T(golden[p + "absmax"], dev), code=T(golden["lin4/code"], dev), out_features=c["out_features"],
+        in_features=c["in_features"], quant_block_size=64, bias=bias, block_size=c["block_size"])
+    assert np.allclose(out.cpu().numpy(), golden[p + "y_tiled"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", ["out_a", "out_b", "out_c"])
+def test_output_linear_4bit_matches_reference_golden(dev, golden, name):
+    from next_step_ai_b200 import triton_sparse_mlp as tsm
+
+    c = {c["name"]: c for c in json.loads(bytes(golden["lin4/cases.json"]).decode())}[name]
+    p = f"lin4/{name}/"
+    bias = T(golden[p + "bias"], dev) if (p + "bias") in golden.files else None
+    out = tsm.triton_sparse_output_linear_4bit(
+        T(golden[p + "x"], dev), T(golden[p + "idx"], dev), T(golden[p + "mask"], dev),
+        packed_weight=T(golden[p + "packed"], dev), absmax=T(golden[p + "absmax"], dev),
+        code=T(golden["lin4/code"], dev), input_dim=c["input_dim"], quant_block_size=64, bias=bias,
+        block_size=c["block_size"])
+    assert np.allclose(out.cpu().numpy(), golden[p + "y"], rtol=1e-5, atol=1e-5)
+
+
+def test_fused_v1_composition_matches_oracle(dev):
+    from next_step_ai_b200 import triton_sparse_mlp as tsm
+
+    rng = np.random.default_rng(77)
+    code = syn.nf4_code()
+    rows, H, bs, nslots, k = 2, 64, 8, 4, 3
+    width = nslots * bs
+
+    def proj(n_elem):
+        return (rng.integers(0, 256, size=n_elem // 2, dtype=np.uint8),
+                rng.uniform(0.01, 0.1, size=n_elem // 64).astype(np.float32))
+
+    gp, ga = proj(((H * bs + width + 127) // 128) * 128)
+    upk, ua = proj(((H * bs + width + 127) // 128) * 128)
+    dp, da = proj(width * H)
+    x = rng.standard_normal((rows, H)).astype(np.float32)
+    idx = np.array([[0, 2, 3], [1, 2, 0]], np.int32)
+    mask = np.zeros((rows, width), np.float32)
+    for r in range(rows):
+        for s in idx[r]:
+            mask[r, s * bs:(s + 1) * bs] = 1
+    out = tsm.triton_fused_sparse_mlp_decode_4bit(
+        T(x, dev), T(idx, dev), T(mask, dev), gate_packed_weight=T(gp, dev), gate_absmax=T(ga, dev),
+        gate_code=T(code, dev), gate_input_dim=H, gate_quant_block_size=64, gate_bias=None,
+        up_packed_weight=T(upk, dev), up_absmax=T(ua, dev), up_code=T(code, dev), up_input_dim=H,
+        up_quant_block_size=64, up_bias=None, down_packed_weight=T(dp, dev), down_absmax=T(da, dev),
+        down_code=T(code, dev), down_out_features=H, down_in_features=width, down_quant_block_size=64,
+        down_bias=None, block_size=bs)
+    ref = l4.fused_sparse_mlp_decode_4bit(
+        x, idx, mask, gate={"packed": gp, "absmax": ga, "code": code, "input_dim": H, "quant_block_size": 64},
+        up={"packed": upk, "absmax": ua, "code": code, "input_dim": H, "quant_block_size": 64},
+        down={"packed": dp, "absmax": da, "code": code, "out_features": H, "in_features": width,
+              "quant_block_size": 64}, block_size=bs)
+    assert np.allclose(out.cpu().numpy(), ref, rtol=1e-4, atol=1e-4)
