@@ -1,0 +1,342 @@
+"""Benchmark: 126-layer 405B-shaped sparse-MLP decode step (tokens/s).
+
+Workload: per token, 126 decoder layers of hidden 16384,
+intermediate 53248 (1664 blocks of 32), learned-basis router rank 64, top-k
+208, NF4 gate/up/down weights (synthetic N(0, 0.02), seeded per layer); the
+residual is carried across layers with attention replaced by identity.
+Intermediate blocks are sharded across ranks (one process per GPU); the router
+is replicated and the bf16 [16384] partial outputs are summed with one NCCL
+all-reduce per layer.  On one GPU the 126 layers do not all fit in HBM
+(126 x 1.47 GB), so as many unique layers as fit are cycled; every layer is
+far larger than L2, so HBM traffic is unchanged.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+(N > 1 is launched with torch.distributed.run, one rank per GPU).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+HIDDEN, INTERMEDIATE, TOP_K, RANK, LAYERS = 16384, 53248, 208, 64, 126
+NB = INTERMEDIATE // 32
+METRIC = "sparse-MLP decode tok/s (126-layer 405B shape)"
+LAYER_BYTES_GPU = 3 * (INTERMEDIATE * HIDDEN // 2 + INTERMEDIATE * HIDDEN // 64 * 4)
+
+
+def algorithmic_bytes_per_layer(k: int = TOP_K, H: int = HIDDEN, nb: int = NB, rank: int = RANK) -> int:
+    """Bytes a layer-step must read or write: per selected block gate and up
+    (32*H/2 packed + 32*H/64 fp32 absmax each) and down (16*H packed + 4*H
+    absmax); router bf16 (rank*H encoder + NB*rank score head + NB bias);
+    x and y bf16."""
+    per_block = 2 * (16 * H + 2 * H) + 16 * H + 4 * H
+    router = 2 * rank * H + 2 * rank * nb + 2 * nb
+    return k * per_block + router + 4 * H
+
+
+def peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        try:
+            rows = [r.split(", ") for r in Path(self.path).read_text().strip().splitlines() if r.strip()]
+        except Exception:
+            return out
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except Exception:
+                continue
+        if sm:
+            out.update(sm_mhz=statistics.median(sm), sm_max_mhz=max(mx), reasons=sorted(reasons), samples=len(sm))
+        return out
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------------------------------- our arm
+def run_ours(args) -> None:
+    import torch
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+        group = torch.distributed.group.WORLD
+    from next_step_ai_b200 import synthetic as dsyn
+    from next_step_ai_b200.engine import DecodeLayer, SparseMlpDecoder
+    from next_step_ai_b200.weights import SparseMlpWeights
+
+    if NB % world:
+        raise SystemExit(f"{NB} blocks do not split over {world} ranks")
+    per = NB // world
+    lo, hi = rank * per, (rank + 1) * per
+    shape = dsyn.SHAPES["cfg1"]
+    shard_bytes = LAYER_BYTES_GPU // world
+    free, _ = torch.cuda.mem_get_info(dev)
+    budget = free - (6 << 30)
+    unique = max(1, min(LAYERS, budget // (shard_bytes + (3 << 20))))
+    t0 = time.time()
+    layers = []
+    for l in range(unique):
+        w = dsyn.make_layer_weights(shape, 1234, l, dev)
+        if world > 1:
+            w = SparseMlpWeights(hidden=w.hidden, intermediate=w.intermediate,
+                                 gate_packed=w.gate_packed[lo:hi].clone(), gate_absmax=w.gate_absmax[lo:hi].clone(),
+                                 up_packed=w.up_packed[lo:hi].clone(), up_absmax=w.up_absmax[lo:hi].clone(),
+                                 down_packed=w.down_packed[lo:hi].clone(), down_absmax=w.down_absmax[lo:hi].clone(),
+                                 gate_code=w.gate_code, up_code=w.up_code, down_code=w.down_code, layout=w.layout)
+            torch.cuda.empty_cache()
+        rw = dsyn.make_router(shape, 1234, l, dev)
+        layers.append(DecodeLayer(router=rw, weights=w,
+                                  norm_weight=torch.ones(HIDDEN, dtype=torch.bfloat16, device=dev)))
+    torch.cuda.synchronize(dev)
+    gen_s = time.time() - t0
+    dec = SparseMlpDecoder(layers, LAYERS, block_range=(lo, hi), group=group)
+    x0 = dsyn.make_x(shape, 99, 1, dev)[0].float()
+    dec.residual.copy_(x0)
+    g = dec.capture()
+
+    def barrier():
+        if group is not None:
+            torch.distributed.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        dec.residual.copy_(x0)
+        g.replay()
+    torch.cuda.synchronize(dev)
+
+    # device-timed region: inputs resident, K token steps
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            g.replay()
+        ev1.record()
+        torch.cuda.synchronize(dev)
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    if group is not None:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    ms_step = ms / args.steps
+
+    # end-to-end through the public API: pinned H2D input, graph step, D2H result read
+    h_in = torch.empty(HIDDEN, dtype=torch.float32, pin_memory=True)
+    h_in.copy_(x0.cpu())
+    h_out = torch.empty(HIDDEN, dtype=torch.float32, pin_memory=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        dec.residual.copy_(h_in, non_blocking=True)
+        g.replay()
+        h_out.copy_(dec.out, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], device=dev)
+    if group is not None:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+
+    alg_layer = algorithmic_bytes_per_layer()
+    pk = peaks()
+    layer_us = ms_step * 1e3 / LAYERS
+    # roofline of the per-layer decode launch group (router + gate/up + down kernels) at N = 1;
+    # at N > 1 each rank reads 1/N of the block bytes plus the whole router
+    if world == 1:
+        achieved = alg_layer / (layer_us * 1e-6) / 1e9
+    else:
+        router_b = 2 * RANK * HIDDEN + 2 * RANK * NB + 2 * NB
+        achieved = ((alg_layer - router_b) / world + router_b) / (layer_us * 1e-6) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": args.steps / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "nf4 weights, fp16 x fp16 -> fp32 MMA, bf16 io",
+            "data": "synthetic: seeded N(0,0.02) NF4 weights, bf16 RMS-normalised N(0,1) input, random-init router",
+            "config": {"workload": "BASELINE config 2: 126-layer 405B-shaped sparse-MLP decode step",
+                       "hidden": HIDDEN, "intermediate": INTERMEDIATE, "blocks": NB, "top_k": TOP_K, "rank": RANK,
+                       "layers": LAYERS, "unique_layers_resident": unique, "layer_cycling": unique < LAYERS,
+                       "parallelism": f"block-shard x{world}, router replicated, NCCL all-reduce bf16 [16384]",
+                       "l2": "inputs larger than L2 (each layer >= 184 MB per rank)",
+                       "cuda_graph": True, "synthetic_gen_s": round(gen_s, 1)},
+            "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
+                    "d2h_bytes_per_step": HIDDEN * 4},
+            "gpu_launches": args.steps * LAYERS * 4,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                         "unit_of_launch": "one layer's decode launch group (router, gate/up, down kernels)",
+                         "algorithmic_bytes": alg_layer, "us_per_layer": round(layer_us, 3),
+                         "peak_source": pk["source"]},
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(samples=2)
+        print(json.dumps(line), flush=True)
+    dec.release()
+    del g
+    if group is not None:
+        torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------------------------------- CPU arms
+def cpu_layer_sample(seed: int, layer: int):
+    """One layer of the workload, generated block by block on the host (only the
+    router and the selected blocks are materialised).  Returns the state the
+    timed CPU step needs."""
+    import numpy as np
+
+    from oracle import synthetic as syn
+    from oracle.router import route_sparse_mlp
+
+    shape = syn.SHAPES["cfg1"]
+    R = syn.make_router(shape, seed, layer)
+    x = syn.make_x(shape, seed + layer, 1)
+    blocks = route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)[0]
+    G = syn.selected_blocks_gathered(shape, seed, layer, blocks)
+    return {"R": R, "x": x, "G": G, "np": np}
+
+
+def cpu_step(state) -> None:
+    """The reference's CPU path for one layer, restated: route, then the
+    fp32 dequant + matmul of the selected NF4 blocks."""
+    from oracle import mlp as om
+    from oracle.router import route_sparse_mlp
+
+    R, x, G = state["R"], state["x"], state["G"]
+    route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], TOP_K, RANK)
+    om.sparse_mlp_gathered(x, G["gate_packed"], G["gate_absmax"], G["code"], G["up_packed"], G["up_absmax"],
+                           G["code"], G["down_cols"], G["down_absmax_cols"], G["code"])
+
+
+def cpu_baseline(samples: int = 2) -> dict:
+    import numpy as np  # noqa: F401
+
+    cores = os.cpu_count() or 1
+    state = cpu_layer_sample(7, 0)
+    cpu_step(state)  # warm
+    t0 = time.perf_counter()
+    for _ in range(samples):
+        cpu_step(state)
+    per_layer = (time.perf_counter() - t0) / samples
+    return {"value": 1.0 / (per_layer * LAYERS), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{samples} timed layer-steps of the 126-layer workload (router + 208-block NF4 MLP, numpy "
+                      f"fp32 with the host BLAS on {cores} threads); tok/s = 1 / (126 x mean layer time)"}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    state = cpu_layer_sample(7, 0)
+    for _ in range(args.warmup):
+        cpu_step(state)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(state)
+    dt = time.perf_counter() - t0
+    per_layer = dt / args.steps
+    value = 1.0 / (per_layer * LAYERS)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (same generator family)",
+        "config": {"workload": "BASELINE config 2: 126-layer 405B-shaped sparse-MLP decode step",
+                   "step": "one layer-step sample of the 126-layer token (value extrapolated x126)"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": "each step = one layer (router + 208-block NF4 MLP) in numpy fp32 on the host"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

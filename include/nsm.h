@@ -119,8 +119,24 @@ typedef struct nsm_mlp_weights {
   int64_t down_absmax_block_stride;
   int64_t down_absmax_row_stride;
   int32_t down_absmax_pair;
-  int32_t reserved;
+  int32_t layout;         /* NSM_LAYOUT_* bits */
 } nsm_mlp_weights;
+
+/* nsm_mlp_weights.layout bits.  Without them gate/up and down use the
+ * bitsandbytes / strided layouts above.  With them a pool row holds the
+ * lane-interleaved "tiled" layout written by nsm_repack_tiled (same bytes
+ * per block: gate/up 16*H packed + H/2 absmax floats, down 16*H + H):
+ *   gate/up packed: [H/64 column tiles][2 row groups][32 lanes][16 B], lane
+ *     (g=lane/4, t=lane%4) holding bytes [8t, 8t+8) of the tile in rows
+ *     16*rg+g and 16*rg+g+8;
+ *   gate/up absmax: [H/64 tiles][8 g][4] = rows g, g+8, 16+g, 24+g;
+ *   down packed: [H/32 row tiles][32 lanes][16 B], lane (g,t) holding bytes
+ *     [4t, 4t+4) of rows g, g+8, 16+g, 24+g of the tile;
+ *   down absmax: [H/32 row tiles][8 g][4] (same four rows).
+ * Block strides are unchanged; the row strides of the strided layouts are
+ * ignored for a tiled part. */
+#define NSM_LAYOUT_GATEUP_TILED 1
+#define NSM_LAYOUT_DOWN_TILED 2
 
 /* Block -> pool-row mapping applied to the router's selection.
  *   slot_of_block [NB] int32 (device): pool row, or <0 = not present here.
@@ -204,6 +220,17 @@ int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32
 int nsm_repack_down_block_major(const uint8_t* down_packed, const float* down_absmax, int32_t hidden,
                                 int32_t intermediate, const int32_t* blocks, int32_t n, uint8_t* out_packed,
                                 float* out_absmax, nsm_stream_t stream);
+
+/* bitsandbytes row-major NF4 weights -> tiled pool rows (layout above).
+ *   gate/up: [n_src][32][H/2] + [n_src][32][H/64] (block b at b*16H bytes);
+ *   down: the whole [H][I/2] + [H][I/64] weight, blocks picked by id.
+ * Block blocks[i] (all blocks when blocks == NULL) goes to destination row
+ * i (dst_rows == NULL) or dst_rows[i]; dst pointers/strides come from `dst`
+ * (its layout bits are ignored).  Either source may be NULL to skip it. */
+int nsm_repack_tiled(const uint8_t* gate_packed, const float* gate_absmax, const uint8_t* up_packed,
+                     const float* up_absmax, const uint8_t* down_packed, const float* down_absmax, int32_t hidden,
+                     int32_t intermediate, const int32_t* blocks, const int32_t* dst_rows, int32_t n,
+                     const nsm_mlp_weights* dst, nsm_stream_t stream);
 
 /* ---- reference Triton API semantics --------------------------------------
  * triton_sparse_input_linear_4bit (triton_sparse_mlp.py:1303-1337, kernels

@@ -26,6 +26,7 @@ NSM_ERR_WORKSPACE = -5
 NSM_ERR_DEVICE = -6
 
 NSM_F32, NSM_F16, NSM_BF16 = 0, 1, 2
+NSM_LAYOUT_GATEUP_TILED, NSM_LAYOUT_DOWN_TILED = 1, 2
 
 # every symbol include/nsm.h declares (checked by tests/test_abi.py)
 EXPORTED = (
@@ -33,6 +34,7 @@ EXPORTED = (
     "nsm_decode_workspace_bytes", "nsm_route", "nsm_sparse_mlp_decode", "nsm_decode_gathered",
     "nsm_decode_rows_workspace_bytes", "nsm_decode_gathered_rows", "nsm_repack_down_block_major",
     "nsm_sparse_input_linear_4bit", "nsm_sparse_output_linear_4bit", "nsm_cache_split", "nsm_cache_promote",
+    "nsm_repack_tiled",
 )
 
 
@@ -53,7 +55,7 @@ class MlpWeightsC(ctypes.Structure):
         ("gateup_block_stride", c_int64), ("gateup_absmax_block_stride", c_int64),
         ("down_block_stride", c_int64), ("down_row_stride", c_int64),
         ("down_absmax_block_stride", c_int64), ("down_absmax_row_stride", c_int64),
-        ("down_absmax_pair", c_int32), ("reserved", c_int32),
+        ("down_absmax_pair", c_int32), ("layout", c_int32),
     ]
 
 
@@ -93,6 +95,8 @@ _SIGS = {
     "nsm_sparse_output_linear_4bit": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_int32,
                                               c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_int32,
                                               c_void_p, c_void_p]),
+    "nsm_repack_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                                 c_void_p, c_void_p, c_int32, POINTER(MlpWeightsC), c_void_p]),
     "nsm_cache_split": (c_int, [c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "nsm_cache_promote": (c_int, [POINTER(MlpWeightsC), c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
                                   c_void_p, c_void_p]),

@@ -56,14 +56,6 @@ int current_device(DeviceInfo* info) {
   return NSM_OK;
 }
 
-size_t decode_ws_counter_bytes(int hidden, int top_k) {
-  size_t off = 0;
-  off = align_up(off + 2 * sizeof(int), 256);
-  off = align_up(off + (size_t)top_k * sizeof(int), 256);
-  off = align_up(off + (size_t)(hidden / 32) * sizeof(int), 256);
-  return off;
-}
-
 DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank) {
   DecodeWs w{};
   char* b = reinterpret_cast<char*>(base);
@@ -74,11 +66,11 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
     return p;
   };
   const int nb = intermediate / 32;
-  char* tick = take(2 * sizeof(int));
-  w.ticket_router_a = reinterpret_cast<int*>(tick);
-  w.ticket_router_b = w.ticket_router_a ? w.ticket_router_a + 1 : nullptr;
-  w.ticket_slot = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
-  w.ticket_rowtile = reinterpret_cast<int*>(take((size_t)(hidden / 32) * sizeof(int)));
+  int* tick = reinterpret_cast<int*>(take((size_t)kCounterInts * sizeof(int)));
+  w.ticket_router_a = tick;
+  w.ticket_router_b = tick ? tick + 1 : nullptr;
+  w.ticket_slot = tick ? tick + 2 : nullptr;
+  w.ticket_rowtile = tick ? tick + 2 + kMaxTopK : nullptr;
   w.latent_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * rank * sizeof(float)));
   w.sumsq_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * sizeof(float)));
   w.latent = reinterpret_cast<float*>(take((size_t)rank * sizeof(float)));

@@ -28,6 +28,78 @@ __global__ void repack_down_kernel(const uint8_t* __restrict__ src, const float*
 }
 
 // ---------------------------------------------------------------------------
+// bitsandbytes row-major -> tiled pool rows (layout documented in nsm.h)
+// ---------------------------------------------------------------------------
+struct RepackParams {
+  const uint8_t* src_pk[3];  // gate, up, down
+  const float* src_am[3];
+  uint8_t* dst_pk[3];
+  float* dst_am[3];
+  int64_t dst_pk_stride[3];  // bytes between destination rows
+  int64_t dst_am_stride[3];  // floats between destination rows
+  int H, I;
+  const int32_t* blocks;
+  const int32_t* dst_rows;
+  int n;
+};
+
+// blockIdx.y: 0/1 gate/up packed, 2/3 gate/up absmax, 4 down packed, 5 down absmax
+__global__ void repack_tiled_kernel(RepackParams p) {
+  const int part = blockIdx.y;
+  const int H = p.H;
+  const int proj = part < 2 ? part : (part < 4 ? part - 2 : 2);
+  const bool is_am = part == 2 || part == 3 || part == 5;
+  if (is_am ? p.src_am[proj] == nullptr : p.src_pk[proj] == nullptr) return;
+  int64_t per_block;  // outputs per block
+  if (part < 2) per_block = H;            // 16-byte chunks
+  else if (part < 4) per_block = H / 8;   // float4s
+  else if (part == 4) per_block = H;      // 16-byte chunks
+  else per_block = H / 4;                 // float4s
+  const int64_t total = per_block * p.n;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    const int i = (int)(q / per_block);
+    const int64_t c = q - (int64_t)i * per_block;
+    const int b = p.blocks ? p.blocks[i] : i;
+    const int d = p.dst_rows ? p.dst_rows[i] : i;
+    if (part < 2) {
+      const int j = (int)(c >> 6), rem = (int)(c & 63), rg = rem >> 5, lane = rem & 31;
+      const int g = lane >> 2, t = lane & 3;
+      const uint8_t* src = p.src_pk[proj] + (int64_t)b * 16 * H;
+      const int r0 = rg * 16 + g;
+      const uint2 a = *reinterpret_cast<const uint2*>(src + (int64_t)r0 * (H / 2) + j * 32 + t * 8);
+      const uint2 e = *reinterpret_cast<const uint2*>(src + (int64_t)(r0 + 8) * (H / 2) + j * 32 + t * 8);
+      *reinterpret_cast<uint4*>(p.dst_pk[proj] + d * p.dst_pk_stride[proj] + (int64_t)c * 16) =
+          make_uint4(a.x, a.y, e.x, e.y);
+    } else if (part < 4) {
+      const int j = (int)(c >> 3), g = (int)(c & 7);
+      const float* src = p.src_am[proj] + (int64_t)b * (H / 2);
+      const int apr = H / 64;
+      const float4 v = make_float4(src[(int64_t)g * apr + j], src[(int64_t)(g + 8) * apr + j],
+                                   src[(int64_t)(g + 16) * apr + j], src[(int64_t)(g + 24) * apr + j]);
+      *reinterpret_cast<float4*>(p.dst_am[proj] + d * p.dst_am_stride[proj] + c * 4) = v;
+    } else if (part == 4) {
+      const int rt = (int)(c >> 5), lane = (int)(c & 31), g = lane >> 2, t = lane & 3;
+      const uint8_t* src = p.src_pk[2] + (int64_t)b * 16 + t * 4;
+      const int64_t bpr = p.I / 2;
+      const int r0 = rt * 32 + g;
+      const uint4 v = make_uint4(*reinterpret_cast<const uint32_t*>(src + (int64_t)r0 * bpr),
+                                 *reinterpret_cast<const uint32_t*>(src + (int64_t)(r0 + 8) * bpr),
+                                 *reinterpret_cast<const uint32_t*>(src + (int64_t)(r0 + 16) * bpr),
+                                 *reinterpret_cast<const uint32_t*>(src + (int64_t)(r0 + 24) * bpr));
+      *reinterpret_cast<uint4*>(p.dst_pk[2] + d * p.dst_pk_stride[2] + (int64_t)c * 16) = v;
+    } else {
+      const int rt = (int)(c >> 3), g = (int)(c & 7);
+      const int64_t apr = p.I / 64;
+      const float* src = p.src_am[2] + (b >> 1);
+      const int r0 = rt * 32 + g;
+      const float4 v = make_float4(src[(int64_t)r0 * apr], src[(int64_t)(r0 + 8) * apr], src[(int64_t)(r0 + 16) * apr],
+                                   src[(int64_t)(r0 + 24) * apr]);
+      *reinterpret_cast<float4*>(p.dst_am[2] + d * p.dst_am_stride[2] + c * 4) = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // triton_sparse_input_linear_4bit semantics (NF4 of weight.t(): element index
 // e = in_idx * out_features + out_idx).
 // ---------------------------------------------------------------------------
@@ -204,6 +276,62 @@ int nsm_repack_down_block_major(const uint8_t* down_packed, const float* down_ab
   repack_down_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(down_packed, down_absmax, hidden,
                                                                                 intermediate, blocks, cnt,
                                                                                 out_packed, out_absmax);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+int nsm_repack_tiled(const uint8_t* gate_packed, const float* gate_absmax, const uint8_t* up_packed,
+                     const float* up_absmax, const uint8_t* down_packed, const float* down_absmax, int32_t hidden,
+                     int32_t intermediate, const int32_t* blocks, const int32_t* dst_rows, int32_t n,
+                     const nsm_mlp_weights* dst, nsm_stream_t stream) {
+  NSM_REQUIRE(dst != nullptr, NSM_ERR_INVALID_ARG, "destination descriptor is NULL");
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0 && intermediate > 0 && intermediate % 64 == 0, NSM_ERR_UNSUPPORTED,
+              "hidden and intermediate must be positive multiples of 64");
+  const int nb = intermediate / 32;
+  const int cnt = blocks ? n : (n > 0 ? n : nb);
+  NSM_REQUIRE(cnt > 0, NSM_ERR_INVALID_ARG, "nothing to repack");
+  RepackParams p{};
+  p.src_pk[0] = gate_packed;
+  p.src_pk[1] = up_packed;
+  p.src_pk[2] = down_packed;
+  p.src_am[0] = gate_absmax;
+  p.src_am[1] = up_absmax;
+  p.src_am[2] = down_absmax;
+  p.dst_pk[0] = const_cast<uint8_t*>(dst->gate_packed);
+  p.dst_pk[1] = const_cast<uint8_t*>(dst->up_packed);
+  p.dst_pk[2] = const_cast<uint8_t*>(dst->down_packed);
+  p.dst_am[0] = const_cast<float*>(dst->gate_absmax);
+  p.dst_am[1] = const_cast<float*>(dst->up_absmax);
+  p.dst_am[2] = const_cast<float*>(dst->down_absmax);
+  const int64_t gs = dst->gateup_block_stride ? dst->gateup_block_stride : (int64_t)16 * hidden;
+  const int64_t gas = dst->gateup_absmax_block_stride ? dst->gateup_absmax_block_stride : (int64_t)hidden / 2;
+  const int64_t ds = dst->down_block_stride ? dst->down_block_stride : (int64_t)16 * hidden;
+  const int64_t das = dst->down_absmax_block_stride ? dst->down_absmax_block_stride : (int64_t)hidden;
+  p.dst_pk_stride[0] = p.dst_pk_stride[1] = gs;
+  p.dst_am_stride[0] = p.dst_am_stride[1] = gas;
+  p.dst_pk_stride[2] = ds;
+  p.dst_am_stride[2] = das;
+  for (int q = 0; q < 3; ++q) {
+    if (p.src_pk[q]) {
+      NSM_REQUIRE(p.dst_pk[q] != nullptr, NSM_ERR_INVALID_ARG, "destination packed pointer is NULL");
+      NSM_REQUIRE(((uintptr_t)p.dst_pk[q] & 15) == 0 && (p.dst_pk_stride[q] & 15) == 0, NSM_ERR_INVALID_ARG,
+                  "destination packed rows must be 16-byte aligned");
+      NSM_REQUIRE(((uintptr_t)p.src_pk[q] & (q < 2 ? 7 : 3)) == 0, NSM_ERR_INVALID_ARG, "misaligned source");
+    }
+    if (p.src_am[q]) {
+      NSM_REQUIRE(p.dst_am[q] != nullptr, NSM_ERR_INVALID_ARG, "destination absmax pointer is NULL");
+      NSM_REQUIRE(((uintptr_t)p.dst_am[q] & 15) == 0 && (p.dst_am_stride[q] & 3) == 0, NSM_ERR_INVALID_ARG,
+                  "destination absmax rows must be 16-byte aligned");
+    }
+  }
+  p.H = hidden;
+  p.I = intermediate;
+  p.blocks = blocks;
+  p.dst_rows = dst_rows;
+  p.n = cnt;
+  const int64_t work = (int64_t)cnt * hidden;
+  const int gx = (int)std::min<int64_t>((work + 255) / 256, 148 * 32);
+  repack_tiled_kernel<<<dim3(gx, 6), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
 }

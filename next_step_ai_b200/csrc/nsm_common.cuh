@@ -66,6 +66,14 @@ __device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
                : "l"(p));
   return r;
 }
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float4 ldg_f4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 __device__ __forceinline__ uint32_t ldg_u32(const void* p) {
   uint32_t r;
   asm volatile("ld.global.nc.L2::128B.u32 %0, [%1];" : "=r"(r) : "l"(p));

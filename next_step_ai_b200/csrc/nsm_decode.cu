@@ -30,295 +30,9 @@
 
 #include "nsm_common.cuh"
 #include "nsm_internal.h"
+#include "nsm_router.h"
 
 namespace nsm {
-
-// ============================================================================
-// 1. router latent (+ x preparation)
-// ============================================================================
-struct RouterAParams {
-  const void* x;
-  int x_dtype;
-  float* residual;
-  const void* y_prev;
-  int y_prev_dtype;
-  const void* norm_w;
-  int norm_w_dtype;
-  float eps;
-  int use_norm;
-  const void* enc_w;  // may be null: x preparation only
-  const void* enc_b;
-  int wdtype;
-  int rank;
-  int basis_top_k;
-  int H;
-  int cols_per_cta;  // multiple of 64
-  DecodeWs ws;
-};
-
-__global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
-  extern __shared__ float xs[];  // [cols_per_cta]
-  __shared__ float red[32];
-  __shared__ int s_last;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c0 = blockIdx.x * p.cols_per_cta;
-  const int c1 = min(p.H, c0 + p.cols_per_cta);
-  const int n = c1 - c0;
-
-  float sumsq = 0.f;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const int c = c0 + i;
-    float v;
-    if (p.residual != nullptr) {
-      v = p.residual[c];
-      if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
-      p.residual[c] = v;
-      sumsq += v * v;
-      if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
-    } else {
-      v = load_as_f32(p.x, p.x_dtype, c);
-    }
-    xs[i] = v;
-  }
-  sumsq = warp_sum(sumsq);
-  if (lane == 0) red[warp] = sumsq;
-  __syncthreads();
-  if (tid == 0) {
-    float t = 0.f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
-    p.ws.sumsq_part[blockIdx.x] = t;
-  }
-
-  // fp16 copy of x with a power-of-two scale per 64-column tile
-  const int ntiles = n >> 6;
-  for (int tl = warp; tl < ntiles; tl += (blockDim.x >> 5)) {
-    const float a = xs[tl * 64 + lane], b = xs[tl * 64 + 32 + lane];
-    const float m = warp_max(fmaxf(fabsf(a), fabsf(b)));
-    const float s = pow2_scale_for(m);
-    const float inv = 1.f / s;  // exact: s is a power of two
-    const int c = c0 + tl * 64;
-    p.ws.x16[c + lane] = __float2half_rn(a * inv);
-    p.ws.x16[c + 32 + lane] = __float2half_rn(b * inv);
-    if (lane == 0) p.ws.xscale[c >> 6] = s;
-  }
-
-  if (p.enc_w != nullptr) {
-    for (int r = warp; r < p.rank; r += (blockDim.x >> 5)) {
-      float acc = 0.f;
-      const int64_t rowoff = (int64_t)r * p.H + c0;
-      for (int i = lane; i < n; i += 32) acc += load_as_f32(p.enc_w, p.wdtype, rowoff + i) * xs[i];
-      acc = warp_sum(acc);
-      if (lane == 0) p.ws.latent_part[blockIdx.x * p.rank + r] = acc;
-    }
-  }
-
-  // last CTA: reduce partials in CTA order
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const int prev = atomicAdd(p.ws.ticket_router_a, 1);
-    s_last = (prev == (int)gridDim.x - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  __shared__ float s_norm;
-  __shared__ float lat[kMaxRank];
-  if (tid == 0) {
-    float ns = 1.f;
-    if (p.use_norm) {
-      double t = 0.0;
-      for (int b = 0; b < (int)gridDim.x; ++b) t += (double)ldcg_f32(&p.ws.sumsq_part[b]);
-      const float var = (float)(t / (double)p.H);
-      ns = 1.f / sqrtf(var + p.eps);
-    }
-    s_norm = ns;
-    *p.ws.norm_scale = ns;
-  }
-  __syncthreads();
-  if (p.enc_w != nullptr) {
-    for (int r = tid; r < p.rank; r += blockDim.x) {
-      float acc = 0.f;
-      for (int b = 0; b < (int)gridDim.x; ++b) acc += ldcg_f32(&p.ws.latent_part[b * p.rank + r]);
-      acc *= s_norm;
-      if (p.enc_b != nullptr) acc += load_as_f32(p.enc_b, p.wdtype, r);
-      lat[r] = acc;
-    }
-    __syncthreads();
-    const int bk = max(1, min(p.basis_top_k, p.rank));
-    for (int r = tid; r < p.rank; r += blockDim.x) {
-      float v = lat[r];
-      if (bk < p.rank) {
-        const float a = fabsf(v);
-        int rank_pos = 0;
-        for (int q = 0; q < p.rank; ++q) {
-          const float b = fabsf(lat[q]);
-          rank_pos += (b > a) || (b == a && q < r);
-        }
-        if (rank_pos >= bk) v = 0.f;
-      }
-      p.ws.latent[r] = v;
-    }
-  }
-  if (tid == 0) *p.ws.ticket_router_a = 0;
-}
-
-// ============================================================================
-// 2. block scores + top-k + selection -> pool rows
-// ============================================================================
-struct RouterBParams {
-  const void* score_w;
-  const void* score_b;
-  int wdtype;
-  const float* dbn;
-  int legacy;
-  int rank;
-  int NB;
-  int top_k;
-  int sort_n;  // power of two >= NB
-  int32_t* idx_out;
-  float* score_out;
-  float* latent_out;
-  const int32_t* slot_of_block;
-  int block_begin;
-  int block_end;
-  int pool_rows;
-  DecodeWs ws;
-};
-
-__device__ __forceinline__ uint32_t orderable(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float from_orderable(uint32_t u) {
-  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
-}
-
-__device__ __forceinline__ int map_block(const RouterBParams& p, int b) {
-  if (b < 0 || b >= p.NB) return -1;
-  int r;
-  if (p.slot_of_block != nullptr) {
-    r = p.slot_of_block[b];
-  } else {
-    r = (b >= p.block_begin && b < p.block_end) ? b - p.block_begin : -1;
-  }
-  return (r >= 0 && r < p.pool_rows) ? r : -1;
-}
-
-// exclusive block scan of 0/1 flags, writes compacted pool rows
-__device__ void compact_selection(const RouterBParams& p, const int* sel, int k) {
-  __shared__ int warp_tot[32];
-  __shared__ int s_base;
-  if (threadIdx.x == 0) s_base = 0;
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int j0 = 0; j0 < k; j0 += blockDim.x) {
-    const int j = j0 + threadIdx.x;
-    int r = -1;
-    if (j < k) r = map_block(p, sel[j]);
-    const int f = r >= 0;
-    const unsigned bal = __ballot_sync(0xffffffffu, f);
-    const int pre = __popc(bal & ((1u << lane) - 1u));
-    if (lane == 0) warp_tot[warp] = __popc(bal);
-    __syncthreads();
-    int wbase = 0;
-    for (int w = 0; w < warp; ++w) wbase += warp_tot[w];
-    if (f) {
-      p.ws.rows[s_base + wbase + pre] = r;
-      p.ws.row_block[s_base + wbase + pre] = sel[j];
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int t = 0;
-      for (int w = 0; w < nw; ++w) t += warp_tot[w];
-      s_base += t;
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) *p.ws.count = s_base;
-}
-
-__global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
-  extern __shared__ unsigned long long keys[];  // [sort_n] (last CTA only)
-  __shared__ float lat[kMaxRank];
-  __shared__ int s_last;
-  const int tid = threadIdx.x;
-  for (int r = tid; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r]);
-  __syncthreads();
-  for (int b = blockIdx.x * blockDim.x + tid; b < p.NB; b += gridDim.x * blockDim.x) {
-    float acc = 0.f;
-    const int64_t off = (int64_t)b * p.rank;
-    if (p.legacy) {
-      for (int r = 0; r < p.rank; ++r) acc += fabsf(lat[r]) * load_as_f32(p.score_w, p.wdtype, off + r);
-    } else {
-      for (int r = 0; r < p.rank; ++r) acc += lat[r] * load_as_f32(p.score_w, p.wdtype, off + r);
-      if (p.score_b != nullptr) acc += load_as_f32(p.score_b, p.wdtype, b);
-      acc = fmaxf(acc, 0.f);
-    }
-    if (p.dbn != nullptr) acc *= p.dbn[b];
-    p.ws.scores[b] = acc;
-  }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const int prev = atomicAdd(p.ws.ticket_router_b, 1);
-    s_last = (prev == (int)gridDim.x - 1);
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int i = tid; i < p.sort_n; i += blockDim.x) {
-    unsigned long long key = 0ull;
-    if (i < p.NB) {
-      const float s = ldcg_f32(&p.ws.scores[i]);
-      key = ((unsigned long long)orderable(s) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
-    }
-    keys[i] = key;
-  }
-  __syncthreads();
-  // bitonic sort, descending
-  for (int k = 2; k <= p.sort_n; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < p.sort_n; i += blockDim.x) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const unsigned long long a = keys[i], b = keys[ixj];
-          const bool desc = (i & k) == 0;
-          if (desc ? (a < b) : (a > b)) {
-            keys[i] = b;
-            keys[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  const int k = p.top_k;
-  for (int j = tid; j < k; j += blockDim.x) {
-    const unsigned long long key = keys[j];
-    const int idx = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
-    p.ws.sel_idx[j] = idx;
-    if (p.idx_out) p.idx_out[j] = idx;
-    if (p.score_out) p.score_out[j] = from_orderable((uint32_t)(key >> 32));
-  }
-  if (p.latent_out) {
-    for (int r = tid; r < p.rank; r += blockDim.x) p.latent_out[r] = lat[r];
-  }
-  __syncthreads();
-  compact_selection(p, p.ws.sel_idx, k);
-  if (tid == 0) *p.ws.ticket_router_b = 0;
-}
-
-// Selection supplied by the caller: copy + compaction (single CTA).
-__global__ void __launch_bounds__(512) select_given_kernel(RouterBParams p, const int32_t* idx_in, int k) {
-  for (int j = threadIdx.x; j < k; j += blockDim.x) {
-    const int b = idx_in[j];
-    p.ws.sel_idx[j] = (b >= 0 && b < p.NB) ? b : -1;
-  }
-  __syncthreads();
-  // invalid ids map to "not present"
-  compact_selection(p, p.ws.sel_idx, k);
-}
 
 // Identity rows 0..count-1 (gathered layouts).
 __global__ void identity_rows_kernel(int* rows, int* count, int* sel, int n) {
@@ -333,6 +47,17 @@ __global__ void identity_rows_kernel(int* rows, int* count, int* sel, int n) {
 // ============================================================================
 // 3. gate/up gather-GEMV + SiLU*up
 // ============================================================================
+// The byte->half2 tables live at the start of the dynamic shared memory of
+// both MLP kernels; indexing the extern array directly lets the compiler fold
+// its offset into the shared-load immediate.
+extern __shared__ __align__(1024) uint32_t g_lut_smem[];
+
+template <int kTable>
+__device__ __forceinline__ uint32_t lut_at(uint32_t w, uint32_t lanebase, int kbyte) {
+  const uint32_t addr = __byte_perm(w, lanebase, 0x5504u | ((uint32_t)kbyte << 4));
+  return *reinterpret_cast<const uint32_t*>(reinterpret_cast<const char*>(g_lut_smem) + addr + kTable * 128);
+}
+
 struct GateUpParams {
   const uint8_t* gate;
   const float* gate_am;
@@ -363,58 +88,94 @@ struct GateUpParams {
   int total_warps;
 };
 
-struct TileRegs {
-  uint2 w[2][2][2];  // [proj][rowgroup][row g / g+8]
-  float am[2][2][2];
+// One 64-column tile of one block, both projections: w[proj][rg] holds the
+// lane's 8 bytes of row 16*rg+g (.x,.y) and of row 16*rg+g+8 (.z,.w);
+// am[proj] holds the absmax of rows g, g+8, 16+g, 24+g.
+struct GuTile {
+  uint4 w[2][2];
+  float4 am[2];
 };
 
-__device__ __forceinline__ void gateup_load_tile(const GateUpParams& p, const uint8_t* gbase, const uint8_t* ubase,
-                                                 const float* gab, const float* uab, int j, int g, int t,
-                                                 TileRegs& r) {
-  const int bpr = p.H >> 1;   // bytes per row
-  const int apr = p.H >> 6;   // absmax per row
+template <bool kTiled>
+__device__ __forceinline__ void gu_load(const GateUpParams& p, const uint8_t* gb, const uint8_t* ub, const float* gab,
+                                        const float* uab, int j, int lane, GuTile& r) {
+  const int g = lane >> 2, t = lane & 3;
+  if (kTiled) {
+    const int64_t off = (int64_t)j * 1024 + lane * 16;
+    r.w[0][0] = ldg_stream_u4(gb + off);
+    r.w[0][1] = ldg_stream_u4(gb + off + 512);
+    r.w[1][0] = ldg_stream_u4(ub + off);
+    r.w[1][1] = ldg_stream_u4(ub + off + 512);
+    r.am[0] = ldg_f4(gab + j * 32 + g * 4);
+    r.am[1] = ldg_f4(uab + j * 32 + g * 4);
+  } else {
+    const int bpr = p.H >> 1, apr = p.H >> 6;
 #pragma unroll
-  for (int rg = 0; rg < 2; ++rg) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = rg * 16 + g + h * 8;
-      const int64_t boff = (int64_t)row * bpr + j * 32 + t * 8;
-      r.w[0][rg][h] = ldg_stream_u2(gbase + boff);
-      r.w[1][rg][h] = ldg_stream_u2(ubase + boff);
-      r.am[0][rg][h] = ldg_f32(gab + (int64_t)row * apr + j);
-      r.am[1][rg][h] = ldg_f32(uab + (int64_t)row * apr + j);
+    for (int rg = 0; rg < 2; ++rg) {
+      const int r0 = rg * 16 + g;
+      const int64_t o0 = (int64_t)r0 * bpr + j * 32 + t * 8;
+      const int64_t o1 = o0 + (int64_t)8 * bpr;
+      const uint2 a0 = ldg_stream_u2(gb + o0), a1 = ldg_stream_u2(gb + o1);
+      const uint2 c0 = ldg_stream_u2(ub + o0), c1 = ldg_stream_u2(ub + o1);
+      r.w[0][rg] = make_uint4(a0.x, a0.y, a1.x, a1.y);
+      r.w[1][rg] = make_uint4(c0.x, c0.y, c1.x, c1.y);
     }
+    r.am[0] = make_float4(ldg_f32(gab + (int64_t)g * apr + j), ldg_f32(gab + (int64_t)(g + 8) * apr + j),
+                          ldg_f32(gab + (int64_t)(g + 16) * apr + j), ldg_f32(gab + (int64_t)(g + 24) * apr + j));
+    r.am[1] = make_float4(ldg_f32(uab + (int64_t)g * apr + j), ldg_f32(uab + (int64_t)(g + 8) * apr + j),
+                          ldg_f32(uab + (int64_t)(g + 16) * apr + j), ldg_f32(uab + (int64_t)(g + 24) * apr + j));
   }
 }
 
+// 16 rows x 64 columns: four k=16 MMAs over the lane's bytes of two rows.
 template <int kTable>
-__device__ __forceinline__ void gateup_mma_rowgroup(const uint32_t* lut, uint32_t lanebase, const uint2 w0,
-                                                    const uint2 w1, const uint32_t b[8], float d[4]) {
+__device__ __forceinline__ void gu_mma_rowgroup(uint32_t lanebase, const uint4 w, const uint32_t b[8], float d[4]) {
   d[0] = d[1] = d[2] = d[3] = 0.f;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const uint32_t x0 = c < 2 ? w0.x : w0.y;
-    const uint32_t x1 = c < 2 ? w1.x : w1.y;
+    const uint32_t r0 = c < 2 ? w.x : w.y;
+    const uint32_t r1 = c < 2 ? w.z : w.w;
     const int kb = (c & 1) * 2;
-    const uint32_t a0 = lut_lookup_rt(lut, x0, lanebase, kb, kTable);
-    const uint32_t a1 = lut_lookup_rt(lut, x1, lanebase, kb, kTable);
-    const uint32_t a2 = lut_lookup_rt(lut, x0, lanebase, kb + 1, kTable);
-    const uint32_t a3 = lut_lookup_rt(lut, x1, lanebase, kb + 1, kTable);
-    mma_16816(d, a0, a1, a2, a3, b[2 * c], b[2 * c + 1]);
+    mma_16816(d, lut_at<kTable>(r0, lanebase, kb), lut_at<kTable>(r1, lanebase, kb),
+              lut_at<kTable>(r0, lanebase, kb + 1), lut_at<kTable>(r1, lanebase, kb + 1), b[2 * c], b[2 * c + 1]);
+  }
+}
+
+__device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& tile, int j, int t, uint32_t lanebase,
+                                           float acc[2][4]) {
+  uint32_t b[8];
+  {
+    const uint4 xa = ldg_u4(p.x16 + j * 64 + t * 16);
+    const uint4 xb = ldg_u4(p.x16 + j * 64 + t * 16 + 8);
+    b[0] = xa.x; b[1] = xa.y; b[2] = xa.z; b[3] = xa.w;
+    b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
+  }
+  const float xs = ldg_f32(p.xscale + j);
+  const float ag[4] = {tile.am[0].x * xs, tile.am[0].y * xs, tile.am[0].z * xs, tile.am[0].w * xs};
+  const float au[4] = {tile.am[1].x * xs, tile.am[1].y * xs, tile.am[1].z * xs, tile.am[1].w * xs};
+#pragma unroll
+  for (int rg = 0; rg < 2; ++rg) {
+    float d[4];
+    gu_mma_rowgroup<0>(lanebase, tile.w[0][rg], b, d);
+    acc[0][rg * 2] = fmaf(d[0], ag[rg * 2], acc[0][rg * 2]);
+    acc[0][rg * 2 + 1] = fmaf(d[2], ag[rg * 2 + 1], acc[0][rg * 2 + 1]);
+    gu_mma_rowgroup<1>(lanebase, tile.w[1][rg], b, d);
+    acc[1][rg * 2] = fmaf(d[0], au[rg * 2], acc[1][rg * 2]);
+    acc[1][rg * 2 + 1] = fmaf(d[2], au[rg * 2 + 1], acc[1][rg * 2 + 1]);
   }
 }
 
 __device__ __forceinline__ int gateup_tiles_per_unit(int count, int tiles_per_row, int total_warps) {
   const int min_tpu = (tiles_per_row + kMaxUnitsPerSlot - 1) / kMaxUnitsPerSlot;
   const long long total = (long long)count * tiles_per_row;
-  long long want = total / (4LL * total_warps);
-  int tpu = (int)max(1LL, min(16LL, want));
+  const long long want = total / (3LL * total_warps);
+  const int tpu = (int)max(1LL, min(16LL, want));
   return max(tpu, min_tpu);
 }
 
+template <bool kTiled>
 __global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
-  extern __shared__ __align__(16) uint32_t lut[];
-  build_lut(lut, p.gate_code, p.up_code);
+  build_lut(g_lut_smem, p.gate_code, p.up_code);
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lanebase = (uint32_t)lane * 4u;
@@ -428,35 +189,24 @@ __global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
   for (int u = warp_global; u < nunits; u += p.total_warps) {
     const int s = u / ups, sub = u - s * ups;
     const int prow = p.rows[s];
-    const uint8_t* gbase = p.gate + (int64_t)prow * p.gstride;
-    const uint8_t* ubase = p.up + (int64_t)prow * p.gstride;
+    const uint8_t* gb = p.gate + (int64_t)prow * p.gstride;
+    const uint8_t* ub = p.up + (int64_t)prow * p.gstride;
     const float* gab = p.gate_am + (int64_t)prow * p.gastride;
     const float* uab = p.up_am + (int64_t)prow * p.gastride;
     const int j0 = sub * tpu, j1 = min(tiles_per_row, j0 + tpu);
-    float acc[2][2][2] = {};  // [proj][rg][h]
-    TileRegs cur, nxt;
-    gateup_load_tile(p, gbase, ubase, gab, uab, j0, g, t, cur);
-    for (int j = j0; j < j1; ++j) {
-      if (j + 1 < j1) gateup_load_tile(p, gbase, ubase, gab, uab, j + 1, g, t, nxt);
-      uint32_t b[8];
-      {
-        const uint4 xa = ldg_u4(p.x16 + j * 64 + t * 16);
-        const uint4 xb = ldg_u4(p.x16 + j * 64 + t * 16 + 8);
-        b[0] = xa.x; b[1] = xa.y; b[2] = xa.z; b[3] = xa.w;
-        b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
-      }
-      const float xs = ldg_f32(p.xscale + j);
-#pragma unroll
-      for (int rg = 0; rg < 2; ++rg) {
-        float d[4];
-        gateup_mma_rowgroup<0>(lut, lanebase, cur.w[0][rg][0], cur.w[0][rg][1], b, d);
-        acc[0][rg][0] = fmaf(d[0], cur.am[0][rg][0] * xs, acc[0][rg][0]);
-        acc[0][rg][1] = fmaf(d[2], cur.am[0][rg][1] * xs, acc[0][rg][1]);
-        gateup_mma_rowgroup<1>(lut, lanebase, cur.w[1][rg][0], cur.w[1][rg][1], b, d);
-        acc[1][rg][0] = fmaf(d[0], cur.am[1][rg][0] * xs, acc[1][rg][0]);
-        acc[1][rg][1] = fmaf(d[2], cur.am[1][rg][1] * xs, acc[1][rg][1]);
-      }
-      cur = nxt;
+    float acc[2][4] = {};
+    GuTile t0, t1, t2;
+    gu_load<kTiled>(p, gb, ub, gab, uab, j0, lane, t0);
+    if (j0 + 1 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j0 + 1, lane, t1);
+    for (int j = j0; j < j1; j += 3) {
+      if (j + 2 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 2, lane, t2);
+      gu_compute(p, t0, j, t, lanebase, acc);
+      if (j + 1 >= j1) break;
+      if (j + 3 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 3, lane, t0);
+      gu_compute(p, t1, j + 1, t, lanebase, acc);
+      if (j + 2 >= j1) break;
+      if (j + 4 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 4, lane, t1);
+      gu_compute(p, t2, j + 2, t, lanebase, acc);
     }
     // column 0 of the accumulator lives in lanes with t == 0
     float* part = p.gu_part + ((int64_t)s * kMaxUnitsPerSlot + sub) * 64;
@@ -464,22 +214,18 @@ __global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
 #pragma unroll
       for (int pr = 0; pr < 2; ++pr)
 #pragma unroll
-        for (int rg = 0; rg < 2; ++rg)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) part[pr * 32 + rg * 16 + g + h * 8] = acc[pr][rg][h];
+        for (int i = 0; i < 4; ++i) part[pr * 32 + (i >> 1) * 16 + g + (i & 1) * 8] = acc[pr][i];
       __threadfence();
     }
     __syncwarp();
     int last = 0;
-    if (lane == 0) {
-      const int prev = atomicAdd(&p.ticket_slot[s], 1);
-      last = prev == ups - 1;
-    }
+    if (lane == 0) last = atomicAdd(&p.ticket_slot[s], 1) == ups - 1;
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) continue;
     __threadfence();
     float gsum = 0.f, usum = 0.f;
     const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
+#pragma unroll 8
     for (int q = 0; q < ups; ++q) {
       gsum += ldcg_f32(base + q * 64 + lane);
       usum += ldcg_f32(base + q * 64 + 32 + lane);
@@ -532,74 +278,116 @@ struct DownParams {
   int total_warps;
 };
 
+constexpr int kDownRowTiles = 2;  // 32-row tiles per unit
+constexpr int kDownBatch = 4;     // blocks whose loads are in flight together
+
+template <bool kTiled>
+__device__ __forceinline__ void down_load(const DownParams& p, int prow, int rt, int lane, uint4& w, float4& am) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* base = p.down + (int64_t)prow * p.dbs;
+  const float* abase = p.down_am + (int64_t)(p.pair ? (prow >> 1) : prow) * p.dabs;
+  if (kTiled) {
+    w = ldg_u4(base + (int64_t)rt * 512 + lane * 16);
+    am = ldg_f4(abase + rt * 32 + g * 4);
+  } else {
+    const int r0 = rt * 32 + g;
+    w.x = ldg_u32(base + (int64_t)r0 * p.drs + t * 4);
+    w.y = ldg_u32(base + (int64_t)(r0 + 8) * p.drs + t * 4);
+    w.z = ldg_u32(base + (int64_t)(r0 + 16) * p.drs + t * 4);
+    w.w = ldg_u32(base + (int64_t)(r0 + 24) * p.drs + t * 4);
+    am.x = ldg_f32(abase + (int64_t)r0 * p.dars);
+    am.y = ldg_f32(abase + (int64_t)(r0 + 8) * p.dars);
+    am.z = ldg_f32(abase + (int64_t)(r0 + 16) * p.dars);
+    am.w = ldg_f32(abase + (int64_t)(r0 + 24) * p.dars);
+  }
+}
+
+__device__ __forceinline__ void down_mma(uint32_t lanebase, uint32_t w0, uint32_t w1, const uint4 bf, float d[4]) {
+  d[0] = d[1] = d[2] = d[3] = 0.f;
+  mma_16816(d, lut_at<0>(w0, lanebase, 0), lut_at<0>(w1, lanebase, 0), lut_at<0>(w0, lanebase, 1),
+            lut_at<0>(w1, lanebase, 1), bf.x, bf.y);
+  mma_16816(d, lut_at<0>(w0, lanebase, 2), lut_at<0>(w1, lanebase, 2), lut_at<0>(w0, lanebase, 3),
+            lut_at<0>(w1, lanebase, 3), bf.z, bf.w);
+}
+
+template <bool kTiled>
 __global__ void __launch_bounds__(256, 2) down_kernel(DownParams p) {
-  extern __shared__ __align__(16) uint32_t lut[];
-  build_lut(lut, p.down_code, p.down_code);
+  build_lut(g_lut_smem, p.down_code, p.down_code);
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t lanebase = (uint32_t)lane * 4u;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int count = *p.count_ptr;
   const int RT = p.H >> 5;
-  int sg = (4 * p.total_warps + RT - 1) / RT;
+  const int RG = (RT + kDownRowTiles - 1) / kDownRowTiles;  // row-tile groups
+  int sg = (3 * p.total_warps + RG - 1) / RG;
   sg = max(1, min(sg, min(max(count, 1), kMaxSlotGroups)));
   const int gs = (count + sg - 1) / sg;
-  const int nunits = RT * sg;
+  const int nunits = RG * sg;
 
   for (int u = warp_global; u < nunits; u += p.total_warps) {
-    const int grp = u / RT, rt = u - grp * RT;
+    const int grp = u / RG, rgi = u - grp * RG;
+    const int rt0 = rgi * kDownRowTiles;
     const int s0 = grp * gs, s1 = min(count, s0 + gs);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, 16+g, 24+g
-    for (int s = s0; s < s1; ++s) {
-      const int prow = p.rows[s];
-      const uint8_t* base = p.down + (int64_t)prow * p.dbs;
-      const float* abase = p.down_am + (int64_t)(p.pair ? (prow >> 1) : prow) * p.dabs;
-      uint32_t w[4];
-      float am[4];
+    float acc[kDownRowTiles][4] = {};
+    for (int sb = s0; sb < s1; sb += kDownBatch) {
+      uint4 w[kDownBatch][kDownRowTiles];
+      float4 am[kDownBatch][kDownRowTiles];
+      uint4 bf[kDownBatch];
+      float as[kDownBatch];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int row = rt * 32 + (i >> 1) * 16 + g + (i & 1) * 8;
-        w[i] = ldg_u32(base + (int64_t)row * p.drs + t * 4);
-        am[i] = ldg_f32(abase + (int64_t)row * p.dars);
-      }
-      const uint4 bf = ldg_u4(p.act16 + (int64_t)s * 32 + t * 8);
-      const float as = ldg_f32(p.act_scale + s);
-      const uint32_t b[4] = {bf.x, bf.y, bf.z, bf.w};
+      for (int i = 0; i < kDownBatch; ++i) {
+        const int s = sb + i;
+        if (s < s1) {
+          const int prow = p.rows[s];
+          bf[i] = ldg_u4(p.act16 + (int64_t)s * 32 + t * 8);
+          as[i] = ldg_f32(p.act_scale + s);
 #pragma unroll
-      for (int rg = 0; rg < 2; ++rg) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t a0 = lut_lookup_rt(lut, w[rg * 2], lanebase, 2 * c, 0);
-          const uint32_t a1 = lut_lookup_rt(lut, w[rg * 2 + 1], lanebase, 2 * c, 0);
-          const uint32_t a2 = lut_lookup_rt(lut, w[rg * 2], lanebase, 2 * c + 1, 0);
-          const uint32_t a3 = lut_lookup_rt(lut, w[rg * 2 + 1], lanebase, 2 * c + 1, 0);
-          mma_16816(d, a0, a1, a2, a3, b[2 * c], b[2 * c + 1]);
+          for (int r = 0; r < kDownRowTiles; ++r)
+            if (rt0 + r < RT) down_load<kTiled>(p, prow, rt0 + r, lane, w[i][r], am[i][r]);
         }
-        acc[rg * 2] = fmaf(d[0], am[rg * 2] * as, acc[rg * 2]);
-        acc[rg * 2 + 1] = fmaf(d[2], am[rg * 2 + 1] * as, acc[rg * 2 + 1]);
+      }
+#pragma unroll
+      for (int i = 0; i < kDownBatch; ++i) {
+        if (sb + i < s1) {
+#pragma unroll
+          for (int r = 0; r < kDownRowTiles; ++r) {
+            if (rt0 + r < RT) {
+              float d[4];
+              down_mma(lanebase, w[i][r].x, w[i][r].y, bf[i], d);
+              acc[r][0] = fmaf(d[0], am[i][r].x * as[i], acc[r][0]);
+              acc[r][1] = fmaf(d[2], am[i][r].y * as[i], acc[r][1]);
+              down_mma(lanebase, w[i][r].z, w[i][r].w, bf[i], d);
+              acc[r][2] = fmaf(d[0], am[i][r].z * as[i], acc[r][2]);
+              acc[r][3] = fmaf(d[2], am[i][r].w * as[i], acc[r][3]);
+            }
+          }
+        }
       }
     }
-    if (t == 0) {
-      float* yp = p.ypart + (int64_t)grp * p.H + rt * 32;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) yp[(i >> 1) * 16 + g + (i & 1) * 8] = acc[i];
+    for (int r = 0; r < kDownRowTiles; ++r) {
+      const int rt = rt0 + r;
+      if (rt >= RT) break;
+      if (t == 0) {
+        float* yp = p.ypart + (int64_t)grp * p.H + rt * 32;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) yp[(i >> 1) * 16 + g + (i & 1) * 8] = acc[r][i];
+        __threadfence();
+      }
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&p.ticket_rt[rt], 1) == sg - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
       __threadfence();
+      float y = 0.f;
+#pragma unroll 8
+      for (int q = 0; q < sg; ++q) y += ldcg_f32(p.ypart + (int64_t)q * p.H + rt * 32 + lane);
+      if (p.down_bias) y += load_as_f32(p.down_bias, p.bias_dtype, rt * 32 + lane);
+      store_from_f32(p.y, p.y_dtype, rt * 32 + lane, y);
+      if (lane == 0) p.ticket_rt[rt] = 0;
     }
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-      const int prev = atomicAdd(&p.ticket_rt[rt], 1);
-      last = prev == sg - 1;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) continue;
-    __threadfence();
-    float y = 0.f;
-    for (int q = 0; q < sg; ++q) y += ldcg_f32(p.ypart + (int64_t)q * p.H + rt * 32 + lane);
-    if (p.down_bias) y += load_as_f32(p.down_bias, p.bias_dtype, rt * 32 + lane);
-    store_from_f32(p.y, p.y_dtype, rt * 32 + lane, y);
-    if (lane == 0) p.ticket_rt[rt] = 0;
   }
 }
 
@@ -610,22 +398,28 @@ static int dtype_ok(int d) { return d == NSM_F32 || d == NSM_F16 || d == NSM_BF1
 
 struct KernelSetup {
   bool done = false;
-  int gateup_ctas_per_sm = 0;
-  int down_ctas_per_sm = 0;
+  int gateup_ctas_per_sm[2] = {0, 0};
+  int down_ctas_per_sm[2] = {0, 0};
 };
 static KernelSetup g_setup[64];
+
+template <typename K>
+static int setup_one(K kernel, int* ctas_per_sm) {
+  NSM_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutBytes));
+  NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, 256, kLutBytes));
+  if (*ctas_per_sm <= 0) return fail(NSM_ERR_CUDA, "kernel occupancy is zero");
+  return NSM_OK;
+}
 
 static int setup_kernels(const DeviceInfo& d, KernelSetup** out) {
   KernelSetup& s = g_setup[d.device];
   if (!s.done) {
-    const int smem = kLutBytes;
-    NSM_CHECK_CUDA(cudaFuncSetAttribute(gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    NSM_CHECK_CUDA(cudaFuncSetAttribute(down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    NSM_CHECK_CUDA(cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        kMaxNumBlocks * 8));
-    NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&s.gateup_ctas_per_sm, gateup_kernel, 256, smem));
-    NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&s.down_ctas_per_sm, down_kernel, 256, smem));
-    if (s.gateup_ctas_per_sm <= 0 || s.down_ctas_per_sm <= 0) return fail(NSM_ERR_CUDA, "kernel occupancy is zero");
+    int st = setup_one(gateup_kernel<false>, &s.gateup_ctas_per_sm[0]);
+    if (!st) st = setup_one(gateup_kernel<true>, &s.gateup_ctas_per_sm[1]);
+    if (!st) st = setup_one(down_kernel<false>, &s.down_ctas_per_sm[0]);
+    if (!st) st = setup_one(down_kernel<true>, &s.down_ctas_per_sm[1]);
+    if (!st) st = router_setup();
+    if (st) return st;
     s.done = true;
   }
   *out = &s;
@@ -704,21 +498,26 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.act16 = ws.act16;
   gp.act_scale = ws.act_scale;
   gp.act_out = m.act_out;
-  const int gu_ctas = dev.sm_count * ks->gateup_ctas_per_sm;
+  const bool gu_tiled = (w->layout & NSM_LAYOUT_GATEUP_TILED) != 0;
+  const int gu_ctas = dev.sm_count * ks->gateup_ctas_per_sm[gu_tiled ? 1 : 0];
   gp.total_warps = gu_ctas * 8;
-  gateup_kernel<<<gu_ctas, 256, kLutBytes, stream>>>(gp);
+  if (gu_tiled)
+    gateup_kernel<true><<<gu_ctas, 256, kLutBytes, stream>>>(gp);
+  else
+    gateup_kernel<false><<<gu_ctas, 256, kLutBytes, stream>>>(gp);
   NSM_CHECK_CUDA(cudaGetLastError());
 
   DownParams dp{};
   dp.down = w->down_packed;
   dp.down_am = w->down_absmax;
-  const bool dflt = !w->down_block_stride && !w->down_row_stride && !w->down_absmax_block_stride &&
-                    !w->down_absmax_row_stride;
-  dp.dbs = dflt ? (int64_t)16 * m.H : w->down_block_stride;
+  const bool dflt = (!w->down_block_stride && !w->down_row_stride && !w->down_absmax_block_stride &&
+                     !w->down_absmax_row_stride) ||
+                    (w->layout & NSM_LAYOUT_DOWN_TILED);
+  dp.dbs = w->down_block_stride ? w->down_block_stride : (int64_t)16 * m.H;
   dp.drs = dflt ? 16 : w->down_row_stride;
-  dp.dabs = dflt ? (int64_t)m.H : w->down_absmax_block_stride;
+  dp.dabs = w->down_absmax_block_stride ? w->down_absmax_block_stride : (int64_t)m.H;
   dp.dars = dflt ? 1 : w->down_absmax_row_stride;
-  dp.pair = w->down_absmax_pair;
+  dp.pair = (w->layout & NSM_LAYOUT_DOWN_TILED) ? 0 : w->down_absmax_pair;
   dp.down_code = w->down_code;
   dp.down_bias = w->down_bias;
   dp.bias_dtype = w->bias_dtype;
@@ -731,15 +530,19 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   dp.ticket_rt = ws.ticket_rowtile;
   dp.y = m.y;
   dp.y_dtype = m.y_dtype;
-  const int dn_ctas = dev.sm_count * ks->down_ctas_per_sm;
+  const bool dn_tiled = (w->layout & NSM_LAYOUT_DOWN_TILED) != 0;
+  const int dn_ctas = dev.sm_count * ks->down_ctas_per_sm[dn_tiled ? 1 : 0];
   dp.total_warps = dn_ctas * 8;
-  down_kernel<<<dn_ctas, 256, kLutBytes, stream>>>(dp);
+  if (dn_tiled)
+    down_kernel<true><<<dn_ctas, 256, kLutBytes, stream>>>(dp);
+  else
+    down_kernel<false><<<dn_ctas, 256, kLutBytes, stream>>>(dp);
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
 }
 
-static int router_a_launch(const void* x, int x_dtype, const nsm_layer_io* io, const nsm_router_weights* rw, int H,
-                           const DecodeWs& ws, cudaStream_t stream) {
+static int router_a_prepare(const void* x, int x_dtype, const nsm_layer_io* io, const nsm_router_weights* rw,
+                            int H, const DecodeWs& ws, cudaStream_t stream) {
   RouterAParams a{};
   a.x = x;
   a.x_dtype = x_dtype;
@@ -760,16 +563,8 @@ static int router_a_launch(const void* x, int x_dtype, const nsm_layer_io* io, c
     a.basis_top_k = rw->basis_top_k;
   }
   a.H = H;
-  int ctas = std::min(kRouterMaxCtas, std::max(1, H / 64));
-  int cpc = ((H + ctas - 1) / ctas + 63) / 64 * 64;
-  // aim for ~128 columns per CTA (one wave of small CTAs)
-  cpc = std::max(cpc, 128);
-  ctas = (H + cpc - 1) / cpc;
-  a.cols_per_cta = cpc;
   a.ws = ws;
-  router_latent_kernel<<<ctas, 256, cpc * sizeof(float), stream>>>(a);
-  NSM_CHECK_CUDA(cudaGetLastError());
-  return NSM_OK;
+  return router_a_launch(a, stream);
 }
 
 static int validate_router(const nsm_router_weights* rw, int H) {
@@ -784,9 +579,9 @@ static int validate_router(const nsm_router_weights* rw, int H) {
   return NSM_OK;
 }
 
-static int router_b_launch(const nsm_router_weights* rw, int k, int32_t* idx_out, float* score_out,
-                           float* latent_out, const nsm_block_map* map, int pool_rows, const DecodeWs& ws,
-                           cudaStream_t stream) {
+static int router_b_prepare(const nsm_router_weights* rw, int k, int32_t* idx_out, float* score_out,
+                            float* latent_out, const nsm_block_map* map, int pool_rows, const DecodeWs& ws,
+                            cudaStream_t stream) {
   RouterBParams b{};
   b.score_w = rw->score_w;
   b.score_b = rw->score_b;
@@ -796,9 +591,6 @@ static int router_b_launch(const nsm_router_weights* rw, int k, int32_t* idx_out
   b.rank = rw->rank;
   b.NB = rw->num_blocks;
   b.top_k = k;
-  int sn = 1;
-  while (sn < b.NB) sn <<= 1;
-  b.sort_n = sn;
   b.idx_out = idx_out;
   b.score_out = score_out;
   b.latent_out = latent_out;
@@ -807,10 +599,7 @@ static int router_b_launch(const nsm_router_weights* rw, int k, int32_t* idx_out
   b.block_end = map ? map->block_end : b.NB;
   b.pool_rows = pool_rows;
   b.ws = ws;
-  const int ctas = (b.NB + 511) / 512;
-  router_select_kernel<<<ctas, 512, sn * 8, stream>>>(b);
-  NSM_CHECK_CUDA(cudaGetLastError());
-  return NSM_OK;
+  return router_b_launch(b, stream);
 }
 
 }  // namespace nsm
@@ -827,7 +616,8 @@ int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_w
   st = validate_router(rw, hidden);
   if (st) return st;
   NSM_REQUIRE(x != nullptr && dtype_ok(x_dtype), NSM_ERR_INVALID_ARG, "x is NULL or has a bad dtype");
-  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0, NSM_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0 && hidden <= kMaxHidden, NSM_ERR_UNSUPPORTED,
+              "hidden must be a positive multiple of 64, at most 65536");
   NSM_REQUIRE(idx_out != nullptr, NSM_ERR_INVALID_ARG, "idx_out is NULL");
   const int k = std::max(1, std::min(rw->top_k, rw->num_blocks));
   NSM_REQUIRE(k <= kMaxTopK, NSM_ERR_UNSUPPORTED, "top_k too large");
@@ -839,9 +629,9 @@ int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_w
   KernelSetup* ks;
   st = setup_kernels(dev, &ks);
   if (st) return st;
-  st = router_a_launch(x, x_dtype, nullptr, rw, hidden, w, s);
+  st = router_a_prepare(x, x_dtype, nullptr, rw, hidden, w, s);
   if (st) return st;
-  return router_b_launch(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w, s);
+  return router_b_prepare(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w, s);
 }
 
 int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_t intermediate,
@@ -851,7 +641,8 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   DeviceInfo dev;
   int st = current_device(&dev);
   if (st) return st;
-  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0, NSM_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0 && hidden <= kMaxHidden, NSM_ERR_UNSUPPORTED,
+              "hidden must be a positive multiple of 64, at most 65536");
   NSM_REQUIRE(intermediate > 0 && intermediate % 64 == 0, NSM_ERR_UNSUPPORTED,
               "intermediate must be a positive multiple of 64");
   const bool resid = io != nullptr && io->residual != nullptr;
@@ -884,10 +675,10 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   st = setup_kernels(dev, &ks);
   if (st) return st;
 
-  st = router_a_launch(x, x_dtype, io, idx_in ? nullptr : rw, hidden, wsl, s);
+  st = router_a_prepare(x, x_dtype, io, idx_in ? nullptr : rw, hidden, wsl, s);
   if (st) return st;
   if (idx_in == nullptr) {
-    st = router_b_launch(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl, s);
+    st = router_b_prepare(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl, s);
     if (st) return st;
   } else {
     RouterBParams b{};
@@ -897,8 +688,8 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
     b.block_end = map ? map->block_end : NB;
     b.pool_rows = w->pool_rows;
     b.ws = wsl;
-    select_given_kernel<<<1, 512, 0, s>>>(b, idx_in, k);
-    NSM_CHECK_CUDA(cudaGetLastError());
+    st = select_given_launch(b, idx_in, k, s);
+    if (st) return st;
   }
   MlpPlan m{};
   m.H = hidden;
@@ -921,7 +712,8 @@ int nsm_decode_gathered(const void* x, int32_t x_dtype, int32_t hidden, int32_t 
   DeviceInfo dev;
   int st = current_device(&dev);
   if (st) return st;
-  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0, NSM_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0 && hidden <= kMaxHidden, NSM_ERR_UNSUPPORTED,
+              "hidden must be a positive multiple of 64, at most 65536");
   NSM_REQUIRE(num_blocks_gathered > 0 && num_blocks_gathered <= kMaxTopK, NSM_ERR_UNSUPPORTED,
               "num_blocks_gathered must be in [1, 4096]");
   NSM_REQUIRE(x != nullptr && dtype_ok(x_dtype), NSM_ERR_INVALID_ARG, "x is NULL or has a bad dtype");
@@ -938,7 +730,7 @@ int nsm_decode_gathered(const void* x, int32_t x_dtype, int32_t hidden, int32_t 
   KernelSetup* ks;
   st = setup_kernels(dev, &ks);
   if (st) return st;
-  st = router_a_launch(x, x_dtype, nullptr, nullptr, hidden, wsl, s);
+  st = router_a_prepare(x, x_dtype, nullptr, nullptr, hidden, wsl, s);
   if (st) return st;
   identity_rows_kernel<<<(k + 255) / 256, 256, 0, s>>>(wsl.rows, wsl.count, wsl.sel_idx, k);
   NSM_CHECK_CUDA(cudaGetLastError());
@@ -972,7 +764,8 @@ int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32
   int st = current_device(&dev);
   if (st) return st;
   NSM_REQUIRE(rows > 0, NSM_ERR_INVALID_ARG, "rows must be > 0");
-  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0, NSM_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0 && hidden <= kMaxHidden, NSM_ERR_UNSUPPORTED,
+              "hidden must be a positive multiple of 64, at most 65536");
   NSM_REQUIRE(num_blocks_gathered > 0 && num_blocks_gathered <= kMaxTopK, NSM_ERR_UNSUPPORTED,
               "num_blocks_gathered must be in [1, 4096]");
   NSM_REQUIRE(x != nullptr && dtype_ok(x_dtype), NSM_ERR_INVALID_ARG, "x is NULL or has a bad dtype");
@@ -995,8 +788,8 @@ int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32
   const int yes = y_dtype == NSM_F32 ? 4 : 2;
   const int mes = mask_dtype == NSM_F32 ? 4 : 2;
   for (int r = 0; r < rows; ++r) {
-    st = router_a_launch(reinterpret_cast<const char*>(x) + (size_t)r * hidden * xes, x_dtype, nullptr, nullptr,
-                         hidden, wsl, s);
+    st = router_a_prepare(reinterpret_cast<const char*>(x) + (size_t)r * hidden * xes, x_dtype, nullptr, nullptr,
+                          hidden, wsl, s);
     if (st) return st;
     MlpPlan m{};
     m.H = hidden;

@@ -47,6 +47,8 @@ constexpr int kMaxNumBlocks = 8192;     // top-k sort capacity of the router
 constexpr int kMaxUnitsPerSlot = 64;    // gate/up column splits per block
 constexpr int kMaxSlotGroups = 32;      // down split-K groups
 constexpr int kRouterMaxCtas = 256;
+constexpr int kMaxHidden = 65536;       // counters are sized for this
+constexpr int kCounterInts = 2 + kMaxTopK + kMaxHidden / 32;
 
 // Decode workspace: one contiguous caller-owned buffer, 256-byte aligned parts.
 struct DecodeWs {
@@ -75,9 +77,9 @@ struct DecodeWs {
   size_t bytes;
 };
 
-// counters live first so a single memset of the head re-zeroes them
+// Counters sit at fixed offsets at the head of every workspace, whatever the
+// shape, so a zeroed workspace stays valid across calls with different shapes.
 DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank);
-size_t decode_ws_counter_bytes(int hidden, int top_k);
 
 // Cached occupancy-derived persistent grid sizes.
 struct LaunchShape {

@@ -1,0 +1,508 @@
+// nsm_router.cu -- learned-basis router for one token on sm_100a.
+//
+// router_latent_kernel (split-H, ~128 columns per CTA):
+//   * x preparation: optional residual += y_prev, RMSNorm sum of squares,
+//     fp16 copy of the MLP input with one power-of-two scale per 64 columns
+//     (consumed by the gate/up kernel);
+//   * partial latent = enc_w[:, slice] . x[slice] with 16-byte loads of enc_w
+//     issued before x is ready;
+//   * the last CTA (atomic ticket) reduces the partials in fixed CTA order,
+//     applies the RMSNorm scale and enc_b, and the optional basis top-k mask
+//     (streaming_llama_runtime.py:4220-4238).
+// router_select_kernel:
+//   * one thread per block: score = clamp0(latent . score_w[b] + score_b[b])
+//     (or |latent| . dec_norm_t[:, b] in legacy mode), times down_block_norm;
+//   * the last CTA selects the top-k with an 8-bit-digit radix select on
+//     order-preserving score bits, resolves ties at the threshold by lower
+//     block id, orders the k winners (score desc, block id asc) and compacts
+//     them into pool rows through the block map (:4324-4352).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "nsm_common.cuh"
+#include "nsm_internal.h"
+#include "nsm_router.h"
+
+namespace nsm {
+
+template <typename T>
+struct Vec8;  // 8 elements from one 16-byte load (T = bf16/f16) or two (f32)
+template <>
+struct Vec8<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p, float v[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+};
+template <>
+struct Vec8<__half> {
+  static __device__ __forceinline__ void load(const __half* p, float v[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+};
+template <>
+struct Vec8<float> {
+  static __device__ __forceinline__ void load(const float* p, float v[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+};
+
+// ---------------------------------------------------------------------------
+// router A
+// ---------------------------------------------------------------------------
+template <typename WT>
+__global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
+  extern __shared__ float xs[];  // [cols_per_cta]
+  __shared__ float red[8];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c0 = blockIdx.x * p.cols_per_cta;
+  const int c1 = min(p.H, c0 + p.cols_per_cta);
+  const int n = c1 - c0;  // multiple of 64
+  const WT* enc = reinterpret_cast<const WT*>(p.enc_w);
+
+  float sumsq = 0.f;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const int c = c0 + i;
+    float v;
+    if (p.residual != nullptr) {
+      v = p.residual[c];
+      if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
+      p.residual[c] = v;
+      sumsq += v * v;
+      if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
+    } else {
+      v = load_as_f32(p.x, p.x_dtype, c);
+    }
+    xs[i] = v;
+  }
+  sumsq = warp_sum(sumsq);
+  if (lane == 0) red[warp] = sumsq;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    p.ws.sumsq_part[blockIdx.x] = t;
+  }
+  const int ntiles = n >> 6;
+  for (int tl = warp; tl < ntiles; tl += 8) {
+    const float a = xs[tl * 64 + lane], b = xs[tl * 64 + 32 + lane];
+    const float m = warp_max(fmaxf(fabsf(a), fabsf(b)));
+    const float s = pow2_scale_for(m);
+    const float inv = 1.f / s;
+    const int c = c0 + tl * 64;
+    p.ws.x16[c + lane] = __float2half_rn(a * inv);
+    p.ws.x16[c + 32 + lane] = __float2half_rn(b * inv);
+    if (lane == 0) p.ws.xscale[c >> 6] = s;
+  }
+  if (enc != nullptr) {
+    // thread (row r, quarter q): columns [q*n/4, (q+1)*n/4) of this slice
+    const int seg = n >> 2;  // multiple of 16
+    for (int r0 = 0; r0 < p.rank; r0 += 64) {
+      const int r = r0 + (tid >> 2), q = tid & 3;
+      float acc = 0.f;
+      if (r < p.rank) {
+        const WT* row = enc + (int64_t)r * p.H + c0 + q * seg;
+        for (int i = 0; i < seg; i += 16) {
+          float a[8], b[8];
+          Vec8<WT>::load(row + i, a);
+          Vec8<WT>::load(row + i + 8, b);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = fmaf(a[e], xs[q * seg + i + e], acc);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = fmaf(b[e], xs[q * seg + i + 8 + e], acc);
+        }
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      if (q == 0 && r < p.rank) p.ws.latent_part[blockIdx.x * p.rank + r] = acc;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(p.ws.ticket_router_a, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __shared__ float s_norm;
+  __shared__ float lat[kMaxRank];
+  __shared__ float part4[4][kMaxRank];
+  const int nparts = gridDim.x;
+  if (warp == 0) {
+    float t = 0.f;
+    if (p.use_norm)
+      for (int b = lane; b < nparts; b += 32) t += ldcg_f32(&p.ws.sumsq_part[b]);
+    t = warp_sum(t);
+    if (lane == 0) {
+      const float ns = p.use_norm ? 1.f / sqrtf(t / (float)p.H + p.eps) : 1.f;
+      s_norm = ns;
+      *p.ws.norm_scale = ns;
+    }
+  }
+  if (enc != nullptr) {
+    for (int e = tid; e < 4 * p.rank; e += blockDim.x) {
+      const int r = e >> 2, q = e & 3;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int b = q; b < nparts; b += 4) acc += ldcg_f32(&p.ws.latent_part[b * p.rank + r]);
+      part4[q][r] = acc;
+    }
+  }
+  __syncthreads();
+  if (enc != nullptr) {
+    for (int r = tid; r < p.rank; r += blockDim.x) {
+      float acc = (part4[0][r] + part4[1][r]) + (part4[2][r] + part4[3][r]);
+      acc *= s_norm;
+      if (p.enc_b != nullptr) acc += load_as_f32(p.enc_b, p.wdtype, r);
+      lat[r] = acc;
+    }
+    __syncthreads();
+    const int bk = max(1, min(p.basis_top_k, p.rank));
+    for (int r = tid; r < p.rank; r += blockDim.x) {
+      float v = lat[r];
+      if (bk < p.rank) {
+        const float a = fabsf(v);
+        int pos = 0;
+        for (int q = 0; q < p.rank; ++q) {
+          const float b = fabsf(lat[q]);
+          pos += (b > a) || (b == a && q < r);
+        }
+        if (pos >= bk) v = 0.f;
+      }
+      p.ws.latent[r] = v;
+    }
+  }
+  if (tid == 0) *p.ws.ticket_router_a = 0;
+}
+
+// ---------------------------------------------------------------------------
+// router B
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t orderable(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float from_orderable(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
+__device__ __forceinline__ int map_block(const RouterBParams& p, int b) {
+  if (b < 0 || b >= p.NB) return -1;
+  int r;
+  if (p.slot_of_block != nullptr) {
+    r = p.slot_of_block[b];
+  } else {
+    r = (b >= p.block_begin && b < p.block_end) ? b - p.block_begin : -1;
+  }
+  return (r >= 0 && r < p.pool_rows) ? r : -1;
+}
+
+// Block-wide exclusive scan of one int per thread (blockDim <= 1024).
+__device__ __forceinline__ int block_exclusive_scan(int v, int* total) {
+  __shared__ int wsum[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int s = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < nw) wsum[lane] = s;  // inclusive
+  }
+  __syncthreads();
+  const int before = (warp > 0 ? wsum[warp - 1] : 0) + x - v;
+  *total = wsum[nw - 1];
+  __syncthreads();
+  return before;
+}
+
+// Compacts sel[0..k) through the block map into ws.rows / ws.row_block / ws.count.
+__device__ void compact_selection(const RouterBParams& p, const int* sel, int k) {
+  __shared__ int s_base;
+  if (threadIdx.x == 0) s_base = 0;
+  __syncthreads();
+  for (int j0 = 0; j0 < k; j0 += blockDim.x) {
+    const int j = j0 + threadIdx.x;
+    const int r = j < k ? map_block(p, sel[j]) : -1;
+    int tot;
+    const int pos = block_exclusive_scan(r >= 0 ? 1 : 0, &tot);
+    if (r >= 0) {
+      p.ws.rows[s_base + pos] = r;
+      p.ws.row_block[s_base + pos] = sel[j];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_base += tot;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *p.ws.count = s_base;
+}
+
+template <typename WT>
+__device__ __forceinline__ float score_row(const RouterBParams& p, const float* lat, int b) {
+  const WT* row = reinterpret_cast<const WT*>(p.score_w) + (int64_t)b * p.rank;
+  float acc = 0.f;
+  if ((p.rank & 7) == 0) {
+    for (int r = 0; r < p.rank; r += 8) {
+      float v[8];
+      Vec8<WT>::load(row + r, v);
+      if (p.legacy) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(fabsf(lat[r + e]), v[e], acc);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(lat[r + e], v[e], acc);
+      }
+    }
+  } else {
+    for (int r = 0; r < p.rank; ++r) {
+      const float v = to_f32(row[r]);
+      acc = fmaf(p.legacy ? fabsf(lat[r]) : lat[r], v, acc);
+    }
+  }
+  if (!p.legacy) {
+    if (p.score_b != nullptr) acc += to_f32(reinterpret_cast<const WT*>(p.score_b)[b]);
+    acc = fmaxf(acc, 0.f);
+  }
+  if (p.dbn != nullptr) acc *= p.dbn[b];
+  return acc;
+}
+
+template <typename WT>
+__global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
+  extern __shared__ uint32_t keys[];  // [NB]  (last CTA)
+  __shared__ float lat[kMaxRank];
+  __shared__ int s_last;
+  __shared__ int hist[256];
+  __shared__ uint32_t s_prefix, s_mask;
+  __shared__ int s_need;
+  __shared__ uint32_t sel_key[1024];
+  __shared__ int sel_id[1024];
+  const int tid = threadIdx.x;
+  for (int r = tid; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r]);
+  __syncthreads();
+  for (int b = blockIdx.x * blockDim.x + tid; b < p.NB; b += gridDim.x * blockDim.x)
+    p.ws.scores[b] = score_row<WT>(p, lat, b);
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(p.ws.ticket_router_b, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int NB = p.NB, k = p.top_k;
+  for (int i = tid; i < NB; i += blockDim.x) keys[i] = orderable(ldcg_f32(&p.ws.scores[i]));
+  if (tid == 0) {
+    s_prefix = 0u;
+    s_mask = 0u;
+    s_need = k;
+  }
+  __syncthreads();
+  // radix select of the k-th largest key, 8 bits per pass
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    __syncthreads();
+    const uint32_t pre = s_prefix, msk = s_mask;
+    for (int i = tid; i < NB; i += blockDim.x) {
+      const uint32_t key = keys[i];
+      if ((key & msk) == pre) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // lane l owns bins [255-8l-7, 255-8l] (descending), finds the bin holding the need-th key
+      int c[8];
+      int loc = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        c[e] = hist[255 - 8 * tid - e];
+        loc += c[e];
+      }
+      int incl = loc;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += y;
+      }
+      const int excl = incl - loc;
+      const int need = s_need;
+      if (excl < need && need <= incl) {
+        int run = excl;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (run < need && need <= run + c[e]) {
+            const uint32_t bin = 255u - 8u * tid - e;
+            s_prefix = pre | (bin << shift);
+            s_mask = msk | (255u << shift);
+            s_need = need - run;
+          }
+          run += c[e];
+        }
+      }
+    }
+    __syncthreads();
+  }
+  const uint32_t thr = s_prefix;
+  const int take_eq = s_need;  // how many keys equal to thr are selected (lowest ids first)
+  // select: key > thr, or key == thr among the first take_eq by block id
+  const int per = (NB + blockDim.x - 1) / blockDim.x;
+  const int lo = tid * per, hi = min(NB, lo + per);
+  int n_eq = 0, n_gt = 0;
+  for (int i = lo; i < hi; ++i) {
+    n_eq += keys[i] == thr;
+    n_gt += keys[i] > thr;
+  }
+  int tot_eq, tot_sel;
+  const int eq_before = block_exclusive_scan(n_eq, &tot_eq);
+  int my_sel = n_gt + max(0, min(n_eq, take_eq - eq_before));
+  const int sel_before = block_exclusive_scan(my_sel, &tot_sel);
+  {
+    int e = eq_before, out = sel_before;
+    for (int i = lo; i < hi; ++i) {
+      const uint32_t key = keys[i];
+      bool s = key > thr;
+      if (key == thr) {
+        s = e < take_eq;
+        ++e;
+      }
+      if (s && out < 1024) {
+        sel_key[out] = key;
+        sel_id[out] = i;
+      }
+      if (s) ++out;
+    }
+  }
+  __syncthreads();
+  // order the k winners: rank by counting (key desc, id asc)
+  if (k <= 1024) {
+    for (int j = tid; j < k; j += blockDim.x) {
+      const uint32_t kj = sel_key[j];
+      const int ij = sel_id[j];
+      int pos = 0;
+      for (int q = 0; q < k; ++q) {
+        const uint32_t kq = sel_key[q];
+        pos += (kq > kj) || (kq == kj && sel_id[q] < ij);
+      }
+      p.ws.sel_idx[pos] = ij;
+      if (p.idx_out) p.idx_out[pos] = ij;
+      if (p.score_out) p.score_out[pos] = from_orderable(kj);
+    }
+  } else {
+    // large k: every block's rank among all blocks (k > 1024 is outside the
+    // configurations this path is tuned for, but stays exact)
+    for (int i = tid; i < NB; i += blockDim.x) {
+      const uint32_t ki = keys[i];
+      int pos = 0;
+      for (int q = 0; q < NB; ++q) {
+        const uint32_t kq = keys[q];
+        pos += (kq > ki) || (kq == ki && q < i);
+      }
+      if (pos < k) {
+        p.ws.sel_idx[pos] = i;
+        if (p.idx_out) p.idx_out[pos] = i;
+        if (p.score_out) p.score_out[pos] = from_orderable(ki);
+      }
+    }
+  }
+  if (p.latent_out)
+    for (int r = tid; r < p.rank; r += blockDim.x) p.latent_out[r] = lat[r];
+  __threadfence_block();
+  __syncthreads();
+  compact_selection(p, p.ws.sel_idx, k);
+  if (tid == 0) *p.ws.ticket_router_b = 0;
+}
+
+__global__ void __launch_bounds__(512) select_given_kernel(RouterBParams p, const int32_t* idx_in, int k) {
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const int b = idx_in[j];
+    p.ws.sel_idx[j] = (b >= 0 && b < p.NB) ? b : -1;
+  }
+  __syncthreads();
+  compact_selection(p, p.ws.sel_idx, k);
+}
+
+// ---------------------------------------------------------------------------
+// launches
+// ---------------------------------------------------------------------------
+int router_setup() {
+  static bool done[64] = {};
+  int dev = 0;
+  NSM_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && done[dev]) return NSM_OK;
+  const int smem = kMaxNumBlocks * 4;
+  NSM_CHECK_CUDA(cudaFuncSetAttribute(router_select_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  NSM_CHECK_CUDA(cudaFuncSetAttribute(router_select_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  NSM_CHECK_CUDA(
+      cudaFuncSetAttribute(router_select_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return NSM_OK;
+}
+
+int router_a_launch(const RouterAParams& a_in, cudaStream_t stream) {
+  RouterAParams a = a_in;
+  int ctas = std::max(1, (a.H + 127) / 128);
+  int cpc = 128;
+  if (ctas > kRouterMaxCtas) {
+    cpc = ((a.H + kRouterMaxCtas - 1) / kRouterMaxCtas + 63) / 64 * 64;
+    ctas = (a.H + cpc - 1) / cpc;
+  }
+  a.cols_per_cta = cpc;
+  const size_t smem = (size_t)cpc * sizeof(float);
+  switch (a.wdtype) {
+    case NSM_F32: router_latent_kernel<float><<<ctas, 256, smem, stream>>>(a); break;
+    case NSM_F16: router_latent_kernel<__half><<<ctas, 256, smem, stream>>>(a); break;
+    default: router_latent_kernel<__nv_bfloat16><<<ctas, 256, smem, stream>>>(a); break;
+  }
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+int router_b_launch(const RouterBParams& b, cudaStream_t stream) {
+  int st = router_setup();
+  if (st) return st;
+  const int ctas = (b.NB + 511) / 512;
+  const size_t smem = (size_t)b.NB * 4;
+  switch (b.wdtype) {
+    case NSM_F32: router_select_kernel<float><<<ctas, 512, smem, stream>>>(b); break;
+    case NSM_F16: router_select_kernel<__half><<<ctas, 512, smem, stream>>>(b); break;
+    default: router_select_kernel<__nv_bfloat16><<<ctas, 512, smem, stream>>>(b); break;
+  }
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+int select_given_launch(const RouterBParams& b, const int32_t* idx_in, int k, cudaStream_t stream) {
+  select_given_kernel<<<1, 512, 0, stream>>>(b, idx_in, k);
+  NSM_CHECK_CUDA(cudaGetLastError());
+  return NSM_OK;
+}
+
+}  // namespace nsm

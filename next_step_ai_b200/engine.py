@@ -1,0 +1,120 @@
+"""Multi-layer decode of the blockwise-sparse MLP stack (one token per step).
+
+This is the B200 counterpart of the reference's per-token layer loop
+(``streaming_llama_runtime.py:7612-7775``) restricted to the MLP path: for
+every decoder layer the residual is updated with the previous layer's MLP
+output, RMS-normalised, routed, and pushed through the sparse NF4 MLP.
+Attention is out of scope (identity), as in the benchmark configuration.
+
+Multi-GPU: every rank holds a contiguous range of each layer's intermediate
+blocks and a full copy of the router; all ranks select the same blocks, each
+computes the partial output of the blocks it owns, and the partials are
+summed with one NCCL all-reduce per layer (``torch.distributed``).  The whole
+token is captured once into a CUDA graph and replayed.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._torch import WORKSPACES, dtype_code, ptr, stream_handle
+from .weights import RouterWeights, SparseMlpWeights
+
+
+@dataclass
+class DecodeLayer:
+    router: RouterWeights
+    weights: SparseMlpWeights
+    norm_weight: torch.Tensor | None = None
+
+
+class SparseMlpDecoder:
+    """Runs ``num_layers`` decode steps over ``layers`` (cycled when fewer
+    unique layers than ``num_layers`` are resident).
+
+    ``block_range``: the intermediate blocks this rank's pools hold
+    (``(0, NB)`` on one GPU).  ``group``: process group for the partial-sum
+    all-reduce (None on one GPU).
+    """
+
+    def __init__(self, layers: list[DecodeLayer], num_layers: int, *, block_range: tuple[int, int] | None = None,
+                 group=None, reduce_dtype: torch.dtype = torch.bfloat16, eps: float = 1e-5):
+        if not layers:
+            raise RuntimeError("no layers")
+        self.layers = layers
+        self.num_layers = int(num_layers)
+        w0 = layers[0].weights
+        self.H, self.I = w0.hidden, w0.intermediate
+        self.dev = w0.gate_packed.device
+        self.block_range = block_range if block_range is not None else (0, self.I // 32)
+        self.group = group
+        self.eps = float(eps)
+        self.residual = torch.zeros(self.H, dtype=torch.float32, device=self.dev)
+        self.y = [torch.zeros(self.H, dtype=reduce_dtype, device=self.dev) for _ in range(2)]
+        self.out = torch.zeros(self.H, dtype=torch.float32, device=self.dev)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self._lib = _lib.load()
+        k = max(l.router.top_k for l in layers)
+        rank = max(l.router.rank for l in layers)
+        self._ws_bytes = self._lib.nsm_decode_workspace_bytes(self.H, self.I, k, rank)
+        self._c = [(l.router.to_c(), l.weights.to_c()) for l in layers]
+        self._bm = _lib.BlockMapC()
+        self._bm.block_begin, self._bm.block_end = int(self.block_range[0]), int(self.block_range[1])
+
+    def _layer(self, i: int, ws: torch.Tensor, st: int) -> None:
+        li = i % len(self.layers)
+        layer = self.layers[li]
+        rc, wc = self._c[li]
+        y_prev = self.y[(i + 1) % 2] if i > 0 else None
+        y = self.y[i % 2]
+        io = _lib.LayerIoC()
+        io.residual = self.residual.data_ptr()
+        io.y_prev = y_prev.data_ptr() if y_prev is not None else None
+        io.y_prev_dtype = dtype_code(y.dtype)
+        io.norm_weight = ptr(layer.norm_weight) if layer.norm_weight is not None else None
+        io.norm_weight_dtype = dtype_code(layer.norm_weight.dtype) if layer.norm_weight is not None else 0
+        io.eps = self.eps
+        _lib.check(self._lib.nsm_sparse_mlp_decode(
+            None, 0, self.H, self.I, ctypes.byref(io), ctypes.byref(rc), None, 0, ctypes.byref(self._bm),
+            ctypes.byref(wc), y.data_ptr(), dtype_code(y.dtype), None, None, ws.data_ptr(), ws.numel(), st),
+            "nsm_sparse_mlp_decode")
+        if self.group is not None:
+            torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM, group=self.group)
+
+    def step_eager(self) -> None:
+        """One token through all layers (no graph).  Input: ``residual``;
+        output: ``out`` = final residual (residual + last MLP output)."""
+        ws = WORKSPACES.get(self._ws_bytes, self.dev)
+        st = stream_handle(self.dev)
+        for i in range(self.num_layers):
+            self._layer(i, ws, st)
+        last = self.y[(self.num_layers - 1) % 2]
+        torch.add(self.residual, last.float(), out=self.out)
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """Capture one token into a CUDA graph (after one eager warm-up)."""
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            saved = self.residual.clone()
+            self.step_eager()  # warm-up: workspace for this stream, kernel attributes, NCCL comms
+            self.residual.copy_(saved)
+            torch.cuda.synchronize(self.dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self.step_eager()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        self.graph = g
+        return g
+
+    def replay(self) -> None:
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()
+
+    def release(self) -> None:
+        self.graph = None

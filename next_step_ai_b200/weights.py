@@ -10,11 +10,17 @@ layout the decode kernels read:
   column slice contiguous, the layout of the reference's down-proj column
   cache entries (``:4506-4513``) -- so one block's rows stream coalesced.
 
+By default pools are repacked into the lane-interleaved "tiled" layout
+(``include/nsm.h``, ``NSM_LAYOUT_*``): every warp load of the decode kernels
+then covers 512 contiguous bytes and a lane's four absmax values arrive in one
+16-byte load.  ``layout=0`` keeps the bitsandbytes / block-major layouts above.
+
 A pool may hold only some blocks (a hot-block cache or a shard); ``pool_rows``
 counts them and a block map sends block ids to pool rows.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass, field
 
 import torch
@@ -96,6 +102,7 @@ class SparseMlpWeights:
     gate_bias: torch.Tensor | None = None
     up_bias: torch.Tensor | None = None
     down_bias: torch.Tensor | None = None
+    layout: int = 0
     _c: object = field(default=None, repr=False)
 
     @property
@@ -123,6 +130,11 @@ class SparseMlpWeights:
         c.down_bias = ptr(self.down_bias)
         c.bias_dtype = dtype_code(bias.dtype) if bias is not None else 0
         c.pool_rows = self.pool_rows
+        c.gateup_block_stride = int(self.gate_packed.stride(0))
+        c.gateup_absmax_block_stride = int(self.gate_absmax.stride(0))
+        c.down_block_stride = int(self.down_packed.stride(0))
+        c.down_absmax_block_stride = int(self.down_absmax.stride(0))
+        c.layout = int(self.layout)
         self._c = c
         return c
 
@@ -130,7 +142,8 @@ class SparseMlpWeights:
     def from_bnb_rowmajor(cls, *, hidden: int, intermediate: int, gate_packed: torch.Tensor, gate_absmax: torch.Tensor,
                           up_packed: torch.Tensor, up_absmax: torch.Tensor, down_packed: torch.Tensor,
                           down_absmax: torch.Tensor, code: torch.Tensor, up_code: torch.Tensor | None = None,
-                          down_code: torch.Tensor | None = None, **biases) -> "SparseMlpWeights":
+                          down_code: torch.Tensor | None = None, tiled: bool = True,
+                          **biases) -> "SparseMlpWeights":
         """From whole bitsandbytes NF4 weights (gate/up ``[I, H]``, down
         ``[H, I]``, packed row-major, fp32 absmax) already on the GPU."""
         H, I = int(hidden), int(intermediate)
@@ -139,22 +152,38 @@ class SparseMlpWeights:
         gm = Nf4ParamMeta(I, H)
         dev = gate_packed.device
         nb = I // 32
+        code = code.to(device=dev, dtype=torch.float32).contiguous()
+        uc = up_code.to(dev, torch.float32).contiguous() if up_code is not None else code
+        dc = down_code.to(dev, torch.float32).contiguous() if down_code is not None else code
+        lib = _lib.load()
+        if tiled:
+            w = cls(hidden=H, intermediate=I,
+                    gate_packed=torch.empty((nb, gm.bytes_per_block), dtype=torch.uint8, device=dev),
+                    gate_absmax=torch.empty((nb, gm.absmax_per_block), dtype=torch.float32, device=dev),
+                    up_packed=torch.empty((nb, gm.bytes_per_block), dtype=torch.uint8, device=dev),
+                    up_absmax=torch.empty((nb, gm.absmax_per_block), dtype=torch.float32, device=dev),
+                    down_packed=torch.empty((nb, H, 16), dtype=torch.uint8, device=dev),
+                    down_absmax=torch.empty((nb, H), dtype=torch.float32, device=dev),
+                    gate_code=code, up_code=uc, down_code=dc,
+                    layout=_lib.NSM_LAYOUT_GATEUP_TILED | _lib.NSM_LAYOUT_DOWN_TILED, **biases)
+            src = [t.contiguous() for t in (gate_packed, gate_absmax.float(), up_packed, up_absmax.float(),
+                                            down_packed, down_absmax.float())]
+            _lib.check(lib.nsm_repack_tiled(*[ptr(t) for t in src], H, I, None, None, nb, ctypes.byref(w.to_c()),
+                                            stream_handle(dev)), "nsm_repack_tiled")
+            del src
+            return w
         dp = torch.empty((nb, H, 16), dtype=torch.uint8, device=dev)
         da = torch.empty((nb, H), dtype=torch.float32, device=dev)
-        _lib.check(_lib.load().nsm_repack_down_block_major(
+        _lib.check(lib.nsm_repack_down_block_major(
             ptr(down_packed.contiguous()), ptr(down_absmax.to(torch.float32).contiguous()), H, I, None, 0,
             ptr(dp), ptr(da), stream_handle(dev)), "nsm_repack_down_block_major")
-        code = code.to(device=dev, dtype=torch.float32).contiguous()
         return cls(
             hidden=H, intermediate=I,
             gate_packed=gate_packed.reshape(nb, gm.bytes_per_block).contiguous(),
             gate_absmax=gate_absmax.to(torch.float32).reshape(nb, gm.absmax_per_block).contiguous(),
             up_packed=up_packed.reshape(nb, gm.bytes_per_block).contiguous(),
             up_absmax=up_absmax.to(torch.float32).reshape(nb, gm.absmax_per_block).contiguous(),
-            down_packed=dp, down_absmax=da, gate_code=code,
-            up_code=(up_code.to(dev, torch.float32).contiguous() if up_code is not None else code),
-            down_code=(down_code.to(dev, torch.float32).contiguous() if down_code is not None else code),
-            **biases)
+            down_packed=dp, down_absmax=da, gate_code=code, up_code=uc, down_code=dc, **biases)
 
 
 def gathered_mlp_c(*, hidden: int, gate_packed: torch.Tensor, gate_absmax: torch.Tensor, up_packed: torch.Tensor,

@@ -227,15 +227,12 @@ def test_decode_cfg1_device_generated(dev):
     ga = bnb["gate_absmax"].view(-1, gm.absmax_per_block)[s].cpu().numpy()
     upk = bnb["up_packed"].view(-1, gm.bytes_per_block)[s].cpu().numpy()
     ua = bnb["up_absmax"].view(-1, gm.absmax_per_block)[s].cpu().numpy()
-    dcols = w.down_packed[s].permute(1, 0, 2).contiguous().cpu().numpy()
-    dabs = w.down_absmax[s].t().contiguous().cpu().numpy()
+    # the reference's down column gather, done on the device for speed
+    dcols = bnb["down_packed"].view(H, dmeta.bytes_per_row)[:, None, :].view(H, -1, 16)[:, s].contiguous().cpu().numpy()
+    dabs = bnb["down_absmax"].view(H, dmeta.absmax_per_row)[:, s // 2].contiguous().cpu().numpy()
     code = bnb["code"].cpu().numpy()
     ref = om.sparse_mlp_gathered(xn, gp, ga, code, upk, ua, code, dcols, dabs, code)[0]
     assert_close(y.cpu().numpy(), ref)
-    # block-major down repack equals the reference column gather of the raw weight
-    raw_cols, raw_abs = om.gather_down_cols(bnb["down_packed"].cpu().numpy(), bnb["down_absmax"].cpu().numpy(),
-                                            dmeta, sel[:5])
-    assert np.array_equal(dcols[:, :5], raw_cols) and np.array_equal(dabs[:, :5], raw_abs)
 
 
 def test_decode_explicit_idx_and_shards_sum(dev):
@@ -263,10 +260,77 @@ def test_decode_explicit_idx_and_shards_sum(dev):
                               gate_absmax=w.gate_absmax[lo:hi].clone(), up_packed=w.up_packed[lo:hi].clone(),
                               up_absmax=w.up_absmax[lo:hi].clone(), down_packed=w.down_packed[lo:hi].clone(),
                               down_absmax=w.down_absmax[lo:hi].clone(), gate_code=w.gate_code, up_code=w.up_code,
-                              down_code=w.down_code)
+                              down_code=w.down_code, layout=w.layout)
         acc += sparse_mlp_decode(xd, None, ws, idx=T(sel, dev), block_range=(lo, hi),
                                  out_dtype=torch.float32).cpu().numpy()
     assert_close(acc, ref)
+
+
+def untile_gateup(packed, absmax, H):
+    """numpy inverse of the tiled gate/up layout (include/nsm.h) for one block."""
+    p = packed.reshape(H // 64, 2, 8, 4, 2, 8)  # tile, rg, g, t, half(row g / g+8), byte
+    rows = np.zeros((32, H // 2), np.uint8)
+    for rg in range(2):
+        for h in range(2):
+            for g in range(8):
+                r = rg * 16 + g + 8 * h
+                rows[r] = p[:, rg, g, :, h, :].reshape(-1)
+    a = absmax.reshape(H // 64, 8, 4)
+    am = np.zeros((32, H // 64), np.float32)
+    for g in range(8):
+        for i in range(4):
+            am[(i >> 1) * 16 + g + (i & 1) * 8] = a[:, g, i]
+    return rows.reshape(-1), am.reshape(-1)
+
+
+def untile_down(packed, absmax, H):
+    p = packed.reshape(H // 32, 8, 4, 4, 4)  # rt, g, t, i(row), byte
+    cols = np.zeros((H, 16), np.uint8)
+    am = np.zeros(H, np.float32)
+    a = absmax.reshape(H // 32, 8, 4)
+    for i in range(4):
+        for g in range(8):
+            r = np.arange(H // 32) * 32 + (i >> 1) * 16 + g + (i & 1) * 8
+            cols[r] = p[:, g, :, i, :].reshape(H // 32, 16)
+            am[r] = a[:, g, i]
+    return cols, am
+
+
+def test_tiled_repack_round_trip(dev):
+    shape = syn.SHAPES["small"]
+    full = full_layer("small", 12)
+    w = weights_for(shape, full, dev)
+    assert w.layout == 3
+    H, I = shape.hidden, shape.intermediate
+    gm = om.Nf4ParamMeta(I, H)
+    dm = om.Nf4ParamMeta(H, I)
+    for b in (0, 7, shape.num_blocks - 1):
+        gp, ga = untile_gateup(w.gate_packed[b].cpu().numpy(), w.gate_absmax[b].cpu().numpy(), H)
+        ref_p, ref_a = om.gather_row_blocks(full["gate_packed"], full["gate_absmax"], gm, [b])
+        assert np.array_equal(gp, ref_p[0]) and np.array_equal(ga, ref_a[0])
+        up, ua = untile_gateup(w.up_packed[b].cpu().numpy(), w.up_absmax[b].cpu().numpy(), H)
+        ref_p, ref_a = om.gather_row_blocks(full["up_packed"], full["up_absmax"], gm, [b])
+        assert np.array_equal(up, ref_p[0]) and np.array_equal(ua, ref_a[0])
+        dc, da = untile_down(w.down_packed[b].cpu().numpy(), w.down_absmax[b].cpu().numpy(), H)
+        rc, ra = om.gather_down_cols(full["down_packed"], full["down_absmax"], dm, [b])
+        assert np.array_equal(dc, rc[:, 0]) and np.array_equal(da, ra[:, 0])
+
+
+def test_row_major_and_tiled_layouts_agree(dev):
+    from next_step_ai_b200 import SparseMlpWeights, sparse_mlp_decode
+
+    shape = syn.SHAPES["cfg0"]
+    full = full_layer("cfg0", 0)
+    rw = router_for(shape, syn.make_router(shape, 0), dev)
+    xd = T(syn.make_x(shape, 5, 1)[0], dev, torch.bfloat16)
+    kw = dict(hidden=shape.hidden, intermediate=shape.intermediate, gate_packed=T(full["gate_packed"], dev),
+              gate_absmax=T(full["gate_absmax"], dev), up_packed=T(full["up_packed"], dev),
+              up_absmax=T(full["up_absmax"], dev), down_packed=T(full["down_packed"], dev),
+              down_absmax=T(full["down_absmax"], dev), code=T(full["code"], dev))
+    a = sparse_mlp_decode(xd, rw, SparseMlpWeights.from_bnb_rowmajor(tiled=True, **kw), out_dtype=torch.float32)
+    b = sparse_mlp_decode(xd, rw, SparseMlpWeights.from_bnb_rowmajor(tiled=False, **kw), out_dtype=torch.float32)
+    # same products, same fixed-order reductions: identical bits
+    assert torch.equal(a, b)
 
 
 def test_decode_edge_cases(dev):
