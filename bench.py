@@ -137,7 +137,7 @@ def run_ours(args) -> None:
     shape = dsyn.SHAPES["cfg1"]
     shard_bytes = LAYER_BYTES_GPU // world
     free, _ = torch.cuda.mem_get_info(dev)
-    budget = free - (6 << 30)
+    budget = free - (10 << 30)
     unique = max(1, min(LAYERS, budget // (shard_bytes + (3 << 20))))
     t0 = time.time()
     layers = []
@@ -150,6 +150,7 @@ def run_ours(args) -> None:
                                  down_packed=w.down_packed[lo:hi].clone(), down_absmax=w.down_absmax[lo:hi].clone(),
                                  gate_code=w.gate_code, up_code=w.up_code, down_code=w.down_code, layout=w.layout)
             torch.cuda.empty_cache()
+        torch.cuda.empty_cache()
         rw = dsyn.make_router(shape, 1234, l, dev)
         layers.append(DecodeLayer(router=rw, weights=w,
                                   norm_weight=torch.ones(HIDDEN, dtype=torch.bfloat16, device=dev)))

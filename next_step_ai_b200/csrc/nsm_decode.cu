@@ -45,19 +45,67 @@ __global__ void identity_rows_kernel(int* rows, int* count, int* sel, int n) {
 }
 
 // ============================================================================
-// 3. gate/up gather-GEMV + SiLU*up
+// 3/4. NF4 gather-GEMV kernels: shared helpers
 // ============================================================================
-// The byte->half2 tables live at the start of the dynamic shared memory of
-// both MLP kernels; indexing the extern array directly lets the compiler fold
-// its offset into the shared-load immediate.
+// Dynamic shared memory of both MLP kernels: [0, 64 KB) byte->half2 tables,
+// then 2 KB of table-building scratch, then per-call vectors staged once per
+// CTA (x16 + xscale for gate/up; act16 + act_scale + rows for down).
 extern __shared__ __align__(1024) uint32_t g_lut_smem[];
+constexpr int kLutScratch = 2048;
+constexpr int kSmemHead = kLutBytes + kLutScratch;
 
-template <int kTable>
-__device__ __forceinline__ uint32_t lut_at(uint32_t w, uint32_t lanebase, int kbyte) {
-  const uint32_t addr = __byte_perm(w, lanebase, 0x5504u | ((uint32_t)kbyte << 4));
-  return *reinterpret_cast<const uint32_t*>(reinterpret_cast<const char*>(g_lut_smem) + addr + kTable * 128);
+// Byte `kbyte` of w -> half2 from table kTable.  kFast: the table starts at a
+// shared address whose bits 8..15 are zero, so one byte-permute builds the
+// whole 32-bit shared address (lane offset and table base bytes from
+// `lanebase`, the entry from w).
+template <bool kFast>
+__device__ __forceinline__ uint32_t lut_get(uint32_t w, uint32_t lanebase, int kbyte, int table) {
+  if (kFast) {
+    const uint32_t addr = __byte_perm(w, lanebase, 0x7604u | ((uint32_t)kbyte << 4)) + table * 128;
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+  } else {
+    const uint32_t addr = __byte_perm(w, lanebase, 0x5504u | ((uint32_t)kbyte << 4));
+    return *reinterpret_cast<const uint32_t*>(reinterpret_cast<const char*>(g_lut_smem) + addr + table * 128);
+  }
 }
 
+__device__ __forceinline__ bool lut_fast_ok(uint32_t* lanebase_fast, uint32_t lane) {
+  const uint32_t base = (uint32_t)__cvta_generic_to_shared(g_lut_smem);
+  *lanebase_fast = base + lane * 4u;
+  return (base & 0xffffu) == 0u;  // table rows never carry into the entry byte
+}
+
+__device__ __forceinline__ void mma_16816_z(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+__device__ __forceinline__ void build_lut_dyn(const float* code0, const float* code1) {
+  uint32_t* pairs = g_lut_smem + kLutBytes / 4;  // scratch [2][256]
+  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+    const int t = i >> 8, e = i & 255;
+    const float* c = t == 0 ? code0 : code1;
+    const __half lo = __float2half_rn(c[e >> 4]);
+    const __half hi = __float2half_rn(c[e & 15]);
+    pairs[i] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+  }
+  __syncthreads();
+  uint4* lut4 = reinterpret_cast<uint4*>(g_lut_smem);
+  for (int i = threadIdx.x; i < 256 * kLutWordsPerEntry / 4; i += blockDim.x) {
+    const uint32_t v = pairs[((i >> 3) & 1) * 256 + (i >> 4)];
+    lut4[i] = make_uint4(v, v, v, v);
+  }
+}
+
+// ============================================================================
+// 3. gate/up gather-GEMV + SiLU*up
+// ============================================================================
 struct GateUpParams {
   const uint8_t* gate;
   const float* gate_am;
@@ -128,40 +176,47 @@ __device__ __forceinline__ void gu_load(const GateUpParams& p, const uint8_t* gb
 }
 
 // 16 rows x 64 columns: four k=16 MMAs over the lane's bytes of two rows.
-template <int kTable>
-__device__ __forceinline__ void gu_mma_rowgroup(uint32_t lanebase, const uint4 w, const uint32_t b[8], float d[4]) {
-  d[0] = d[1] = d[2] = d[3] = 0.f;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint32_t r0 = c < 2 ? w.x : w.y;
-    const uint32_t r1 = c < 2 ? w.z : w.w;
-    const int kb = (c & 1) * 2;
-    mma_16816(d, lut_at<kTable>(r0, lanebase, kb), lut_at<kTable>(r1, lanebase, kb),
-              lut_at<kTable>(r0, lanebase, kb + 1), lut_at<kTable>(r1, lanebase, kb + 1), b[2 * c], b[2 * c + 1]);
-  }
+template <bool kFast, int kTable>
+__device__ __forceinline__ void gu_mma_rowgroup(uint32_t lb, const uint4 w, const uint32_t b[8], float d[4]) {
+  mma_16816_z(d, lut_get<kFast>(w.x, lb, 0, kTable), lut_get<kFast>(w.z, lb, 0, kTable),
+              lut_get<kFast>(w.x, lb, 1, kTable), lut_get<kFast>(w.z, lb, 1, kTable), b[0], b[1]);
+  mma_16816(d, lut_get<kFast>(w.x, lb, 2, kTable), lut_get<kFast>(w.z, lb, 2, kTable),
+            lut_get<kFast>(w.x, lb, 3, kTable), lut_get<kFast>(w.z, lb, 3, kTable), b[2], b[3]);
+  mma_16816(d, lut_get<kFast>(w.y, lb, 0, kTable), lut_get<kFast>(w.w, lb, 0, kTable),
+            lut_get<kFast>(w.y, lb, 1, kTable), lut_get<kFast>(w.w, lb, 1, kTable), b[4], b[5]);
+  mma_16816(d, lut_get<kFast>(w.y, lb, 2, kTable), lut_get<kFast>(w.w, lb, 2, kTable),
+            lut_get<kFast>(w.y, lb, 3, kTable), lut_get<kFast>(w.w, lb, 3, kTable), b[6], b[7]);
 }
 
-__device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& tile, int j, int t, uint32_t lanebase,
-                                           float acc[2][4]) {
+template <bool kFast, bool kStageX>
+__device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& tile, int j, int t, uint32_t lb,
+                                           const __half* xs16, const float* xss, float acc[2][4]) {
   uint32_t b[8];
-  {
+  float xs;
+  if (kStageX) {
+    const uint4 xa = *reinterpret_cast<const uint4*>(xs16 + j * 64 + t * 16);
+    const uint4 xb = *reinterpret_cast<const uint4*>(xs16 + j * 64 + t * 16 + 8);
+    b[0] = xa.x; b[1] = xa.y; b[2] = xa.z; b[3] = xa.w;
+    b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
+    xs = xss[j];
+  } else {
     const uint4 xa = ldg_u4(p.x16 + j * 64 + t * 16);
     const uint4 xb = ldg_u4(p.x16 + j * 64 + t * 16 + 8);
     b[0] = xa.x; b[1] = xa.y; b[2] = xa.z; b[3] = xa.w;
     b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
+    xs = ldg_f32(p.xscale + j);
   }
-  const float xs = ldg_f32(p.xscale + j);
-  const float ag[4] = {tile.am[0].x * xs, tile.am[0].y * xs, tile.am[0].z * xs, tile.am[0].w * xs};
-  const float au[4] = {tile.am[1].x * xs, tile.am[1].y * xs, tile.am[1].z * xs, tile.am[1].w * xs};
+  float d[4];
 #pragma unroll
   for (int rg = 0; rg < 2; ++rg) {
-    float d[4];
-    gu_mma_rowgroup<0>(lanebase, tile.w[0][rg], b, d);
-    acc[0][rg * 2] = fmaf(d[0], ag[rg * 2], acc[0][rg * 2]);
-    acc[0][rg * 2 + 1] = fmaf(d[2], ag[rg * 2 + 1], acc[0][rg * 2 + 1]);
-    gu_mma_rowgroup<1>(lanebase, tile.w[1][rg], b, d);
-    acc[1][rg * 2] = fmaf(d[0], au[rg * 2], acc[1][rg * 2]);
-    acc[1][rg * 2 + 1] = fmaf(d[2], au[rg * 2 + 1], acc[1][rg * 2 + 1]);
+    gu_mma_rowgroup<kFast, 0>(lb, tile.w[0][rg], b, d);
+    const float g0 = rg ? tile.am[0].z : tile.am[0].x, g1 = rg ? tile.am[0].w : tile.am[0].y;
+    acc[0][rg * 2] = fmaf(d[0], g0 * xs, acc[0][rg * 2]);
+    acc[0][rg * 2 + 1] = fmaf(d[2], g1 * xs, acc[0][rg * 2 + 1]);
+    gu_mma_rowgroup<kFast, 1>(lb, tile.w[1][rg], b, d);
+    const float u0 = rg ? tile.am[1].z : tile.am[1].x, u1 = rg ? tile.am[1].w : tile.am[1].y;
+    acc[1][rg * 2] = fmaf(d[0], u0 * xs, acc[1][rg * 2]);
+    acc[1][rg * 2 + 1] = fmaf(d[2], u1 * xs, acc[1][rg * 2 + 1]);
   }
 }
 
@@ -173,12 +228,10 @@ __device__ __forceinline__ int gateup_tiles_per_unit(int count, int tiles_per_ro
   return max(tpu, min_tpu);
 }
 
-template <bool kTiled>
-__global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
-  build_lut(g_lut_smem, p.gate_code, p.up_code);
+template <bool kTiled, bool kStageX, bool kFast>
+__device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, const __half* xs16, const float* xss) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t lanebase = (uint32_t)lane * 4u;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int count = *p.count_ptr;
   const int tiles_per_row = p.H >> 6;
@@ -200,13 +253,13 @@ __global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
     if (j0 + 1 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j0 + 1, lane, t1);
     for (int j = j0; j < j1; j += 3) {
       if (j + 2 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 2, lane, t2);
-      gu_compute(p, t0, j, t, lanebase, acc);
+      gu_compute<kFast, kStageX>(p, t0, j, t, lb, xs16, xss, acc);
       if (j + 1 >= j1) break;
       if (j + 3 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 3, lane, t0);
-      gu_compute(p, t1, j + 1, t, lanebase, acc);
+      gu_compute<kFast, kStageX>(p, t1, j + 1, t, lb, xs16, xss, acc);
       if (j + 2 >= j1) break;
       if (j + 4 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 4, lane, t1);
-      gu_compute(p, t2, j + 2, t, lanebase, acc);
+      gu_compute<kFast, kStageX>(p, t2, j + 2, t, lb, xs16, xss, acc);
     }
     // column 0 of the accumulator lives in lanes with t == 0
     float* part = p.gu_part + ((int64_t)s * kMaxUnitsPerSlot + sub) * 64;
@@ -255,6 +308,28 @@ __global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
   }
 }
 
+constexpr int kStageXMaxHidden = 16384;
+
+template <bool kTiled, bool kStageX>
+__global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
+  build_lut_dyn(p.gate_code, p.up_code);
+  __half* xs16 = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
+  float* xss = reinterpret_cast<float*>(xs16 + (kStageX ? p.H : 0));
+  if (kStageX) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.x16);
+    uint4* dst = reinterpret_cast<uint4*>(xs16);
+    for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = __ldcg(src + i);
+    for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
+  }
+  __syncthreads();
+  uint32_t lb_fast;
+  const uint32_t lane = threadIdx.x & 31;
+  if (lut_fast_ok(&lb_fast, lane))
+    gateup_body<kTiled, kStageX, true>(p, lb_fast, xs16, xss);
+  else
+    gateup_body<kTiled, kStageX, false>(p, lane * 4u, xs16, xss);
+}
+
 // ============================================================================
 // 4. down column gather-GEMV (split-K over blocks)
 // ============================================================================
@@ -278,8 +353,8 @@ struct DownParams {
   int total_warps;
 };
 
-constexpr int kDownRowTiles = 2;  // 32-row tiles per unit
-constexpr int kDownBatch = 4;     // blocks whose loads are in flight together
+constexpr int kDownBatch = 4;          // blocks per load batch (two batches in flight)
+constexpr int kStageActMaxSlots = 256;  // act16 + scale + row staged in shared memory up to this k
 
 template <bool kTiled>
 __device__ __forceinline__ void down_load(const DownParams& p, int prow, int rt, int lane, uint4& w, float4& am) {
@@ -287,7 +362,7 @@ __device__ __forceinline__ void down_load(const DownParams& p, int prow, int rt,
   const uint8_t* base = p.down + (int64_t)prow * p.dbs;
   const float* abase = p.down_am + (int64_t)(p.pair ? (prow >> 1) : prow) * p.dabs;
   if (kTiled) {
-    w = ldg_u4(base + (int64_t)rt * 512 + lane * 16);
+    w = ldg_stream_u4(base + (int64_t)rt * 512 + lane * 16);
     am = ldg_f4(abase + rt * 32 + g * 4);
   } else {
     const int r0 = rt * 32 + g;
@@ -302,93 +377,128 @@ __device__ __forceinline__ void down_load(const DownParams& p, int prow, int rt,
   }
 }
 
-__device__ __forceinline__ void down_mma(uint32_t lanebase, uint32_t w0, uint32_t w1, const uint4 bf, float d[4]) {
-  d[0] = d[1] = d[2] = d[3] = 0.f;
-  mma_16816(d, lut_at<0>(w0, lanebase, 0), lut_at<0>(w1, lanebase, 0), lut_at<0>(w0, lanebase, 1),
-            lut_at<0>(w1, lanebase, 1), bf.x, bf.y);
-  mma_16816(d, lut_at<0>(w0, lanebase, 2), lut_at<0>(w1, lanebase, 2), lut_at<0>(w0, lanebase, 3),
-            lut_at<0>(w1, lanebase, 3), bf.z, bf.w);
+template <bool kFast>
+__device__ __forceinline__ void down_mma(uint32_t lb, uint32_t w0, uint32_t w1, const uint4 bf, float d[4]) {
+  mma_16816_z(d, lut_get<kFast>(w0, lb, 0, 0), lut_get<kFast>(w1, lb, 0, 0), lut_get<kFast>(w0, lb, 1, 0),
+              lut_get<kFast>(w1, lb, 1, 0), bf.x, bf.y);
+  mma_16816(d, lut_get<kFast>(w0, lb, 2, 0), lut_get<kFast>(w1, lb, 2, 0), lut_get<kFast>(w0, lb, 3, 0),
+            lut_get<kFast>(w1, lb, 3, 0), bf.z, bf.w);
 }
 
-template <bool kTiled>
-__global__ void __launch_bounds__(256, 2) down_kernel(DownParams p) {
-  build_lut(g_lut_smem, p.down_code, p.down_code);
-  const int lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-  const uint32_t lanebase = (uint32_t)lane * 4u;
-  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int count = *p.count_ptr;
-  const int RT = p.H >> 5;
-  const int RG = (RT + kDownRowTiles - 1) / kDownRowTiles;  // row-tile groups
-  int sg = (3 * p.total_warps + RG - 1) / RG;
-  sg = max(1, min(sg, min(max(count, 1), kMaxSlotGroups)));
-  const int gs = (count + sg - 1) / sg;
-  const int nunits = RG * sg;
+struct DownBatch {
+  uint4 w[kDownBatch];
+  float4 am[kDownBatch];
+};
 
-  for (int u = warp_global; u < nunits; u += p.total_warps) {
-    const int grp = u / RG, rgi = u - grp * RG;
-    const int rt0 = rgi * kDownRowTiles;
-    const int s0 = grp * gs, s1 = min(count, s0 + gs);
-    float acc[kDownRowTiles][4] = {};
-    for (int sb = s0; sb < s1; sb += kDownBatch) {
-      uint4 w[kDownBatch][kDownRowTiles];
-      float4 am[kDownBatch][kDownRowTiles];
-      uint4 bf[kDownBatch];
-      float as[kDownBatch];
+template <bool kTiled, bool kStage>
+__device__ __forceinline__ void down_batch_load(const DownParams& p, const int* srows, int sb, int s1, int rt,
+                                                int lane, DownBatch& b) {
 #pragma unroll
-      for (int i = 0; i < kDownBatch; ++i) {
-        const int s = sb + i;
-        if (s < s1) {
-          const int prow = p.rows[s];
-          bf[i] = ldg_u4(p.act16 + (int64_t)s * 32 + t * 8);
-          as[i] = ldg_f32(p.act_scale + s);
-#pragma unroll
-          for (int r = 0; r < kDownRowTiles; ++r)
-            if (rt0 + r < RT) down_load<kTiled>(p, prow, rt0 + r, lane, w[i][r], am[i][r]);
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < kDownBatch; ++i) {
-        if (sb + i < s1) {
-#pragma unroll
-          for (int r = 0; r < kDownRowTiles; ++r) {
-            if (rt0 + r < RT) {
-              float d[4];
-              down_mma(lanebase, w[i][r].x, w[i][r].y, bf[i], d);
-              acc[r][0] = fmaf(d[0], am[i][r].x * as[i], acc[r][0]);
-              acc[r][1] = fmaf(d[2], am[i][r].y * as[i], acc[r][1]);
-              down_mma(lanebase, w[i][r].z, w[i][r].w, bf[i], d);
-              acc[r][2] = fmaf(d[0], am[i][r].z * as[i], acc[r][2]);
-              acc[r][3] = fmaf(d[2], am[i][r].w * as[i], acc[r][3]);
-            }
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < kDownRowTiles; ++r) {
-      const int rt = rt0 + r;
-      if (rt >= RT) break;
-      if (t == 0) {
-        float* yp = p.ypart + (int64_t)grp * p.H + rt * 32;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) yp[(i >> 1) * 16 + g + (i & 1) * 8] = acc[r][i];
-        __threadfence();
-      }
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) last = atomicAdd(&p.ticket_rt[rt], 1) == sg - 1;
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) continue;
-      __threadfence();
-      float y = 0.f;
-#pragma unroll 8
-      for (int q = 0; q < sg; ++q) y += ldcg_f32(p.ypart + (int64_t)q * p.H + rt * 32 + lane);
-      if (p.down_bias) y += load_as_f32(p.down_bias, p.bias_dtype, rt * 32 + lane);
-      store_from_f32(p.y, p.y_dtype, rt * 32 + lane, y);
-      if (lane == 0) p.ticket_rt[rt] = 0;
+  for (int i = 0; i < kDownBatch; ++i) {
+    if (sb + i < s1) {
+      const int prow = kStage ? srows[sb + i] : p.rows[sb + i];
+      down_load<kTiled>(p, prow, rt, lane, b.w[i], b.am[i]);
     }
   }
+}
+
+template <bool kFast, bool kStage>
+__device__ __forceinline__ void down_batch_compute(const DownParams& p, const __half* sact, const float* sscale,
+                                                   int sb, int s1, int t, uint32_t lb, const DownBatch& b,
+                                                   float acc[4]) {
+#pragma unroll
+  for (int i = 0; i < kDownBatch; ++i) {
+    const int s = sb + i;
+    if (s < s1) {
+      uint4 bf;
+      float as;
+      if (kStage) {
+        bf = *reinterpret_cast<const uint4*>(sact + s * 32 + t * 8);
+        as = sscale[s];
+      } else {
+        bf = ldg_u4(p.act16 + (int64_t)s * 32 + t * 8);
+        as = ldg_f32(p.act_scale + s);
+      }
+      float d[4];
+      down_mma<kFast>(lb, b.w[i].x, b.w[i].y, bf, d);
+      acc[0] = fmaf(d[0], b.am[i].x * as, acc[0]);
+      acc[1] = fmaf(d[2], b.am[i].y * as, acc[1]);
+      down_mma<kFast>(lb, b.w[i].z, b.w[i].w, bf, d);
+      acc[2] = fmaf(d[0], b.am[i].z * as, acc[2]);
+      acc[3] = fmaf(d[2], b.am[i].w * as, acc[3]);
+    }
+  }
+}
+
+template <bool kTiled, bool kStage, bool kFast>
+__device__ __forceinline__ void down_body(const DownParams& p, uint32_t lb, const __half* sact, const float* sscale,
+                                          const int* srows, int count) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int RT = p.H >> 5;
+  int sg = (3 * p.total_warps + RT - 1) / RT;
+  sg = max(1, min(sg, min(max(count, 1), kMaxSlotGroups)));
+  const int gs = (count + sg - 1) / sg;
+  const int nunits = RT * sg;
+
+  for (int u = warp_global; u < nunits; u += p.total_warps) {
+    const int grp = u / RT, rt = u - grp * RT;
+    const int s0 = grp * gs, s1 = min(count, s0 + gs);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, 16+g, 24+g of the tile
+    DownBatch b0, b1;
+    if (s0 < s1) down_batch_load<kTiled, kStage>(p, srows, s0, s1, rt, lane, b0);
+    for (int sb = s0; sb < s1; sb += 2 * kDownBatch) {
+      if (sb + kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + kDownBatch, s1, rt, lane, b1);
+      down_batch_compute<kFast, kStage>(p, sact, sscale, sb, s1, t, lb, b0, acc);
+      if (sb + kDownBatch >= s1) break;
+      if (sb + 2 * kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + 2 * kDownBatch, s1, rt, lane, b0);
+      down_batch_compute<kFast, kStage>(p, sact, sscale, sb + kDownBatch, s1, t, lb, b1, acc);
+    }
+    if (t == 0) {
+      float* yp = p.ypart + (int64_t)grp * p.H + rt * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) yp[(i >> 1) * 16 + g + (i & 1) * 8] = acc[i];
+      __threadfence();
+    }
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&p.ticket_rt[rt], 1) == sg - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) continue;
+    __threadfence();
+    float y = 0.f;
+#pragma unroll 8
+    for (int q = 0; q < sg; ++q) y += ldcg_f32(p.ypart + (int64_t)q * p.H + rt * 32 + lane);
+    if (p.down_bias) y += load_as_f32(p.down_bias, p.bias_dtype, rt * 32 + lane);
+    store_from_f32(p.y, p.y_dtype, rt * 32 + lane, y);
+    if (lane == 0) p.ticket_rt[rt] = 0;
+  }
+}
+
+template <bool kTiled, bool kStage>
+__global__ void __launch_bounds__(256, 2) down_kernel(DownParams p) {
+  build_lut_dyn(p.down_code, p.down_code);
+  const int count = *p.count_ptr;
+  __half* sact = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
+  float* sscale = reinterpret_cast<float*>(sact + kStageActMaxSlots * 32);
+  int* srows = reinterpret_cast<int*>(sscale + kStageActMaxSlots);
+  if (kStage) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.act16);
+    uint4* dst = reinterpret_cast<uint4*>(sact);
+    for (int i = threadIdx.x; i < count * 4; i += blockDim.x) dst[i] = __ldcg(src + i);
+    for (int i = threadIdx.x; i < count; i += blockDim.x) {
+      sscale[i] = __ldcg(p.act_scale + i);
+      srows[i] = __ldcg(p.rows + i);
+    }
+  }
+  __syncthreads();
+  uint32_t lb_fast;
+  const uint32_t lane = threadIdx.x & 31;
+  if (lut_fast_ok(&lb_fast, lane))
+    down_body<kTiled, kStage, true>(p, lb_fast, sact, sscale, srows, count);
+  else
+    down_body<kTiled, kStage, false>(p, lane * 4u, sact, sscale, srows, count);
 }
 
 // ============================================================================
@@ -396,17 +506,20 @@ __global__ void __launch_bounds__(256, 2) down_kernel(DownParams p) {
 // ============================================================================
 static int dtype_ok(int d) { return d == NSM_F32 || d == NSM_F16 || d == NSM_BF16; }
 
+constexpr int kGateupSmemStaged = kSmemHead + kStageXMaxHidden * 2 + (kStageXMaxHidden / 64) * 4;
+constexpr int kDownSmemStaged = kSmemHead + kStageActMaxSlots * (64 + 4 + 4);
+
 struct KernelSetup {
   bool done = false;
-  int gateup_ctas_per_sm[2] = {0, 0};
-  int down_ctas_per_sm[2] = {0, 0};
+  int gu[2][2] = {{0, 0}, {0, 0}};  // [tiled][staged] CTAs per SM
+  int dn[2][2] = {{0, 0}, {0, 0}};
 };
 static KernelSetup g_setup[64];
 
 template <typename K>
-static int setup_one(K kernel, int* ctas_per_sm) {
-  NSM_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLutBytes));
-  NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, 256, kLutBytes));
+static int setup_one(K kernel, int smem, int* ctas_per_sm) {
+  NSM_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, 256, smem));
   if (*ctas_per_sm <= 0) return fail(NSM_ERR_CUDA, "kernel occupancy is zero");
   return NSM_OK;
 }
@@ -414,10 +527,14 @@ static int setup_one(K kernel, int* ctas_per_sm) {
 static int setup_kernels(const DeviceInfo& d, KernelSetup** out) {
   KernelSetup& s = g_setup[d.device];
   if (!s.done) {
-    int st = setup_one(gateup_kernel<false>, &s.gateup_ctas_per_sm[0]);
-    if (!st) st = setup_one(gateup_kernel<true>, &s.gateup_ctas_per_sm[1]);
-    if (!st) st = setup_one(down_kernel<false>, &s.down_ctas_per_sm[0]);
-    if (!st) st = setup_one(down_kernel<true>, &s.down_ctas_per_sm[1]);
+    int st = setup_one(gateup_kernel<false, false>, kSmemHead, &s.gu[0][0]);
+    if (!st) st = setup_one(gateup_kernel<false, true>, kGateupSmemStaged, &s.gu[0][1]);
+    if (!st) st = setup_one(gateup_kernel<true, false>, kSmemHead, &s.gu[1][0]);
+    if (!st) st = setup_one(gateup_kernel<true, true>, kGateupSmemStaged, &s.gu[1][1]);
+    if (!st) st = setup_one(down_kernel<false, false>, kSmemHead, &s.dn[0][0]);
+    if (!st) st = setup_one(down_kernel<false, true>, kDownSmemStaged, &s.dn[0][1]);
+    if (!st) st = setup_one(down_kernel<true, false>, kSmemHead, &s.dn[1][0]);
+    if (!st) st = setup_one(down_kernel<true, true>, kDownSmemStaged, &s.dn[1][1]);
     if (!st) st = router_setup();
     if (st) return st;
     s.done = true;
@@ -499,24 +616,27 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.act_scale = ws.act_scale;
   gp.act_out = m.act_out;
   const bool gu_tiled = (w->layout & NSM_LAYOUT_GATEUP_TILED) != 0;
-  const int gu_ctas = dev.sm_count * ks->gateup_ctas_per_sm[gu_tiled ? 1 : 0];
+  const bool gu_stage = m.H <= kStageXMaxHidden;
+  const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
   gp.total_warps = gu_ctas * 8;
-  if (gu_tiled)
-    gateup_kernel<true><<<gu_ctas, 256, kLutBytes, stream>>>(gp);
-  else
-    gateup_kernel<false><<<gu_ctas, 256, kLutBytes, stream>>>(gp);
+  const int gu_smem = gu_stage ? kGateupSmemStaged : kSmemHead;
+  if (gu_tiled) {
+    if (gu_stage) gateup_kernel<true, true><<<gu_ctas, 256, gu_smem, stream>>>(gp);
+    else gateup_kernel<true, false><<<gu_ctas, 256, gu_smem, stream>>>(gp);
+  } else {
+    if (gu_stage) gateup_kernel<false, true><<<gu_ctas, 256, gu_smem, stream>>>(gp);
+    else gateup_kernel<false, false><<<gu_ctas, 256, gu_smem, stream>>>(gp);
+  }
   NSM_CHECK_CUDA(cudaGetLastError());
 
   DownParams dp{};
   dp.down = w->down_packed;
   dp.down_am = w->down_absmax;
-  const bool dflt = (!w->down_block_stride && !w->down_row_stride && !w->down_absmax_block_stride &&
-                     !w->down_absmax_row_stride) ||
-                    (w->layout & NSM_LAYOUT_DOWN_TILED);
+  const bool dn_tiled_layout = (w->layout & NSM_LAYOUT_DOWN_TILED) != 0;
   dp.dbs = w->down_block_stride ? w->down_block_stride : (int64_t)16 * m.H;
-  dp.drs = dflt ? 16 : w->down_row_stride;
+  dp.drs = (w->down_row_stride && !dn_tiled_layout) ? w->down_row_stride : 16;
   dp.dabs = w->down_absmax_block_stride ? w->down_absmax_block_stride : (int64_t)m.H;
-  dp.dars = dflt ? 1 : w->down_absmax_row_stride;
+  dp.dars = (w->down_absmax_row_stride && !dn_tiled_layout) ? w->down_absmax_row_stride : 1;
   dp.pair = (w->layout & NSM_LAYOUT_DOWN_TILED) ? 0 : w->down_absmax_pair;
   dp.down_code = w->down_code;
   dp.down_bias = w->down_bias;
@@ -531,12 +651,17 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   dp.y = m.y;
   dp.y_dtype = m.y_dtype;
   const bool dn_tiled = (w->layout & NSM_LAYOUT_DOWN_TILED) != 0;
-  const int dn_ctas = dev.sm_count * ks->down_ctas_per_sm[dn_tiled ? 1 : 0];
+  const bool dn_stage = m.k <= kStageActMaxSlots;
+  const int dn_ctas = dev.sm_count * ks->dn[dn_tiled][dn_stage];
   dp.total_warps = dn_ctas * 8;
-  if (dn_tiled)
-    down_kernel<true><<<dn_ctas, 256, kLutBytes, stream>>>(dp);
-  else
-    down_kernel<false><<<dn_ctas, 256, kLutBytes, stream>>>(dp);
+  const int dn_smem = dn_stage ? kDownSmemStaged : kSmemHead;
+  if (dn_tiled) {
+    if (dn_stage) down_kernel<true, true><<<dn_ctas, 256, dn_smem, stream>>>(dp);
+    else down_kernel<true, false><<<dn_ctas, 256, dn_smem, stream>>>(dp);
+  } else {
+    if (dn_stage) down_kernel<false, true><<<dn_ctas, 256, dn_smem, stream>>>(dp);
+    else down_kernel<false, false><<<dn_ctas, 256, dn_smem, stream>>>(dp);
+  }
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
 }

@@ -21,6 +21,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 
 #include "nsm_common.cuh"
 #include "nsm_internal.h"
@@ -79,22 +80,22 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
   const int n = c1 - c0;  // multiple of 64
   const WT* enc = reinterpret_cast<const WT*>(p.enc_w);
 
+  // encoder rows for this slice: issue the loads before x is ready
+  // (fast path: rank <= 64 and 32 columns per thread of 2-byte weights)
+  const int seg = n >> 2;  // multiple of 16
+  const bool fast = enc != nullptr && p.rank <= 64 && seg == 32 && sizeof(WT) == 2;
+  uint4 pre[4];
+  if (fast) {
+    const int r = tid >> 2, q = tid & 3;
+    if (r < p.rank) {
+      const uint4* row = reinterpret_cast<const uint4*>(enc + (int64_t)r * p.H + c0 + q * seg);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pre[i] = __ldg(row + i);
+    }
+  }
   float sumsq = 0.f;
   for (int i = tid; i < n; i += blockDim.x) {
-    const int c = c0 + i;
-    float v;
-    if (p.residual != nullptr) {
-      v = p.residual[c];
-      if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
-      p.residual[c] = v;
-      sumsq += v * v;
-      if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
-    } else {
-      v = load_as_f32(p.x, p.x_dtype, c);
-    }
-    xs[i] = v;
-  }
-  sumsq = warp_sum(sumsq);
+    const int c = c0 + i;  sumsq = warp_sum(sumsq);
   if (lane == 0) red[warp] = sumsq;
   __syncthreads();
   if (tid == 0) {
@@ -113,9 +114,34 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
     p.ws.x16[c + 32 + lane] = __float2half_rn(b * inv);
     if (lane == 0) p.ws.xscale[c >> 6] = s;
   }
-  if (enc != nullptr) {
+  if (fast) {
+    const int r = tid >> 2, q = tid & 3;
+    float acc = 0.f;
+    if (r < p.rank) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t w4[4] = {pre[i].x, pre[i].y, pre[i].z, pre[i].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float lo, hi;
+          if (sizeof(WT) == 2 && std::is_same<WT, __half>::value) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+            lo = f.x;
+            hi = f.y;
+          } else {
+            lo = __uint_as_float(w4[e] << 16);
+            hi = __uint_as_float(w4[e] & 0xffff0000u);
+          }
+          acc = fmaf(lo, xs[q * seg + i * 8 + 2 * e], acc);
+          acc = fmaf(hi, xs[q * seg + i * 8 + 2 * e + 1], acc);
+        }
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (q == 0 && r < p.rank) p.ws.latent_part[blockIdx.x * p.rank + r] = acc;
+  } else if (enc != nullptr) {
     // thread (row r, quarter q): columns [q*n/4, (q+1)*n/4) of this slice
-    const int seg = n >> 2;  // multiple of 16
     for (int r0 = 0; r0 < p.rank; r0 += 64) {
       const int r = r0 + (tid >> 2), q = tid & 3;
       float acc = 0.f;
@@ -163,7 +189,7 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
     for (int e = tid; e < 4 * p.rank; e += blockDim.x) {
       const int r = e >> 2, q = e & 3;
       float acc = 0.f;
-#pragma unroll 8
+#pragma unroll 32
       for (int b = q; b < nparts; b += 4) acc += ldcg_f32(&p.ws.latent_part[b * p.rank + r]);
       part4[q][r] = acc;
     }
@@ -270,23 +296,27 @@ template <typename WT>
 __device__ __forceinline__ float score_row(const RouterBParams& p, const float* lat, int b) {
   const WT* row = reinterpret_cast<const WT*>(p.score_w) + (int64_t)b * p.rank;
   float acc = 0.f;
-  if ((p.rank & 7) == 0) {
+  if (p.rank == 64) {
+    // all of the row's loads in flight at once
+    float v[64];
+#pragma unroll
+    for (int r = 0; r < 64; r += 8) Vec8<WT>::load(row + r, v + r);
+    if (p.legacy) {
+#pragma unroll
+      for (int r = 0; r < 64; ++r) acc = fmaf(fabsf(lat[r]), v[r], acc);
+    } else {
+#pragma unroll
+      for (int r = 0; r < 64; ++r) acc = fmaf(lat[r], v[r], acc);
+    }
+  } else if ((p.rank & 7) == 0) {
     for (int r = 0; r < p.rank; r += 8) {
       float v[8];
       Vec8<WT>::load(row + r, v);
-      if (p.legacy) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc = fmaf(fabsf(lat[r + e]), v[e], acc);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc = fmaf(lat[r + e], v[e], acc);
-      }
+      for (int e = 0; e < 8; ++e) acc = fmaf(p.legacy ? fabsf(lat[r + e]) : lat[r + e], v[e], acc);
     }
   } else {
-    for (int r = 0; r < p.rank; ++r) {
-      const float v = to_f32(row[r]);
-      acc = fmaf(p.legacy ? fabsf(lat[r]) : lat[r], v, acc);
-    }
+    for (int r = 0; r < p.rank; ++r) acc = fmaf(p.legacy ? fabsf(lat[r]) : lat[r], to_f32(row[r]), acc);
   }
   if (!p.legacy) {
     if (p.score_b != nullptr) acc += to_f32(reinterpret_cast<const WT*>(p.score_b)[b]);
@@ -332,9 +362,14 @@ __global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t pre = s_prefix, msk = s_mask;
-    for (int i = tid; i < NB; i += blockDim.x) {
-      const uint32_t key = keys[i];
-      if ((key & msk) == pre) atomicAdd(&hist[(key >> shift) & 255u], 1);
+    // warp-aggregated increments: scores cluster in a few top-digit bins
+    for (int i0 = 0; i0 < NB; i0 += blockDim.x) {
+      const int i = i0 + tid;
+      const uint32_t key = i < NB ? keys[i] : 0u;
+      const bool on = i < NB && (key & msk) == pre;
+      const uint32_t bin = on ? ((key >> shift) & 255u) : 256u;
+      const unsigned grp = __match_any_sync(0xffffffffu, bin);
+      if (on && (threadIdx.x & 31) == (__ffs(grp) - 1)) atomicAdd(&hist[bin], __popc(grp));
     }
     __syncthreads();
     if (tid < 32) {

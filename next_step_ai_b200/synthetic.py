@@ -75,16 +75,17 @@ def make_router(shape: LayerShape, seed: int, layer: int = 0, device="cuda",
 
 
 def make_nf4_matrix(rows: int, cols: int, seed: int, device="cuda", code: torch.Tensor | None = None,
-                    chunk_rows: int = 4096):
+                    chunk_elems: int = 1 << 25):
     """NF4 of an N(0, 0.02) ``[rows, cols]`` weight: packed ``[rows*cols/2]``, absmax ``[rows*cols/64]``."""
     code = nf4_code(device) if code is None else code
     g = _gen(seed, device)
     packed = torch.empty(rows * cols // 2, dtype=torch.uint8, device=device)
     absmax = torch.empty(rows * cols // 64, dtype=torch.float32, device=device)
+    chunk_rows = max(1, chunk_elems // cols)
     for r0 in range(0, rows, chunk_rows):
         r1 = min(rows, r0 + chunk_rows)
         w = torch.randn((r1 - r0, cols), generator=g, device=device) * WEIGHT_STD
-        p, a = quantize_nf4(w, code)
+        p, a = quantize_nf4(w, code, chunk_rows=chunk_rows)
         packed[r0 * cols // 2:r1 * cols // 2] = p
         absmax[r0 * cols // 64:r1 * cols // 64] = a
         del w

@@ -133,7 +133,9 @@ class SparseMlpWeights:
         c.gateup_block_stride = int(self.gate_packed.stride(0))
         c.gateup_absmax_block_stride = int(self.gate_absmax.stride(0))
         c.down_block_stride = int(self.down_packed.stride(0))
+        c.down_row_stride = 16
         c.down_absmax_block_stride = int(self.down_absmax.stride(0))
+        c.down_absmax_row_stride = 1
         c.layout = int(self.layout)
         self._c = c
         return c
