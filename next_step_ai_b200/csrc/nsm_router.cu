@@ -95,7 +95,20 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
   }
   float sumsq = 0.f;
   for (int i = tid; i < n; i += blockDim.x) {
-    const int c = c0 + i;  sumsq = warp_sum(sumsq);
+    const int c = c0 + i;
+    float v;
+    if (p.residual != nullptr) {
+      v = p.residual[c];
+      if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
+      p.residual[c] = v;
+      sumsq += v * v;
+      if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
+    } else {
+      v = load_as_f32(p.x, p.x_dtype, c);
+    }
+    xs[i] = v;
+  }
+  sumsq = warp_sum(sumsq);
   if (lane == 0) red[warp] = sumsq;
   __syncthreads();
   if (tid == 0) {
