@@ -137,7 +137,7 @@ def run_ours(args) -> None:
     shape = dsyn.SHAPES["cfg1"]
     shard_bytes = LAYER_BYTES_GPU // world
     free, _ = torch.cuda.mem_get_info(dev)
-    budget = free - (10 << 30)
+    budget = free - (12 << 30)
     unique = max(1, min(LAYERS, budget // (shard_bytes + (3 << 20))))
     t0 = time.time()
     layers = []
@@ -340,4 +340,5 @@ def main() -> None:
 
 
 if __name__ == "__main__":
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     main()

@@ -150,6 +150,12 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait (no-op without the launch attribute) until the previous
+// kernel has completed and its writes are visible.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.f + expf(-g)); }
 
 }  // namespace nsm

@@ -36,6 +36,8 @@ namespace nsm {
 
 // Identity rows 0..count-1 (gathered layouts).
 __global__ void identity_rows_kernel(int* rows, int* count, int* sel, int n) {
+  pdl_trigger();
+  pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     rows[i] = i;
     sel[i] = i;
@@ -312,7 +314,9 @@ constexpr int kStageXMaxHidden = 16384;
 
 template <bool kTiled, bool kStageX>
 __global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
+  pdl_trigger();
   build_lut_dyn(p.gate_code, p.up_code);
+  pdl_wait();  // rows, count, x16 come from the router kernels
   __half* xs16 = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
   float* xss = reinterpret_cast<float*>(xs16 + (kStageX ? p.H : 0));
   if (kStageX) {
@@ -478,7 +482,9 @@ __device__ __forceinline__ void down_body(const DownParams& p, uint32_t lb, cons
 
 template <bool kTiled, bool kStage>
 __global__ void __launch_bounds__(256, 2) down_kernel(DownParams p) {
+  pdl_trigger();
   build_lut_dyn(p.down_code, p.down_code);
+  pdl_wait();  // act16 / act_scale come from the gate/up kernel
   const int count = *p.count_ptr;
   __half* sact = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
   float* sscale = reinterpret_cast<float*>(sact + kStageActMaxSlots * 32);
@@ -620,13 +626,15 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
   gp.total_warps = gu_ctas * 8;
   const int gu_smem = gu_stage ? kGateupSmemStaged : kSmemHead;
+  cudaError_t e;
   if (gu_tiled) {
-    if (gu_stage) gateup_kernel<true, true><<<gu_ctas, 256, gu_smem, stream>>>(gp);
-    else gateup_kernel<true, false><<<gu_ctas, 256, gu_smem, stream>>>(gp);
+    if (gu_stage) e = launch_pdl(gateup_kernel<true, true>, gu_ctas, 256, gu_smem, stream, gp);
+    else e = launch_pdl(gateup_kernel<true, false>, gu_ctas, 256, gu_smem, stream, gp);
   } else {
-    if (gu_stage) gateup_kernel<false, true><<<gu_ctas, 256, gu_smem, stream>>>(gp);
-    else gateup_kernel<false, false><<<gu_ctas, 256, gu_smem, stream>>>(gp);
+    if (gu_stage) e = launch_pdl(gateup_kernel<false, true>, gu_ctas, 256, gu_smem, stream, gp);
+    else e = launch_pdl(gateup_kernel<false, false>, gu_ctas, 256, gu_smem, stream, gp);
   }
+  NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(cudaGetLastError());
 
   DownParams dp{};
@@ -656,12 +664,13 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   dp.total_warps = dn_ctas * 8;
   const int dn_smem = dn_stage ? kDownSmemStaged : kSmemHead;
   if (dn_tiled) {
-    if (dn_stage) down_kernel<true, true><<<dn_ctas, 256, dn_smem, stream>>>(dp);
-    else down_kernel<true, false><<<dn_ctas, 256, dn_smem, stream>>>(dp);
+    if (dn_stage) e = launch_pdl(down_kernel<true, true>, dn_ctas, 256, dn_smem, stream, dp);
+    else e = launch_pdl(down_kernel<true, false>, dn_ctas, 256, dn_smem, stream, dp);
   } else {
-    if (dn_stage) down_kernel<false, true><<<dn_ctas, 256, dn_smem, stream>>>(dp);
-    else down_kernel<false, false><<<dn_ctas, 256, dn_smem, stream>>>(dp);
+    if (dn_stage) e = launch_pdl(down_kernel<false, true>, dn_ctas, 256, dn_smem, stream, dp);
+    else e = launch_pdl(down_kernel<false, false>, dn_ctas, 256, dn_smem, stream, dp);
   }
+  NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
 }
@@ -857,8 +866,7 @@ int nsm_decode_gathered(const void* x, int32_t x_dtype, int32_t hidden, int32_t 
   if (st) return st;
   st = router_a_prepare(x, x_dtype, nullptr, nullptr, hidden, wsl, s);
   if (st) return st;
-  identity_rows_kernel<<<(k + 255) / 256, 256, 0, s>>>(wsl.rows, wsl.count, wsl.sel_idx, k);
-  NSM_CHECK_CUDA(cudaGetLastError());
+  NSM_CHECK_CUDA(launch_pdl(identity_rows_kernel, (k + 255) / 256, 256, 0, s, wsl.rows, wsl.count, wsl.sel_idx, k));
   MlpPlan m{};
   m.H = hidden;
   m.I = I;
@@ -907,8 +915,7 @@ int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32
   KernelSetup* ks;
   st = setup_kernels(dev, &ks);
   if (st) return st;
-  identity_rows_kernel<<<(k + 255) / 256, 256, 0, s>>>(wsl.rows, wsl.count, wsl.sel_idx, k);
-  NSM_CHECK_CUDA(cudaGetLastError());
+  NSM_CHECK_CUDA(launch_pdl(identity_rows_kernel, (k + 255) / 256, 256, 0, s, wsl.rows, wsl.count, wsl.sel_idx, k));
   const int xes = x_dtype == NSM_F32 ? 4 : 2;
   const int yes = y_dtype == NSM_F32 ? 4 : 2;
   const int mes = mask_dtype == NSM_F32 ? 4 : 2;

@@ -9,10 +9,10 @@
 //   * the last CTA (atomic ticket) reduces the partials in fixed CTA order,
 //     applies the RMSNorm scale and enc_b, and the optional basis top-k mask
 //     (streaming_llama_runtime.py:4220-4238).
-// router_select_kernel:
+// router_scores_kernel / router_topk_kernel:
 //   * one thread per block: score = clamp0(latent . score_w[b] + score_b[b])
 //     (or |latent| . dec_norm_t[:, b] in legacy mode), times down_block_norm;
-//   * the last CTA selects the top-k with an 8-bit-digit radix select on
+//   * one 1024-thread CTA selects the top-k with an 8-bit-digit radix select on
 //     order-preserving score bits, resolves ties at the threshold by lower
 //     block id, orders the k winners (score desc, block id asc) and compacts
 //     them into pool rows through the block map (:4324-4352).
@@ -93,6 +93,8 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
       for (int i = 0; i < 4; ++i) pre[i] = __ldg(row + i);
     }
   }
+  pdl_trigger();
+  pdl_wait();  // residual / x / y_prev come from earlier kernels
   float sumsq = 0.f;
   for (int i = tid; i < n; i += blockDim.x) {
     const int c = c0 + i;
@@ -339,29 +341,32 @@ __device__ __forceinline__ float score_row(const RouterBParams& p, const float* 
   return acc;
 }
 
+// Block scores, one thread per block (grid-wide; waits for the latent).
 template <typename WT>
-__global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
-  extern __shared__ uint32_t keys[];  // [NB]  (last CTA)
+__global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
   __shared__ float lat[kMaxRank];
-  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  for (int r = threadIdx.x; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r]);
+  __syncthreads();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < p.NB) p.ws.scores[b] = score_row<WT>(p, lat, b);
+}
+
+// Top-k of the block scores in one CTA of 1024 threads: radix select of the
+// k-th largest order-preserving key (8-bit digits, warp-aggregated histogram
+// increments), threshold ties resolved by lower block id.  The winners are
+// compacted in block-id order; when the caller wants the indices they are
+// also ordered score-descending (ties: lower id first) by a bitonic sort.
+__global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
+  extern __shared__ uint32_t keys[];  // [NB]
   __shared__ int hist[256];
   __shared__ uint32_t s_prefix, s_mask;
   __shared__ int s_need;
-  __shared__ uint32_t sel_key[1024];
-  __shared__ int sel_id[1024];
+  __shared__ unsigned long long sorted[1024];
+  pdl_trigger();
+  pdl_wait();
   const int tid = threadIdx.x;
-  for (int r = tid; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r]);
-  __syncthreads();
-  for (int b = blockIdx.x * blockDim.x + tid; b < p.NB; b += gridDim.x * blockDim.x)
-    p.ws.scores[b] = score_row<WT>(p, lat, b);
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    s_last = atomicAdd(p.ws.ticket_router_b, 1) == (int)gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
   const int NB = p.NB, k = p.top_k;
   for (int i = tid; i < NB; i += blockDim.x) keys[i] = orderable(ldcg_f32(&p.ws.scores[i]));
   if (tid == 0) {
@@ -370,12 +375,10 @@ __global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
     s_need = k;
   }
   __syncthreads();
-  // radix select of the k-th largest key, 8 bits per pass
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t pre = s_prefix, msk = s_mask;
-    // warp-aggregated increments: scores cluster in a few top-digit bins
     for (int i0 = 0; i0 < NB; i0 += blockDim.x) {
       const int i = i0 + tid;
       const uint32_t key = i < NB ? keys[i] : 0u;
@@ -386,7 +389,7 @@ __global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
     }
     __syncthreads();
     if (tid < 32) {
-      // lane l owns bins [255-8l-7, 255-8l] (descending), finds the bin holding the need-th key
+      // lane l owns bins [255-8l-7, 255-8l] (descending)
       int c[8];
       int loc = 0;
 #pragma unroll
@@ -419,19 +422,20 @@ __global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
     __syncthreads();
   }
   const uint32_t thr = s_prefix;
-  const int take_eq = s_need;  // how many keys equal to thr are selected (lowest ids first)
-  // select: key > thr, or key == thr among the first take_eq by block id
+  const int take_eq = s_need;
+  // winners in block-id order (contiguous chunk per thread)
   const int per = (NB + blockDim.x - 1) / blockDim.x;
-  const int lo = tid * per, hi = min(NB, lo + per);
+  const int lo = min(NB, tid * per), hi = min(NB, lo + per);
   int n_eq = 0, n_gt = 0;
   for (int i = lo; i < hi; ++i) {
     n_eq += keys[i] == thr;
     n_gt += keys[i] > thr;
   }
-  int tot_eq, tot_sel;
-  const int eq_before = block_exclusive_scan(n_eq, &tot_eq);
-  int my_sel = n_gt + max(0, min(n_eq, take_eq - eq_before));
-  const int sel_before = block_exclusive_scan(my_sel, &tot_sel);
+  int tot;
+  const int eq_before = block_exclusive_scan(n_eq, &tot);
+  const int my_sel = n_gt + max(0, min(n_eq, take_eq - eq_before));
+  const int sel_before = block_exclusive_scan(my_sel, &tot);
+  const bool ordered = p.idx_out != nullptr || p.score_out != nullptr;
   {
     int e = eq_before, out = sel_before;
     for (int i = lo; i < hi; ++i) {
@@ -441,54 +445,67 @@ __global__ void __launch_bounds__(512) router_select_kernel(RouterBParams p) {
         s = e < take_eq;
         ++e;
       }
-      if (s && out < 1024) {
-        sel_key[out] = key;
-        sel_id[out] = i;
-      }
-      if (s) ++out;
-    }
-  }
-  __syncthreads();
-  // order the k winners: rank by counting (key desc, id asc)
-  if (k <= 1024) {
-    for (int j = tid; j < k; j += blockDim.x) {
-      const uint32_t kj = sel_key[j];
-      const int ij = sel_id[j];
-      int pos = 0;
-      for (int q = 0; q < k; ++q) {
-        const uint32_t kq = sel_key[q];
-        pos += (kq > kj) || (kq == kj && sel_id[q] < ij);
-      }
-      p.ws.sel_idx[pos] = ij;
-      if (p.idx_out) p.idx_out[pos] = ij;
-      if (p.score_out) p.score_out[pos] = from_orderable(kj);
-    }
-  } else {
-    // large k: every block's rank among all blocks (k > 1024 is outside the
-    // configurations this path is tuned for, but stays exact)
-    for (int i = tid; i < NB; i += blockDim.x) {
-      const uint32_t ki = keys[i];
-      int pos = 0;
-      for (int q = 0; q < NB; ++q) {
-        const uint32_t kq = keys[q];
-        pos += (kq > ki) || (kq == ki && q < i);
-      }
-      if (pos < k) {
-        p.ws.sel_idx[pos] = i;
-        if (p.idx_out) p.idx_out[pos] = i;
-        if (p.score_out) p.score_out[pos] = from_orderable(ki);
+      if (s) {
+        p.ws.sel_idx[out] = i;
+        if (ordered && out < 1024) sorted[out] = ((unsigned long long)key << 32) | (0xffffffffu - (uint32_t)i);
+        ++out;
       }
     }
   }
   if (p.latent_out)
-    for (int r = tid; r < p.rank; r += blockDim.x) p.latent_out[r] = lat[r];
+    for (int r = tid; r < p.rank; r += blockDim.x) p.latent_out[r] = ldcg_f32(&p.ws.latent[r]);
   __threadfence_block();
   __syncthreads();
+  if (ordered) {
+    if (k <= 1024) {
+      int n2 = 1;
+      while (n2 < k) n2 <<= 1;
+      for (int i = k + tid; i < n2; i += blockDim.x) sorted[i] = 0ull;
+      __syncthreads();
+      for (int len = 2; len <= n2; len <<= 1) {
+        for (int j = len >> 1; j > 0; j >>= 1) {
+          for (int i = tid; i < n2; i += blockDim.x) {
+            const int ixj = i ^ j;
+            if (ixj > i) {
+              const unsigned long long a = sorted[i], b = sorted[ixj];
+              const bool desc = (i & len) == 0;
+              if (desc ? (a < b) : (a > b)) {
+                sorted[i] = b;
+                sorted[ixj] = a;
+              }
+            }
+          }
+          __syncthreads();
+        }
+      }
+      for (int j = tid; j < k; j += blockDim.x) {
+        const unsigned long long key = sorted[j];
+        const int id = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
+        if (p.idx_out) p.idx_out[j] = id;
+        if (p.score_out) p.score_out[j] = from_orderable((uint32_t)(key >> 32));
+      }
+    } else {
+      // large k: rank of every block among all blocks (exact, slower)
+      for (int i = tid; i < NB; i += blockDim.x) {
+        const uint32_t ki = keys[i];
+        int pos = 0;
+        for (int q = 0; q < NB; ++q) {
+          const uint32_t kq = keys[q];
+          pos += (kq > ki) || (kq == ki && q < i);
+        }
+        if (pos < k) {
+          if (p.idx_out) p.idx_out[pos] = i;
+          if (p.score_out) p.score_out[pos] = from_orderable(ki);
+        }
+      }
+    }
+  }
   compact_selection(p, p.ws.sel_idx, k);
-  if (tid == 0) *p.ws.ticket_router_b = 0;
 }
 
 __global__ void __launch_bounds__(512) select_given_kernel(RouterBParams p, const int32_t* idx_in, int k) {
+  pdl_trigger();
+  pdl_wait();
   for (int j = threadIdx.x; j < k; j += blockDim.x) {
     const int b = idx_in[j];
     p.ws.sel_idx[j] = (b >= 0 && b < p.NB) ? b : -1;
@@ -505,11 +522,8 @@ int router_setup() {
   int dev = 0;
   NSM_CHECK_CUDA(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && done[dev]) return NSM_OK;
-  const int smem = kMaxNumBlocks * 4;
-  NSM_CHECK_CUDA(cudaFuncSetAttribute(router_select_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  NSM_CHECK_CUDA(cudaFuncSetAttribute(router_select_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   NSM_CHECK_CUDA(
-      cudaFuncSetAttribute(router_select_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxNumBlocks * 4));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return NSM_OK;
 }
@@ -524,32 +538,33 @@ int router_a_launch(const RouterAParams& a_in, cudaStream_t stream) {
   }
   a.cols_per_cta = cpc;
   const size_t smem = (size_t)cpc * sizeof(float);
+  cudaError_t e;
   switch (a.wdtype) {
-    case NSM_F32: router_latent_kernel<float><<<ctas, 256, smem, stream>>>(a); break;
-    case NSM_F16: router_latent_kernel<__half><<<ctas, 256, smem, stream>>>(a); break;
-    default: router_latent_kernel<__nv_bfloat16><<<ctas, 256, smem, stream>>>(a); break;
+    case NSM_F32: e = launch_pdl(router_latent_kernel<float>, ctas, 256, smem, stream, a); break;
+    case NSM_F16: e = launch_pdl(router_latent_kernel<__half>, ctas, 256, smem, stream, a); break;
+    default: e = launch_pdl(router_latent_kernel<__nv_bfloat16>, ctas, 256, smem, stream, a); break;
   }
-  NSM_CHECK_CUDA(cudaGetLastError());
+  NSM_CHECK_CUDA(e);
   return NSM_OK;
 }
 
 int router_b_launch(const RouterBParams& b, cudaStream_t stream) {
   int st = router_setup();
   if (st) return st;
-  const int ctas = (b.NB + 511) / 512;
-  const size_t smem = (size_t)b.NB * 4;
+  const int ctas = (b.NB + 127) / 128;
+  cudaError_t e;
   switch (b.wdtype) {
-    case NSM_F32: router_select_kernel<float><<<ctas, 512, smem, stream>>>(b); break;
-    case NSM_F16: router_select_kernel<__half><<<ctas, 512, smem, stream>>>(b); break;
-    default: router_select_kernel<__nv_bfloat16><<<ctas, 512, smem, stream>>>(b); break;
+    case NSM_F32: e = launch_pdl(router_scores_kernel<float>, ctas, 128, 0, stream, b); break;
+    case NSM_F16: e = launch_pdl(router_scores_kernel<__half>, ctas, 128, 0, stream, b); break;
+    default: e = launch_pdl(router_scores_kernel<__nv_bfloat16>, ctas, 128, 0, stream, b); break;
   }
-  NSM_CHECK_CUDA(cudaGetLastError());
+  NSM_CHECK_CUDA(e);
+  NSM_CHECK_CUDA(launch_pdl(router_topk_kernel, 1, 1024, (size_t)b.NB * 4, stream, b));
   return NSM_OK;
 }
 
 int select_given_launch(const RouterBParams& b, const int32_t* idx_in, int k, cudaStream_t stream) {
-  select_given_kernel<<<1, 512, 0, stream>>>(b, idx_in, k);
-  NSM_CHECK_CUDA(cudaGetLastError());
+  NSM_CHECK_CUDA(launch_pdl(select_given_kernel, 1, 512, 0, stream, b, idx_in, k));
   return NSM_OK;
 }
 
