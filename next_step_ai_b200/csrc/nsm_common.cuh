@@ -82,6 +82,12 @@ __device__ __forceinline__ uint32_t ldg_u32(const void* p) {
 __device__ __forceinline__ float ldg_f32(const float* p) { return __ldg(p); }
 __device__ __forceinline__ uint4 ldg_u4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
+// Bulk prefetch of [p, p + bytes) into L2 (no registers, no shared memory).
+// p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Loads of data written by other CTAs of the same kernel (skip L1).
 __device__ __forceinline__ float ldcg_f32(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ int ldcg_i32(const int* p) { return __ldcg(p); }

@@ -54,30 +54,30 @@ __global__ void identity_rows_kernel(int* rows, int* count, int* sel, int n) {
 // CTA (x16 + xscale for gate/up; act16 + act_scale + rows for down).
 extern __shared__ __align__(1024) uint32_t g_lut_smem[];
 constexpr int kLutScratch = 2048;
+constexpr int kMlpThreads = 256;  // 8 warps per CTA, two CTAs per SM
 constexpr int kSmemHead = kLutBytes + kLutScratch;
 
-// Byte `kbyte` of w -> half2 from table kTable.  kFast: the table starts at a
-// shared address whose bits 8..15 are zero, so one byte-permute builds the
-// whole 32-bit shared address (lane offset and table base bytes from
-// `lanebase`, the entry from w).
-template <bool kFast>
+// Byte `kbyte` of w -> half2 from table `table`.  One byte-permute builds
+// the table-relative address e*256 + lane*4; kBase >= 0 is the shared-window
+// address of the table, folded into the load's immediate offset (the user
+// shared memory of a CTA starts after a reserved 1 KB, so the base is 0x400
+// when the kernel has no static shared variables).  kBase < 0: generic path.
+template <int kBase>
 __device__ __forceinline__ uint32_t lut_get(uint32_t w, uint32_t lanebase, int kbyte, int table) {
-  if (kFast) {
-    const uint32_t addr = __byte_perm(w, lanebase, 0x7604u | ((uint32_t)kbyte << 4)) + table * 128;
+  const uint32_t addr = __byte_perm(w, lanebase, 0x5504u | ((uint32_t)kbyte << 4));
+  if (kBase >= 0) {
     uint32_t v;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    if (table == 0)
+      asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(kBase));
+    else
+      asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(kBase + 128));
     return v;
   } else {
-    const uint32_t addr = __byte_perm(w, lanebase, 0x5504u | ((uint32_t)kbyte << 4));
     return *reinterpret_cast<const uint32_t*>(reinterpret_cast<const char*>(g_lut_smem) + addr + table * 128);
   }
 }
 
-__device__ __forceinline__ bool lut_fast_ok(uint32_t* lanebase_fast, uint32_t lane) {
-  const uint32_t base = (uint32_t)__cvta_generic_to_shared(g_lut_smem);
-  *lanebase_fast = base + lane * 4u;
-  return (base & 0xffffu) == 0u;  // table rows never carry into the entry byte
-}
+__device__ __forceinline__ uint32_t lut_base_addr() { return (uint32_t)__cvta_generic_to_shared(g_lut_smem); }
 
 __device__ __forceinline__ void mma_16816_z(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                             uint32_t b0, uint32_t b1) {
@@ -178,19 +178,19 @@ __device__ __forceinline__ void gu_load(const GateUpParams& p, const uint8_t* gb
 }
 
 // 16 rows x 64 columns: four k=16 MMAs over the lane's bytes of two rows.
-template <bool kFast, int kTable>
+template <int kBase, int kTable>
 __device__ __forceinline__ void gu_mma_rowgroup(uint32_t lb, const uint4 w, const uint32_t b[8], float d[4]) {
-  mma_16816_z(d, lut_get<kFast>(w.x, lb, 0, kTable), lut_get<kFast>(w.z, lb, 0, kTable),
-              lut_get<kFast>(w.x, lb, 1, kTable), lut_get<kFast>(w.z, lb, 1, kTable), b[0], b[1]);
-  mma_16816(d, lut_get<kFast>(w.x, lb, 2, kTable), lut_get<kFast>(w.z, lb, 2, kTable),
-            lut_get<kFast>(w.x, lb, 3, kTable), lut_get<kFast>(w.z, lb, 3, kTable), b[2], b[3]);
-  mma_16816(d, lut_get<kFast>(w.y, lb, 0, kTable), lut_get<kFast>(w.w, lb, 0, kTable),
-            lut_get<kFast>(w.y, lb, 1, kTable), lut_get<kFast>(w.w, lb, 1, kTable), b[4], b[5]);
-  mma_16816(d, lut_get<kFast>(w.y, lb, 2, kTable), lut_get<kFast>(w.w, lb, 2, kTable),
-            lut_get<kFast>(w.y, lb, 3, kTable), lut_get<kFast>(w.w, lb, 3, kTable), b[6], b[7]);
+  mma_16816_z(d, lut_get<kBase>(w.x, lb, 0, kTable), lut_get<kBase>(w.z, lb, 0, kTable),
+              lut_get<kBase>(w.x, lb, 1, kTable), lut_get<kBase>(w.z, lb, 1, kTable), b[0], b[1]);
+  mma_16816(d, lut_get<kBase>(w.x, lb, 2, kTable), lut_get<kBase>(w.z, lb, 2, kTable),
+            lut_get<kBase>(w.x, lb, 3, kTable), lut_get<kBase>(w.z, lb, 3, kTable), b[2], b[3]);
+  mma_16816(d, lut_get<kBase>(w.y, lb, 0, kTable), lut_get<kBase>(w.w, lb, 0, kTable),
+            lut_get<kBase>(w.y, lb, 1, kTable), lut_get<kBase>(w.w, lb, 1, kTable), b[4], b[5]);
+  mma_16816(d, lut_get<kBase>(w.y, lb, 2, kTable), lut_get<kBase>(w.w, lb, 2, kTable),
+            lut_get<kBase>(w.y, lb, 3, kTable), lut_get<kBase>(w.w, lb, 3, kTable), b[6], b[7]);
 }
 
-template <bool kFast, bool kStageX>
+template <int kBase, bool kStageX>
 __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& tile, int j, int t, uint32_t lb,
                                            const __half* xs16, const float* xss, float acc[2][4]) {
   uint32_t b[8];
@@ -211,11 +211,11 @@ __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& 
   float d[4];
 #pragma unroll
   for (int rg = 0; rg < 2; ++rg) {
-    gu_mma_rowgroup<kFast, 0>(lb, tile.w[0][rg], b, d);
+    gu_mma_rowgroup<kBase, 0>(lb, tile.w[0][rg], b, d);
     const float g0 = rg ? tile.am[0].z : tile.am[0].x, g1 = rg ? tile.am[0].w : tile.am[0].y;
     acc[0][rg * 2] = fmaf(d[0], g0 * xs, acc[0][rg * 2]);
     acc[0][rg * 2 + 1] = fmaf(d[2], g1 * xs, acc[0][rg * 2 + 1]);
-    gu_mma_rowgroup<kFast, 1>(lb, tile.w[1][rg], b, d);
+    gu_mma_rowgroup<kBase, 1>(lb, tile.w[1][rg], b, d);
     const float u0 = rg ? tile.am[1].z : tile.am[1].x, u1 = rg ? tile.am[1].w : tile.am[1].y;
     acc[1][rg * 2] = fmaf(d[0], u0 * xs, acc[1][rg * 2]);
     acc[1][rg * 2 + 1] = fmaf(d[2], u1 * xs, acc[1][rg * 2 + 1]);
@@ -225,12 +225,28 @@ __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& 
 __device__ __forceinline__ int gateup_tiles_per_unit(int count, int tiles_per_row, int total_warps) {
   const int min_tpu = (tiles_per_row + kMaxUnitsPerSlot - 1) / kMaxUnitsPerSlot;
   const long long total = (long long)count * tiles_per_row;
-  const long long want = total / (3LL * total_warps);
+  const long long want = total / (4LL * total_warps);
   const int tpu = (int)max(1LL, min(16LL, want));
   return max(tpu, min_tpu);
 }
 
-template <bool kTiled, bool kStageX, bool kFast>
+// L2 prefetch of one gate/up unit's bytes (tiled layout: contiguous ranges).
+__device__ __forceinline__ void gateup_prefetch_unit(const GateUpParams& p, int u, int ups, int tpu, int tiles_per_row,
+                                                     int lane) {
+  if (lane >= 4) return;
+  const int s = u / ups, sub = u - s * ups;
+  const int prow = p.rows[s];
+  const int j0 = sub * tpu, j1 = min(tiles_per_row, j0 + tpu);
+  if (lane < 2) {
+    const uint8_t* base = (lane == 0 ? p.gate : p.up) + (int64_t)prow * p.gstride;
+    prefetch_l2_bulk(base + (int64_t)j0 * 1024, (uint32_t)(j1 - j0) * 1024u);
+  } else {
+    const float* base = (lane == 2 ? p.gate_am : p.up_am) + (int64_t)prow * p.gastride;
+    prefetch_l2_bulk(base + j0 * 32, (uint32_t)(j1 - j0) * 128u);
+  }
+}
+
+template <bool kTiled, bool kStageX, int kBase>
 __device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, const __half* xs16, const float* xss) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -241,7 +257,10 @@ __device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, 
   const int ups = (tiles_per_row + tpu - 1) / tpu;
   const int nunits = count * ups;
 
+  if (kTiled && warp_global < nunits) gateup_prefetch_unit(p, warp_global, ups, tpu, tiles_per_row, lane);
   for (int u = warp_global; u < nunits; u += p.total_warps) {
+    // the next unit of this warp streams into L2 while this one computes
+    if (kTiled && u + p.total_warps < nunits) gateup_prefetch_unit(p, u + p.total_warps, ups, tpu, tiles_per_row, lane);
     const int s = u / ups, sub = u - s * ups;
     const int prow = p.rows[s];
     const uint8_t* gb = p.gate + (int64_t)prow * p.gstride;
@@ -250,70 +269,85 @@ __device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, 
     const float* uab = p.up_am + (int64_t)prow * p.gastride;
     const int j0 = sub * tpu, j1 = min(tiles_per_row, j0 + tpu);
     float acc[2][4] = {};
-    GuTile t0, t1, t2;
+    GuTile t0, t1;
     gu_load<kTiled>(p, gb, ub, gab, uab, j0, lane, t0);
-    if (j0 + 1 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j0 + 1, lane, t1);
-    for (int j = j0; j < j1; j += 3) {
-      if (j + 2 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 2, lane, t2);
-      gu_compute<kFast, kStageX>(p, t0, j, t, lb, xs16, xss, acc);
+    for (int j = j0; j < j1; j += 2) {
+      if (j + 1 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 1, lane, t1);
+      gu_compute<kBase, kStageX>(p, t0, j, t, lb, xs16, xss, acc);
       if (j + 1 >= j1) break;
-      if (j + 3 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 3, lane, t0);
-      gu_compute<kFast, kStageX>(p, t1, j + 1, t, lb, xs16, xss, acc);
-      if (j + 2 >= j1) break;
-      if (j + 4 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 4, lane, t1);
-      gu_compute<kFast, kStageX>(p, t2, j + 2, t, lb, xs16, xss, acc);
+      if (j + 2 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 2, lane, t0);
+      gu_compute<kBase, kStageX>(p, t1, j + 1, t, lb, xs16, xss, acc);
     }
-    // column 0 of the accumulator lives in lanes with t == 0
-    float* part = p.gu_part + ((int64_t)s * kMaxUnitsPerSlot + sub) * 64;
+    // column 0 of the accumulator lives in lanes with t == 0; the split-K
+    // reduction and SiLU*up happen in gateup_finalize_kernel
     if (t == 0) {
+      float* part = p.gu_part + ((int64_t)s * kMaxUnitsPerSlot + sub) * 64;
 #pragma unroll
       for (int pr = 0; pr < 2; ++pr)
 #pragma unroll
         for (int i = 0; i < 4; ++i) part[pr * 32 + (i >> 1) * 16 + g + (i & 1) * 8] = acc[pr][i];
-      __threadfence();
-    }
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = atomicAdd(&p.ticket_slot[s], 1) == ups - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) continue;
-    __threadfence();
-    float gsum = 0.f, usum = 0.f;
-    const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
-#pragma unroll 8
-    for (int q = 0; q < ups; ++q) {
-      gsum += ldcg_f32(base + q * 64 + lane);
-      usum += ldcg_f32(base + q * 64 + 32 + lane);
-    }
-    const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
-    gsum *= ns;
-    usum *= ns;
-    if (p.gate_bias != nullptr || p.up_bias != nullptr) {
-      const int bi = (p.bias_by_block ? p.row_block[s] : s) * 32 + lane;
-      if (p.gate_bias) gsum += load_as_f32(p.gate_bias, p.bias_dtype, bi);
-      if (p.up_bias) usum += load_as_f32(p.up_bias, p.bias_dtype, bi);
-    }
-    if (p.act_mask != nullptr) {
-      const float m = load_as_f32(p.act_mask, p.mask_dtype, (int64_t)s * 32 + lane);
-      gsum *= m;
-      usum *= m;
-    }
-    const float act = silu_f32(gsum) * usum;
-    if (p.act_out) p.act_out[(int64_t)s * 32 + lane] = act;
-    const float m = warp_max(fabsf(act));
-    const float sc = pow2_scale_for(m);
-    p.act16[(int64_t)s * 32 + lane] = __float2half_rn(act * (1.f / sc));
-    if (lane == 0) {
-      p.act_scale[s] = sc;
-      p.ticket_slot[s] = 0;
     }
   }
+}
+
+// One CTA (256 threads) per block: thread (q, lane) sums the column-range
+// partials q, q+8, ... of neuron `lane` (gate and up), the 8 sums combine in
+// fixed order, then RMSNorm scale, biases, mask and SiLU(gate)*up are applied
+// and written as fp16 with a per-block power-of-two scale.
+__global__ void __launch_bounds__(256) gateup_finalize_kernel(GateUpParams p) {
+  __shared__ float red[2][8][32];
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31, q0 = threadIdx.x >> 5;
+  const int s = blockIdx.x;
+  const int count = *p.count_ptr;
+  if (s >= count) return;
+  const int tiles_per_row = p.H >> 6;
+  const int tpu = gateup_tiles_per_unit(count, tiles_per_row, p.total_warps);
+  const int ups = (tiles_per_row + tpu - 1) / tpu;
+  const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
+  float gsum = 0.f, usum = 0.f;
+#pragma unroll 8
+  for (int q = q0; q < ups; q += 8) {
+    gsum += ldcg_f32(base + q * 64 + lane);
+    usum += ldcg_f32(base + q * 64 + 32 + lane);
+  }
+  red[0][q0][lane] = gsum;
+  red[1][q0][lane] = usum;
+  __syncthreads();
+  if (q0 != 0) return;
+  gsum = 0.f;
+  usum = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    gsum += red[0][q][lane];
+    usum += red[1][q][lane];
+  }
+  const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
+  gsum *= ns;
+  usum *= ns;
+  if (p.gate_bias != nullptr || p.up_bias != nullptr) {
+    const int bi = (p.bias_by_block ? p.row_block[s] : s) * 32 + lane;
+    if (p.gate_bias) gsum += load_as_f32(p.gate_bias, p.bias_dtype, bi);
+    if (p.up_bias) usum += load_as_f32(p.up_bias, p.bias_dtype, bi);
+  }
+  if (p.act_mask != nullptr) {
+    const float m = load_as_f32(p.act_mask, p.mask_dtype, (int64_t)s * 32 + lane);
+    gsum *= m;
+    usum *= m;
+  }
+  const float act = silu_f32(gsum) * usum;
+  if (p.act_out) p.act_out[(int64_t)s * 32 + lane] = act;
+  const float m = warp_max(fabsf(act));
+  const float sc = pow2_scale_for(m);
+  p.act16[(int64_t)s * 32 + lane] = __float2half_rn(act * (1.f / sc));
+  if (lane == 0) p.act_scale[s] = sc;
 }
 
 constexpr int kStageXMaxHidden = 16384;
 
 template <bool kTiled, bool kStageX>
-__global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
+__global__ void __launch_bounds__(kMlpThreads, 2) gateup_kernel(GateUpParams p) {
   pdl_trigger();
   build_lut_dyn(p.gate_code, p.up_code);
   pdl_wait();  // rows, count, x16 come from the router kernels
@@ -326,12 +360,12 @@ __global__ void __launch_bounds__(256, 2) gateup_kernel(GateUpParams p) {
     for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
   }
   __syncthreads();
-  uint32_t lb_fast;
-  const uint32_t lane = threadIdx.x & 31;
-  if (lut_fast_ok(&lb_fast, lane))
-    gateup_body<kTiled, kStageX, true>(p, lb_fast, xs16, xss);
+  const uint32_t lb = (threadIdx.x & 31) * 4u;
+  const uint32_t base = lut_base_addr();
+  if (base == 0x400u)
+    gateup_body<kTiled, kStageX, 0x400>(p, lb, xs16, xss);
   else
-    gateup_body<kTiled, kStageX, false>(p, lane * 4u, xs16, xss);
+    gateup_body<kTiled, kStageX, -1>(p, lb, xs16, xss);
 }
 
 // ============================================================================
@@ -381,12 +415,12 @@ __device__ __forceinline__ void down_load(const DownParams& p, int prow, int rt,
   }
 }
 
-template <bool kFast>
+template <int kBase>
 __device__ __forceinline__ void down_mma(uint32_t lb, uint32_t w0, uint32_t w1, const uint4 bf, float d[4]) {
-  mma_16816_z(d, lut_get<kFast>(w0, lb, 0, 0), lut_get<kFast>(w1, lb, 0, 0), lut_get<kFast>(w0, lb, 1, 0),
-              lut_get<kFast>(w1, lb, 1, 0), bf.x, bf.y);
-  mma_16816(d, lut_get<kFast>(w0, lb, 2, 0), lut_get<kFast>(w1, lb, 2, 0), lut_get<kFast>(w0, lb, 3, 0),
-            lut_get<kFast>(w1, lb, 3, 0), bf.z, bf.w);
+  mma_16816_z(d, lut_get<kBase>(w0, lb, 0, 0), lut_get<kBase>(w1, lb, 0, 0), lut_get<kBase>(w0, lb, 1, 0),
+              lut_get<kBase>(w1, lb, 1, 0), bf.x, bf.y);
+  mma_16816(d, lut_get<kBase>(w0, lb, 2, 0), lut_get<kBase>(w1, lb, 2, 0), lut_get<kBase>(w0, lb, 3, 0),
+            lut_get<kBase>(w1, lb, 3, 0), bf.z, bf.w);
 }
 
 struct DownBatch {
@@ -406,7 +440,7 @@ __device__ __forceinline__ void down_batch_load(const DownParams& p, const int* 
   }
 }
 
-template <bool kFast, bool kStage>
+template <int kBase, bool kStage>
 __device__ __forceinline__ void down_batch_compute(const DownParams& p, const __half* sact, const float* sscale,
                                                    int sb, int s1, int t, uint32_t lb, const DownBatch& b,
                                                    float acc[4]) {
@@ -424,64 +458,106 @@ __device__ __forceinline__ void down_batch_compute(const DownParams& p, const __
         as = ldg_f32(p.act_scale + s);
       }
       float d[4];
-      down_mma<kFast>(lb, b.w[i].x, b.w[i].y, bf, d);
+      down_mma<kBase>(lb, b.w[i].x, b.w[i].y, bf, d);
       acc[0] = fmaf(d[0], b.am[i].x * as, acc[0]);
       acc[1] = fmaf(d[2], b.am[i].y * as, acc[1]);
-      down_mma<kFast>(lb, b.w[i].z, b.w[i].w, bf, d);
+      down_mma<kBase>(lb, b.w[i].z, b.w[i].w, bf, d);
       acc[2] = fmaf(d[0], b.am[i].z * as, acc[2]);
       acc[3] = fmaf(d[2], b.am[i].w * as, acc[3]);
     }
   }
 }
 
-template <bool kTiled, bool kStage, bool kFast>
+constexpr int kDownRowTiles = 2;  // 32-row tiles per down unit
+
+__device__ __forceinline__ int down_slot_groups(int count, int RT, int total_warps) {
+  const int RG = (RT + kDownRowTiles - 1) / kDownRowTiles;
+  int sg = (3 * total_warps + RG - 1) / RG;
+  return max(1, min(sg, min(max(count, 1), kMaxSlotGroups)));
+}
+
+
+// L2 prefetch of one down unit: for each of its blocks, the rows of its row
+// tiles are contiguous in the tiled layout (512 B packed + 128 B absmax each).
+template <bool kStage>
+__device__ __forceinline__ void down_prefetch_unit(const DownParams& p, const int* srows, int u, int RG, int gs,
+                                                   int count, int RT, int lane) {
+  const int grp = u / RG, rgi = u - grp * RG;
+  const int rt0 = rgi * kDownRowTiles, rt1 = min(RT, rt0 + kDownRowTiles);
+  const int s0 = grp * gs, s1 = min(count, s0 + gs);
+  for (int q = lane; q < 2 * (s1 - s0); q += 32) {
+    const int s = s0 + (q >> 1);
+    const int prow = kStage ? srows[s] : p.rows[s];
+    if ((q & 1) == 0)
+      prefetch_l2_bulk(p.down + (int64_t)prow * p.dbs + (int64_t)rt0 * 512, (uint32_t)(rt1 - rt0) * 512u);
+    else
+      prefetch_l2_bulk(p.down_am + (int64_t)prow * p.dabs + rt0 * 32, (uint32_t)(rt1 - rt0) * 128u);
+  }
+}
+
+template <bool kTiled, bool kStage, int kBase>
 __device__ __forceinline__ void down_body(const DownParams& p, uint32_t lb, const __half* sact, const float* sscale,
                                           const int* srows, int count) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int RT = p.H >> 5;
-  int sg = (3 * p.total_warps + RT - 1) / RT;
-  sg = max(1, min(sg, min(max(count, 1), kMaxSlotGroups)));
+  const int RG = (RT + kDownRowTiles - 1) / kDownRowTiles;
+  const int sg = down_slot_groups(count, RT, p.total_warps);
   const int gs = (count + sg - 1) / sg;
-  const int nunits = RT * sg;
+  const int nunits = RG * sg;
 
+  if (kTiled && warp_global < nunits) down_prefetch_unit<kStage>(p, srows, warp_global, RG, gs, count, RT, lane);
   for (int u = warp_global; u < nunits; u += p.total_warps) {
-    const int grp = u / RT, rt = u - grp * RT;
+    if (kTiled && u + p.total_warps < nunits)
+      down_prefetch_unit<kStage>(p, srows, u + p.total_warps, RG, gs, count, RT, lane);
+    const int grp = u / RG, rgi = u - grp * RG;
     const int s0 = grp * gs, s1 = min(count, s0 + gs);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, 16+g, 24+g of the tile
-    DownBatch b0, b1;
-    if (s0 < s1) down_batch_load<kTiled, kStage>(p, srows, s0, s1, rt, lane, b0);
-    for (int sb = s0; sb < s1; sb += 2 * kDownBatch) {
-      if (sb + kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + kDownBatch, s1, rt, lane, b1);
-      down_batch_compute<kFast, kStage>(p, sact, sscale, sb, s1, t, lb, b0, acc);
-      if (sb + kDownBatch >= s1) break;
-      if (sb + 2 * kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + 2 * kDownBatch, s1, rt, lane, b0);
-      down_batch_compute<kFast, kStage>(p, sact, sscale, sb + kDownBatch, s1, t, lb, b1, acc);
-    }
-    if (t == 0) {
-      float* yp = p.ypart + (int64_t)grp * p.H + rt * 32;
+    for (int rt = rgi * kDownRowTiles; rt < min(RT, (rgi + 1) * kDownRowTiles); ++rt) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, 16+g, 24+g of the tile
+      DownBatch b0, b1;
+      if (s0 < s1) down_batch_load<kTiled, kStage>(p, srows, s0, s1, rt, lane, b0);
+      for (int sb = s0; sb < s1; sb += 2 * kDownBatch) {
+        if (sb + kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + kDownBatch, s1, rt, lane, b1);
+        down_batch_compute<kBase, kStage>(p, sact, sscale, sb, s1, t, lb, b0, acc);
+        if (sb + kDownBatch >= s1) break;
+        if (sb + 2 * kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + 2 * kDownBatch, s1, rt, lane, b0);
+        down_batch_compute<kBase, kStage>(p, sact, sscale, sb + kDownBatch, s1, t, lb, b1, acc);
+      }
+      if (t == 0) {
+        float* yp = p.ypart + (int64_t)grp * p.H + rt * 32;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) yp[(i >> 1) * 16 + g + (i & 1) * 8] = acc[i];
-      __threadfence();
+        for (int i = 0; i < 4; ++i) yp[(i >> 1) * 16 + g + (i & 1) * 8] = acc[i];
+      }
     }
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) last = atomicAdd(&p.ticket_rt[rt], 1) == sg - 1;
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (!last) continue;
-    __threadfence();
-    float y = 0.f;
-#pragma unroll 8
-    for (int q = 0; q < sg; ++q) y += ldcg_f32(p.ypart + (int64_t)q * p.H + rt * 32 + lane);
-    if (p.down_bias) y += load_as_f32(p.down_bias, p.bias_dtype, rt * 32 + lane);
-    store_from_f32(p.y, p.y_dtype, rt * 32 + lane, y);
-    if (lane == 0) p.ticket_rt[rt] = 0;
   }
 }
 
+// Four threads per output row: each sums every fourth block-group partial,
+// the four sums combine in fixed order.
+__global__ void __launch_bounds__(256) down_finalize_kernel(DownParams p) {
+  pdl_trigger();
+  pdl_wait();
+  const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int h = gtid >> 2, q0 = gtid & 3;
+  const int count = *p.count_ptr;
+  const int sg = down_slot_groups(count, p.H >> 5, p.total_warps);
+  float y = 0.f;
+  if (h < p.H) {
+#pragma unroll 8
+    for (int q = q0; q < sg; q += 4) y += ldcg_f32(p.ypart + (int64_t)q * p.H + h);
+  }
+  const float y1 = __shfl_down_sync(0xffffffffu, y, 1);
+  const float y2 = __shfl_down_sync(0xffffffffu, y, 2);
+  const float y3 = __shfl_down_sync(0xffffffffu, y, 3);
+  if (h >= p.H || q0 != 0) return;
+  y = (y + y1) + (y2 + y3);
+  if (p.down_bias) y += load_as_f32(p.down_bias, p.bias_dtype, h);
+  store_from_f32(p.y, p.y_dtype, h, y);
+}
+
 template <bool kTiled, bool kStage>
-__global__ void __launch_bounds__(256, 2) down_kernel(DownParams p) {
+__global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
   pdl_trigger();
   build_lut_dyn(p.down_code, p.down_code);
   pdl_wait();  // act16 / act_scale come from the gate/up kernel
@@ -499,12 +575,12 @@ __global__ void __launch_bounds__(256, 2) down_kernel(DownParams p) {
     }
   }
   __syncthreads();
-  uint32_t lb_fast;
-  const uint32_t lane = threadIdx.x & 31;
-  if (lut_fast_ok(&lb_fast, lane))
-    down_body<kTiled, kStage, true>(p, lb_fast, sact, sscale, srows, count);
+  const uint32_t lb = (threadIdx.x & 31) * 4u;
+  const uint32_t base = lut_base_addr();
+  if (base == 0x400u)
+    down_body<kTiled, kStage, 0x400>(p, lb, sact, sscale, srows, count);
   else
-    down_body<kTiled, kStage, false>(p, lane * 4u, sact, sscale, srows, count);
+    down_body<kTiled, kStage, -1>(p, lb, sact, sscale, srows, count);
 }
 
 // ============================================================================
@@ -525,7 +601,7 @@ static KernelSetup g_setup[64];
 template <typename K>
 static int setup_one(K kernel, int smem, int* ctas_per_sm) {
   NSM_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, 256, smem));
+  NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, kMlpThreads, smem));
   if (*ctas_per_sm <= 0) return fail(NSM_ERR_CUDA, "kernel occupancy is zero");
   return NSM_OK;
 }
@@ -624,18 +700,18 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   const bool gu_tiled = (w->layout & NSM_LAYOUT_GATEUP_TILED) != 0;
   const bool gu_stage = m.H <= kStageXMaxHidden;
   const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
-  gp.total_warps = gu_ctas * 8;
+  gp.total_warps = gu_ctas * (kMlpThreads / 32);
   const int gu_smem = gu_stage ? kGateupSmemStaged : kSmemHead;
   cudaError_t e;
   if (gu_tiled) {
-    if (gu_stage) e = launch_pdl(gateup_kernel<true, true>, gu_ctas, 256, gu_smem, stream, gp);
-    else e = launch_pdl(gateup_kernel<true, false>, gu_ctas, 256, gu_smem, stream, gp);
+    if (gu_stage) e = launch_pdl(gateup_kernel<true, true>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
+    else e = launch_pdl(gateup_kernel<true, false>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
   } else {
-    if (gu_stage) e = launch_pdl(gateup_kernel<false, true>, gu_ctas, 256, gu_smem, stream, gp);
-    else e = launch_pdl(gateup_kernel<false, false>, gu_ctas, 256, gu_smem, stream, gp);
+    if (gu_stage) e = launch_pdl(gateup_kernel<false, true>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
+    else e = launch_pdl(gateup_kernel<false, false>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
   }
   NSM_CHECK_CUDA(e);
-  NSM_CHECK_CUDA(cudaGetLastError());
+  NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
 
   DownParams dp{};
   dp.down = w->down_packed;
@@ -661,16 +737,17 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   const bool dn_tiled = (w->layout & NSM_LAYOUT_DOWN_TILED) != 0;
   const bool dn_stage = m.k <= kStageActMaxSlots;
   const int dn_ctas = dev.sm_count * ks->dn[dn_tiled][dn_stage];
-  dp.total_warps = dn_ctas * 8;
+  dp.total_warps = dn_ctas * (kMlpThreads / 32);
   const int dn_smem = dn_stage ? kDownSmemStaged : kSmemHead;
   if (dn_tiled) {
-    if (dn_stage) e = launch_pdl(down_kernel<true, true>, dn_ctas, 256, dn_smem, stream, dp);
-    else e = launch_pdl(down_kernel<true, false>, dn_ctas, 256, dn_smem, stream, dp);
+    if (dn_stage) e = launch_pdl(down_kernel<true, true>, dn_ctas, kMlpThreads, dn_smem, stream, dp);
+    else e = launch_pdl(down_kernel<true, false>, dn_ctas, kMlpThreads, dn_smem, stream, dp);
   } else {
-    if (dn_stage) e = launch_pdl(down_kernel<false, true>, dn_ctas, 256, dn_smem, stream, dp);
-    else e = launch_pdl(down_kernel<false, false>, dn_ctas, 256, dn_smem, stream, dp);
+    if (dn_stage) e = launch_pdl(down_kernel<false, true>, dn_ctas, kMlpThreads, dn_smem, stream, dp);
+    else e = launch_pdl(down_kernel<false, false>, dn_ctas, kMlpThreads, dn_smem, stream, dp);
   }
   NSM_CHECK_CUDA(e);
+  NSM_CHECK_CUDA(launch_pdl(down_finalize_kernel, (4 * m.H + 255) / 256, 256, 0, stream, dp));
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
 }
