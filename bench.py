@@ -139,6 +139,8 @@ def run_ours(args) -> None:
     free, _ = torch.cuda.mem_get_info(dev)
     budget = free - (12 << 30)
     unique = max(1, min(LAYERS, budget // (shard_bytes + (3 << 20))))
+    if args.unique_layers:
+        unique = max(1, min(unique, args.unique_layers))
     t0 = time.time()
     layers = []
     for l in range(unique):
@@ -234,7 +236,7 @@ def run_ours(args) -> None:
                        "cuda_graph": True, "synthetic_gen_s": round(gen_s, 1)},
             "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
                     "d2h_bytes_per_step": HIDDEN * 4},
-            "gpu_launches": args.steps * LAYERS * 4,
+            "gpu_launches": args.steps * dec.kernels_per_step,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
                          "unit_of_launch": "one layer's decode launch group (router, gate/up, down kernels)",
@@ -330,6 +332,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--unique-layers", type=int, default=0,
+                    help="cap the resident layers (cycled over the 126); for small profiling captures")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -84,6 +84,16 @@ class SparseMlpDecoder:
         if self.group is not None:
             torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM, group=self.group)
 
+    # kernels nsm_sparse_mlp_decode launches per layer: router latent, block
+    # scores, top-k, gate/up, gate/up finalize, down, down finalize
+    KERNELS_PER_LAYER = 7
+
+    @property
+    def kernels_per_step(self) -> int:
+        """This library's kernel launches per token (library collectives and
+        the final residual add are not counted)."""
+        return self.KERNELS_PER_LAYER * self.num_layers
+
     def step_eager(self) -> None:
         """One token through all layers (no graph).  Input: ``residual``;
         output: ``out`` = final residual (residual + last MLP output)."""
