@@ -211,6 +211,23 @@ int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32
                              const nsm_mlp_weights* w, void* y, int32_t y_dtype, void* ws, size_t ws_bytes,
                              nsm_stream_t stream);
 
+/* nsm_decode_gathered without a workspace argument, for callers that cannot
+ * allocate device memory when they decode (a fixed pool sized before serving
+ * starts, a binding with no access to the CUDA allocator).  It has no
+ * counterpart in the reference.  It allocates nothing: its scratch is a
+ * 6.5 MiB array inside the library that each device using it holds until the
+ * process exits.  Limits: hidden <= NSM_STATIC_MAX_HIDDEN, num_blocks_gathered
+ * <= NSM_STATIC_MAX_BLOCKS; larger calls return NSM_ERR_UNSUPPORTED.  All
+ * calls on a device share the array (each clears what must start at zero), so
+ * calls that overlap on the GPU race.  The first call on a device sets up the
+ * array's address with that device current; make it before any stream
+ * capture.  Results equal nsm_decode_gathered's. */
+#define NSM_STATIC_MAX_HIDDEN 16384
+#define NSM_STATIC_MAX_BLOCKS 256
+int nsm_decode_gathered_static(const void* x, int32_t x_dtype, int32_t hidden, int32_t num_blocks_gathered,
+                               const nsm_mlp_weights* w, void* y, int32_t y_dtype, float* act_out,
+                               nsm_stream_t stream);
+
 /* ---- layout helpers ----------------------------------------------------- */
 /* bitsandbytes down weight [H][I/2] + absmax [H][I/64] -> block-major
  * [n][H][16] + [n][H] for the listed blocks (blocks == NULL: all I/32).
