@@ -1,24 +1,25 @@
 // nsm_decode.cu -- single-token blockwise-sparse NF4 decode MLP for sm_100a.
 //
-// Pipeline of one decode step (one decoder layer, one token), all on one stream:
+// Pipeline of one decode step (one decoder layer, one token), all on one stream,
+// chained with programmatic dependent launch:
 //   1. router_latent_kernel   x prep (optional residual add + RMSNorm), fp16 x
 //                             with per-64-column power-of-two scales, split-H
 //                             partial latent x . enc_w^T; the last CTA reduces,
 //                             applies the norm scale, bias and basis top-k.
-//   2. router_select_kernel   block scores clamp0(latent . score_w^T + b)
-//                             (* down_block_norm), the last CTA sorts (score
-//                             desc, index asc), emits the top-k and compacts
-//                             the selection into pool rows through the block
-//                             map (resident table or shard range).
-//   3. gateup_kernel          persistent warps over (block, column-range)
-//                             units: NF4 gather-GEMV of gate and up, fp32
-//                             partials, the last unit of a block reduces them
-//                             in fixed order and writes SiLU(g)*u as fp16 with
-//                             a per-block power-of-two scale.
-//   4. down_kernel            persistent warps over (32-row tile, block group)
-//                             units: NF4 column gather-GEMV, split-K partials,
-//                             the last group of a row tile reduces in fixed
-//                             order and writes y.
+//   2. router_scores_kernel   block scores clamp0(latent . score_w^T + b)
+//                             (* down_block_norm).
+//   3. router_topk_kernel     top-k (score desc, index asc) by radix select;
+//                             compacts the selection into pool rows through
+//                             the block map (resident table or shard range).
+//   4. gateup_kernel          warps stream equal ranges of the (block, 64-column
+//                             tile) pairs: NF4 gather-GEMV of gate and up, fp32
+//                             partials per block segment.
+//   5. gateup_finalize_kernel fixed-order segment sums, SiLU(g)*u as fp16 with a
+//                             per-block power-of-two scale.
+//   6. down_kernel            warps stream equal ranges of the (32-row tile,
+//                             block) pairs: NF4 column gather-GEMV, fp32
+//                             partials per row-tile segment.
+//   7. down_finalize_kernel   fixed-order segment sums (+ bias) -> y.
 // Reference semantics: streaming_llama_runtime.py:4209-4238 (latent),
 // :4311-4352 (scores/top-k), :5433-5492 (MLP math).
 #include <cuda_fp16.h>
@@ -222,71 +223,101 @@ __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& 
   }
 }
 
-__device__ __forceinline__ int gateup_tiles_per_unit(int count, int tiles_per_row, int total_warps) {
-  const int min_tpu = (tiles_per_row + kMaxUnitsPerSlot - 1) / kMaxUnitsPerSlot;
-  const long long total = (long long)count * tiles_per_row;
-  const long long want = total / (4LL * total_warps);
-  const int tpu = (int)max(1LL, min(16LL, want));
-  return max(tpu, min_tpu);
+// ---- balanced work streams ---------------------------------------------------
+// Both gather-GEMVs split their (block, tile) pairs into `nw` contiguous,
+// equal ranges, one per warp (sizes differ by at most one pair), so every warp
+// finishes at the same time and its load pipeline never restarts at a block
+// boundary.  A warp flushes its fp32 accumulators whenever its range crosses
+// the boundary of a reduction group (a block for gate/up, a 32-row tile for
+// down); the segments of one group are reduced in fixed order by the
+// finalize kernels, so results are deterministic.
+__device__ __forceinline__ int stream_begin(int total, int nw, int w) {
+  return (int)(((long long)total * w) / nw);
+}
+// The warp whose range holds pair x: the largest w with stream_begin(w) <= x.
+__device__ __forceinline__ int stream_owner(int total, int nw, int x) {
+  return (int)((((long long)x + 1) * nw - 1) / total);
+}
+// Warps for `groups` reduction groups of `len` pairs with at most `max_seg`
+// segments per group: every range holds >= ceil(len / (max_seg - 2)) pairs.
+__device__ __forceinline__ int stream_warps(int groups, int len, int max_seg, int total_warps) {
+  const int total = groups * len;
+  const int m = max(1, (len + max_seg - 3) / (max_seg - 2));
+  return max(1, min(total_warps, total / m));
 }
 
-// L2 prefetch of one gate/up unit's bytes (tiled layout: contiguous ranges).
-__device__ __forceinline__ void gateup_prefetch_unit(const GateUpParams& p, int u, int ups, int tpu, int tiles_per_row,
-                                                     int lane) {
-  if (lane >= 4) return;
-  const int s = u / ups, sub = u - s * ups;
-  const int prow = p.rows[s];
-  const int j0 = sub * tpu, j1 = min(tiles_per_row, j0 + tpu);
-  if (lane < 2) {
-    const uint8_t* base = (lane == 0 ? p.gate : p.up) + (int64_t)prow * p.gstride;
-    prefetch_l2_bulk(base + (int64_t)j0 * 1024, (uint32_t)(j1 - j0) * 1024u);
-  } else {
-    const float* base = (lane == 2 ? p.gate_am : p.up_am) + (int64_t)prow * p.gastride;
-    prefetch_l2_bulk(base + j0 * 32, (uint32_t)(j1 - j0) * 128u);
+constexpr int kStageRowsMax = 1024;  // pool rows staged in shared memory up to this count
+
+struct GuPtrs {
+  const uint8_t* g;
+  const uint8_t* u;
+  const float* ga;
+  const float* ua;
+};
+
+__device__ __forceinline__ GuPtrs gu_ptrs(const GateUpParams& p, int prow) {
+  return GuPtrs{p.gate + (int64_t)prow * p.gstride, p.up + (int64_t)prow * p.gstride,
+                p.gate_am + (int64_t)prow * p.gastride, p.up_am + (int64_t)prow * p.gastride};
+}
+
+__device__ __forceinline__ void gu_flush(const GateUpParams& p, int s, int seg, int g, int t, float acc[2][4]) {
+  // column 0 of the accumulator lives in lanes with t == 0
+  if (t == 0) {
+    float* part = p.gu_part + ((int64_t)s * kMaxUnitsPerSlot + seg) * 64;
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) part[pr * 32 + (i >> 1) * 16 + g + (i & 1) * 8] = acc[pr][i];
   }
+#pragma unroll
+  for (int pr = 0; pr < 2; ++pr)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[pr][i] = 0.f;
 }
 
 template <bool kTiled, bool kStageX, int kBase>
-__device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, const __half* xs16, const float* xss) {
+__device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, const __half* xs16, const float* xss,
+                                            const int* rows, int count) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int count = *p.count_ptr;
-  const int tiles_per_row = p.H >> 6;
-  const int tpu = gateup_tiles_per_unit(count, tiles_per_row, p.total_warps);
-  const int ups = (tiles_per_row + tpu - 1) / tpu;
-  const int nunits = count * ups;
-
-  if (kTiled && warp_global < nunits) gateup_prefetch_unit(p, warp_global, ups, tpu, tiles_per_row, lane);
-  for (int u = warp_global; u < nunits; u += p.total_warps) {
-    // the next unit of this warp streams into L2 while this one computes
-    if (kTiled && u + p.total_warps < nunits) gateup_prefetch_unit(p, u + p.total_warps, ups, tpu, tiles_per_row, lane);
-    const int s = u / ups, sub = u - s * ups;
-    const int prow = p.rows[s];
-    const uint8_t* gb = p.gate + (int64_t)prow * p.gstride;
-    const uint8_t* ub = p.up + (int64_t)prow * p.gstride;
-    const float* gab = p.gate_am + (int64_t)prow * p.gastride;
-    const float* uab = p.up_am + (int64_t)prow * p.gastride;
-    const int j0 = sub * tpu, j1 = min(tiles_per_row, j0 + tpu);
-    float acc[2][4] = {};
-    GuTile t0, t1;
-    gu_load<kTiled>(p, gb, ub, gab, uab, j0, lane, t0);
-    for (int j = j0; j < j1; j += 2) {
-      if (j + 1 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 1, lane, t1);
-      gu_compute<kBase, kStageX>(p, t0, j, t, lb, xs16, xss, acc);
-      if (j + 1 >= j1) break;
-      if (j + 2 < j1) gu_load<kTiled>(p, gb, ub, gab, uab, j + 2, lane, t0);
-      gu_compute<kBase, kStageX>(p, t1, j + 1, t, lb, xs16, xss, acc);
+  const int tpr = p.H >> 6;
+  const int total = count * tpr;
+  const int nw = stream_warps(count, tpr, kMaxUnitsPerSlot, p.total_warps);
+  if (warp_global >= nw) return;
+  const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
+  int s = q0 / tpr, j = q0 - s * tpr;
+  int seg = warp_global - stream_owner(total, nw, s * tpr);
+  GuPtrs cp = gu_ptrs(p, rows[s]);
+  GuTile ta, tb;
+  gu_load<kTiled>(p, cp.g, cp.u, cp.ga, cp.ua, j, lane, ta);
+  float acc[2][4] = {};
+  int q = q0;
+  // one pair: load the next pair into `nx`, compute `cur`, flush at a block
+  // boundary or at the end of the range
+  auto step = [&](GuTile& cur, GuTile& nx) -> bool {
+    int sn = s, jn = j + 1;
+    if (jn == tpr) { jn = 0; ++sn; }
+    const bool more = q + 1 < q1;
+    GuPtrs np = cp;
+    if (more) {
+      if (sn != s) np = gu_ptrs(p, rows[sn]);
+      gu_load<kTiled>(p, np.g, np.u, np.ga, np.ua, jn, lane, nx);
     }
-    // column 0 of the accumulator lives in lanes with t == 0; the split-K
-    // reduction and SiLU*up happen in gateup_finalize_kernel
-    if (t == 0) {
-      float* part = p.gu_part + ((int64_t)s * kMaxUnitsPerSlot + sub) * 64;
-#pragma unroll
-      for (int pr = 0; pr < 2; ++pr)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) part[pr * 32 + (i >> 1) * 16 + g + (i & 1) * 8] = acc[pr][i];
+    gu_compute<kBase, kStageX>(p, cur, j, t, lb, xs16, xss, acc);
+    if (!more || sn != s) {
+      gu_flush(p, s, seg, g, t, acc);
+      seg = 0;  // this warp holds the first pair of the next block
     }
+    s = sn;
+    j = jn;
+    cp = np;
+    ++q;
+    return more;
+  };
+  while (true) {
+    if (!step(ta, tb)) break;
+    if (!step(tb, ta)) break;
   }
 }
 
@@ -302,9 +333,9 @@ __global__ void __launch_bounds__(256) gateup_finalize_kernel(GateUpParams p) {
   const int s = blockIdx.x;
   const int count = *p.count_ptr;
   if (s >= count) return;
-  const int tiles_per_row = p.H >> 6;
-  const int tpu = gateup_tiles_per_unit(count, tiles_per_row, p.total_warps);
-  const int ups = (tiles_per_row + tpu - 1) / tpu;
+  const int tpr = p.H >> 6;
+  const int nw = stream_warps(count, tpr, kMaxUnitsPerSlot, p.total_warps);
+  const int ups = stream_owner(count * tpr, nw, s * tpr + tpr - 1) - stream_owner(count * tpr, nw, s * tpr) + 1;
   const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
   float gsum = 0.f, usum = 0.f;
 #pragma unroll 8
@@ -353,19 +384,25 @@ __global__ void __launch_bounds__(kMlpThreads, 2) gateup_kernel(GateUpParams p) 
   pdl_wait();  // rows, count, x16 come from the router kernels
   __half* xs16 = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
   float* xss = reinterpret_cast<float*>(xs16 + (kStageX ? p.H : 0));
+  int* srows = reinterpret_cast<int*>(xss + (kStageX ? p.H / 64 : 0));
+  const int count = *p.count_ptr;
   if (kStageX) {
     const uint4* src = reinterpret_cast<const uint4*>(p.x16);
     uint4* dst = reinterpret_cast<uint4*>(xs16);
     for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = __ldcg(src + i);
     for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
   }
+  const bool stage_rows = count <= kStageRowsMax;
+  if (stage_rows)
+    for (int i = threadIdx.x; i < count; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
   __syncthreads();
+  const int* rows = stage_rows ? srows : p.rows;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
   const uint32_t base = lut_base_addr();
   if (base == 0x400u)
-    gateup_body<kTiled, kStageX, 0x400>(p, lb, xs16, xss);
+    gateup_body<kTiled, kStageX, 0x400>(p, lb, xs16, xss, rows, count);
   else
-    gateup_body<kTiled, kStageX, -1>(p, lb, xs16, xss);
+    gateup_body<kTiled, kStageX, -1>(p, lb, xs16, xss, rows, count);
 }
 
 // ============================================================================
@@ -428,108 +465,77 @@ struct DownBatch {
   float4 am[kDownBatch];
 };
 
-template <bool kTiled, bool kStage>
-__device__ __forceinline__ void down_batch_load(const DownParams& p, const int* srows, int sb, int s1, int rt,
-                                                int lane, DownBatch& b) {
-#pragma unroll
-  for (int i = 0; i < kDownBatch; ++i) {
-    if (sb + i < s1) {
-      const int prow = kStage ? srows[sb + i] : p.rows[sb + i];
-      down_load<kTiled>(p, prow, rt, lane, b.w[i], b.am[i]);
-    }
-  }
-}
-
-template <int kBase, bool kStage>
-__device__ __forceinline__ void down_batch_compute(const DownParams& p, const __half* sact, const float* sscale,
-                                                   int sb, int s1, int t, uint32_t lb, const DownBatch& b,
-                                                   float acc[4]) {
-#pragma unroll
-  for (int i = 0; i < kDownBatch; ++i) {
-    const int s = sb + i;
-    if (s < s1) {
-      uint4 bf;
-      float as;
-      if (kStage) {
-        bf = *reinterpret_cast<const uint4*>(sact + s * 32 + t * 8);
-        as = sscale[s];
-      } else {
-        bf = ldg_u4(p.act16 + (int64_t)s * 32 + t * 8);
-        as = ldg_f32(p.act_scale + s);
-      }
-      float d[4];
-      down_mma<kBase>(lb, b.w[i].x, b.w[i].y, bf, d);
-      acc[0] = fmaf(d[0], b.am[i].x * as, acc[0]);
-      acc[1] = fmaf(d[2], b.am[i].y * as, acc[1]);
-      down_mma<kBase>(lb, b.w[i].z, b.w[i].w, bf, d);
-      acc[2] = fmaf(d[0], b.am[i].z * as, acc[2]);
-      acc[3] = fmaf(d[2], b.am[i].w * as, acc[3]);
-    }
-  }
-}
-
-constexpr int kDownRowTiles = 2;  // 32-row tiles per down unit
-
-__device__ __forceinline__ int down_slot_groups(int count, int RT, int total_warps) {
-  const int RG = (RT + kDownRowTiles - 1) / kDownRowTiles;
-  int sg = (3 * total_warps + RG - 1) / RG;
-  return max(1, min(sg, min(max(count, 1), kMaxSlotGroups)));
-}
-
-
-// L2 prefetch of one down unit: for each of its blocks, the rows of its row
-// tiles are contiguous in the tiled layout (512 B packed + 128 B absmax each).
-template <bool kStage>
-__device__ __forceinline__ void down_prefetch_unit(const DownParams& p, const int* srows, int u, int RG, int gs,
-                                                   int count, int RT, int lane) {
-  const int grp = u / RG, rgi = u - grp * RG;
-  const int rt0 = rgi * kDownRowTiles, rt1 = min(RT, rt0 + kDownRowTiles);
-  const int s0 = grp * gs, s1 = min(count, s0 + gs);
-  for (int q = lane; q < 2 * (s1 - s0); q += 32) {
-    const int s = s0 + (q >> 1);
-    const int prow = kStage ? srows[s] : p.rows[s];
-    if ((q & 1) == 0)
-      prefetch_l2_bulk(p.down + (int64_t)prow * p.dbs + (int64_t)rt0 * 512, (uint32_t)(rt1 - rt0) * 512u);
-    else
-      prefetch_l2_bulk(p.down_am + (int64_t)prow * p.dabs + rt0 * 32, (uint32_t)(rt1 - rt0) * 128u);
-  }
+// Down pairs are (32-row tile rt, slot s), rt-major: pair q = rt * count + s.
+__device__ __forceinline__ int down_stream_warps(int count, int RT, int total_warps) {
+  return stream_warps(RT, count, kMaxSlotGroups, total_warps);
 }
 
 template <bool kTiled, bool kStage, int kBase>
 __device__ __forceinline__ void down_body(const DownParams& p, uint32_t lb, const __half* sact, const float* sscale,
-                                          const int* srows, int count) {
+                                          const int* rows, int count) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int RT = p.H >> 5;
-  const int RG = (RT + kDownRowTiles - 1) / kDownRowTiles;
-  const int sg = down_slot_groups(count, RT, p.total_warps);
-  const int gs = (count + sg - 1) / sg;
-  const int nunits = RG * sg;
-
-  if (kTiled && warp_global < nunits) down_prefetch_unit<kStage>(p, srows, warp_global, RG, gs, count, RT, lane);
-  for (int u = warp_global; u < nunits; u += p.total_warps) {
-    if (kTiled && u + p.total_warps < nunits)
-      down_prefetch_unit<kStage>(p, srows, u + p.total_warps, RG, gs, count, RT, lane);
-    const int grp = u / RG, rgi = u - grp * RG;
-    const int s0 = grp * gs, s1 = min(count, s0 + gs);
-    for (int rt = rgi * kDownRowTiles; rt < min(RT, (rgi + 1) * kDownRowTiles); ++rt) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, 16+g, 24+g of the tile
-      DownBatch b0, b1;
-      if (s0 < s1) down_batch_load<kTiled, kStage>(p, srows, s0, s1, rt, lane, b0);
-      for (int sb = s0; sb < s1; sb += 2 * kDownBatch) {
-        if (sb + kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + kDownBatch, s1, rt, lane, b1);
-        down_batch_compute<kBase, kStage>(p, sact, sscale, sb, s1, t, lb, b0, acc);
-        if (sb + kDownBatch >= s1) break;
-        if (sb + 2 * kDownBatch < s1) down_batch_load<kTiled, kStage>(p, srows, sb + 2 * kDownBatch, s1, rt, lane, b0);
-        down_batch_compute<kBase, kStage>(p, sact, sscale, sb + kDownBatch, s1, t, lb, b1, acc);
-      }
-      if (t == 0) {
-        float* yp = p.ypart + (int64_t)grp * p.H + rt * 32;
+  const int total = RT * count;
+  const int nw = down_stream_warps(count, RT, p.total_warps);
+  if (warp_global >= nw) return;
+  const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
+  int rt = q0 / count, s = q0 - rt * count;  // compute cursor
+  int seg = warp_global - stream_owner(total, nw, rt * count);
+  int lrt = rt, ls = s;                      // load cursor
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};  // rows g, g+8, 16+g, 24+g of tile rt
+  DownBatch b0, b1;
+  auto load_batch = [&](int qb, DownBatch& b) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) yp[(i >> 1) * 16 + g + (i & 1) * 8] = acc[i];
+    for (int i = 0; i < kDownBatch; ++i) {
+      if (qb + i < q1) {
+        down_load<kTiled>(p, rows[ls], lrt, lane, b.w[i], b.am[i]);
+        if (++ls == count) { ls = 0; ++lrt; }
       }
     }
+  };
+  auto compute_batch = [&](int qb, const DownBatch& b) {
+#pragma unroll
+    for (int i = 0; i < kDownBatch; ++i) {
+      const int q = qb + i;
+      if (q < q1) {
+        uint4 bf;
+        float as;
+        if (kStage) {
+          bf = *reinterpret_cast<const uint4*>(sact + s * 32 + t * 8);
+          as = sscale[s];
+        } else {
+          bf = ldg_u4(p.act16 + (int64_t)s * 32 + t * 8);
+          as = ldg_f32(p.act_scale + s);
+        }
+        float d[4];
+        down_mma<kBase>(lb, b.w[i].x, b.w[i].y, bf, d);
+        acc[0] = fmaf(d[0], b.am[i].x * as, acc[0]);
+        acc[1] = fmaf(d[2], b.am[i].y * as, acc[1]);
+        down_mma<kBase>(lb, b.w[i].z, b.w[i].w, bf, d);
+        acc[2] = fmaf(d[0], b.am[i].z * as, acc[2]);
+        acc[3] = fmaf(d[2], b.am[i].w * as, acc[3]);
+        if (++s == count || q + 1 == q1) {
+          if (t == 0) {
+            float* yp = p.ypart + (int64_t)seg * p.H + rt * 32;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) yp[(r >> 1) * 16 + g + (r & 1) * 8] = acc[r];
+          }
+          acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+          seg = 0;  // this warp holds the first pair of the next row tile
+          if (s == count) { s = 0; ++rt; }
+        }
+      }
+    }
+  };
+  load_batch(q0, b0);
+  for (int qb = q0; qb < q1; qb += 2 * kDownBatch) {
+    if (qb + kDownBatch < q1) load_batch(qb + kDownBatch, b1);
+    compute_batch(qb, b0);
+    if (qb + kDownBatch >= q1) break;
+    if (qb + 2 * kDownBatch < q1) load_batch(qb + 2 * kDownBatch, b0);
+    compute_batch(qb + kDownBatch, b1);
   }
 }
 
@@ -541,10 +547,12 @@ __global__ void __launch_bounds__(256) down_finalize_kernel(DownParams p) {
   const int gtid = blockIdx.x * blockDim.x + threadIdx.x;
   const int h = gtid >> 2, q0 = gtid & 3;
   const int count = *p.count_ptr;
-  const int sg = down_slot_groups(count, p.H >> 5, p.total_warps);
   float y = 0.f;
-  if (h < p.H) {
-#pragma unroll 8
+  if (h < p.H && count > 0) {
+    const int RT = p.H >> 5, rt = h >> 5;
+    const int nw = down_stream_warps(count, RT, p.total_warps);
+    const int sg = stream_owner(RT * count, nw, rt * count + count - 1) - stream_owner(RT * count, nw, rt * count) + 1;
+#pragma unroll 4
     for (int q = q0; q < sg; q += 4) y += ldcg_f32(p.ypart + (int64_t)q * p.H + h);
   }
   const float y1 = __shfl_down_sync(0xffffffffu, y, 1);
@@ -575,12 +583,13 @@ __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
     }
   }
   __syncthreads();
+  const int* rows = kStage ? srows : p.rows;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
   const uint32_t base = lut_base_addr();
   if (base == 0x400u)
-    down_body<kTiled, kStage, 0x400>(p, lb, sact, sscale, srows, count);
+    down_body<kTiled, kStage, 0x400>(p, lb, sact, sscale, rows, count);
   else
-    down_body<kTiled, kStage, -1>(p, lb, sact, sscale, srows, count);
+    down_body<kTiled, kStage, -1>(p, lb, sact, sscale, rows, count);
 }
 
 // ============================================================================
@@ -588,7 +597,8 @@ __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
 // ============================================================================
 static int dtype_ok(int d) { return d == NSM_F32 || d == NSM_F16 || d == NSM_BF16; }
 
-constexpr int kGateupSmemStaged = kSmemHead + kStageXMaxHidden * 2 + (kStageXMaxHidden / 64) * 4;
+constexpr int kGateupSmem = kSmemHead + kStageRowsMax * 4;
+constexpr int kGateupSmemStaged = kGateupSmem + kStageXMaxHidden * 2 + (kStageXMaxHidden / 64) * 4;
 constexpr int kDownSmemStaged = kSmemHead + kStageActMaxSlots * (64 + 4 + 4);
 
 struct KernelSetup {
@@ -609,9 +619,9 @@ static int setup_one(K kernel, int smem, int* ctas_per_sm) {
 static int setup_kernels(const DeviceInfo& d, KernelSetup** out) {
   KernelSetup& s = g_setup[d.device];
   if (!s.done) {
-    int st = setup_one(gateup_kernel<false, false>, kSmemHead, &s.gu[0][0]);
+    int st = setup_one(gateup_kernel<false, false>, kGateupSmem, &s.gu[0][0]);
     if (!st) st = setup_one(gateup_kernel<false, true>, kGateupSmemStaged, &s.gu[0][1]);
-    if (!st) st = setup_one(gateup_kernel<true, false>, kSmemHead, &s.gu[1][0]);
+    if (!st) st = setup_one(gateup_kernel<true, false>, kGateupSmem, &s.gu[1][0]);
     if (!st) st = setup_one(gateup_kernel<true, true>, kGateupSmemStaged, &s.gu[1][1]);
     if (!st) st = setup_one(down_kernel<false, false>, kSmemHead, &s.dn[0][0]);
     if (!st) st = setup_one(down_kernel<false, true>, kDownSmemStaged, &s.dn[0][1]);
@@ -701,7 +711,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   const bool gu_stage = m.H <= kStageXMaxHidden;
   const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
   gp.total_warps = gu_ctas * (kMlpThreads / 32);
-  const int gu_smem = gu_stage ? kGateupSmemStaged : kSmemHead;
+  const int gu_smem = gu_stage ? kGateupSmemStaged : kGateupSmem;
   cudaError_t e;
   if (gu_tiled) {
     if (gu_stage) e = launch_pdl(gateup_kernel<true, true>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
