@@ -51,6 +51,10 @@ const char* nsm_status_string(int status);
 const char* nsm_last_error(void);
 /* Zero-fills a workspace (stream-ordered). */
 int nsm_workspace_init(void* ws, size_t ws_bytes, nsm_stream_t stream);
+/* Reads (and clears) the workspace's device error word: kernels that give up
+ * on a bounded wait record a status there (NSM_ERR_TIMEOUT) instead of
+ * spinning.  Synchronises `stream`.  *code_out = 0 when no kernel failed. */
+int nsm_workspace_error(void* ws, size_t ws_bytes, int32_t* code_out, nsm_stream_t stream);
 
 /* ---- router ------------------------------------------------------------
  * Learned-basis router weights.  Replaces the per-layer routing dict the

@@ -34,7 +34,7 @@ EXPORTED = (
     "nsm_decode_workspace_bytes", "nsm_route", "nsm_sparse_mlp_decode", "nsm_decode_gathered",
     "nsm_decode_rows_workspace_bytes", "nsm_decode_gathered_rows", "nsm_repack_down_block_major",
     "nsm_sparse_input_linear_4bit", "nsm_sparse_output_linear_4bit", "nsm_cache_split", "nsm_cache_promote",
-    "nsm_repack_tiled", "nsm_decode_gathered_static",
+    "nsm_repack_tiled", "nsm_decode_gathered_static", "nsm_workspace_error",
 )
 
 
@@ -84,6 +84,7 @@ _SIGS = {
                                       c_size_t, c_void_p]),
     "nsm_decode_gathered": (c_int, [c_void_p, c_int32, c_int32, c_int32, POINTER(MlpWeightsC), c_void_p, c_int32,
                                     c_void_p, c_void_p, c_size_t, c_void_p]),
+    "nsm_workspace_error": (c_int, [c_void_p, c_size_t, POINTER(c_int32), c_void_p]),
     "nsm_decode_gathered_static": (c_int, [c_void_p, c_int32, c_int32, c_int32, POINTER(MlpWeightsC), c_void_p,
                                            c_int32, c_void_p, c_void_p]),
     "nsm_decode_rows_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),

@@ -1,6 +1,7 @@
 """Small torch <-> C-ABI helpers: dtype codes, raw pointers, streams, workspaces."""
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -58,6 +59,19 @@ class WorkspacePool:
                 _lib.check(_lib.load().nsm_workspace_init(buf.data_ptr(), buf.numel(), key[1]), "nsm_workspace_init")
                 self._ws[key] = buf
             return buf
+
+    def errors(self) -> dict[tuple[int, int], int]:
+        """Read and clear the device error word of every cached workspace
+        (non-zero: a kernel gave up on a bounded wait).  Synchronises."""
+        out = {}
+        with self._lock:
+            for key, buf in self._ws.items():
+                code = ctypes.c_int32(0)
+                with torch.cuda.device(key[0]):
+                    _lib.check(_lib.load().nsm_workspace_error(buf.data_ptr(), buf.numel(), ctypes.byref(code), key[1]),
+                               "nsm_workspace_error")
+                out[key] = int(code.value)
+        return out
 
     def clear(self) -> None:
         with self._lock:

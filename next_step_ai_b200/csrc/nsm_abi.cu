@@ -69,8 +69,7 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   int* tick = reinterpret_cast<int*>(take((size_t)kCounterInts * sizeof(int)));
   w.ticket_router_a = tick;
   w.ticket_router_b = tick ? tick + 1 : nullptr;
-  w.ticket_slot = tick ? tick + 2 : nullptr;
-  w.ticket_rowtile = tick ? tick + 2 + kMaxTopK : nullptr;
+  w.err = tick ? tick + 2 : nullptr;
   w.latent_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * rank * sizeof(float)));
   w.sumsq_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * sizeof(float)));
   w.latent = reinterpret_cast<float*>(take((size_t)rank * sizeof(float)));
@@ -116,6 +115,20 @@ const char* nsm_last_error(void) { return g_last_error.c_str(); }
 int nsm_workspace_init(void* ws, size_t ws_bytes, nsm_stream_t stream) {
   if (ws == nullptr || ws_bytes == 0) return fail(NSM_ERR_WORKSPACE, "nsm_workspace_init: empty workspace");
   NSM_CHECK_CUDA(cudaMemsetAsync(ws, 0, ws_bytes, reinterpret_cast<cudaStream_t>(stream)));
+  return NSM_OK;
+}
+
+int nsm_workspace_error(void* ws, size_t ws_bytes, int32_t* code_out, nsm_stream_t stream) {
+  if (code_out == nullptr) return fail(NSM_ERR_INVALID_ARG, "nsm_workspace_error: code_out is NULL");
+  if (ws == nullptr || ws_bytes < (size_t)kCounterInts * sizeof(int))
+    return fail(NSM_ERR_WORKSPACE, "nsm_workspace_error: workspace missing or too small");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int* err = decode_ws_layout(ws, 64, 64, 1, 1).err;
+  int32_t v = 0;
+  NSM_CHECK_CUDA(cudaMemcpyAsync(&v, err, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  NSM_CHECK_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), s));
+  NSM_CHECK_CUDA(cudaStreamSynchronize(s));
+  *code_out = v;
   return NSM_OK;
 }
 

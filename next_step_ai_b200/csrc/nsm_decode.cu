@@ -67,11 +67,14 @@ template <int kBase>
 __device__ __forceinline__ uint32_t lut_get(uint32_t w, uint32_t lanebase, int kbyte, int table) {
   const uint32_t addr = __byte_perm(w, lanebase, 0x5504u | ((uint32_t)kbyte << 4));
   if (kBase >= 0) {
+    // not volatile: the tables are constant after the prologue's barrier and
+    // the address depends on weight bytes loaded after it, so the compiler may
+    // interleave these loads with independent MMA chains
     uint32_t v;
     if (table == 0)
-      asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(kBase));
+      asm("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(kBase));
     else
-      asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(kBase + 128));
+      asm("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(addr), "n"(kBase + 128));
     return v;
   } else {
     return *reinterpret_cast<const uint32_t*>(reinterpret_cast<const char*>(g_lut_smem) + addr + table * 128);
@@ -82,8 +85,7 @@ __device__ __forceinline__ uint32_t lut_base_addr() { return (uint32_t)__cvta_ge
 
 __device__ __forceinline__ void mma_16816_z(float d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                             uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%10,%10,%10};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
@@ -132,7 +134,7 @@ struct GateUpParams {
   const void* act_mask;  // optional [U*32] (one row of flat_mask)
   int mask_dtype;
   float* gu_part;
-  int* ticket_slot;
+  int* err;
   __half* act16;
   float* act_scale;
   float* act_out;  // optional fp32 [k][32]
@@ -191,6 +193,24 @@ __device__ __forceinline__ void gu_mma_rowgroup(uint32_t lb, const uint4 w, cons
             lut_get<kBase>(w.y, lb, 3, kTable), lut_get<kBase>(w.w, lb, 3, kTable), b[6], b[7]);
 }
 
+// Both projections of one tile: acc[proj][i] += (W_rows . x_tile) * absmax * xscale.
+template <int kBase>
+__device__ __forceinline__ void gu_tile_mma(const GuTile& tile, const uint32_t b[8], float xs, uint32_t lb,
+                                            float acc[2][4]) {
+  float d[4];
+#pragma unroll
+  for (int rg = 0; rg < 2; ++rg) {
+    gu_mma_rowgroup<kBase, 0>(lb, tile.w[0][rg], b, d);
+    const float g0 = rg ? tile.am[0].z : tile.am[0].x, g1 = rg ? tile.am[0].w : tile.am[0].y;
+    acc[0][rg * 2] = fmaf(d[0], g0 * xs, acc[0][rg * 2]);
+    acc[0][rg * 2 + 1] = fmaf(d[2], g1 * xs, acc[0][rg * 2 + 1]);
+    gu_mma_rowgroup<kBase, 1>(lb, tile.w[1][rg], b, d);
+    const float u0 = rg ? tile.am[1].z : tile.am[1].x, u1 = rg ? tile.am[1].w : tile.am[1].y;
+    acc[1][rg * 2] = fmaf(d[0], u0 * xs, acc[1][rg * 2]);
+    acc[1][rg * 2 + 1] = fmaf(d[2], u1 * xs, acc[1][rg * 2 + 1]);
+  }
+}
+
 template <int kBase, bool kStageX>
 __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& tile, int j, int t, uint32_t lb,
                                            const __half* xs16, const float* xss, float acc[2][4]) {
@@ -209,18 +229,7 @@ __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& 
     b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
     xs = ldg_f32(p.xscale + j);
   }
-  float d[4];
-#pragma unroll
-  for (int rg = 0; rg < 2; ++rg) {
-    gu_mma_rowgroup<kBase, 0>(lb, tile.w[0][rg], b, d);
-    const float g0 = rg ? tile.am[0].z : tile.am[0].x, g1 = rg ? tile.am[0].w : tile.am[0].y;
-    acc[0][rg * 2] = fmaf(d[0], g0 * xs, acc[0][rg * 2]);
-    acc[0][rg * 2 + 1] = fmaf(d[2], g1 * xs, acc[0][rg * 2 + 1]);
-    gu_mma_rowgroup<kBase, 1>(lb, tile.w[1][rg], b, d);
-    const float u0 = rg ? tile.am[1].z : tile.am[1].x, u1 = rg ? tile.am[1].w : tile.am[1].y;
-    acc[1][rg * 2] = fmaf(d[0], u0 * xs, acc[1][rg * 2]);
-    acc[1][rg * 2 + 1] = fmaf(d[2], u1 * xs, acc[1][rg * 2 + 1]);
-  }
+  gu_tile_mma<kBase>(tile, b, xs, lb, acc);
 }
 
 // ---- balanced work streams ---------------------------------------------------
@@ -422,7 +431,8 @@ struct DownParams {
   const __half* act16;
   const float* act_scale;
   float* ypart;
-  int* ticket_rt;
+  int* err;
+  int group_log2;  // log2 of the rows per down reduction group (5 or 6)
   void* y;
   int y_dtype;
   int total_warps;
@@ -549,8 +559,9 @@ __global__ void __launch_bounds__(256) down_finalize_kernel(DownParams p) {
   const int count = *p.count_ptr;
   float y = 0.f;
   if (h < p.H && count > 0) {
-    const int RT = p.H >> 5, rt = h >> 5;
-    const int nw = down_stream_warps(count, RT, p.total_warps);
+    // reduction groups: 32-row tiles (register kernel) or 64-row groups (bulk-copy kernel)
+    const int RT = p.H >> p.group_log2, rt = h >> p.group_log2;
+    const int nw = stream_warps(RT, count, kMaxSlotGroups, p.total_warps);
     const int sg = stream_owner(RT * count, nw, rt * count + count - 1) - stream_owner(RT * count, nw, rt * count) + 1;
 #pragma unroll 4
     for (int q = q0; q < sg; q += 4) y += ldcg_f32(p.ypart + (int64_t)q * p.H + h);
@@ -593,6 +604,350 @@ __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
 }
 
 // ============================================================================
+// 4b/6b. bulk-copy pipelined variants for the tiled pool layouts
+// ============================================================================
+// One CTA of kTmaWarps warps per SM.  Each warp owns a ring of shared-memory
+// stages that its lane 0 fills with cp.async.bulk (one copy per contiguous
+// tiled run: a 1 KB gate/up tile, a 512 B down row tile, their absmax), so a
+// warp keeps kStages tiles in flight without holding them in registers.  A
+// stage is refilled only after the warp's MMAs consumed the registers read
+// from it.  Waits are bounded; a wait that runs out records NSM_ERR_TIMEOUT in
+// the workspace error word, waits (bounded) for the warp's copies still in
+// flight and stops the warp.
+#ifndef NSM_TMA_WARPS
+#define NSM_TMA_WARPS 16
+#endif
+#ifndef NSM_GU_STAGES
+#define NSM_GU_STAGES 3
+#endif
+#ifndef NSM_DN_STAGES
+#define NSM_DN_STAGES 3
+#endif
+constexpr int kTmaWarps = NSM_TMA_WARPS;
+constexpr int kTmaThreads = kTmaWarps * 32;
+constexpr int kGuStages = NSM_GU_STAGES;
+constexpr int kGuStageBytes = 2048 + 256;  // gate tile, up tile, gate absmax, up absmax
+constexpr int kDnStages = NSM_DN_STAGES;
+#ifndef NSM_DN_PAIRS_PER_STAGE
+#define NSM_DN_PAIRS_PER_STAGE 2
+#endif
+constexpr int kDnPairsPerStage = NSM_DN_PAIRS_PER_STAGE;
+constexpr int kDnStageBytes = kDnPairsPerStage * (1024 + 256);
+// shared-memory layout (bytes from the dynamic base)
+constexpr int kGuX16Off = kSmemHead;
+constexpr int kGuXsOff = kGuX16Off + kStageXMaxHidden * 2;
+constexpr int kGuRowsOff = kGuXsOff + (kStageXMaxHidden / 64) * 4;
+constexpr int kGuRingOff = kGuRowsOff + kStageRowsMax * 4;
+constexpr int kGuBarOff = kGuRingOff + kTmaWarps * kGuStages * kGuStageBytes;
+constexpr int kGuTmaSmem = kGuBarOff + kTmaWarps * kGuStages * 8;
+constexpr int kDnActOff = kSmemHead;
+constexpr int kDnScaleOff = kDnActOff + kStageActMaxSlots * 64;
+constexpr int kDnRowsOff = kDnScaleOff + kStageActMaxSlots * 4;
+constexpr int kDnRingOff = kDnRowsOff + kStageActMaxSlots * 4;
+constexpr int kDnBarOff = kDnRingOff + kTmaWarps * kDnStages * kDnStageBytes;
+constexpr int kDnTmaSmem = kDnBarOff + kTmaWarps * kDnStages * 8;
+static_assert(kGuTmaSmem <= 227 * 1024, "gate/up ring does not fit in shared memory");
+static_assert(kDnTmaSmem <= 227 * 1024, "down ring does not fit in shared memory");
+static_assert(kGuRingOff % 128 == 0 && kDnRingOff % 128 == 0, "rings must be 128-byte aligned");
+
+__device__ __forceinline__ void record_error(int* err, int code) {
+  if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+// After a failed wait: bounded waits for the batches [consumed, issued) that a
+// warp's ring may still be receiving (batch b sits in stage b % kStages and
+// completes phase (b / kStages) & 1 of that stage's mbarrier).
+template <int kStages>
+__device__ __forceinline__ void drain_ring(uint32_t wbar, int consumed, int issued) {
+  for (int b = consumed; b < issued; ++b) mbar_wait(wbar + 8u * (uint32_t)(b % kStages), (uint32_t)((b / kStages) & 1));
+}
+
+template <int kBase>
+__device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t lb, uint32_t xs16_s, uint32_t xss_s,
+                                                const int* rows, int count, uint32_t ring, uint32_t bar0) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int warp = threadIdx.x >> 5;
+  const int warp_global = blockIdx.x * kTmaWarps + warp;
+  const int tpr = p.H >> 6;
+  const int total = count * tpr;
+  const int nw = stream_warps(count, tpr, kMaxUnitsPerSlot, p.total_warps);
+  if (warp_global >= nw) return;
+  const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
+  const uint32_t wring = ring + (uint32_t)(warp * kGuStages * kGuStageBytes);
+  const uint32_t wbar = bar0 + (uint32_t)(warp * kGuStages * 8);
+  const uint64_t pol = l2_evict_first_policy();
+  // load cursor: source pointers of the next pair to fetch
+  int ls = q0 / tpr, lj = q0 - ls * tpr;
+  const uint8_t* lg;
+  const uint8_t* lu;
+  const float* lga;
+  const float* lua;
+  auto load_slot = [&]() {
+    const int prow = rows[ls];
+    lg = p.gate + (int64_t)prow * p.gstride + (int64_t)lj * 1024;
+    lu = p.up + (int64_t)prow * p.gstride + (int64_t)lj * 1024;
+    lga = p.gate_am + (int64_t)prow * p.gastride + lj * 32;
+    lua = p.up_am + (int64_t)prow * p.gastride + lj * 32;
+  };
+  int issued = 0;
+  auto issue_next = [&](int stage) {  // fetch the cursor's pair into `stage`, advance the cursor
+    ++issued;
+    if (lane == 0) {
+      fence_proxy_async_smem();  // the warp's reads of this stage come first
+      const uint32_t dst = wring + (uint32_t)(stage * kGuStageBytes);
+      const uint32_t bar = wbar + 8u * (uint32_t)stage;
+      mbar_arrive_expect_tx(bar, kGuStageBytes);
+      bulk_g2s(dst, lg, 1024u, bar, pol);
+      bulk_g2s(dst + 1024, lu, 1024u, bar, pol);
+      bulk_g2s(dst + 2048, lga, 128u, bar, pol);
+      bulk_g2s(dst + 2176, lua, 128u, bar, pol);
+    }
+    lg += 1024;
+    lu += 1024;
+    lga += 32;
+    lua += 32;
+    if (++lj == tpr) {
+      lj = 0;
+      if (++ls < count) load_slot();
+    }
+  };
+  load_slot();
+#pragma unroll
+  for (int i = 0; i < kGuStages; ++i)
+    if (q0 + i < q1) issue_next(i);
+
+  int s = q0 / tpr, j = q0 - s * tpr;
+  int seg = warp_global - stream_owner(total, nw, s * tpr);
+  uint32_t xa = xs16_s + (uint32_t)(j * 128 + t * 32);  // this lane's x fragment of tile j
+  uint32_t xsa = xss_s + (uint32_t)(j * 4);
+  float acc[2][4] = {};
+  uint32_t phase = 0;
+  int q = q0;
+  bool ok = true;
+  while (q < q1 && ok) {
+#pragma unroll
+    for (int st = 0; st < kGuStages; ++st) {
+      if (q < q1 && ok) {
+        const uint32_t bar = wbar + 8u * st;
+        if (!mbar_wait(bar, phase)) {
+          ok = false;
+        } else {
+          const uint32_t sb = wring + (uint32_t)(st * kGuStageBytes);
+          GuTile tile;
+          tile.w[0][0] = lds_u4(sb + lane * 16);
+          tile.w[0][1] = lds_u4(sb + 512 + lane * 16);
+          tile.w[1][0] = lds_u4(sb + 1024 + lane * 16);
+          tile.w[1][1] = lds_u4(sb + 1536 + lane * 16);
+          tile.am[0] = lds_f4(sb + 2048 + g * 16);
+          tile.am[1] = lds_f4(sb + 2176 + g * 16);
+          const uint4 x0 = lds_u4(xa), x1 = lds_u4(xa + 16);
+          const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+          float xs;
+          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xs) : "r"(xsa));
+          gu_tile_mma<kBase>(tile, bx, xs, lb, acc);
+          __syncwarp();
+          if (q + kGuStages < q1) issue_next(st);
+          ++q;
+          xa += 128;
+          xsa += 4;
+          if (++j == tpr || q == q1) {
+            gu_flush(p, s, seg, g, t, acc);
+            seg = 0;  // this warp holds the first pair of the next block
+            if (j == tpr) {
+              j = 0;
+              ++s;
+              xa = xs16_s + (uint32_t)(t * 32);
+              xsa = xss_s;
+            }
+          }
+        }
+      }
+    }
+    phase ^= 1u;
+  }
+  if (!ok) {
+    record_error(p.err, NSM_ERR_TIMEOUT);
+    drain_ring<kGuStages>(wbar, q - q0, issued);
+  }
+}
+
+__global__ void __launch_bounds__(kTmaThreads, 1) gateup_tma_kernel(GateUpParams p) {
+  char* smem = reinterpret_cast<char*>(g_lut_smem);
+  const uint32_t bar0 = smem_u32(smem + kGuBarOff);
+  if (threadIdx.x < kTmaWarps * kGuStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
+  mbar_init_fence();
+  pdl_trigger();
+  build_lut_dyn(p.gate_code, p.up_code);
+  pdl_wait();  // rows, count, x16 come from the router kernels
+  __half* xs16 = reinterpret_cast<__half*>(smem + kGuX16Off);
+  float* xss = reinterpret_cast<float*>(smem + kGuXsOff);
+  int* srows = reinterpret_cast<int*>(smem + kGuRowsOff);
+  const int count = *p.count_ptr;
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(p.x16);
+    uint4* dst = reinterpret_cast<uint4*>(xs16);
+    for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = __ldcg(src + i);
+    for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
+  }
+  const bool stage_rows = count <= kStageRowsMax;
+  if (stage_rows)
+    for (int i = threadIdx.x; i < count; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
+  __syncthreads();
+  const int* rows = stage_rows ? srows : p.rows;
+  const uint32_t lb = (threadIdx.x & 31) * 4u;
+  const uint32_t ring = smem_u32(smem + kGuRingOff);
+  if (lut_base_addr() == 0x400u)
+    gateup_tma_body<0x400>(p, lb, smem_u32(xs16), smem_u32(xss), rows, count, ring, bar0);
+  else
+    gateup_tma_body<-1>(p, lb, smem_u32(xs16), smem_u32(xss), rows, count, ring, bar0);
+}
+
+// Down, bulk-copy variant: a pair is (64-row group rp, slot s) = two adjacent
+// 32-row tiles of one block (1 KB packed + 256 B absmax, contiguous in the
+// tiled layout); pairs are rp-major.  A stage holds kDnPairsPerStage pairs.
+template <int kBase>
+__device__ __forceinline__ void down_tma_body(const DownParams& p, uint32_t lb, uint32_t sact_s, uint32_t sscale_s,
+                                              const int* rows, int count, uint32_t ring, uint32_t bar0) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int warp = threadIdx.x >> 5;
+  const int warp_global = blockIdx.x * kTmaWarps + warp;
+  const int RP = p.H >> 6;
+  const int total = RP * count;
+  const int nw = stream_warps(RP, count, kMaxSlotGroups, p.total_warps);
+  if (warp_global >= nw) return;
+  const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
+  const uint32_t wring = ring + (uint32_t)(warp * kDnStages * kDnStageBytes);
+  const uint32_t wbar = bar0 + (uint32_t)(warp * kDnStages * 8);
+  const uint64_t pol = l2_evict_first_policy();
+  int lrp = q0 / count, ls = q0 - lrp * count;  // load cursor
+  int lq = q0;
+  int issued = 0;
+  auto issue_next = [&](int stage) {  // up to kDnPairsPerStage pairs into `stage`
+    ++issued;
+    const int n = min(kDnPairsPerStage, q1 - lq);
+    if (lane == 0) {
+      fence_proxy_async_smem();  // the warp's reads of this stage come first
+      const uint32_t dst = wring + (uint32_t)(stage * kDnStageBytes);
+      const uint32_t bar = wbar + 8u * (uint32_t)stage;
+      mbar_arrive_expect_tx(bar, (uint32_t)n * 1280u);
+      int rp = lrp, sl = ls;
+      for (int i = 0; i < n; ++i) {
+        const int prow = rows[sl];
+        bulk_g2s(dst + i * 1024, p.down + (int64_t)prow * p.dbs + (int64_t)rp * 1024, 1024u, bar, pol);
+        bulk_g2s(dst + kDnPairsPerStage * 1024 + i * 256, p.down_am + (int64_t)prow * p.dabs + rp * 64, 256u, bar,
+                 pol);
+        if (++sl == count) { sl = 0; ++rp; }
+      }
+    }
+    lq += n;
+    ls += n;
+    while (ls >= count) { ls -= count; ++lrp; }
+  };
+#pragma unroll
+  for (int i = 0; i < kDnStages; ++i)
+    if (q0 + i * kDnPairsPerStage < q1) issue_next(i);
+
+  int rp = q0 / count, s = q0 - rp * count;
+  int seg = warp_global - stream_owner(total, nw, rp * count);
+  float acc[2][4] = {};  // tile r of the group: rows g, g+8, 16+g, 24+g
+  uint32_t phase = 0;
+  int q = q0;
+  bool ok = true;
+  while (q < q1 && ok) {
+#pragma unroll
+    for (int st = 0; st < kDnStages; ++st) {
+      if (q < q1 && ok) {
+        if (!mbar_wait(wbar + 8u * st, phase)) {
+          ok = false;
+        } else {
+          const uint32_t sb = wring + (uint32_t)(st * kDnStageBytes);
+#pragma unroll
+          for (int i = 0; i < kDnPairsPerStage; ++i) {
+            if (q < q1) {
+              const uint4 w0 = lds_u4(sb + i * 1024 + lane * 16);
+              const uint4 w1 = lds_u4(sb + i * 1024 + 512 + lane * 16);
+              const float4 a0 = lds_f4(sb + kDnPairsPerStage * 1024 + i * 256 + g * 16);
+              const float4 a1 = lds_f4(sb + kDnPairsPerStage * 1024 + i * 256 + 128 + g * 16);
+              const uint4 bf = lds_u4(sact_s + (uint32_t)(s * 64 + t * 16));
+              float as;
+              asm volatile("ld.shared.f32 %0, [%1];" : "=f"(as) : "r"(sscale_s + (uint32_t)(s * 4)));
+              float d[4];
+              down_mma<kBase>(lb, w0.x, w0.y, bf, d);
+              acc[0][0] = fmaf(d[0], a0.x * as, acc[0][0]);
+              acc[0][1] = fmaf(d[2], a0.y * as, acc[0][1]);
+              down_mma<kBase>(lb, w0.z, w0.w, bf, d);
+              acc[0][2] = fmaf(d[0], a0.z * as, acc[0][2]);
+              acc[0][3] = fmaf(d[2], a0.w * as, acc[0][3]);
+              down_mma<kBase>(lb, w1.x, w1.y, bf, d);
+              acc[1][0] = fmaf(d[0], a1.x * as, acc[1][0]);
+              acc[1][1] = fmaf(d[2], a1.y * as, acc[1][1]);
+              down_mma<kBase>(lb, w1.z, w1.w, bf, d);
+              acc[1][2] = fmaf(d[0], a1.z * as, acc[1][2]);
+              acc[1][3] = fmaf(d[2], a1.w * as, acc[1][3]);
+              ++q;
+              if (++s == count || q == q1) {
+                if (t == 0) {
+                  float* yp = p.ypart + (int64_t)seg * p.H + rp * 64;
+#pragma unroll
+                  for (int r = 0; r < 2; ++r)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) yp[r * 32 + (c >> 1) * 16 + g + (c & 1) * 8] = acc[r][c];
+                }
+#pragma unroll
+                for (int r = 0; r < 2; ++r)
+#pragma unroll
+                  for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
+                seg = 0;  // this warp holds the first pair of the next group
+                if (s == count) { s = 0; ++rp; }
+              }
+            }
+          }
+          __syncwarp();
+          if (lq < q1) issue_next(st);
+        }
+      }
+    }
+    phase ^= 1u;
+  }
+  if (!ok) {
+    record_error(p.err, NSM_ERR_TIMEOUT);
+    drain_ring<kDnStages>(wbar, (q - q0) / kDnPairsPerStage, issued);
+  }
+}
+
+__global__ void __launch_bounds__(kTmaThreads, 1) down_tma_kernel(DownParams p) {
+  char* smem = reinterpret_cast<char*>(g_lut_smem);
+  const uint32_t bar0 = smem_u32(smem + kDnBarOff);
+  if (threadIdx.x < kTmaWarps * kDnStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
+  mbar_init_fence();
+  pdl_trigger();
+  build_lut_dyn(p.down_code, p.down_code);
+  pdl_wait();  // act16 / act_scale come from the gate/up kernels
+  const int count = *p.count_ptr;
+  __half* sact = reinterpret_cast<__half*>(smem + kDnActOff);
+  float* sscale = reinterpret_cast<float*>(smem + kDnScaleOff);
+  int* srows = reinterpret_cast<int*>(smem + kDnRowsOff);
+  {
+    const uint4* src = reinterpret_cast<const uint4*>(p.act16);
+    uint4* dst = reinterpret_cast<uint4*>(sact);
+    for (int i = threadIdx.x; i < count * 4; i += blockDim.x) dst[i] = __ldcg(src + i);
+    for (int i = threadIdx.x; i < count; i += blockDim.x) {
+      sscale[i] = __ldcg(p.act_scale + i);
+      srows[i] = __ldcg(p.rows + i);
+    }
+  }
+  __syncthreads();
+  const uint32_t lb = (threadIdx.x & 31) * 4u;
+  const uint32_t ring = smem_u32(smem + kDnRingOff);
+  if (lut_base_addr() == 0x400u)
+    down_tma_body<0x400>(p, lb, smem_u32(sact), smem_u32(sscale), srows, count, ring, bar0);
+  else
+    down_tma_body<-1>(p, lb, smem_u32(sact), smem_u32(sscale), srows, count, ring, bar0);
+}
+
+// ============================================================================
 // host side
 // ============================================================================
 static int dtype_ok(int d) { return d == NSM_F32 || d == NSM_F16 || d == NSM_BF16; }
@@ -605,13 +960,15 @@ struct KernelSetup {
   bool done = false;
   int gu[2][2] = {{0, 0}, {0, 0}};  // [tiled][staged] CTAs per SM
   int dn[2][2] = {{0, 0}, {0, 0}};
+  int gu_tma = 0;  // CTAs per SM of the bulk-copy variants (1 when they fit)
+  int dn_tma = 0;
 };
 static KernelSetup g_setup[64];
 
 template <typename K>
-static int setup_one(K kernel, int smem, int* ctas_per_sm) {
+static int setup_one(K kernel, int smem, int* ctas_per_sm, int threads = kMlpThreads) {
   NSM_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, kMlpThreads, smem));
+  NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, kernel, threads, smem));
   if (*ctas_per_sm <= 0) return fail(NSM_ERR_CUDA, "kernel occupancy is zero");
   return NSM_OK;
 }
@@ -627,6 +984,8 @@ static int setup_kernels(const DeviceInfo& d, KernelSetup** out) {
     if (!st) st = setup_one(down_kernel<false, true>, kDownSmemStaged, &s.dn[0][1]);
     if (!st) st = setup_one(down_kernel<true, false>, kSmemHead, &s.dn[1][0]);
     if (!st) st = setup_one(down_kernel<true, true>, kDownSmemStaged, &s.dn[1][1]);
+    if (!st) st = setup_one(gateup_tma_kernel, kGuTmaSmem, &s.gu_tma, kTmaThreads);
+    if (!st) st = setup_one(down_tma_kernel, kDnTmaSmem, &s.dn_tma, kTmaThreads);
     if (!st) st = router_setup();
     if (st) return st;
     s.done = true;
@@ -703,22 +1062,30 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.act_mask = m.act_mask;
   gp.mask_dtype = m.mask_dtype;
   gp.gu_part = ws.gu_part;
-  gp.ticket_slot = ws.ticket_slot;
+  gp.err = ws.err;
   gp.act16 = ws.act16;
   gp.act_scale = ws.act_scale;
   gp.act_out = m.act_out;
   const bool gu_tiled = (w->layout & NSM_LAYOUT_GATEUP_TILED) != 0;
   const bool gu_stage = m.H <= kStageXMaxHidden;
+  const bool gu_aligned = ((uintptr_t)gp.gate | (uintptr_t)gp.up | (uintptr_t)gp.gate_am | (uintptr_t)gp.up_am) % 16 == 0 &&
+                          gp.gstride % 16 == 0 && (gp.gastride * 4) % 16 == 0;
+  const bool gu_tma = gu_tiled && gu_stage && gu_aligned && ks->gu_tma > 0;
+  cudaError_t e;
+  if (gu_tma) {
+    gp.total_warps = dev.sm_count * kTmaWarps;
+    e = launch_pdl(gateup_tma_kernel, dev.sm_count, kTmaThreads, kGuTmaSmem, stream, gp);
+  } else {
   const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
   gp.total_warps = gu_ctas * (kMlpThreads / 32);
   const int gu_smem = gu_stage ? kGateupSmemStaged : kGateupSmem;
-  cudaError_t e;
   if (gu_tiled) {
     if (gu_stage) e = launch_pdl(gateup_kernel<true, true>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
     else e = launch_pdl(gateup_kernel<true, false>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
   } else {
     if (gu_stage) e = launch_pdl(gateup_kernel<false, true>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
     else e = launch_pdl(gateup_kernel<false, false>, gu_ctas, kMlpThreads, gu_smem, stream, gp);
+  }
   }
   NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
@@ -741,11 +1108,19 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   dp.act16 = ws.act16;
   dp.act_scale = ws.act_scale;
   dp.ypart = ws.ypart;
-  dp.ticket_rt = ws.ticket_rowtile;
+  dp.err = ws.err;
   dp.y = m.y;
   dp.y_dtype = m.y_dtype;
   const bool dn_tiled = (w->layout & NSM_LAYOUT_DOWN_TILED) != 0;
   const bool dn_stage = m.k <= kStageActMaxSlots;
+  const bool dn_aligned = ((uintptr_t)dp.down | (uintptr_t)dp.down_am) % 16 == 0 && dp.dbs % 16 == 0 &&
+                          (dp.dabs * 4) % 16 == 0;
+  const bool dn_tma = dn_tiled && dn_stage && dn_aligned && ks->dn_tma > 0;
+  dp.group_log2 = dn_tma ? 6 : 5;
+  if (dn_tma) {
+    dp.total_warps = dev.sm_count * kTmaWarps;
+    e = launch_pdl(down_tma_kernel, dev.sm_count, kTmaThreads, kDnTmaSmem, stream, dp);
+  } else {
   const int dn_ctas = dev.sm_count * ks->dn[dn_tiled][dn_stage];
   dp.total_warps = dn_ctas * (kMlpThreads / 32);
   const int dn_smem = dn_stage ? kDownSmemStaged : kSmemHead;
@@ -756,14 +1131,15 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
     if (dn_stage) e = launch_pdl(down_kernel<false, true>, dn_ctas, kMlpThreads, dn_smem, stream, dp);
     else e = launch_pdl(down_kernel<false, false>, dn_ctas, kMlpThreads, dn_smem, stream, dp);
   }
+  }
   NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(launch_pdl(down_finalize_kernel, (4 * m.H + 255) / 256, 256, 0, stream, dp));
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
 }
 
-static int router_a_prepare(const void* x, int x_dtype, const nsm_layer_io* io, const nsm_router_weights* rw,
-                            int H, const DecodeWs& ws, cudaStream_t stream) {
+static RouterAParams router_a_params(const void* x, int x_dtype, const nsm_layer_io* io,
+                                     const nsm_router_weights* rw, int H, const DecodeWs& ws) {
   RouterAParams a{};
   a.x = x;
   a.x_dtype = x_dtype;
@@ -785,7 +1161,12 @@ static int router_a_prepare(const void* x, int x_dtype, const nsm_layer_io* io, 
   }
   a.H = H;
   a.ws = ws;
-  return router_a_launch(a, stream);
+  return a;
+}
+
+static int router_a_prepare(const void* x, int x_dtype, const nsm_layer_io* io, const nsm_router_weights* rw,
+                            int H, const DecodeWs& ws, cudaStream_t stream) {
+  return router_a_launch(router_a_params(x, x_dtype, io, rw, H, ws), stream);
 }
 
 static int validate_router(const nsm_router_weights* rw, int H) {
@@ -800,9 +1181,9 @@ static int validate_router(const nsm_router_weights* rw, int H) {
   return NSM_OK;
 }
 
-static int router_b_prepare(const nsm_router_weights* rw, int k, int32_t* idx_out, float* score_out,
-                            float* latent_out, const nsm_block_map* map, int pool_rows, const DecodeWs& ws,
-                            cudaStream_t stream) {
+static RouterBParams router_b_params(const nsm_router_weights* rw, int k, int32_t* idx_out, float* score_out,
+                                     float* latent_out, const nsm_block_map* map, int pool_rows,
+                                     const DecodeWs& ws) {
   RouterBParams b{};
   b.score_w = rw->score_w;
   b.score_b = rw->score_b;
@@ -820,7 +1201,7 @@ static int router_b_prepare(const nsm_router_weights* rw, int k, int32_t* idx_ou
   b.block_end = map ? map->block_end : b.NB;
   b.pool_rows = pool_rows;
   b.ws = ws;
-  return router_b_launch(b, stream);
+  return b;
 }
 
 }  // namespace nsm
@@ -852,7 +1233,7 @@ int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_w
   if (st) return st;
   st = router_a_prepare(x, x_dtype, nullptr, rw, hidden, w, s);
   if (st) return st;
-  return router_b_prepare(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w, s);
+  return router_b_launch(router_b_params(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w), s);
 }
 
 int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_t intermediate,
@@ -899,7 +1280,7 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   st = router_a_prepare(x, x_dtype, io, idx_in ? nullptr : rw, hidden, wsl, s);
   if (st) return st;
   if (idx_in == nullptr) {
-    st = router_b_prepare(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl, s);
+    st = router_b_launch(router_b_params(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl), s);
     if (st) return st;
   } else {
     RouterBParams b{};

@@ -56,8 +56,7 @@ struct DecodeWs {
   // counters (must be zero between calls)
   int* ticket_router_a;          // [1]
   int* ticket_router_b;          // [1]
-  int* ticket_slot;              // [top_k]
-  int* ticket_rowtile;           // [H/32]
+  int* err;                      // [1] device-side error code (0 = none), sticky
   // router
   float* latent_part;            // [kRouterMaxCtas][rank]
   float* sumsq_part;             // [kRouterMaxCtas]

@@ -329,8 +329,10 @@ def test_row_major_and_tiled_layouts_agree(dev):
               down_absmax=T(full["down_absmax"], dev), code=T(full["code"], dev))
     a = sparse_mlp_decode(xd, rw, SparseMlpWeights.from_bnb_rowmajor(tiled=True, **kw), out_dtype=torch.float32)
     b = sparse_mlp_decode(xd, rw, SparseMlpWeights.from_bnb_rowmajor(tiled=False, **kw), out_dtype=torch.float32)
-    # same products, same fixed-order reductions: identical bits
-    assert torch.equal(a, b)
+    # same products; the tiled layout's down kernel reduces 64-row groups, the
+    # row-major one 32-row tiles, so the split of the block sum into segments
+    # (and only the fp32 rounding of the sums) differs
+    assert torch.allclose(a, b, rtol=1e-5, atol=1e-5), float((a - b).abs().max())
 
 
 def test_decode_edge_cases(dev):
@@ -517,3 +519,13 @@ def test_fused_v1_composition_matches_oracle(dev):
         down={"packed": dp, "absmax": da, "code": code, "out_features": H, "in_features": width,
               "quant_block_size": 64}, block_size=bs)
     assert np.allclose(out.cpu().numpy(), ref, rtol=1e-4, atol=1e-4)
+
+
+def test_no_kernel_recorded_a_wait_timeout(dev):
+    """Every bounded device wait of the calls above completed: the error word
+    of each cached workspace is still zero."""
+    from next_step_ai_b200._torch import WORKSPACES
+
+    torch.cuda.synchronize()
+    errs = WORKSPACES.errors()
+    assert errs and all(v == 0 for v in errs.values()), errs
