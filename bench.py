@@ -44,6 +44,17 @@ def algorithmic_bytes_per_layer(k: int = TOP_K, H: int = HIDDEN, nb: int = NB, r
     return k * per_block + router + 4 * H
 
 
+def gateup_bytes_per_launch(k: int = TOP_K, H: int = HIDDEN) -> int:
+    """Bytes one gate/up launch must read: per selected block, gate and up each
+    32*H/2 packed bytes + 32*H/64 fp32 absmax."""
+    return k * 2 * (16 * H + 2 * H)
+
+
+# DRAM bytes (read + write) of one gateup_tma_kernel launch at this workload, from one
+# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; profiles/gateup_tma_kernel_cfg1.txt)
+GATEUP_DRAM_BYTES_PER_LAUNCH = 122_789_888 + 3_802_112
+
+
 def peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -130,10 +141,9 @@ def run_ours(args) -> None:
     from next_step_ai_b200.engine import DecodeLayer, SparseMlpDecoder
     from next_step_ai_b200.weights import SparseMlpWeights
 
-    if NB % world:
-        raise SystemExit(f"{NB} blocks do not split over {world} ranks")
-    per = NB // world
-    lo, hi = rank * per, (rank + 1) * per
+    from next_step_ai_b200.engine import shard_range
+
+    lo, hi = shard_range(NB, world, rank)
     shape = dsyn.SHAPES["cfg1"]
     shard_bytes = LAYER_BYTES_GPU // world
     free, _ = torch.cuda.mem_get_info(dev)
@@ -215,13 +225,15 @@ def run_ours(args) -> None:
     alg_layer = algorithmic_bytes_per_layer()
     pk = peaks()
     layer_us = ms_step * 1e3 / LAYERS
-    # roofline of the per-layer decode launch group (router + gate/up + down kernels) at N = 1;
-    # at N > 1 each rank reads 1/N of the block bytes plus the whole router
-    if world == 1:
-        achieved = alg_layer / (layer_us * 1e-6) / 1e9
-    else:
-        router_b = 2 * RANK * HIDDEN + 2 * RANK * NB + 2 * NB
-        achieved = ((alg_layer - router_b) / world + router_b) / (layer_us * 1e-6) / 1e9
+    # whole layer group (router + gate/up + down kernels) inside the graph; at N > 1 each
+    # rank reads 1/N of the block bytes plus the whole router
+    router_b = 2 * RANK * HIDDEN + 2 * RANK * NB + 2 * NB
+    group_gbs = ((alg_layer - router_b) / world + router_b) / (layer_us * 1e-6) / 1e9
+    # dominant kernel (gate/up gather-GEMV): device time per launch from CUDA events the
+    # library records around each stage, in an eager pass after the timed region
+    stage_us = dec.time_stages(min(LAYERS, 2 * unique))
+    gu_bytes = gateup_bytes_per_launch() / world  # expected share of the selected blocks per rank
+    gu_gbs = gu_bytes / (stage_us["gateup"] * 1e-6) / 1e9
     if rank == 0:
         line = {
             "metric": METRIC, "value": args.steps / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
@@ -237,11 +249,16 @@ def run_ours(args) -> None:
             "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
                     "d2h_bytes_per_step": HIDDEN * 4},
             "gpu_launches": args.steps * dec.kernels_per_step,
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-                         "unit_of_launch": "one layer's decode launch group (router, gate/up, down kernels)",
-                         "algorithmic_bytes": alg_layer, "us_per_layer": round(layer_us, 3),
-                         "peak_source": pk["source"]},
+            "roofline": {"bound": "hbm", "achieved": round(gu_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gu_gbs / pk["hbm_gbs"], 4),
+                         "traffic": GATEUP_DRAM_BYTES_PER_LAUNCH if world == 1 else None,
+                         "kernel": "gateup_tma_kernel (NF4 gate+up gather-GEMV, one launch per layer)",
+                         "algorithmic_bytes": int(gu_bytes), "us_per_launch": round(stage_us["gateup"], 3),
+                         "peak_source": pk["source"], "peak_note": "of measured (MEASURED_PEAKS.json hbm_gbs)",
+                         "stage_us": {k: round(v, 3) for k, v in stage_us.items()},
+                         "layer_group": {"algorithmic_bytes": alg_layer, "us_per_layer": round(layer_us, 3),
+                                         "achieved": round(group_gbs, 1),
+                                         "frac": round(group_gbs / pk["hbm_gbs"], 4)}},
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:

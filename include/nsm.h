@@ -165,7 +165,14 @@ typedef struct nsm_layer_io {
   const void* norm_weight; /* [H] or NULL (= ones) */
   float eps;
   int32_t reserved;
+  /* Optional timing hook: NSM_STAGE_EVENTS cudaEvent_t handles recorded on the
+   * stream before the router, before gate/up, before the gate/up reduction,
+   * before down, before the down reduction and after it.  Recording them
+   * separates the kernels (no programmatic dependent launch across a stage
+   * boundary), so use it for per-kernel timing only.  NULL: no events. */
+  void* const* stage_events;
 } nsm_layer_io;
+#define NSM_STAGE_EVENTS 6
 
 size_t nsm_decode_workspace_bytes(int hidden, int intermediate, int top_k, int rank);
 

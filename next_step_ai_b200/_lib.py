@@ -27,6 +27,8 @@ NSM_ERR_DEVICE = -6
 
 NSM_F32, NSM_F16, NSM_BF16 = 0, 1, 2
 NSM_LAYOUT_GATEUP_TILED, NSM_LAYOUT_DOWN_TILED = 1, 2
+NSM_STAGE_EVENTS = 6
+ABI_VERSION = 2
 
 # every symbol include/nsm.h declares (checked by tests/test_abi.py)
 EXPORTED = (
@@ -66,7 +68,7 @@ class BlockMapC(ctypes.Structure):
 class LayerIoC(ctypes.Structure):
     _fields_ = [
         ("residual", c_void_p), ("y_prev", c_void_p), ("y_prev_dtype", c_int32), ("norm_weight_dtype", c_int32),
-        ("norm_weight", c_void_p), ("eps", c_float), ("reserved", c_int32),
+        ("norm_weight", c_void_p), ("eps", c_float), ("reserved", c_int32), ("stage_events", c_void_p),
     ]
 
 

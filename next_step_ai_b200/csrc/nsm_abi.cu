@@ -95,7 +95,7 @@ using namespace nsm;
 
 extern "C" {
 
-int nsm_abi_version(void) { return 1; }
+int nsm_abi_version(void) { return 2; }
 
 const char* nsm_status_string(int status) {
   switch (status) {

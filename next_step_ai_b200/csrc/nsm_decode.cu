@@ -1009,7 +1009,12 @@ struct MlpPlan {
   void* y;
   int y_dtype;
   const float* norm_scale;
+  void* const* events;  // optional NSM_STAGE_EVENTS stage events (index 1..5 recorded here)
 };
+
+static cudaError_t stage_event(void* const* ev, int i, cudaStream_t s) {
+  return ev != nullptr ? cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev[i]), s) : cudaSuccess;
+}
 
 static int validate_weights(const nsm_mlp_weights* w, int H) {
   NSM_REQUIRE(w != nullptr, NSM_ERR_INVALID_ARG, "weights descriptor is NULL");
@@ -1071,6 +1076,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   const bool gu_aligned = ((uintptr_t)gp.gate | (uintptr_t)gp.up | (uintptr_t)gp.gate_am | (uintptr_t)gp.up_am) % 16 == 0 &&
                           gp.gstride % 16 == 0 && (gp.gastride * 4) % 16 == 0;
   const bool gu_tma = gu_tiled && gu_stage && gu_aligned && ks->gu_tma > 0;
+  NSM_CHECK_CUDA(stage_event(m.events, 1, stream));
   cudaError_t e;
   if (gu_tma) {
     gp.total_warps = dev.sm_count * kTmaWarps;
@@ -1088,7 +1094,9 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   }
   }
   NSM_CHECK_CUDA(e);
+  NSM_CHECK_CUDA(stage_event(m.events, 2, stream));
   NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
+  NSM_CHECK_CUDA(stage_event(m.events, 3, stream));
 
   DownParams dp{};
   dp.down = w->down_packed;
@@ -1133,7 +1141,9 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   }
   }
   NSM_CHECK_CUDA(e);
+  NSM_CHECK_CUDA(stage_event(m.events, 4, stream));
   NSM_CHECK_CUDA(launch_pdl(down_finalize_kernel, (4 * m.H + 255) / 256, 256, 0, stream, dp));
+  NSM_CHECK_CUDA(stage_event(m.events, 5, stream));
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
 }
@@ -1277,6 +1287,8 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   st = setup_kernels(dev, &ks);
   if (st) return st;
 
+  void* const* events = io != nullptr ? io->stage_events : nullptr;
+  NSM_CHECK_CUDA(stage_event(events, 0, s));
   st = router_a_prepare(x, x_dtype, io, idx_in ? nullptr : rw, hidden, wsl, s);
   if (st) return st;
   if (idx_in == nullptr) {
@@ -1305,6 +1317,7 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   m.y = y;
   m.y_dtype = y_dtype;
   m.norm_scale = wsl.norm_scale;
+  m.events = events;
   return launch_mlp(m, wsl, s);
 }
 

@@ -31,6 +31,17 @@ class DecodeLayer:
     norm_weight: torch.Tensor | None = None
 
 
+def shard_range(num_blocks: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous block range [lo, hi) of ``rank`` when ``num_blocks``
+    intermediate blocks are split over ``world`` GPUs (sizes differ by at most
+    one block).  Every rank routes all blocks (the router is replicated) and
+    computes the MLP over the selected blocks inside its range; the partial
+    outputs are summed across ranks."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of world {world}")
+    return (num_blocks * rank) // world, (num_blocks * (rank + 1)) // world
+
+
 class SparseMlpDecoder:
     """Runs ``num_layers`` decode steps over ``layers`` (cycled when fewer
     unique layers than ``num_layers`` are resident).
@@ -64,7 +75,7 @@ class SparseMlpDecoder:
         self._bm = _lib.BlockMapC()
         self._bm.block_begin, self._bm.block_end = int(self.block_range[0]), int(self.block_range[1])
 
-    def _layer(self, i: int, ws: torch.Tensor, st: int) -> None:
+    def _layer(self, i: int, ws: torch.Tensor, st: int, events=None) -> None:
         li = i % len(self.layers)
         layer = self.layers[li]
         rc, wc = self._c[li]
@@ -77,6 +88,7 @@ class SparseMlpDecoder:
         io.norm_weight = ptr(layer.norm_weight) if layer.norm_weight is not None else None
         io.norm_weight_dtype = dtype_code(layer.norm_weight.dtype) if layer.norm_weight is not None else 0
         io.eps = self.eps
+        io.stage_events = ctypes.cast(events, ctypes.c_void_p) if events is not None else None
         _lib.check(self._lib.nsm_sparse_mlp_decode(
             None, 0, self.H, self.I, ctypes.byref(io), ctypes.byref(rc), None, 0, ctypes.byref(self._bm),
             ctypes.byref(wc), y.data_ptr(), dtype_code(y.dtype), None, None, ws.data_ptr(), ws.numel(), st),
@@ -103,6 +115,33 @@ class SparseMlpDecoder:
             self._layer(i, ws, st)
         last = self.y[(self.num_layers - 1) % 2]
         torch.add(self.residual, last.float(), out=self.out)
+
+    STAGES = ("router", "gateup", "gateup_finalize", "down", "down_finalize")
+
+    def time_stages(self, num_layers: int | None = None) -> dict[str, float]:
+        """One eager pass over ``num_layers`` layers with the library's stage
+        events recorded around each stage; returns the mean device time of
+        each stage in microseconds.  The events separate the kernels (no
+        programmatic dependent launch across stages), so the sum is larger
+        than a graph replay's layer time.  The pass advances ``residual``."""
+        n = int(num_layers or self.num_layers)
+        ws = WORKSPACES.get(self._ws_bytes, self.dev)
+        st = stream_handle(self.dev)
+        evs, arrs = [], []
+        for _ in range(n):
+            row = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.NSM_STAGE_EVENTS)]
+            for e in row:
+                e.record()  # creates the event
+            evs.append(row)
+            arrs.append((ctypes.c_void_p * _lib.NSM_STAGE_EVENTS)(*[e.cuda_event for e in row]))
+        torch.cuda.synchronize(self.dev)
+        for i in range(n):
+            self._layer(i, ws, st, events=arrs[i])
+        torch.cuda.synchronize(self.dev)
+        out = {}
+        for j, name in enumerate(self.STAGES):
+            out[name] = 1e3 * sum(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(n)) / n
+        return out
 
     def capture(self) -> torch.cuda.CUDAGraph:
         """Capture one token into a CUDA graph (after one eager warm-up)."""
