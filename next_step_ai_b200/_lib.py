@@ -36,7 +36,7 @@ EXPORTED = (
     "nsm_decode_workspace_bytes", "nsm_route", "nsm_sparse_mlp_decode", "nsm_decode_gathered",
     "nsm_decode_rows_workspace_bytes", "nsm_decode_gathered_rows", "nsm_repack_down_block_major",
     "nsm_sparse_input_linear_4bit", "nsm_sparse_output_linear_4bit", "nsm_cache_split", "nsm_cache_promote",
-    "nsm_repack_tiled", "nsm_decode_gathered_static", "nsm_workspace_error",
+    "nsm_repack_tiled", "nsm_decode_gathered_static", "nsm_workspace_error", "nsm_cache_stage",
 )
 
 
@@ -103,6 +103,7 @@ _SIGS = {
     "nsm_repack_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                  c_void_p, c_void_p, c_int32, POINTER(MlpWeightsC), c_void_p]),
     "nsm_cache_split": (c_int, [c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "nsm_cache_stage": (c_int, [c_void_p, c_void_p, c_int32, c_size_t, c_void_p, c_void_p, c_int32, c_void_p]),
     "nsm_cache_promote": (c_int, [POINTER(MlpWeightsC), c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
                                   c_void_p, c_void_p]),
 }

@@ -28,6 +28,18 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return t.data_ptr()
 
 
+def row_ptr(t: torch.Tensor | None) -> int | None:
+    """Base pointer of a pool tensor whose rows may be strided (a view into a
+    larger record per row); each row itself must be contiguous."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("expected a CUDA tensor")
+    if t.dim() == 0 or not t[0].is_contiguous():
+        raise RuntimeError("expected contiguous pool rows")
+    return t.data_ptr()
+
+
 def stream_handle(device: torch.device | None = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 

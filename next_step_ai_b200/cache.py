@@ -1,0 +1,370 @@
+"""VRAM hot-block cache for the decode MLP, with misses streamed from pinned host memory.
+
+Reference behaviour (``llama3_neuroplastic/experiments/streaming_llama_runtime.py``):
+a per-layer VRAM bank of hot blocks addressed by a block -> slot table
+(``:2619-2786``); blocks the router selects that are not resident are copied
+from pinned host memory on a side stream (``_copy_cpu_to_gpu``, ``:3443-3493``;
+cold loads ``:3885-4002``) and merged with the resident ones; after use, the
+misses are promoted into the bank by the fixed-capacity policy
+``_plan_fixed_capacity_bank_update`` (``:2577-2617``) -- free slots first, then
+the lowest score; a novel block gets ``max(active scores) + 1 + (i+1)*1e-3`` --
+and every decode hit adds 1 to the hit block's score (``:5262-5271``).  The
+initial bank of ``n`` pre-warmed blocks is scored ``linspace(n, 1)``
+(``:2699-2706``).
+
+Design here:
+
+* one device pool of ``capacity + staging`` block *records*; a record holds
+  all of one block's bytes in the tiled layout (gate, up and down packed, then
+  their fp32 absmax: 56*H bytes, the per-block algorithmic bytes), so a miss is
+  ONE contiguous ``cudaMemcpyAsync`` and the decode kernels read bank and
+  staging rows through the same strided descriptor;
+* a pinned host store with every block of the layer in the same record layout;
+* per token: route on the main stream, read the selection back, stage the
+  misses on a side stream (``nsm_cache_stage``) while the main stream computes
+  the resident blocks (the block map drops the misses), then compute the staged
+  blocks and add the two partial outputs;
+* promotion after the token: the bank policy picks the slots on the host, the
+  staged records are copied device-to-device into them and the block table is
+  rewritten.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._torch import WORKSPACES, dtype_code, stream_handle
+from .weights import RouterWeights, SparseMlpWeights
+
+
+# --------------------------------------------------------------------------- record layout
+def record_layout(hidden: int) -> dict[str, tuple[int, int]]:
+    """Byte (offset, size) of each part of one block record (tiled layout)."""
+    H = int(hidden)
+    g = 16 * H  # 32 rows x H/2 bytes
+    return {"gate": (0, g), "up": (g, g), "down": (2 * g, g),
+            "gate_absmax": (3 * g, 2 * H), "up_absmax": (3 * g + 2 * H, 2 * H), "down_absmax": (3 * g + 4 * H, 4 * H)}
+
+
+def record_bytes(hidden: int) -> int:
+    return 56 * int(hidden)
+
+
+def pool_weights(pool: torch.Tensor, hidden: int, intermediate: int, gate_code: torch.Tensor,
+                 up_code: torch.Tensor, down_code: torch.Tensor) -> SparseMlpWeights:
+    """Decode-kernel view of a record pool ``[P, 56*H]`` uint8 (rows strided by the record)."""
+    H = int(hidden)
+    lay = record_layout(H)
+
+    def part(name, dtype=torch.uint8):
+        o, n = lay[name]
+        v = pool[:, o:o + n]
+        return v.view(dtype) if dtype != torch.uint8 else v
+
+    return SparseMlpWeights(hidden=H, intermediate=int(intermediate), gate_packed=part("gate"),
+                            gate_absmax=part("gate_absmax", torch.float32), up_packed=part("up"),
+                            up_absmax=part("up_absmax", torch.float32),
+                            down_packed=part("down").view(pool.shape[0], H, 16),
+                            down_absmax=part("down_absmax", torch.float32), gate_code=gate_code, up_code=up_code,
+                            down_code=down_code,
+                            layout=_lib.NSM_LAYOUT_GATEUP_TILED | _lib.NSM_LAYOUT_DOWN_TILED)
+
+
+def records_from_weights(w: SparseMlpWeights, blocks: torch.Tensor | None = None) -> torch.Tensor:
+    """Device records ``[n, 56*H]`` of the listed blocks (all when None) of a
+    full tiled layer."""
+    if w.layout != (_lib.NSM_LAYOUT_GATEUP_TILED | _lib.NSM_LAYOUT_DOWN_TILED):
+        raise RuntimeError("records are built from tiled gate/up and down pools")
+    H = w.hidden
+    idx = torch.arange(w.pool_rows, device=w.gate_packed.device) if blocks is None else blocks.to(torch.int64)
+    out = torch.empty((idx.numel(), record_bytes(H)), dtype=torch.uint8, device=w.gate_packed.device)
+    lay = record_layout(H)
+    for name, src in (("gate", w.gate_packed), ("up", w.up_packed), ("down", w.down_packed),
+                      ("gate_absmax", w.gate_absmax), ("up_absmax", w.up_absmax), ("down_absmax", w.down_absmax)):
+        o, n = lay[name]
+        out[:, o:o + n].copy_(src.reshape(src.shape[0], -1).index_select(0, idx).view(torch.uint8))
+    return out
+
+
+class HostBlockStore:
+    """Every block of one layer in pinned host memory, one record per block."""
+
+    def __init__(self, records: torch.Tensor, hidden: int, intermediate: int, gate_code: torch.Tensor,
+                 up_code: torch.Tensor, down_code: torch.Tensor):
+        if records.device.type != "cpu" or not records.is_pinned():
+            raise RuntimeError("the host block store must be pinned host memory")
+        if records.dtype != torch.uint8 or records.shape[1] != record_bytes(hidden) or not records.is_contiguous():
+            raise RuntimeError("records must be contiguous uint8 [NB, 56*H]")
+        self.records = records
+        self.hidden, self.intermediate = int(hidden), int(intermediate)
+        self.codes = (gate_code, up_code, down_code)
+
+    @property
+    def num_blocks(self) -> int:
+        return int(self.records.shape[0])
+
+    @classmethod
+    def from_weights(cls, w: SparseMlpWeights, chunk: int = 128) -> "HostBlockStore":
+        nb = w.pool_rows
+        host = torch.empty((nb, record_bytes(w.hidden)), dtype=torch.uint8, pin_memory=True)
+        for b0 in range(0, nb, chunk):
+            ids = torch.arange(b0, min(nb, b0 + chunk), device=w.gate_packed.device)
+            host[b0:b0 + ids.numel()].copy_(records_from_weights(w, ids))
+        return cls(host, w.hidden, w.intermediate, w.gate_code, w.up_code, w.down_code)
+
+
+# --------------------------------------------------------------------------- bank policy
+class FixedCapacityBank:
+    """Host-side state and replacement policy of a fixed-capacity block bank.
+
+    ``block_ids[slot]`` / ``scores[slot]`` for the first ``active`` slots; the
+    policy is the reference's ``_plan_fixed_capacity_bank_update``
+    (``streaming_llama_runtime.py:2577-2617``) and hit scoring (``:5262-5271``).
+    """
+
+    def __init__(self, capacity: int):
+        self.capacity = int(capacity)
+        self.block_ids = np.full(self.capacity, -1, np.int64)
+        self.scores = np.zeros(self.capacity, np.float32)
+        self.active = 0
+
+    @classmethod
+    def from_state(cls, block_ids, scores, active: int, capacity: int | None = None) -> "FixedCapacityBank":
+        ids = np.asarray(block_ids, np.int64).reshape(-1)
+        cap = int(capacity) if capacity is not None else ids.size
+        bank = cls(cap)
+        n = min(ids.size, cap)
+        bank.block_ids[:n] = ids[:n]
+        bank.scores[:n] = np.asarray(scores, np.float32).reshape(-1)[:n]
+        bank.active = max(0, min(int(active), n, cap))
+        return bank
+
+    def prewarm(self, blocks) -> None:
+        b = np.asarray(blocks, np.int64).reshape(-1)[: self.capacity]
+        n = b.size
+        self.block_ids[:] = -1
+        self.block_ids[:n] = b
+        self.scores[:] = 0
+        if n:
+            self.scores[:n] = np.linspace(float(n), 1.0, n, dtype=np.float32)
+        self.active = n
+
+    def add_hits(self, slots) -> None:
+        np.add.at(self.scores, np.asarray(slots, np.int64).reshape(-1), np.float32(1.0))
+
+    def plan_update(self, novel) -> np.ndarray:
+        """Slots that receive the novel blocks (in order), updating ids/scores.
+        Free slots are used first, then the lowest current score (the first
+        one on ties); at most ``capacity`` novel blocks are taken."""
+        cap = self.capacity
+        novel = np.asarray(novel, np.int64).reshape(-1)
+        if cap <= 0 or novel.size == 0:
+            return np.zeros(0, np.int64)
+        novel = novel[:cap]
+        cur = self.scores
+        base = float(cur[: self.active].max()) + 1.0 if self.active > 0 else 1.0
+        slots = np.empty(novel.size, np.int64)
+        for i, blk in enumerate(novel):
+            if self.active < cap:
+                slot = self.active
+                self.active += 1
+            else:
+                slot = int(np.argmin(cur[:cap]))
+            self.block_ids[slot] = int(blk)
+            cur[slot] = np.float32(base + float(i + 1) * 1e-3)
+            slots[i] = slot
+        return slots
+
+
+def record_calibration_hits(counts: np.ndarray | None, active_blocks: np.ndarray, num_blocks: int,
+                            recency_power: float) -> np.ndarray:
+    """Recency-weighted hit counts for choosing a layer's hot set: row ``r`` of
+    ``R`` selection rows adds ``((r+1)/R) ** recency_power`` to each of its
+    valid blocks (``_record_hot_cache_calibration_blocks``,
+    ``streaming_llama_runtime.py:2205-2243``)."""
+    nb = int(num_blocks)
+    c = np.zeros(nb, np.float32) if counts is None or np.asarray(counts).size != nb \
+        else np.asarray(counts, np.float32).copy()
+    ab = np.asarray(active_blocks, np.int64)
+    if ab.size == 0:
+        return c
+    rows = ab.reshape(-1, ab.shape[-1])
+    n = rows.shape[0]
+    w = np.power(np.arange(1, n + 1, dtype=np.float32) / np.float32(n), np.float32(recency_power)).astype(np.float32)
+    for r in range(n):
+        valid = rows[r][(rows[r] >= 0) & (rows[r] < nb)]
+        np.add.at(c, valid, w[r])
+    return c
+
+
+def target_hot_blocks(*, layer_idx: int, runtime_top_k: int, count_slots: int, previous_hot_count: int,
+                      limit_bytes: int | None, used_bytes: int, sparse_layers: int, bytes_per_block: int) -> int:
+    """Hot-bank capacity of a layer from the VRAM budget left for the
+    remaining layers, at least the previous size or k
+    (``_target_hot_blocks_for_layer``, ``streaming_llama_runtime.py:2275-2311``)."""
+    fallback = int(previous_hot_count) if int(previous_hot_count) > 0 else max(1, int(runtime_top_k))
+    if limit_bytes is None or int(limit_bytes) <= 0:
+        return max(1, min(fallback, int(count_slots)))
+    remaining = max(int(limit_bytes) - int(used_bytes), 0)
+    remaining_layers = max(1, max(1, int(sparse_layers)) - max(0, int(layer_idx)))
+    per_layer = int((float(remaining) * 0.97) / float(remaining_layers))
+    return max(1, min(max(fallback, per_layer // max(1, int(bytes_per_block))), int(count_slots)))
+
+
+# --------------------------------------------------------------------------- cached decode
+@dataclass
+class CacheStats:
+    hits: int
+    misses: int
+    h2d_bytes: int
+    promoted: int
+
+
+class CachedSparseMlp:
+    """One layer's decode MLP over a VRAM bank of ``capacity`` hot blocks plus
+    ``staging`` rows for the misses of one token (default: the router's k)."""
+
+    def __init__(self, router: RouterWeights, store: HostBlockStore, capacity: int, *, staging: int | None = None,
+                 device: torch.device | None = None, promote: bool = True):
+        self.router = router
+        self.store = store
+        self.H, self.I = store.hidden, store.intermediate
+        self.NB = self.I // 32
+        self.dev = device or router.enc_w.device
+        self.capacity = int(capacity)
+        self.staging = int(staging or router.top_k)
+        self.promote = bool(promote)
+        self.rec = record_bytes(self.H)
+        self.pool = torch.empty((self.capacity + self.staging, self.rec), dtype=torch.uint8, device=self.dev)
+        codes = [c.to(self.dev) for c in store.codes]
+        self.bank_w = pool_weights(self.pool[: self.capacity], self.H, self.I, *codes)
+        self.stage_w = pool_weights(self.pool[self.capacity:], self.H, self.I, *codes)
+        self.bank = FixedCapacityBank(self.capacity)
+        self.slot_host = np.full(self.NB, -1, np.int32)  # block -> bank slot
+        self.slot_dev = torch.full((self.NB,), -1, dtype=torch.int32, device=self.dev)
+        self.stage_map_host = torch.full((self.NB,), -1, dtype=torch.int32, pin_memory=True)
+        self.stage_map_dev = torch.full((self.NB,), -1, dtype=torch.int32, device=self.dev)
+        self.table_host = torch.full((self.NB,), -1, dtype=torch.int32, pin_memory=True)
+        self.idx_dev = torch.empty(self.router.top_k, dtype=torch.int32, device=self.dev)
+        self.idx_host = torch.empty(self.router.top_k, dtype=torch.int32, pin_memory=True)
+        self.side = torch.cuda.Stream(device=self.dev)
+        self._lib = _lib.load()
+
+    # ---- bank contents
+    def _upload_table(self, stream: torch.cuda.Stream) -> None:
+        self.table_host.numpy()[:] = self.slot_host
+        with torch.cuda.stream(stream):
+            self.slot_dev.copy_(self.table_host, non_blocking=True)
+
+    def pre_warm(self, blocks) -> None:
+        """Load ``blocks`` (at most ``capacity``) into the bank, scored
+        ``linspace(n, 1)`` in the given order (the reference's pre-warm)."""
+        b = np.asarray(blocks, np.int64).reshape(-1)[: self.capacity]
+        self.bank.prewarm(b)
+        self.slot_host[:] = -1
+        self.slot_host[b] = np.arange(b.size, dtype=np.int32)
+        main = torch.cuda.current_stream(self.dev)
+        self._stage(b, np.arange(b.size, dtype=np.int32), self.pool, self.capacity, main)
+        self._upload_table(main)
+        torch.cuda.synchronize(self.dev)
+
+    # ---- one token
+    def decode(self, x: torch.Tensor, idx: torch.Tensor | None = None, out_dtype=torch.float32):
+        """MLP output for one token ``x [H]``.  The router always runs; ``idx``
+        (int32 block ids on the device) replaces its selection when given."""
+        from .mlp import sparse_mlp_decode
+
+        main = torch.cuda.current_stream(self.dev)
+        k = self.router.top_k
+        # route on the main stream; the selection comes back to the host
+        sel = self.idx_dev
+        sparse_route_only(x, self.router, sel)
+        if idx is not None:
+            sel = idx.to(device=self.dev, dtype=torch.int32).reshape(-1)
+            k = int(sel.numel())
+        self.idx_host[:k].copy_(sel[:k], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(main)
+        ev.synchronize()
+        blocks = self.idx_host[:k].numpy().astype(np.int64)
+        if blocks.size and (blocks.min() < 0 or blocks.max() >= self.NB):
+            raise RuntimeError("selected block id out of range")
+        if np.unique(blocks).size != blocks.size:
+            raise RuntimeError("the selection lists a block twice")
+        slots = self.slot_host[blocks]
+        hit_mask = slots >= 0
+        misses = blocks[~hit_mask]
+        if misses.size > self.staging:
+            raise RuntimeError(f"{misses.size} misses exceed the {self.staging} staging rows")
+        # misses: pinned host -> staging rows on the side stream
+        smap = self.stage_map_host.numpy()
+        smap[:] = -1
+        smap[misses] = np.arange(misses.size, dtype=np.int32)
+        self.side.wait_stream(main)  # staging rows are free once the previous token is done
+        if misses.size:
+            self._stage(misses, np.arange(misses.size, dtype=np.int32), self.pool[self.capacity:], self.staging,
+                        self.side)
+        with torch.cuda.stream(self.side):
+            self.stage_map_dev.copy_(self.stage_map_host, non_blocking=True)
+        staged = torch.cuda.Event()
+        staged.record(self.side)
+        # resident blocks while the copies land (the block map drops the misses)
+        y = sparse_mlp_decode(x, None, self.bank_w, idx=sel, slot_of_block=self.slot_dev, out_dtype=torch.float32)
+        main.wait_event(staged)
+        if misses.size:
+            y2 = sparse_mlp_decode(x, None, self.stage_w, idx=sel, slot_of_block=self.stage_map_dev,
+                                   out_dtype=torch.float32)
+            y.add_(y2)
+        promoted = 0
+        if hit_mask.any():
+            self.bank.add_hits(slots[hit_mask])
+        if self.promote and misses.size:
+            promoted = self._promote(misses, main)
+        stats = CacheStats(hits=int(hit_mask.sum()), misses=int(misses.size), h2d_bytes=int(misses.size) * self.rec,
+                           promoted=promoted)
+        return (y if out_dtype == torch.float32 else y.to(out_dtype)), stats
+
+    def _stage(self, blocks: np.ndarray, rows: np.ndarray, pool: torch.Tensor, pool_rows: int,
+               stream: torch.cuda.Stream) -> None:
+        blk = np.ascontiguousarray(blocks, dtype=np.int32)
+        dst = np.ascontiguousarray(rows, dtype=np.int32)
+        _lib.check(self._lib.nsm_cache_stage(self.store.records.data_ptr(),
+                                             blk.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), int(blk.size),
+                                             self.rec, pool.data_ptr(),
+                                             dst.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), int(pool_rows),
+                                             stream.cuda_stream), "nsm_cache_stage")
+
+    def _promote(self, misses: np.ndarray, main: torch.cuda.Stream) -> int:
+        old = self.bank.block_ids.copy()
+        active_before = self.bank.active
+        slots = self.bank.plan_update(misses)
+        n = slots.size
+        if n == 0:
+            return 0
+        for i, slot in enumerate(slots):
+            ob = old[slot] if slot < active_before else -1
+            if ob >= 0 and self.slot_host[ob] == slot:
+                self.slot_host[ob] = -1
+            self.slot_host[misses[i]] = slot
+        # staged record i -> bank slot (device to device), after the staged compute
+        src = torch.from_numpy(np.arange(n, dtype=np.int64) + self.capacity).to(self.dev, non_blocking=True)
+        dst = torch.from_numpy(slots.astype(np.int64)).to(self.dev, non_blocking=True)
+        self.pool.index_copy_(0, dst, self.pool.index_select(0, src))
+        self._upload_table(main)
+        return int(n)
+
+
+def sparse_route_only(x: torch.Tensor, router: RouterWeights, idx_out: torch.Tensor) -> None:
+    """Router for one token into ``idx_out`` (int32, score-descending)."""
+    lib = _lib.load()
+    H = router.hidden
+    xv = x.reshape(-1).contiguous()
+    ws = WORKSPACES.get(lib.nsm_decode_workspace_bytes(H, router.num_blocks * 32, router.top_k, router.rank),
+                        xv.device)
+    rc = router.to_c()
+    _lib.check(lib.nsm_route(xv.data_ptr(), dtype_code(xv.dtype), H, ctypes.byref(rc), idx_out.data_ptr(), None, None,
+                             ws.data_ptr(), ws.numel(), stream_handle(xv.device)), "nsm_route")

@@ -389,17 +389,35 @@ int nsm_cache_split(const int32_t* idx, int32_t k, const int32_t* slot_of_block,
   return NSM_OK;
 }
 
+int nsm_cache_stage(const void* host_base, const int32_t* blocks, int32_t n, size_t record_bytes, void* pool_base,
+                    const int32_t* dst_rows, int32_t pool_rows, nsm_stream_t stream) {
+  if (n <= 0) return NSM_OK;
+  NSM_REQUIRE(host_base && blocks && pool_base && dst_rows, NSM_ERR_INVALID_ARG, "NULL pointer");
+  NSM_REQUIRE(record_bytes > 0, NSM_ERR_INVALID_ARG, "record_bytes must be > 0");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const char* src = reinterpret_cast<const char*>(host_base);
+  char* dst = reinterpret_cast<char*>(pool_base);
+  for (int i = 0; i < n; ++i) {
+    NSM_REQUIRE(blocks[i] >= 0, NSM_ERR_INVALID_ARG, "negative block id");
+    NSM_REQUIRE(dst_rows[i] >= 0 && dst_rows[i] < pool_rows, NSM_ERR_INVALID_ARG, "destination row out of range");
+    NSM_CHECK_CUDA(cudaMemcpyAsync(dst + (size_t)dst_rows[i] * record_bytes, src + (size_t)blocks[i] * record_bytes,
+                                   record_bytes, cudaMemcpyHostToDevice, s));
+  }
+  return NSM_OK;
+}
+
 int nsm_cache_promote(const nsm_mlp_weights* w, int32_t hidden, const int32_t* src_rows, const int32_t* dst_rows,
                       const int32_t* block_ids, const int32_t* evicted_ids, int32_t n, int32_t* slot_of_block,
                       nsm_stream_t stream) {
   NSM_REQUIRE(w != nullptr, NSM_ERR_INVALID_ARG, "weights descriptor is NULL");
   NSM_REQUIRE(src_rows && dst_rows && block_ids && slot_of_block, NSM_ERR_INVALID_ARG, "NULL pointer");
   NSM_REQUIRE(hidden > 0 && hidden % 64 == 0, NSM_ERR_UNSUPPORTED, "hidden must be a positive multiple of 64");
-  const bool block_major = (w->down_block_stride == 0 || w->down_block_stride == (int64_t)16 * hidden) &&
-                           (w->down_row_stride == 0 || w->down_row_stride == 16) &&
-                           (w->down_absmax_row_stride == 0 || w->down_absmax_row_stride == 1) &&
-                           w->down_absmax_pair == 0;
-  NSM_REQUIRE(block_major, NSM_ERR_UNSUPPORTED, "cache pools must use the block-major down layout");
+  const bool down_tiled = (w->layout & NSM_LAYOUT_DOWN_TILED) != 0;
+  const bool block_major = down_tiled ||
+                           ((w->down_row_stride == 0 || w->down_row_stride == 16) &&
+                            (w->down_absmax_row_stride == 0 || w->down_absmax_row_stride == 1) &&
+                            w->down_absmax_pair == 0);
+  NSM_REQUIRE(block_major, NSM_ERR_UNSUPPORTED, "cache pools must use the block-major or tiled down layout");
   if (n <= 0) return NSM_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   PromoteParams p{};
@@ -411,7 +429,7 @@ int nsm_cache_promote(const nsm_mlp_weights* w, int32_t hidden, const int32_t* s
   p.down_am = const_cast<float*>(w->down_absmax);
   p.gstride = w->gateup_block_stride ? w->gateup_block_stride : (int64_t)16 * hidden;
   p.gastride = w->gateup_absmax_block_stride ? w->gateup_absmax_block_stride : (int64_t)hidden / 2;
-  p.dbs = (int64_t)16 * hidden;
+  p.dbs = w->down_block_stride ? w->down_block_stride : (int64_t)16 * hidden;
   p.dabs = w->down_absmax_block_stride ? w->down_absmax_block_stride : hidden;
   p.H = hidden;
   p.src = src_rows;

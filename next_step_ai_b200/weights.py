@@ -26,7 +26,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib
-from ._torch import dtype_code, ptr, stream_handle
+from ._torch import dtype_code, ptr, row_ptr, stream_handle
 from .nf4 import Nf4ParamMeta
 
 
@@ -115,12 +115,12 @@ class SparseMlpWeights:
 
     def to_c(self) -> _lib.MlpWeightsC:
         c = _lib.MlpWeightsC()
-        c.gate_packed = ptr(self.gate_packed)
-        c.gate_absmax = ptr(self.gate_absmax)
-        c.up_packed = ptr(self.up_packed)
-        c.up_absmax = ptr(self.up_absmax)
-        c.down_packed = ptr(self.down_packed)
-        c.down_absmax = ptr(self.down_absmax)
+        c.gate_packed = row_ptr(self.gate_packed)
+        c.gate_absmax = row_ptr(self.gate_absmax)
+        c.up_packed = row_ptr(self.up_packed)
+        c.up_absmax = row_ptr(self.up_absmax)
+        c.down_packed = row_ptr(self.down_packed)
+        c.down_absmax = row_ptr(self.down_absmax)
         c.gate_code = ptr(self.gate_code)
         c.up_code = ptr(self.up_code)
         c.down_code = ptr(self.down_code)

@@ -1,0 +1,79 @@
+"""Host side of the VRAM hot-block cache (no GPU): the bank replacement
+policy, calibration weighting and capacity target of next_step_ai_b200.cache
+against the reference's golden cases and the oracle, and the block record
+layout."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import cache_policy as cp
+
+torch = pytest.importorskip("torch")
+from next_step_ai_b200 import cache  # noqa: E402
+
+
+def test_bank_update_matches_reference_golden(cache_policy_golden):
+    for c in cache_policy_golden["bank"]:
+        bank = cache.FixedCapacityBank.from_state(c["ids"], c["scores"], c["active"], c["capacity"])
+        slots = bank.plan_update(c["novel"])
+        assert slots.tolist() == c["out_slots"]
+        assert bank.block_ids.tolist() == c["out_ids"]
+        assert np.array_equal(bank.scores, np.array(c["out_scores"], np.float32))
+        assert bank.active == c["out_active"]
+
+
+def test_bank_update_reference_unit_case():
+    # the reference's own pinned case (tests/test_throughput_contract.py:308-321)
+    bank = cache.FixedCapacityBank.from_state([10, 11, -1], [5.0, 1.0, 0.0], 2, 3)
+    slots = bank.plan_update([20, 21])
+    assert bank.active == 3 and slots.tolist() == [2, 1] and bank.block_ids.tolist() == [10, 21, 20]
+    assert bank.scores[1] > 5.0 and bank.scores[2] > 5.0
+
+
+def test_bank_sequence_matches_oracle():
+    rng = np.random.default_rng(3)
+    cap, nb = 24, 200
+    bank = cache.FixedCapacityBank(cap)
+    bank.prewarm(rng.choice(nb, 10, replace=False))
+    ids, scores, active = bank.block_ids.copy(), bank.scores.copy(), bank.active
+    assert np.array_equal(scores, cp.initial_bank_scores(10, cap))
+    for step in range(40):
+        resident = set(ids[:active].tolist())
+        sel = rng.choice(nb, 12, replace=False)
+        hits = [int(np.flatnonzero(ids[:active] == b)[0]) for b in sel if b in resident]
+        misses = np.array([b for b in sel if b not in resident], np.int64)
+        bank.add_hits(hits)
+        scores = cp.add_hit_scores(scores, np.array(hits, np.int64))
+        got = bank.plan_update(misses)
+        slots, ids, scores, active = cp.plan_fixed_capacity_bank_update(ids, scores, active, cap, misses)
+        assert got.tolist() == slots.tolist()
+        assert np.array_equal(bank.block_ids, ids) and np.array_equal(bank.scores, scores)
+        assert bank.active == active
+
+
+def test_calibration_and_target_match_reference_golden(cache_policy_golden):
+    for c in cache_policy_golden["calibration"]:
+        ab = np.array(c["active_blocks"], np.int64)
+        counts = cache.record_calibration_hits(None, ab, c["num_blocks"], c["power"])
+        counts = cache.record_calibration_hits(counts, ab[::-1], c["num_blocks"], c["power"])
+        assert np.allclose(counts, np.array(c["counts"], np.float32), rtol=0, atol=1e-6)
+    for c in cache_policy_golden["target"]:
+        got = cache.target_hot_blocks(layer_idx=c["layer_idx"], runtime_top_k=c["runtime_top_k"],
+                                      count_slots=c["count_slots"], previous_hot_count=c["prev"],
+                                      limit_bytes=c["limit"], used_bytes=c["used"], sparse_layers=c["layers"],
+                                      bytes_per_block=c["bpb"])
+        assert got == c["target"], c
+
+
+@pytest.mark.parametrize("hidden", [256, 1024, 4096, 16384])
+def test_record_layout(hidden):
+    lay = cache.record_layout(hidden)
+    end = 0
+    for name in ("gate", "up", "down", "gate_absmax", "up_absmax", "down_absmax"):
+        off, n = lay[name]
+        assert off == end and off % 16 == 0 and n % 16 == 0
+        end = off + n
+    assert end == cache.record_bytes(hidden)
+    # the per-block algorithmic bytes of the decode (gate+up packed+absmax, down packed+absmax)
+    assert end == 2 * (16 * hidden + 2 * hidden) + 16 * hidden + 4 * hidden

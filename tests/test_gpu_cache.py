@@ -1,0 +1,134 @@
+"""The VRAM hot-block cache on the GPU: resident blocks computed from the bank,
+misses staged from pinned host memory on a side stream, promotion after use.
+
+Each token's output must equal the all-resident decode of the same selection
+within the decode tolerances (the two passes only regroup the block sum), the
+device block table must mirror the host bank after every promotion, and the
+bank must evolve exactly like the reference policy (the oracle) on the same
+hit/miss sequence.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+from oracle import cache_policy as cp  # noqa: E402
+from oracle import synthetic as syn  # noqa: E402
+
+MAX_ABS = 2e-2
+REL_L2 = 5e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from next_step_ai_b200 import _lib
+
+    _lib.load()
+    return torch.device("cuda", 0)
+
+
+def _close(got, ref):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rel = np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
+    assert rel <= REL_L2, f"relative L2 {rel:.3e}"
+    assert float(np.abs(got - ref).max()) <= MAX_ABS
+
+
+def _layer(shape_name, dev, seed=5):
+    from next_step_ai_b200 import synthetic as dsyn
+
+    shape = dsyn.SHAPES[shape_name]
+    return shape, dsyn.make_layer_weights(shape, seed, 0, dev), dsyn.make_router(shape, seed, 0, dev)
+
+
+@pytest.mark.parametrize("shape_name,capacity", [("small", 40), ("cfg0", 112)])
+def test_cached_decode_matches_resident_and_policy(dev, shape_name, capacity):
+    from next_step_ai_b200 import sparse_mlp_decode
+    from next_step_ai_b200 import synthetic as dsyn
+    from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore
+
+    shape, w, rw = _layer(shape_name, dev)
+    store = HostBlockStore.from_weights(w)
+    rng = np.random.default_rng(11)
+    nb, k = shape.num_blocks, shape.top_k
+    hot = rng.choice(nb, capacity, replace=False)
+    cm = CachedSparseMlp(rw, store, capacity)
+    cm.pre_warm(hot)
+    # oracle bank state
+    ids = np.full(capacity, -1, np.int64)
+    ids[: hot.size] = hot
+    scores, active = cp.initial_bank_scores(hot.size, capacity), hot.size
+    for tok in range(6):
+        x = dsyn.make_x(shape, 100 + tok, 1, dev)[0]
+        res = set(ids[:active].tolist())
+        n_hit = int(0.7 * k)
+        sel = np.concatenate([rng.choice(sorted(res), n_hit, replace=False),
+                              rng.choice(sorted(set(range(nb)) - res), k - n_hit, replace=False)])
+        rng.shuffle(sel)
+        idx = torch.from_numpy(sel.astype(np.int32)).to(dev)
+        y, st = cm.decode(x, idx=idx)
+        ref = sparse_mlp_decode(x, None, w, idx=idx, out_dtype=torch.float32)
+        _close(y.cpu().numpy(), ref.cpu().numpy())
+        assert (st.hits, st.misses) == (n_hit, k - n_hit)
+        assert st.h2d_bytes == (k - n_hit) * 56 * shape.hidden
+        # the reference policy on the same token
+        hit_slots = np.array([int(np.flatnonzero(ids[:active] == b)[0]) for b in sel if b in res], np.int64)
+        scores = cp.add_hit_scores(scores, hit_slots)
+        misses = np.array([b for b in sel if b not in res], np.int64)
+        _, ids, scores, active = cp.plan_fixed_capacity_bank_update(ids, scores, active, capacity, misses)
+        assert np.array_equal(cm.bank.block_ids, ids) and np.array_equal(cm.bank.scores, scores)
+        # device table == host mirror == bank
+        torch.cuda.synchronize()
+        table = cm.slot_dev.cpu().numpy()
+        assert np.array_equal(table, cm.slot_host)
+        for slot, b in enumerate(ids[:active]):
+            assert table[b] == slot
+        assert int((table >= 0).sum()) == active
+
+
+def test_cached_decode_router_path_and_promoted_hits(dev):
+    from next_step_ai_b200 import route_sparse_mlp, sparse_mlp_decode
+    from next_step_ai_b200 import synthetic as dsyn
+    from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore
+
+    shape, w, rw = _layer("small", dev, seed=9)
+    store = HostBlockStore.from_weights(w)
+    cm = CachedSparseMlp(rw, store, 24)
+    cm.pre_warm(np.arange(24))
+    x = dsyn.make_x(shape, 3, 1, dev)[0]
+    y, st = cm.decode(x)  # router selection
+    sel = route_sparse_mlp(x, rw)[0].to(torch.int32)
+    ref = sparse_mlp_decode(x, None, w, idx=sel, out_dtype=torch.float32)
+    _close(y.cpu().numpy(), ref.cpu().numpy())
+    assert st.hits + st.misses == shape.top_k and st.promoted == st.misses
+    # the same token again: every block promoted last time is now a hit; a
+    # block the promotion evicted (lowest score, possibly one of this token's
+    # hits) is the only kind of miss left
+    blocks = sel.cpu().numpy()
+    resident = cm.slot_host[blocks] >= 0
+    first_misses = set(blocks[~np.isin(blocks, np.arange(24))].tolist())
+    assert all(cm.slot_host[b] >= 0 for b in first_misses)
+    y2, st2 = cm.decode(x)
+    assert st2.misses == int((~resident).sum()) and st2.hits == int(resident.sum())
+    _close(y2.cpu().numpy(), ref.cpu().numpy())
+
+
+def test_cache_rejects_bad_selections(dev):
+    from next_step_ai_b200 import synthetic as dsyn
+    from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore
+
+    shape, w, rw = _layer("tiny", dev, seed=2)
+    cm = CachedSparseMlp(rw, HostBlockStore.from_weights(w), 8)
+    cm.pre_warm(np.arange(8))
+    x = dsyn.make_x(shape, 1, 1, dev)[0]
+    with pytest.raises(RuntimeError):
+        cm.decode(x, idx=torch.tensor([0, 0, 1, 2], dtype=torch.int32, device=dev))
+    with pytest.raises(RuntimeError):
+        cm.decode(x, idx=torch.tensor([0, 1, 2, shape.num_blocks], dtype=torch.int32, device=dev))
