@@ -239,6 +239,24 @@ int nsm_decode_gathered_static(const void* x, int32_t x_dtype, int32_t hidden, i
                                const nsm_mlp_weights* w, void* y, int32_t y_dtype, float* act_out,
                                nsm_stream_t stream);
 
+/* ---- multi-token decode over the union of the tokens' blocks ------------
+ * Up to 32 tokens: x [rows][H] (x_dtype), idx [rows][k] int32 block ids (each
+ * row's router selection; ids < 0 or >= NB are ignored), the resident pools
+ * (tiled gate/up and down layouts, no biases) and block map -> y [rows][H]
+ * (y_dtype).  The union of the rows' blocks present in the pool is formed in
+ * ascending block order with one row mask per union block -- the reference's
+ * _build_sparse_active_layout (streaming_llama_runtime.py:4857-4908) -- and
+ * each union block's NF4 tiles are dequantised once and multiplied against all
+ * rows on the tensor cores; row r's SiLU(g)*u is zero outside its own blocks
+ * (the reference's flat_mask, :5451-5492).
+ *   union_out [min(NB, rows*k)] (may be NULL): the union's block ids;
+ *   union_count_out (device int32, may be NULL): its size. */
+size_t nsm_union_workspace_bytes(int hidden, int intermediate, int rows, int k);
+int nsm_union_decode(const void* x, int32_t x_dtype, int32_t rows, int32_t hidden, int32_t intermediate,
+                     const int32_t* idx, int32_t k, const nsm_block_map* map, const nsm_mlp_weights* w, void* y,
+                     int32_t y_dtype, int32_t* union_out, int32_t* union_count_out, void* ws, size_t ws_bytes,
+                     nsm_stream_t stream);
+
 /* ---- layout helpers ----------------------------------------------------- */
 /* bitsandbytes down weight [H][I/2] + absmax [H][I/64] -> block-major
  * [n][H][16] + [n][H] for the listed blocks (blocks == NULL: all I/32).

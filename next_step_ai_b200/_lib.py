@@ -37,6 +37,7 @@ EXPORTED = (
     "nsm_decode_rows_workspace_bytes", "nsm_decode_gathered_rows", "nsm_repack_down_block_major",
     "nsm_sparse_input_linear_4bit", "nsm_sparse_output_linear_4bit", "nsm_cache_split", "nsm_cache_promote",
     "nsm_repack_tiled", "nsm_decode_gathered_static", "nsm_workspace_error", "nsm_cache_stage",
+    "nsm_union_workspace_bytes", "nsm_union_decode",
 )
 
 
@@ -103,6 +104,10 @@ _SIGS = {
     "nsm_repack_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                  c_void_p, c_void_p, c_int32, POINTER(MlpWeightsC), c_void_p]),
     "nsm_cache_split": (c_int, [c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "nsm_union_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "nsm_union_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32,
+                                 POINTER(BlockMapC), POINTER(MlpWeightsC), c_void_p, c_int32, c_void_p, c_void_p,
+                                 c_void_p, c_size_t, c_void_p]),
     "nsm_cache_stage": (c_int, [c_void_p, c_void_p, c_int32, c_size_t, c_void_p, c_void_p, c_int32, c_void_p]),
     "nsm_cache_promote": (c_int, [POINTER(MlpWeightsC), c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
                                   c_void_p, c_void_p]),

@@ -172,3 +172,40 @@ def decode_gathered_rows(x: torch.Tensor, flat_mask: torch.Tensor | None, *, gat
                "nsm_decode_gathered_rows")
     del keep
     return y
+
+
+def union_decode(x: torch.Tensor, idx: torch.Tensor, weights: SparseMlpWeights, *, slot_of_block=None,
+                 block_range: tuple[int, int] | None = None, out_dtype: torch.dtype | None = None,
+                 return_union: bool = False):
+    """Multi-token decode (``rows <= 32``) over the union of the rows' selected
+    blocks: each union block's NF4 tiles are dequantised once for all rows and
+    row ``r`` only sees its own blocks -- ``_build_sparse_active_layout`` +
+    ``_sparse_mlp_forward_fast`` for rows > 1 (``streaming_llama_runtime.py:4857-4908``,
+    ``:5433-5492``) with resident weights.
+
+    ``x [rows, H]``, ``idx [rows, k]`` block ids (device).  Returns ``y [rows, H]``
+    (and the union's block ids when ``return_union``)."""
+    require_cuda(x, "x")
+    rows, H = int(x.shape[0]), int(x.shape[-1])
+    if H != weights.hidden:
+        raise RuntimeError(f"x has hidden {H}, weights {weights.hidden}")
+    xv = x.reshape(rows, H).contiguous()
+    iv = idx.reshape(rows, -1).to(device=xv.device, dtype=torch.int32).contiguous()
+    k = int(iv.shape[1])
+    lib = _lib.load()
+    wc = weights.to_c()
+    bm = _lib.BlockMapC()
+    bm.slot_of_block = ptr(slot_of_block) if slot_of_block is not None else None
+    lo, hi = block_range if block_range is not None else (0, weights.intermediate // 32)
+    bm.block_begin, bm.block_end = int(lo), int(hi)
+    y = torch.empty((rows, H), dtype=out_dtype or xv.dtype, device=xv.device)
+    umax = min(weights.intermediate // 32, rows * k)
+    uni = torch.empty(umax, dtype=torch.int32, device=xv.device)
+    cnt = torch.zeros(1, dtype=torch.int32, device=xv.device)
+    ws = WORKSPACES.get(lib.nsm_union_workspace_bytes(H, weights.intermediate, rows, k), xv.device)
+    _lib.check(lib.nsm_union_decode(ptr(xv), dtype_code(xv.dtype), rows, H, weights.intermediate, ptr(iv), k,
+                                    ctypes.byref(bm), ctypes.byref(wc), ptr(y), dtype_code(y.dtype), ptr(uni), ptr(cnt),
+                                    ws.data_ptr(), ws.numel(), stream_handle(xv.device)), "nsm_union_decode")
+    if return_union:
+        return y, uni[: int(cnt.item())]
+    return y
