@@ -459,6 +459,103 @@ def run_cache(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------------------------------- config 4
+UNION_ROWS = 32
+UNION_SHARED = 0.85  # shared component of the token inputs (x_t = rms(a z + sqrt(1-a^2) e_t))
+
+
+def run_union(args) -> None:
+    """32 tokens of one 405B-shaped layer, each routed to its
+    own top-208 blocks; the union is gathered once and contracted on the tensor
+    cores (route + union decode in one CUDA graph), against 32 per-token GEMV
+    decodes of the same tokens (route + MLP each, also one graph)."""
+    import numpy as np
+    import torch
+
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from next_step_ai_b200 import route_sparse_mlp, sparse_mlp_decode, union_decode
+    from next_step_ai_b200 import synthetic as dsyn
+
+    shape = dsyn.SHAPES["cfg1"]
+    t0 = time.time()
+    w = dsyn.make_layer_weights(shape, 1234, 0, dev)
+    rw = dsyn.make_router(shape, 1234, 0, dev)
+    x = dsyn.make_x(shape, 99, UNION_ROWS, dev, shared=UNION_SHARED)
+    idx = torch.empty((UNION_ROWS, TOP_K), dtype=torch.int32, device=dev)
+    y = torch.empty((UNION_ROWS, HIDDEN), dtype=torch.bfloat16, device=dev)
+    y_tok = torch.empty((UNION_ROWS, HIDDEN), dtype=torch.bfloat16, device=dev)
+    gen_s = time.time() - t0
+
+    def union_step():
+        idx.copy_(route_sparse_mlp(x, rw).to(torch.int32))
+        y.copy_(union_decode(x, idx, w))
+
+    def per_token_step():
+        for r in range(UNION_ROWS):
+            sparse_mlp_decode(x[r], rw, w, out=y_tok[r])
+
+    def graph_of(fn):
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            fn()
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        return g
+
+    def timed(g, n):
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    gu, gt = graph_of(union_step), graph_of(per_token_step)
+    with ClockSampler(local) as clk:
+        ms_union = timed(gu, args.steps)
+        ms_tok = timed(gt, max(3, args.steps // 4))
+    _, uni = union_decode(x, idx, w, return_union=True)
+    U = int(uni.numel())
+    err = float((y.float() - y_tok.float()).abs().max())
+    rel = float((y.float() - y_tok.float()).norm() / y_tok.float().norm())
+    bytes_union = U * (2 * (16 * HIDDEN + 2 * HIDDEN) + 16 * HIDDEN + 4 * HIDDEN) + 2 * RANK * HIDDEN + 2 * RANK * NB
+    flops = U * 3 * 2 * 32 * HIDDEN * UNION_ROWS
+    pk = peaks()
+    gbs = bytes_union / (ms_union * 1e-3) / 1e9
+    line = {
+        "metric": "multi-token sparse-MLP decode tok/s, one 405B-shaped layer, 32 tokens per step",
+        "value": UNION_ROWS / (ms_union * 1e-3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_union, "higher_is_better": True, "scaling": "none",
+        "vs_baseline": None, "dtype": "nf4 weights, fp16 x fp16 -> fp32 MMA, bf16 io",
+        "data": f"synthetic: seeded NF4 layer; 32 token inputs rms(a z + sqrt(1-a^2) e_t), a={UNION_SHARED}",
+        "config": {"workload": "BASELINE config 4: 32-token decode over the union of the tokens' top-208 sets",
+                   "hidden": HIDDEN, "blocks": NB, "top_k": TOP_K, "rows": UNION_ROWS, "union_blocks": U,
+                   "synthetic_gen_s": round(gen_s, 1)},
+        "per_token_gemv": {"ms_per_step": ms_tok, "tok_s": UNION_ROWS / (ms_tok * 1e-3),
+                           "speedup_of_union": ms_tok / ms_union},
+        "parity_vs_per_token": {"max_abs": err, "rel_l2": rel},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / pk["hbm_gbs"], 4), "algorithmic_bytes": bytes_union,
+                     "tensor_tflops": round(flops / (ms_union * 1e-3) / 1e12, 2),
+                     "unit_of_launch": "router x32 + union decode launch group"},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -468,13 +565,17 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--unique-layers", type=int, default=0,
                     help="cap the resident layers (cycled over the 126); for small profiling captures")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3],
-                    help="2: the 126-layer headline step (default); 3: hot-block cache layer")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+                    help="2: the 126-layer headline step (default); 3: hot-block cache layer; "
+                         "4: 32-token union decode")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.config == 3 and args.impl != "reference":
         run_cache(args)
+        return
+    if args.config == 4 and args.impl != "reference":
+        run_union(args)
         return
     if args.impl == "reference":
         run_reference(args)
