@@ -164,7 +164,20 @@ typedef struct nsm_layer_io {
   int32_t norm_weight_dtype;
   const void* norm_weight; /* [H] or NULL (= ones) */
   float eps;
-  int32_t reserved;
+  /* flags: NSM_IO_PENDING_Y -- instead of y_prev, the previous layer's output
+   *   is still pending in this workspace as down-projection partials (from a
+   *   call with NSM_IO_DEFER_Y on the same workspace); they are summed here in
+   *   fixed order (and across ranks through `exchange`) before the residual add.
+   * NSM_IO_DEFER_Y -- leave this layer's output pending in the workspace
+   *   instead of writing y (y may be NULL); the next layer (NSM_IO_PENDING_Y)
+   *   or nsm_residual_flush consumes it.  Needs a down projection without bias. */
+  int32_t flags;
+  int32_t reserved2;
+  /* Cross-GPU sum of the pending output (NULL on one GPU): every rank's
+   * partial is pushed to every rank over NVLink and summed in rank order inside
+   * the router's first kernel -- the all-reduce of the reference configuration
+   * fused with the residual add. */
+  const struct nsm_exchange* exchange;
   /* Optional timing hook: NSM_STAGE_EVENTS cudaEvent_t handles recorded on the
    * stream before the router, before gate/up, before the gate/up reduction,
    * before down, before the down reduction and after it.  Recording them
@@ -173,6 +186,28 @@ typedef struct nsm_layer_io {
   void* const* stage_events;
 } nsm_layer_io;
 #define NSM_STAGE_EVENTS 6
+#define NSM_IO_PENDING_Y 1
+#define NSM_IO_DEFER_Y 2
+
+/* residual += the pending output of the last NSM_IO_DEFER_Y layer (summed
+ * across ranks through io->exchange when set).  io->residual is required;
+ * io->flags must include NSM_IO_PENDING_Y. */
+int nsm_residual_flush(int32_t hidden, const nsm_layer_io* io, void* ws, size_t ws_bytes, nsm_stream_t stream);
+
+/* ---- cross-GPU exchange buffers --------------------------------------------
+ * One per rank (one process per GPU of a node).  nsm_exchange_create
+ * allocates this rank's buffer (cudaMalloc, zeroed; the only allocating calls
+ * of this library besides nothing else) and writes its CUDA IPC handle
+ * (NSM_IPC_HANDLE_BYTES bytes) for the other ranks; nsm_exchange_connect
+ * opens the peers' buffers from all ranks' handles (world x
+ * NSM_IPC_HANDLE_BYTES, in rank order).  No counterpart in the reference (it
+ * is single-GPU); replaces the NCCL all-reduce of the multi-GPU configuration. */
+#define NSM_IPC_HANDLE_BYTES 64
+typedef struct nsm_exchange nsm_exchange;
+size_t nsm_exchange_bytes(int world, int hidden);
+int nsm_exchange_create(int32_t world, int32_t rank, int32_t hidden, nsm_exchange** ex_out, void* ipc_handle_out);
+int nsm_exchange_connect(nsm_exchange* ex, const void* handles);
+int nsm_exchange_destroy(nsm_exchange* ex);
 
 size_t nsm_decode_workspace_bytes(int hidden, int intermediate, int top_k, int rank);
 

@@ -28,7 +28,9 @@ NSM_ERR_DEVICE = -6
 NSM_F32, NSM_F16, NSM_BF16 = 0, 1, 2
 NSM_LAYOUT_GATEUP_TILED, NSM_LAYOUT_DOWN_TILED = 1, 2
 NSM_STAGE_EVENTS = 6
-ABI_VERSION = 2
+NSM_IO_PENDING_Y, NSM_IO_DEFER_Y = 1, 2
+NSM_IPC_HANDLE_BYTES = 64
+ABI_VERSION = 3
 
 # every symbol include/nsm.h declares (checked by tests/test_abi.py)
 EXPORTED = (
@@ -37,7 +39,8 @@ EXPORTED = (
     "nsm_decode_rows_workspace_bytes", "nsm_decode_gathered_rows", "nsm_repack_down_block_major",
     "nsm_sparse_input_linear_4bit", "nsm_sparse_output_linear_4bit", "nsm_cache_split", "nsm_cache_promote",
     "nsm_repack_tiled", "nsm_decode_gathered_static", "nsm_workspace_error", "nsm_cache_stage",
-    "nsm_union_workspace_bytes", "nsm_union_decode",
+    "nsm_union_workspace_bytes", "nsm_union_decode", "nsm_residual_flush", "nsm_exchange_bytes",
+    "nsm_exchange_create", "nsm_exchange_connect", "nsm_exchange_destroy",
 )
 
 
@@ -69,7 +72,8 @@ class BlockMapC(ctypes.Structure):
 class LayerIoC(ctypes.Structure):
     _fields_ = [
         ("residual", c_void_p), ("y_prev", c_void_p), ("y_prev_dtype", c_int32), ("norm_weight_dtype", c_int32),
-        ("norm_weight", c_void_p), ("eps", c_float), ("reserved", c_int32), ("stage_events", c_void_p),
+        ("norm_weight", c_void_p), ("eps", c_float), ("flags", c_int32), ("reserved2", c_int32),
+        ("exchange", c_void_p), ("stage_events", c_void_p),
     ]
 
 
@@ -104,6 +108,11 @@ _SIGS = {
     "nsm_repack_tiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                  c_void_p, c_void_p, c_int32, POINTER(MlpWeightsC), c_void_p]),
     "nsm_cache_split": (c_int, [c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "nsm_residual_flush": (c_int, [c_int32, POINTER(LayerIoC), c_void_p, c_size_t, c_void_p]),
+    "nsm_exchange_bytes": (c_size_t, [c_int, c_int]),
+    "nsm_exchange_create": (c_int, [c_int32, c_int32, c_int32, POINTER(c_void_p), c_void_p]),
+    "nsm_exchange_connect": (c_int, [c_void_p, c_void_p]),
+    "nsm_exchange_destroy": (c_int, [c_void_p]),
     "nsm_union_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "nsm_union_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32,
                                  POINTER(BlockMapC), POINTER(MlpWeightsC), c_void_p, c_int32, c_void_p, c_void_p,

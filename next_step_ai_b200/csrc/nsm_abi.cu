@@ -70,6 +70,11 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   w.ticket_router_a = tick;
   w.ticket_router_b = tick ? tick + 1 : nullptr;
   w.err = tick ? tick + 2 : nullptr;
+  w.down_meta = tick ? tick + 3 : nullptr;
+  w.count = tick ? tick + 5 : nullptr;
+  // the down partials sit at a fixed offset too: a layer's pending output is
+  // read by the next call, whose router may have a different k or rank
+  w.ypart = reinterpret_cast<float*>(take((size_t)kMaxSlotGroups * hidden * sizeof(float)));
   w.latent_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * rank * sizeof(float)));
   w.sumsq_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * sizeof(float)));
   w.latent = reinterpret_cast<float*>(take((size_t)rank * sizeof(float)));
@@ -78,13 +83,11 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   w.x16 = reinterpret_cast<__half*>(take((size_t)hidden * sizeof(__half)));
   w.xscale = reinterpret_cast<float*>(take((size_t)(hidden / 64) * sizeof(float)));
   w.rows = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
-  w.count = reinterpret_cast<int*>(take(sizeof(int)));
   w.sel_idx = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
   w.row_block = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
   w.gu_part = reinterpret_cast<float*>(take((size_t)top_k * kMaxUnitsPerSlot * 64 * sizeof(float)));
   w.act16 = reinterpret_cast<__half*>(take((size_t)top_k * 32 * sizeof(__half)));
   w.act_scale = reinterpret_cast<float*>(take((size_t)top_k * sizeof(float)));
-  w.ypart = reinterpret_cast<float*>(take((size_t)kMaxSlotGroups * hidden * sizeof(float)));
   w.bytes = off;
   return w;
 }
@@ -95,7 +98,7 @@ using namespace nsm;
 
 extern "C" {
 
-int nsm_abi_version(void) { return 2; }
+int nsm_abi_version(void) { return 3; }
 
 const char* nsm_status_string(int status) {
   switch (status) {

@@ -148,9 +148,21 @@ __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
   return r;
 }
 
+// 8-byte system-scope relaxed store / load: a value and its epoch travel in one
+// single-copy-atomic word between GPUs.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Loads of data written by other CTAs of the same kernel (skip L1).
 __device__ __forceinline__ float ldcg_f32(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ int ldcg_i32(const int* p) { return __ldcg(p); }
+__device__ __forceinline__ uint32_t ldcg_u32(const uint32_t* p) { return __ldcg(p); }
 
 // Fill the per-lane-replicated byte->half2 tables from up to two 16-entry
 // fp32 codebooks.  Table t at word e*64 + t*32 + lane.
@@ -220,6 +232,29 @@ __device__ __forceinline__ float warp_sum(float v) {
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait (no-op without the launch attribute) until the previous
 // kernel has completed and its writes are visible.
+// ---- balanced work streams ---------------------------------------------------
+// Both gather-GEMVs split their (block, tile) pairs into `nw` contiguous,
+// equal ranges, one per warp (sizes differ by at most one pair), so every warp
+// finishes at the same time and its load pipeline never restarts at a block
+// boundary.  A warp flushes its fp32 accumulators whenever its range crosses
+// the boundary of a reduction group (a block for gate/up, a row group for
+// down); the segments of one group are reduced in fixed order by the
+// finalize kernels, so results are deterministic.
+__device__ __forceinline__ int stream_begin(int total, int nw, int w) {
+  return (int)(((long long)total * w) / nw);
+}
+// The warp whose range holds pair x: the largest w with stream_begin(w) <= x.
+__device__ __forceinline__ int stream_owner(int total, int nw, int x) {
+  return (int)((((long long)x + 1) * nw - 1) / total);
+}
+// Warps for `groups` reduction groups of `len` pairs with at most `max_seg`
+// segments per group: every range holds >= ceil(len / (max_seg - 2)) pairs.
+__device__ __forceinline__ int stream_warps(int groups, int len, int max_seg, int total_warps) {
+  const int total = groups * len;
+  const int m = max(1, (len + max_seg - 3) / (max_seg - 2));
+  return max(1, min(total_warps, total / m));
+}
+
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 

@@ -177,29 +177,6 @@ __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& 
   gu_tile_mma<kBase>(tile, b, xs, lb, acc);
 }
 
-// ---- balanced work streams ---------------------------------------------------
-// Both gather-GEMVs split their (block, tile) pairs into `nw` contiguous,
-// equal ranges, one per warp (sizes differ by at most one pair), so every warp
-// finishes at the same time and its load pipeline never restarts at a block
-// boundary.  A warp flushes its fp32 accumulators whenever its range crosses
-// the boundary of a reduction group (a block for gate/up, a 32-row tile for
-// down); the segments of one group are reduced in fixed order by the
-// finalize kernels, so results are deterministic.
-__device__ __forceinline__ int stream_begin(int total, int nw, int w) {
-  return (int)(((long long)total * w) / nw);
-}
-// The warp whose range holds pair x: the largest w with stream_begin(w) <= x.
-__device__ __forceinline__ int stream_owner(int total, int nw, int x) {
-  return (int)((((long long)x + 1) * nw - 1) / total);
-}
-// Warps for `groups` reduction groups of `len` pairs with at most `max_seg`
-// segments per group: every range holds >= ceil(len / (max_seg - 2)) pairs.
-__device__ __forceinline__ int stream_warps(int groups, int len, int max_seg, int total_warps) {
-  const int total = groups * len;
-  const int m = max(1, (len + max_seg - 3) / (max_seg - 2));
-  return max(1, min(total_warps, total / m));
-}
-
 constexpr int kStageRowsMax = 1024;  // pool rows staged in shared memory up to this count
 
 struct GuPtrs {
@@ -378,10 +355,18 @@ struct DownParams {
   float* ypart;
   int* err;
   int group_log2;  // log2 of the rows per down reduction group (5 or 6)
+  int* meta;       // ws.down_meta: the launch records total_warps and group_log2 there
   void* y;
   int y_dtype;
   int total_warps;
 };
+
+__device__ __forceinline__ void record_down_meta(const DownParams& p) {
+  if (blockIdx.x == 0 && threadIdx.x == 0 && p.meta != nullptr) {
+    p.meta[0] = p.total_warps;
+    p.meta[1] = p.group_log2;
+  }
+}
 
 constexpr int kDownBatch = 4;          // blocks per load batch (two batches in flight)
 constexpr int kStageActMaxSlots = 256;  // act16 + scale + row staged in shared memory up to this k
@@ -525,6 +510,7 @@ __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
   pdl_trigger();
   build_lut_dyn(p.down_code, p.down_code);
   pdl_wait();  // act16 / act_scale come from the gate/up kernel
+  record_down_meta(p);
   const int count = *p.count_ptr;
   __half* sact = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
   float* sscale = reinterpret_cast<float*>(sact + kStageActMaxSlots * 32);
@@ -870,6 +856,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) down_tma_kernel(DownParams p) 
   pdl_trigger();
   build_lut_dyn(p.down_code, p.down_code);
   pdl_wait();  // act16 / act_scale come from the gate/up kernels
+  record_down_meta(p);
   const int count = *p.count_ptr;
   __half* sact = reinterpret_cast<__half*>(smem + kDnActOff);
   float* sscale = reinterpret_cast<float*>(smem + kDnScaleOff);
@@ -955,6 +942,7 @@ struct MlpPlan {
   int y_dtype;
   const float* norm_scale;
   void* const* events;  // optional NSM_STAGE_EVENTS stage events (index 1..5 recorded here)
+  bool defer_y;         // leave the output as down partials in the workspace
 };
 
 static cudaError_t stage_event(void* const* ev, int i, cudaStream_t s) {
@@ -1070,6 +1058,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
                           (dp.dabs * 4) % 16 == 0;
   const bool dn_tma = dn_tiled && dn_stage && dn_aligned && ks->dn_tma > 0;
   dp.group_log2 = dn_tma ? 6 : 5;
+  dp.meta = ws.down_meta;
   if (dn_tma) {
     dp.total_warps = dev.sm_count * kTmaWarps;
     e = launch_pdl(down_tma_kernel, dev.sm_count, kTmaThreads, kDnTmaSmem, stream, dp);
@@ -1087,7 +1076,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   }
   NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(stage_event(m.events, 4, stream));
-  NSM_CHECK_CUDA(launch_pdl(down_finalize_kernel, (4 * m.H + 255) / 256, 256, 0, stream, dp));
+  if (!m.defer_y) NSM_CHECK_CUDA(launch_pdl(down_finalize_kernel, (4 * m.H + 255) / 256, 256, 0, stream, dp));
   NSM_CHECK_CUDA(stage_event(m.events, 5, stream));
   NSM_CHECK_CUDA(cudaGetLastError());
   return NSM_OK;
@@ -1100,7 +1089,9 @@ static RouterAParams router_a_params(const void* x, int x_dtype, const nsm_layer
   a.x_dtype = x_dtype;
   if (io && io->residual) {
     a.residual = io->residual;
-    a.y_prev = io->y_prev;
+    a.pending = (io->flags & NSM_IO_PENDING_Y) != 0;
+    if (a.pending && io->exchange) a.ex = *exchange_dev(io->exchange);
+    a.y_prev = a.pending ? nullptr : io->y_prev;
     a.y_prev_dtype = io->y_prev_dtype;
     a.norm_w = io->norm_weight;
     a.norm_w_dtype = io->norm_weight_dtype;
@@ -1207,9 +1198,14 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   if (resid && io->y_prev) NSM_REQUIRE(dtype_ok(io->y_prev_dtype), NSM_ERR_INVALID_ARG, "bad y_prev dtype");
   if (resid && io->norm_weight)
     NSM_REQUIRE(dtype_ok(io->norm_weight_dtype), NSM_ERR_INVALID_ARG, "bad norm weight dtype");
-  NSM_REQUIRE(y != nullptr && dtype_ok(y_dtype), NSM_ERR_INVALID_ARG, "y is NULL or has a bad dtype");
+  const bool defer = io != nullptr && (io->flags & NSM_IO_DEFER_Y) != 0;
+  NSM_REQUIRE(defer || (y != nullptr && dtype_ok(y_dtype)), NSM_ERR_INVALID_ARG, "y is NULL or has a bad dtype");
+  if (io && (io->flags & NSM_IO_PENDING_Y)) NSM_REQUIRE(resid, NSM_ERR_INVALID_ARG, "NSM_IO_PENDING_Y needs io->residual");
+  if (io && io->exchange) NSM_REQUIRE(exchange_dev(io->exchange)->hidden == hidden && exchange_dev(io->exchange)->data[0],
+                                      NSM_ERR_INVALID_ARG, "exchange not connected or built for another hidden size");
   st = validate_weights(w, hidden);
   if (st) return st;
+  if (defer) NSM_REQUIRE(w->down_bias == nullptr, NSM_ERR_UNSUPPORTED, "NSM_IO_DEFER_Y needs a down projection without bias");
   const int NB = intermediate / 32;
   int k, rank = 1;
   if (idx_in != nullptr) {
@@ -1263,7 +1259,24 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   m.y_dtype = y_dtype;
   m.norm_scale = wsl.norm_scale;
   m.events = events;
+  m.defer_y = defer;
   return launch_mlp(m, wsl, s);
+}
+
+int nsm_residual_flush(int32_t hidden, const nsm_layer_io* io, void* ws, size_t ws_bytes, nsm_stream_t stream) {
+  DeviceInfo dev;
+  int st = current_device(&dev);
+  if (st) return st;
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0 && hidden <= kMaxHidden, NSM_ERR_UNSUPPORTED,
+              "hidden must be a positive multiple of 64, at most 65536");
+  NSM_REQUIRE(io != nullptr && io->residual != nullptr && (io->flags & NSM_IO_PENDING_Y), NSM_ERR_INVALID_ARG,
+              "nsm_residual_flush needs io->residual and NSM_IO_PENDING_Y");
+  if (io->exchange) NSM_REQUIRE(exchange_dev(io->exchange)->hidden == hidden && exchange_dev(io->exchange)->data[0],
+                                NSM_ERR_INVALID_ARG, "exchange not connected or built for another hidden size");
+  const size_t need = decode_ws_layout(nullptr, hidden, 64, 1, 1).bytes;
+  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_residual_flush");
+  DecodeWs wsl = decode_ws_layout(ws, hidden, 64, 1, 1);
+  return router_a_prepare(nullptr, 0, io, nullptr, hidden, wsl, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int nsm_decode_gathered(const void* x, int32_t x_dtype, int32_t hidden, int32_t num_blocks_gathered,

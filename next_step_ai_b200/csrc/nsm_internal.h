@@ -52,11 +52,30 @@ constexpr int kMaxHidden = 65536;       // counters are sized for this
 constexpr int kCounterInts = 2 + kMaxTopK + kMaxHidden / 32;
 
 // Decode workspace: one contiguous caller-owned buffer, 256-byte aligned parts.
+// Cross-GPU exchange of a layer's output (device view of nsm_exchange).
+// Rank r's buffer: counter (epoch of the last completed exchange) | data
+// [2 slots][world][H] 8-byte words (fp32 value bits | epoch << 32; slot =
+// epoch & 1).  Every rank stores its chunk of the layer output into every
+// rank's buffer and sums the ranks' words in rank order once each carries the
+// current epoch.
+constexpr int kMaxWorld = 8;
+struct ExchangeDev {
+  unsigned long long* data[kMaxWorld];  // peer p's data region (mapped into this process)
+  uint32_t* counter;                    // this rank's epoch counter
+  int world;
+  int rank;
+  int hidden;
+};
+
+const ExchangeDev* exchange_dev(const nsm_exchange* ex);
+
 struct DecodeWs {
   // counters (must be zero between calls)
   int* ticket_router_a;          // [1]
   int* ticket_router_b;          // [1]
   int* err;                      // [1] device-side error code (0 = none), sticky
+  int* down_meta;                // [2] last down launch: total warps, log2 rows per reduction group
+  // (count below and ypart live at fixed offsets after the counter head)
   // router
   float* latent_part;            // [kRouterMaxCtas][rank]
   float* sumsq_part;             // [kRouterMaxCtas]

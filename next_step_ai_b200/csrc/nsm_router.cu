@@ -69,9 +69,68 @@ struct Vec8<float> {
 // ---------------------------------------------------------------------------
 // router A
 // ---------------------------------------------------------------------------
+// The previous layer's output for columns [c0, c0+n): fixed-order sum of the
+// down kernel's segments (the down launch records its warp count and row-group
+// size in ws.down_meta; the segment arithmetic mirrors the down kernels').
+__device__ __forceinline__ void pending_output(const RouterAParams& p, int c0, int n, float* ybuf) {
+  const int count = ldcg_i32(p.ws.count);
+  const int nw_down = ldcg_i32(p.ws.down_meta), glog = ldcg_i32(p.ws.down_meta + 1);
+  const int G = p.H >> glog;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int c = c0 + i;
+    float y = 0.f;
+    if (count > 0 && nw_down > 0) {
+      const int g = c >> glog, total = G * count;
+      const int nw = stream_warps(G, count, kMaxSlotGroups, nw_down);
+      const int nseg = stream_owner(total, nw, g * count + count - 1) - stream_owner(total, nw, g * count) + 1;
+      for (int q = 0; q < nseg; ++q) y += ldcg_f32(p.ws.ypart + (int64_t)q * p.H + c);
+    }
+    ybuf[i] = y;
+  }
+  __syncthreads();
+}
+
+// Cross-GPU sum of this CTA's chunk.  Every value travels with its epoch in one
+// 8-byte store (value bits | epoch << 32), so a receiver polls the words
+// themselves -- no fences and no separate flag round trip: rank r stores its
+// chunk into every rank's buffer (slot epoch & 1, row r); each thread then
+// waits (bounded) until its columns carry the current epoch from every rank
+// and sums them in rank order -- identical bits on every rank.
+constexpr int kExchangeSpinLimit = 1 << 24;
+__device__ __forceinline__ void exchange_chunk(const RouterAParams& p, int c0, int n, float* ybuf, uint32_t epoch) {
+  const ExchangeDev& ex = p.ex;
+  const int slot = (int)(epoch & 1u);
+  for (int r = 0; r < ex.world; ++r) {
+    unsigned long long* dst = ex.data[r] + ((int64_t)slot * ex.world + ex.rank) * ex.hidden + c0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      st_relaxed_sys_u64(dst + i, (unsigned long long)__float_as_uint(ybuf[i]) | ((unsigned long long)epoch << 32));
+  }
+  const unsigned long long* src = ex.data[ex.rank] + (int64_t)slot * ex.world * ex.hidden + c0;
+  bool timed_out = false;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float y = 0.f;
+    for (int r = 0; r < ex.world; ++r) {
+      const unsigned long long* w = src + (int64_t)r * ex.hidden + i;
+      unsigned long long v = ld_relaxed_sys_u64(w);
+      int it = 0;
+      while ((uint32_t)(v >> 32) != epoch && !timed_out) {
+        if (++it >= kExchangeSpinLimit) {
+          timed_out = true;
+          break;
+        }
+        v = ld_relaxed_sys_u64(w);
+      }
+      y += __uint_as_float((uint32_t)v);
+    }
+    ybuf[i] = y;
+  }
+  if (timed_out) atomicCAS(p.ws.err, 0, NSM_ERR_TIMEOUT);
+  __syncthreads();
+}
+
 template <typename WT>
 __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
-  extern __shared__ float xs[];  // [cols_per_cta]
+  extern __shared__ float xs[];  // [cols_per_cta] x slice | [cols_per_cta] pending output
   __shared__ float red[8];
   __shared__ int s_last;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -95,13 +154,23 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
   }
   pdl_trigger();
   pdl_wait();  // residual / x / y_prev come from earlier kernels
+  float* ybuf = xs + p.cols_per_cta;  // [cols_per_cta]: the pending output of the previous layer
+  uint32_t epoch = 0;
+  if (p.pending) {
+    pending_output(p, c0, n, ybuf);
+    if (p.ex.world > 1) {
+      epoch = ldcg_u32(p.ex.counter) + 1u;
+      exchange_chunk(p, c0, n, ybuf, epoch);
+    }
+  }
   float sumsq = 0.f;
   for (int i = tid; i < n; i += blockDim.x) {
     const int c = c0 + i;
     float v;
     if (p.residual != nullptr) {
       v = p.residual[c];
-      if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
+      if (p.pending) v += ybuf[i];
+      else if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
       p.residual[c] = v;
       sumsq += v * v;
       if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
@@ -233,7 +302,10 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
       p.ws.latent[r] = v;
     }
   }
-  if (tid == 0) *p.ws.ticket_router_a = 0;
+  if (tid == 0) {
+    *p.ws.ticket_router_a = 0;
+    if (p.pending && p.ex.world > 1) *p.ex.counter = epoch;  // this rank finished exchange `epoch`
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -537,7 +609,7 @@ int router_a_launch(const RouterAParams& a_in, cudaStream_t stream) {
     ctas = (a.H + cpc - 1) / cpc;
   }
   a.cols_per_cta = cpc;
-  const size_t smem = (size_t)cpc * sizeof(float);
+  const size_t smem = 2 * (size_t)cpc * sizeof(float);
   cudaError_t e;
   switch (a.wdtype) {
     case NSM_F32: e = launch_pdl(router_latent_kernel<float>, ctas, 256, smem, stream, a); break;

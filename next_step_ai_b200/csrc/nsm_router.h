@@ -25,6 +25,10 @@ struct RouterAParams {
   int basis_top_k;
   int H;
   int cols_per_cta;  // set by router_a_launch
+  // y_prev = the previous layer's down partials pending in ws (summed here,
+  // across ranks through `ex` when ex.world > 1)
+  int pending;
+  ExchangeDev ex;
   DecodeWs ws;
 };
 

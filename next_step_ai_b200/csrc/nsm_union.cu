@@ -203,16 +203,6 @@ struct UnionMlpParams {
   int y_dtype;
 };
 
-__device__ __forceinline__ int stream_begin_u(int total, int nw, int w) { return (int)(((long long)total * w) / nw); }
-__device__ __forceinline__ int stream_owner_u(int total, int nw, int x) {
-  return (int)((((long long)x + 1) * nw - 1) / total);
-}
-__device__ __forceinline__ int stream_warps_u(int groups, int len, int max_seg, int total_warps) {
-  const int total = groups * len;
-  const int m = max(1, (len + max_seg - 3) / (max_seg - 2));
-  return max(1, min(total_warps, total / m));
-}
-
 struct UTile {
   uint4 w[2][2];  // [proj][row group]
   float4 am[2];
@@ -274,11 +264,11 @@ __device__ __forceinline__ void union_gateup_body(const UnionMlpParams& p, uint3
   const int tpr = p.H >> 6;
   const int total = count * tpr;
   if (total == 0) return;
-  const int nw = stream_warps_u(count, tpr, kUnionGuMaxSeg, p.total_warps);
+  const int nw = stream_warps(count, tpr, kUnionGuMaxSeg, p.total_warps);
   if (warp_global >= nw) return;
-  const int q0 = stream_begin_u(total, nw, warp_global), q1 = stream_begin_u(total, nw, warp_global + 1);
+  const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
   int s = q0 / tpr, j = q0 - s * tpr;
-  int seg = warp_global - stream_owner_u(total, nw, s * tpr);
+  int seg = warp_global - stream_owner(total, nw, s * tpr);
   float acc[2][2][4][4];
 #pragma unroll
   for (int a = 0; a < 2; ++a)
@@ -354,8 +344,8 @@ __global__ void __launch_bounds__(1024) union_act_kernel(UnionMlpParams p) {
   if (s >= count) return;
   const int tok = threadIdx.x >> 5, row = threadIdx.x & 31;
   const int tpr = p.H >> 6, total = count * tpr;
-  const int nw = stream_warps_u(count, tpr, kUnionGuMaxSeg, p.total_warps);
-  const int nseg = stream_owner_u(total, nw, s * tpr + tpr - 1) - stream_owner_u(total, nw, s * tpr) + 1;
+  const int nw = stream_warps(count, tpr, kUnionGuMaxSeg, p.total_warps);
+  const int nseg = stream_owner(total, nw, s * tpr + tpr - 1) - stream_owner(total, nw, s * tpr) + 1;
   const float* base = p.ws.gu_part + (int64_t)s * kUnionGuMaxSeg * (2 * kUnionRows * 32);
   float g = 0.f, u = 0.f;
   for (int q = 0; q < nseg; ++q) {
@@ -383,11 +373,11 @@ __device__ __forceinline__ void union_down_body(const UnionMlpParams& p, uint32_
   const int RT = p.H >> 5;
   const int total = RT * count;
   if (total == 0) return;
-  const int nw = stream_warps_u(RT, count, kUnionDnMaxSeg, p.total_warps);
+  const int nw = stream_warps(RT, count, kUnionDnMaxSeg, p.total_warps);
   if (warp_global >= nw) return;
-  const int q0 = stream_begin_u(total, nw, warp_global), q1 = stream_begin_u(total, nw, warp_global + 1);
+  const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
   int rt = q0 / count, s = q0 - rt * count;
-  int seg = warp_global - stream_owner_u(total, nw, rt * count);
+  int seg = warp_global - stream_owner(total, nw, rt * count);
   float acc[2][4][4];
 #pragma unroll
   for (int a = 0; a < 2; ++a)
@@ -467,8 +457,8 @@ __global__ void __launch_bounds__(256) union_y_kernel(UnionMlpParams p) {
   float y = 0.f;
   if (count > 0) {
     const int RT = p.H >> 5, rt = h >> 5, total = RT * count;
-    const int nw = stream_warps_u(RT, count, kUnionDnMaxSeg, p.total_warps);
-    const int nseg = stream_owner_u(total, nw, rt * count + count - 1) - stream_owner_u(total, nw, rt * count) + 1;
+    const int nw = stream_warps(RT, count, kUnionDnMaxSeg, p.total_warps);
+    const int nseg = stream_owner(total, nw, rt * count + count - 1) - stream_owner(total, nw, rt * count) + 1;
     for (int q = 0; q < nseg; ++q) y += __ldcg(p.ws.ypart + ((int64_t)q * p.H + h) * kUnionRows + tok);
   }
   if (tok < p.rows) store_from_f32(p.y, p.y_dtype, (int64_t)tok * p.H + h, y);

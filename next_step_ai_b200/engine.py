@@ -46,13 +46,20 @@ class SparseMlpDecoder:
     """Runs ``num_layers`` decode steps over ``layers`` (cycled when fewer
     unique layers than ``num_layers`` are resident).
 
+    A layer's output stays in the workspace as down-projection partials
+    (``NSM_IO_DEFER_Y``); the next layer's router kernel sums them, adds them
+    to the fp32 residual and applies the RMSNorm (``NSM_IO_PENDING_Y``), so
+    there is no separate output kernel between layers.  With ``group`` (one
+    process per GPU) the partials of all ranks are summed inside that same
+    kernel over NVLink through an exchange buffer per rank (CUDA IPC), in rank
+    order, instead of an NCCL all-reduce.
+
     ``block_range``: the intermediate blocks this rank's pools hold
-    (``(0, NB)`` on one GPU).  ``group``: process group for the partial-sum
-    all-reduce (None on one GPU).
+    (``(0, NB)`` on one GPU).
     """
 
     def __init__(self, layers: list[DecodeLayer], num_layers: int, *, block_range: tuple[int, int] | None = None,
-                 group=None, reduce_dtype: torch.dtype = torch.bfloat16, eps: float = 1e-5):
+                 group=None, eps: float = 1e-5):
         if not layers:
             raise RuntimeError("no layers")
         self.layers = layers
@@ -64,7 +71,6 @@ class SparseMlpDecoder:
         self.group = group
         self.eps = float(eps)
         self.residual = torch.zeros(self.H, dtype=torch.float32, device=self.dev)
-        self.y = [torch.zeros(self.H, dtype=reduce_dtype, device=self.dev) for _ in range(2)]
         self.out = torch.zeros(self.H, dtype=torch.float32, device=self.dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self._lib = _lib.load()
@@ -74,47 +80,71 @@ class SparseMlpDecoder:
         self._c = [(l.router.to_c(), l.weights.to_c()) for l in layers]
         self._bm = _lib.BlockMapC()
         self._bm.block_begin, self._bm.block_end = int(self.block_range[0]), int(self.block_range[1])
+        self._ex = None
+        if group is not None and torch.distributed.get_world_size(group) > 1:
+            self._ex = self._connect_exchange(group)
+
+    def _connect_exchange(self, group) -> ctypes.c_void_p:
+        world = torch.distributed.get_world_size(group)
+        rank = torch.distributed.get_rank(group)
+        ex = ctypes.c_void_p()
+        handle = (ctypes.c_char * _lib.NSM_IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.dev):
+            _lib.check(self._lib.nsm_exchange_create(world, rank, self.H, ctypes.byref(ex), handle),
+                       "nsm_exchange_create")
+        handles = [None] * world
+        torch.distributed.all_gather_object(handles, bytes(handle), group=group)
+        blob = b"".join(handles)
+        with torch.cuda.device(self.dev):
+            _lib.check(self._lib.nsm_exchange_connect(ex, blob), "nsm_exchange_connect")
+        torch.distributed.barrier(group=group)
+        return ex
+
+    def _io(self, flags: int, events=None, norm_weight=None) -> _lib.LayerIoC:
+        io = _lib.LayerIoC()
+        io.residual = self.residual.data_ptr()
+        io.norm_weight = ptr(norm_weight) if norm_weight is not None else None
+        io.norm_weight_dtype = dtype_code(norm_weight.dtype) if norm_weight is not None else 0
+        io.eps = self.eps
+        io.flags = flags
+        io.exchange = self._ex
+        io.stage_events = ctypes.cast(events, ctypes.c_void_p) if events is not None else None
+        return io
 
     def _layer(self, i: int, ws: torch.Tensor, st: int, events=None) -> None:
         li = i % len(self.layers)
         layer = self.layers[li]
         rc, wc = self._c[li]
-        y_prev = self.y[(i + 1) % 2] if i > 0 else None
-        y = self.y[i % 2]
-        io = _lib.LayerIoC()
-        io.residual = self.residual.data_ptr()
-        io.y_prev = y_prev.data_ptr() if y_prev is not None else None
-        io.y_prev_dtype = dtype_code(y.dtype)
-        io.norm_weight = ptr(layer.norm_weight) if layer.norm_weight is not None else None
-        io.norm_weight_dtype = dtype_code(layer.norm_weight.dtype) if layer.norm_weight is not None else 0
-        io.eps = self.eps
-        io.stage_events = ctypes.cast(events, ctypes.c_void_p) if events is not None else None
+        flags = _lib.NSM_IO_DEFER_Y | (_lib.NSM_IO_PENDING_Y if i > 0 else 0)
+        io = self._io(flags, events, layer.norm_weight)
         _lib.check(self._lib.nsm_sparse_mlp_decode(
             None, 0, self.H, self.I, ctypes.byref(io), ctypes.byref(rc), None, 0, ctypes.byref(self._bm),
-            ctypes.byref(wc), y.data_ptr(), dtype_code(y.dtype), None, None, ws.data_ptr(), ws.numel(), st),
-            "nsm_sparse_mlp_decode")
-        if self.group is not None:
-            torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM, group=self.group)
+            ctypes.byref(wc), None, 0, None, None, ws.data_ptr(), ws.numel(), st), "nsm_sparse_mlp_decode")
 
-    # kernels nsm_sparse_mlp_decode launches per layer: router latent, block
-    # scores, top-k, gate/up, gate/up finalize, down, down finalize
-    KERNELS_PER_LAYER = 7
+    def _flush(self, ws: torch.Tensor, st: int) -> None:
+        io = self._io(_lib.NSM_IO_PENDING_Y)
+        _lib.check(self._lib.nsm_residual_flush(self.H, ctypes.byref(io), ws.data_ptr(), ws.numel(), st),
+                   "nsm_residual_flush")
+
+    # kernels per layer: router latent (+ previous layer's output), block scores,
+    # top-k, gate/up, gate/up reduction, down; plus one output kernel per token
+    KERNELS_PER_LAYER = 6
 
     @property
     def kernels_per_step(self) -> int:
-        """This library's kernel launches per token (library collectives and
-        the final residual add are not counted)."""
-        return self.KERNELS_PER_LAYER * self.num_layers
+        """This library's kernel launches per token (the final copy to ``out``
+        is not counted)."""
+        return self.KERNELS_PER_LAYER * self.num_layers + 1
 
     def step_eager(self) -> None:
         """One token through all layers (no graph).  Input: ``residual``;
-        output: ``out`` = final residual (residual + last MLP output)."""
+        output: ``out`` = final residual (residual + every layer's MLP output)."""
         ws = WORKSPACES.get(self._ws_bytes, self.dev)
         st = stream_handle(self.dev)
         for i in range(self.num_layers):
             self._layer(i, ws, st)
-        last = self.y[(self.num_layers - 1) % 2]
-        torch.add(self.residual, last.float(), out=self.out)
+        self._flush(ws, st)
+        self.out.copy_(self.residual)
 
     STAGES = ("router", "gateup", "gateup_finalize", "down", "down_finalize")
 
@@ -123,7 +153,10 @@ class SparseMlpDecoder:
         events recorded around each stage; returns the mean device time of
         each stage in microseconds.  The events separate the kernels (no
         programmatic dependent launch across stages), so the sum is larger
-        than a graph replay's layer time.  The pass advances ``residual``."""
+        than a graph replay's layer time.  "router" includes summing the
+        previous layer's output (and the cross-GPU exchange); "down_finalize"
+        is empty because each layer's output stays pending for the next.  The
+        pass advances ``residual``."""
         n = int(num_layers or self.num_layers)
         ws = WORKSPACES.get(self._ws_bytes, self.dev)
         st = stream_handle(self.dev)
@@ -137,6 +170,7 @@ class SparseMlpDecoder:
         torch.cuda.synchronize(self.dev)
         for i in range(n):
             self._layer(i, ws, st, events=arrs[i])
+        self._flush(ws, st)
         torch.cuda.synchronize(self.dev)
         out = {}
         for j, name in enumerate(self.STAGES):
@@ -166,4 +200,12 @@ class SparseMlpDecoder:
         self.graph.replay()
 
     def release(self) -> None:
+        """Drops the captured graph (the exchange buffers stay until close())."""
         self.graph = None
+
+    def close(self) -> None:
+        self.graph = None
+        if self._ex is not None:
+            torch.cuda.synchronize(self.dev)
+            self._lib.nsm_exchange_destroy(self._ex)
+            self._ex = None

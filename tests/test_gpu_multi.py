@@ -1,0 +1,119 @@
+"""Two GPUs, one process each: the decode engine with the intermediate blocks
+sharded over the ranks and each layer's partial outputs summed inside the next
+layer's router kernel over NVLink (the fused exchange).
+
+Both ranks must end with bit-identical outputs (the sum runs in rank order on
+every rank), equal to the single-process oracle of the whole model within the
+decode tolerances, for the eager pass and the CUDA-graph replay.  Skipped on a
+box with fewer than two GPUs.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+REL_L2 = 5e-3
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, shape_name: str, n_unique: int, num_layers: int, out) -> None:
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    try:
+        from next_step_ai_b200 import SparseMlpWeights
+        from next_step_ai_b200.engine import SparseMlpDecoder, shard_range
+        from tests.test_gpu_engine import _build
+
+        shape, layers, _ = _build(shape_name, n_unique, dev)
+        lo, hi = shard_range(shape.num_blocks, world, rank)
+        for L in layers:
+            w = L.weights
+            L.weights = SparseMlpWeights(hidden=w.hidden, intermediate=w.intermediate,
+                                         gate_packed=w.gate_packed[lo:hi].contiguous(),
+                                         gate_absmax=w.gate_absmax[lo:hi].contiguous(),
+                                         up_packed=w.up_packed[lo:hi].contiguous(),
+                                         up_absmax=w.up_absmax[lo:hi].contiguous(),
+                                         down_packed=w.down_packed[lo:hi].contiguous(),
+                                         down_absmax=w.down_absmax[lo:hi].contiguous(), gate_code=w.gate_code,
+                                         up_code=w.up_code, down_code=w.down_code, layout=w.layout)
+        x0 = (np.random.default_rng(7).standard_normal(shape.hidden) * 2).astype(np.float32)
+        dec = SparseMlpDecoder(layers, num_layers, block_range=(lo, hi), group=dist.group.WORLD)
+        dec.residual.copy_(torch.from_numpy(x0).to(dev))
+        dec.step_eager()
+        eager = dec.out.clone()
+        dec.residual.copy_(torch.from_numpy(x0).to(dev))
+        g = dec.capture()
+        dec.residual.copy_(torch.from_numpy(x0).to(dev))
+        g.replay()
+        torch.cuda.synchronize(dev)
+        graph = dec.out.clone()
+        from next_step_ai_b200._torch import WORKSPACES
+
+        errs = WORKSPACES.errors()
+        dec.release()
+        del g
+        dist.barrier()
+        dec.close()
+        out.put((rank, eager.cpu().numpy(), graph.cpu().numpy(), errs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("shape_name,n_unique,num_layers", [("small", 3, 5)])
+def test_two_gpu_fused_exchange_matches_oracle(shape_name, n_unique, num_layers):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    from oracle import synthetic as syn
+    from tests.test_gpu_engine import _oracle
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape_name, n_unique, num_layers, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        rank, eager, graph, errs = q.get(timeout=300)
+        res[rank] = (eager, graph, errs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert np.array_equal(res[0][0], res[1][0]) and np.array_equal(res[0][1], res[1][1])
+    assert np.array_equal(res[0][0], res[0][1])
+    assert all(v == 0 for r in res.values() for v in r[2].values())
+    # oracle of the unsharded model (host-side weights regenerated with the same seeds)
+    from tests.test_gpu_engine import _build
+
+    dev = torch.device("cuda", 0)
+    shape, _, host = _build(shape_name, n_unique, dev)
+    x0 = (np.random.default_rng(7).standard_normal(shape.hidden) * 2).astype(np.float32)
+    ref = _oracle(shape, host, num_layers, x0)
+    got = res[0][0].astype(np.float64)
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert rel <= REL_L2, rel
+    assert float(np.abs(got - ref).max()) <= MAX_ABS * max(1.0, float(np.abs(ref).max()) / 8)
+    del syn
