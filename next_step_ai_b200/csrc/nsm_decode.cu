@@ -1115,6 +1115,25 @@ static int router_a_prepare(const void* x, int x_dtype, const nsm_layer_io* io, 
   return router_a_launch(router_a_params(x, x_dtype, io, rw, H, ws), stream);
 }
 
+// Router kernel + scores/top-k kernels; the scores kernel reduces the router
+// kernel's partial latents (and advances the exchange epoch).
+static int router_launch_pair(const RouterAParams& a_in, RouterBParams b, cudaStream_t stream) {
+  RouterAParams a = a_in;
+  a.reduce_in_scores = 1;
+  int cpc;
+  b.reduce_latent = 1;
+  b.nparts = router_a_ctas(a.H, &cpc);
+  b.use_norm = a.use_norm;
+  b.eps = a.eps;
+  b.H = a.H;
+  b.enc_b = a.enc_b;
+  b.basis_top_k = a.basis_top_k;
+  b.epoch_counter = (a.pending && a.ex.world > 1) ? a.ex.counter : nullptr;
+  int st = router_a_launch(a, stream);
+  if (st) return st;
+  return router_b_launch(b, stream);
+}
+
 static int validate_router(const nsm_router_weights* rw, int H) {
   NSM_REQUIRE(rw != nullptr, NSM_ERR_INVALID_ARG, "router weights are NULL");
   NSM_REQUIRE(rw->enc_w && rw->score_w, NSM_ERR_INVALID_ARG, "router enc_w/score_w is NULL");
@@ -1177,9 +1196,8 @@ int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_w
   KernelSetup* ks;
   st = setup_kernels(dev, &ks);
   if (st) return st;
-  st = router_a_prepare(x, x_dtype, nullptr, rw, hidden, w, s);
-  if (st) return st;
-  return router_b_launch(router_b_params(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w), s);
+  return router_launch_pair(router_a_params(x, x_dtype, nullptr, rw, hidden, w),
+                            router_b_params(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w), s);
 }
 
 int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_t intermediate,
@@ -1230,12 +1248,13 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
 
   void* const* events = io != nullptr ? io->stage_events : nullptr;
   NSM_CHECK_CUDA(stage_event(events, 0, s));
-  st = router_a_prepare(x, x_dtype, io, idx_in ? nullptr : rw, hidden, wsl, s);
-  if (st) return st;
   if (idx_in == nullptr) {
-    st = router_b_launch(router_b_params(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl), s);
+    st = router_launch_pair(router_a_params(x, x_dtype, io, rw, hidden, wsl),
+                            router_b_params(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl), s);
     if (st) return st;
   } else {
+    st = router_a_prepare(x, x_dtype, io, nullptr, hidden, wsl, s);
+    if (st) return st;
     RouterBParams b{};
     b.NB = NB;
     b.slot_of_block = map ? map->slot_of_block : nullptr;

@@ -83,7 +83,15 @@ __device__ __forceinline__ void pending_output(const RouterAParams& p, int c0, i
       const int g = c >> glog, total = G * count;
       const int nw = stream_warps(G, count, kMaxSlotGroups, nw_down);
       const int nseg = stream_owner(total, nw, g * count + count - 1) - stream_owner(total, nw, g * count) + 1;
-      for (int q = 0; q < nseg; ++q) y += ldcg_f32(p.ws.ypart + (int64_t)q * p.H + c);
+      // 16 segment loads in flight at a time, summed in fixed order
+      for (int q0 = 0; q0 < nseg; q0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u)
+          v[u] = q0 + u < nseg ? ldcg_f32(p.ws.ypart + (int64_t)(q0 + u) * p.H + c) : 0.f;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) y += v[u];
+      }
     }
     ybuf[i] = y;
   }
@@ -129,7 +137,7 @@ __device__ __forceinline__ void exchange_chunk(const RouterAParams& p, int c0, i
 }
 
 template <typename WT>
-__global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
+__global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) {
   extern __shared__ float xs[];  // [cols_per_cta] x slice | [cols_per_cta] pending output
   __shared__ float red[8];
   __shared__ int s_last;
@@ -246,6 +254,7 @@ __global__ void __launch_bounds__(256) router_latent_kernel(RouterAParams p) {
       if (q == 0 && r < p.rank) p.ws.latent_part[blockIdx.x * p.rank + r] = acc;
     }
   }
+  if (p.reduce_in_scores) return;  // the scores kernel reduces the partials (and advances the epoch)
   __syncthreads();
   if (tid == 0) {
     __threadfence();
@@ -414,13 +423,78 @@ __device__ __forceinline__ float score_row(const RouterBParams& p, const float* 
 }
 
 // Block scores, one thread per block (grid-wide; waits for the latent).
+// The router kernel's partial latents reduced in fixed order -- every scores
+// CTA computes the same values: thread (row r, half h) sums partials h, h+2,
+// ...; the halves combine, then the RMSNorm scale, enc_b and the basis top-k
+// mask apply (streaming_llama_runtime.py:4220-4238).
+__device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat) {
+  __shared__ float half[2][kMaxRank];
+  __shared__ float s_norm;
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (tid < 32) {
+    float t = 0.f;
+    if (p.use_norm)
+      for (int b = lane; b < p.nparts; b += 32) t += ldcg_f32(&p.ws.sumsq_part[b]);
+    t = warp_sum(t);
+    if (lane == 0) s_norm = p.use_norm ? 1.f / sqrtf(t / (float)p.H + p.eps) : 1.f;
+  }
+  for (int e = tid; e < 2 * p.rank; e += blockDim.x) {
+    const int r = e % p.rank, h = e / p.rank;
+    float acc = 0.f;
+    int b = h;
+    for (; b + 14 < p.nparts; b += 16) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = ldcg_f32(&p.ws.latent_part[(b + 2 * u) * p.rank + r]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += v[u];
+    }
+    for (; b < p.nparts; b += 2) acc += ldcg_f32(&p.ws.latent_part[b * p.rank + r]);
+    half[h][r] = acc;
+  }
+  __syncthreads();
+  for (int r = tid; r < p.rank; r += blockDim.x) {
+    float acc = (half[0][r] + half[1][r]) * s_norm;
+    if (p.enc_b != nullptr) acc += load_as_f32(p.enc_b, p.wdtype, r);
+    lat[r] = acc;
+  }
+  __syncthreads();
+  const int bk = max(1, min(p.basis_top_k, p.rank));
+  if (bk < p.rank) {
+    float keep[2] = {0.f, 0.f};
+    for (int r = tid, j = 0; r < p.rank; r += blockDim.x, ++j) {
+      const float a = fabsf(lat[r]);
+      int pos = 0;
+      for (int q = 0; q < p.rank; ++q) {
+        const float b = fabsf(lat[q]);
+        pos += (b > a) || (b == a && q < r);
+      }
+      keep[j] = pos < bk ? lat[r] : 0.f;
+    }
+    __syncthreads();
+    for (int r = tid, j = 0; r < p.rank; r += blockDim.x, ++j) lat[r] = keep[j];
+    __syncthreads();
+  }
+  if (blockIdx.x == 0) {
+    for (int r = tid; r < p.rank; r += blockDim.x) p.ws.latent[r] = lat[r];
+    if (tid == 0) {
+      *p.ws.norm_scale = s_norm;
+      if (p.epoch_counter) *p.epoch_counter = *p.epoch_counter + 1u;  // this rank finished its exchange
+    }
+  }
+}
+
 template <typename WT>
 __global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
   __shared__ float lat[kMaxRank];
   pdl_trigger();
   pdl_wait();
-  for (int r = threadIdx.x; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r]);
-  __syncthreads();
+  if (p.reduce_latent) {
+    reduce_latent(p, lat);
+  } else {
+    for (int r = threadIdx.x; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r]);
+    __syncthreads();
+  }
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < p.NB) p.ws.scores[b] = score_row<WT>(p, lat, b);
 }
@@ -600,14 +674,21 @@ int router_setup() {
   return NSM_OK;
 }
 
-int router_a_launch(const RouterAParams& a_in, cudaStream_t stream) {
-  RouterAParams a = a_in;
-  int ctas = std::max(1, (a.H + 127) / 128);
+int router_a_ctas(int H, int* cols_per_cta) {
+  int ctas = std::max(1, (H + 127) / 128);
   int cpc = 128;
   if (ctas > kRouterMaxCtas) {
-    cpc = ((a.H + kRouterMaxCtas - 1) / kRouterMaxCtas + 63) / 64 * 64;
-    ctas = (a.H + cpc - 1) / cpc;
+    cpc = ((H + kRouterMaxCtas - 1) / kRouterMaxCtas + 63) / 64 * 64;
+    ctas = (H + cpc - 1) / cpc;
   }
+  *cols_per_cta = cpc;
+  return ctas;
+}
+
+int router_a_launch(const RouterAParams& a_in, cudaStream_t stream) {
+  RouterAParams a = a_in;
+  int cpc;
+  const int ctas = router_a_ctas(a.H, &cpc);
   a.cols_per_cta = cpc;
   const size_t smem = 2 * (size_t)cpc * sizeof(float);
   cudaError_t e;

@@ -29,6 +29,9 @@ struct RouterAParams {
   // across ranks through `ex` when ex.world > 1)
   int pending;
   ExchangeDev ex;
+  // 1: the scores kernel that follows reduces the partial latents (no last-CTA
+  // reduction here); 0: the last CTA reduces them (x-prep-only launches)
+  int reduce_in_scores;
   DecodeWs ws;
 };
 
@@ -48,8 +51,19 @@ struct RouterBParams {
   int block_begin;
   int block_end;
   int pool_rows;
+  // reduction of the router kernel's partials, done by every scores CTA
+  int reduce_latent;
+  int nparts;         // router kernel CTAs
+  int use_norm;
+  float eps;
+  int H;
+  const void* enc_b;
+  int basis_top_k;
+  uint32_t* epoch_counter;  // exchange epoch to advance (NULL without an exchange)
   DecodeWs ws;
 };
+// CTAs of the router kernel for hidden size H (kRouterMaxCtas at most).
+int router_a_ctas(int H, int* cols_per_cta);
 
 int router_setup();
 int router_a_launch(const RouterAParams& a, cudaStream_t stream);
