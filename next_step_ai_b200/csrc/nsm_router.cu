@@ -508,17 +508,19 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   extern __shared__ uint32_t keys[];  // [NB]
   __shared__ int hist[256];
   __shared__ uint32_t s_prefix, s_mask;
-  __shared__ int s_need;
+  __shared__ int s_need, s_bin_count;
   __shared__ unsigned long long sorted[1024];
   pdl_trigger();
   pdl_wait();
   const int tid = threadIdx.x;
   const int NB = p.NB, k = p.top_k;
+  const bool want_order = p.idx_out != nullptr || p.score_out != nullptr;
   for (int i = tid; i < NB; i += blockDim.x) keys[i] = orderable(ldcg_f32(&p.ws.scores[i]));
   if (tid == 0) {
     s_prefix = 0u;
     s_mask = 0u;
     s_need = k;
+    s_bin_count = -1;
   }
   __syncthreads();
   for (int shift = 24; shift >= 0; shift -= 8) {
@@ -560,18 +562,43 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
             s_prefix = pre | (bin << shift);
             s_mask = msk | (255u << shift);
             s_need = need - run;
+            s_bin_count = c[e];  // after the last pass: keys equal to the threshold
           }
           run += c[e];
         }
       }
     }
     __syncthreads();
+    // unordered selection: once the whole threshold bin is needed, every key
+    // with this prefix is selected and the lower bits do not matter
+    if (!want_order && s_need == s_bin_count) break;
   }
   const uint32_t thr = s_prefix;
   const int take_eq = s_need;
   // winners in block-id order (contiguous chunk per thread)
   const int per = (NB + blockDim.x - 1) / blockDim.x;
   const int lo = min(NB, tid * per), hi = min(NB, lo + per);
+  const bool ordered = want_order;
+  if (!ordered && take_eq == s_bin_count) {
+    // no tie is split at the threshold: the selection is key >= thr; one scan
+    // compacts the selected blocks present here into pool rows (block-id order)
+    int m = 0;
+    for (int i = lo; i < hi; ++i) m += keys[i] >= thr && map_block(p, i) >= 0;
+    int tot;
+    int pos = block_exclusive_scan(m, &tot);
+    for (int i = lo; i < hi; ++i) {
+      if (keys[i] < thr) continue;
+      const int r = map_block(p, i);
+      if (r < 0) continue;
+      p.ws.rows[pos] = r;
+      p.ws.row_block[pos] = i;
+      ++pos;
+    }
+    if (p.latent_out)
+      for (int r = tid; r < p.rank; r += blockDim.x) p.latent_out[r] = ldcg_f32(&p.ws.latent[r]);
+    if (tid == 0) *p.ws.count = tot;
+    return;
+  }
   int n_eq = 0, n_gt = 0;
   for (int i = lo; i < hi; ++i) {
     n_eq += keys[i] == thr;
@@ -581,7 +608,6 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   const int eq_before = block_exclusive_scan(n_eq, &tot);
   const int my_sel = n_gt + max(0, min(n_eq, take_eq - eq_before));
   const int sel_before = block_exclusive_scan(my_sel, &tot);
-  const bool ordered = p.idx_out != nullptr || p.score_out != nullptr;
   {
     int e = eq_before, out = sel_before;
     for (int i = lo; i < hi; ++i) {
