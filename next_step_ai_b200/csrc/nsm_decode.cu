@@ -84,6 +84,7 @@ struct GateUpParams {
   float* act_scale;
   float* act_out;  // optional fp32 [k][32]
   int total_warps;
+  int unit_tiles;  // tiles per stream unit (the partial segments follow the units)
 };
 
 // One 64-column tile of one block, both projections: w[proj][rg] holds the
@@ -264,9 +265,9 @@ __global__ void __launch_bounds__(256) gateup_finalize_kernel(GateUpParams p) {
   const int s = blockIdx.x;
   const int count = *p.count_ptr;
   if (s >= count) return;
-  const int tpr = p.H >> 6;
-  const int nw = stream_warps(count, tpr, kMaxUnitsPerSlot, p.total_warps);
-  const int ups = stream_owner(count * tpr, nw, s * tpr + tpr - 1) - stream_owner(count * tpr, nw, s * tpr) + 1;
+  const int cps = (p.H >> 6) / p.unit_tiles;
+  const int nw = stream_warps(count, cps, kMaxUnitsPerSlot, p.total_warps);
+  const int ups = stream_owner(count * cps, nw, s * cps + cps - 1) - stream_owner(count * cps, nw, s * cps) + 1;
   const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
   float gsum = 0.f, usum = 0.f;
 #pragma unroll 8
@@ -549,15 +550,24 @@ __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
 #define NSM_TMA_WARPS 16
 #endif
 #ifndef NSM_GU_STAGES
-#define NSM_GU_STAGES 3
+#define NSM_GU_STAGES 2
+#endif
+#ifndef NSM_GU_UNIT_TILES
+#define NSM_GU_UNIT_TILES 2
 #endif
 #ifndef NSM_DN_STAGES
 #define NSM_DN_STAGES 3
 #endif
 constexpr int kTmaWarps = NSM_TMA_WARPS;
 constexpr int kTmaThreads = kTmaWarps * 32;
+#ifndef NSM_GU_WARPS
+#define NSM_GU_WARPS 12
+#endif
+constexpr int kGuWarps = NSM_GU_WARPS;  // gate/up: fewer warps, two-tile stages
+constexpr int kGuThreads = kGuWarps * 32;
 constexpr int kGuStages = NSM_GU_STAGES;
-constexpr int kGuStageBytes = 2048 + 256;  // gate tile, up tile, gate absmax, up absmax
+constexpr int kGuUnitTiles = NSM_GU_UNIT_TILES;
+constexpr int kGuStageBytes = kGuUnitTiles * (2048 + 256);  // gate tiles, up tiles, gate absmax, up absmax
 constexpr int kDnStages = NSM_DN_STAGES;
 #ifndef NSM_DN_PAIRS_PER_STAGE
 #define NSM_DN_PAIRS_PER_STAGE 2
@@ -569,8 +579,8 @@ constexpr int kGuX16Off = kSmemHead;
 constexpr int kGuXsOff = kGuX16Off + kStageXMaxHidden * 2;
 constexpr int kGuRowsOff = kGuXsOff + (kStageXMaxHidden / 64) * 4;
 constexpr int kGuRingOff = kGuRowsOff + kStageRowsMax * 4;
-constexpr int kGuBarOff = kGuRingOff + kTmaWarps * kGuStages * kGuStageBytes;
-constexpr int kGuTmaSmem = kGuBarOff + kTmaWarps * kGuStages * 8;
+constexpr int kGuBarOff = kGuRingOff + kGuWarps * kGuStages * kGuStageBytes;
+constexpr int kGuTmaSmem = kGuBarOff + kGuWarps * kGuStages * 8;
 constexpr int kDnActOff = kSmemHead;
 constexpr int kDnScaleOff = kDnActOff + kStageActMaxSlots * 64;
 constexpr int kDnRowsOff = kDnScaleOff + kStageActMaxSlots * 4;
@@ -593,52 +603,56 @@ __device__ __forceinline__ void drain_ring(uint32_t wbar, int consumed, int issu
   for (int b = consumed; b < issued; ++b) mbar_wait(wbar + 8u * (uint32_t)(b % kStages), (uint32_t)((b / kStages) & 1));
 }
 
+// A ring stage holds one *unit* of kGuUnitTiles adjacent tiles of one block
+// (gate kGuUnitTiles KB, up kGuUnitTiles KB, their absmax runs): four bulk
+// copies and one round of cursor bookkeeping per unit instead of per tile.
 template <int kBase>
 __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t lb, uint32_t xs16_s, uint32_t xss_s,
                                                 const int* rows, int count, uint32_t ring, uint32_t bar0) {
+  constexpr int UT = kGuUnitTiles;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int warp = threadIdx.x >> 5;
-  const int warp_global = blockIdx.x * kTmaWarps + warp;
-  const int tpr = p.H >> 6;
-  const int total = count * tpr;
-  const int nw = stream_warps(count, tpr, kMaxUnitsPerSlot, p.total_warps);
+  const int warp_global = blockIdx.x * kGuWarps + warp;
+  const int cps = (p.H >> 6) / UT;  // units per block
+  const int total = count * cps;
+  const int nw = stream_warps(count, cps, kMaxUnitsPerSlot, p.total_warps);
   if (warp_global >= nw) return;
   const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
   const uint32_t wring = ring + (uint32_t)(warp * kGuStages * kGuStageBytes);
   const uint32_t wbar = bar0 + (uint32_t)(warp * kGuStages * 8);
   const uint64_t pol = l2_evict_first_policy();
-  // load cursor: source pointers of the next pair to fetch
-  int ls = q0 / tpr, lj = q0 - ls * tpr;
+  // load cursor: source pointers of the next unit to fetch
+  int ls = q0 / cps, lj = q0 - ls * cps;
   const uint8_t* lg;
   const uint8_t* lu;
   const float* lga;
   const float* lua;
   auto load_slot = [&]() {
     const int prow = rows[ls];
-    lg = p.gate + (int64_t)prow * p.gstride + (int64_t)lj * 1024;
-    lu = p.up + (int64_t)prow * p.gstride + (int64_t)lj * 1024;
-    lga = p.gate_am + (int64_t)prow * p.gastride + lj * 32;
-    lua = p.up_am + (int64_t)prow * p.gastride + lj * 32;
+    lg = p.gate + (int64_t)prow * p.gstride + (int64_t)lj * (UT * 1024);
+    lu = p.up + (int64_t)prow * p.gstride + (int64_t)lj * (UT * 1024);
+    lga = p.gate_am + (int64_t)prow * p.gastride + lj * (UT * 32);
+    lua = p.up_am + (int64_t)prow * p.gastride + lj * (UT * 32);
   };
   int issued = 0;
-  auto issue_next = [&](int stage) {  // fetch the cursor's pair into `stage`, advance the cursor
+  auto issue_next = [&](int stage) {  // fetch the cursor's unit into `stage`, advance the cursor
     ++issued;
     if (lane == 0) {
       fence_proxy_async_smem();  // the warp's reads of this stage come first
       const uint32_t dst = wring + (uint32_t)(stage * kGuStageBytes);
       const uint32_t bar = wbar + 8u * (uint32_t)stage;
       mbar_arrive_expect_tx(bar, kGuStageBytes);
-      bulk_g2s(dst, lg, 1024u, bar, pol);
-      bulk_g2s(dst + 1024, lu, 1024u, bar, pol);
-      bulk_g2s(dst + 2048, lga, 128u, bar, pol);
-      bulk_g2s(dst + 2176, lua, 128u, bar, pol);
+      bulk_g2s(dst, lg, UT * 1024u, bar, pol);
+      bulk_g2s(dst + UT * 1024, lu, UT * 1024u, bar, pol);
+      bulk_g2s(dst + UT * 2048, lga, UT * 128u, bar, pol);
+      bulk_g2s(dst + UT * 2048 + UT * 128, lua, UT * 128u, bar, pol);
     }
-    lg += 1024;
-    lu += 1024;
-    lga += 32;
-    lua += 32;
-    if (++lj == tpr) {
+    lg += UT * 1024;
+    lu += UT * 1024;
+    lga += UT * 32;
+    lua += UT * 32;
+    if (++lj == cps) {
       lj = 0;
       if (++ls < count) load_slot();
     }
@@ -648,10 +662,10 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
   for (int i = 0; i < kGuStages; ++i)
     if (q0 + i < q1) issue_next(i);
 
-  int s = q0 / tpr, j = q0 - s * tpr;
-  int seg = warp_global - stream_owner(total, nw, s * tpr);
-  uint32_t xa = xs16_s + (uint32_t)(j * 128 + t * 32);  // this lane's x fragment of tile j
-  uint32_t xsa = xss_s + (uint32_t)(j * 4);
+  int s = q0 / cps, j = q0 - s * cps;  // unit j of block s
+  int seg = warp_global - stream_owner(total, nw, s * cps);
+  uint32_t xa = xs16_s + (uint32_t)(j * UT * 128 + t * 32);  // this lane's x fragment of the unit's first tile
+  uint32_t xsa = xss_s + (uint32_t)(j * UT * 4);
   float acc[2][4] = {};
   uint32_t phase = 0;
   int q = q0;
@@ -665,27 +679,30 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
           ok = false;
         } else {
           const uint32_t sb = wring + (uint32_t)(st * kGuStageBytes);
-          GuTile tile;
-          tile.w[0][0] = lds_u4(sb + lane * 16);
-          tile.w[0][1] = lds_u4(sb + 512 + lane * 16);
-          tile.w[1][0] = lds_u4(sb + 1024 + lane * 16);
-          tile.w[1][1] = lds_u4(sb + 1536 + lane * 16);
-          tile.am[0] = lds_f4(sb + 2048 + g * 16);
-          tile.am[1] = lds_f4(sb + 2176 + g * 16);
-          const uint4 x0 = lds_u4(xa), x1 = lds_u4(xa + 16);
-          const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-          float xs;
-          asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xs) : "r"(xsa));
-          gu_tile_mma<kBase>(tile, bx, xs, lb, acc);
+#pragma unroll
+          for (int tt = 0; tt < UT; ++tt) {
+            GuTile tile;
+            tile.w[0][0] = lds_u4(sb + tt * 1024 + lane * 16);
+            tile.w[0][1] = lds_u4(sb + tt * 1024 + 512 + lane * 16);
+            tile.w[1][0] = lds_u4(sb + UT * 1024 + tt * 1024 + lane * 16);
+            tile.w[1][1] = lds_u4(sb + UT * 1024 + tt * 1024 + 512 + lane * 16);
+            tile.am[0] = lds_f4(sb + UT * 2048 + tt * 128 + g * 16);
+            tile.am[1] = lds_f4(sb + UT * 2048 + UT * 128 + tt * 128 + g * 16);
+            const uint4 x0 = lds_u4(xa + tt * 128), x1 = lds_u4(xa + tt * 128 + 16);
+            const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+            float xs;
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xs) : "r"(xsa + tt * 4));
+            gu_tile_mma<kBase>(tile, bx, xs, lb, acc);
+          }
           __syncwarp();
           if (q + kGuStages < q1) issue_next(st);
           ++q;
-          xa += 128;
-          xsa += 4;
-          if (++j == tpr || q == q1) {
+          xa += UT * 128;
+          xsa += UT * 4;
+          if (++j == cps || q == q1) {
             gu_flush(p, s, seg, g, t, acc);
-            seg = 0;  // this warp holds the first pair of the next block
-            if (j == tpr) {
+            seg = 0;  // this warp holds the first unit of the next block
+            if (j == cps) {
               j = 0;
               ++s;
               xa = xs16_s + (uint32_t)(t * 32);
@@ -703,10 +720,10 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
   }
 }
 
-__global__ void __launch_bounds__(kTmaThreads, 1) gateup_tma_kernel(GateUpParams p) {
+__global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams p) {
   char* smem = reinterpret_cast<char*>(g_lut_smem);
   const uint32_t bar0 = smem_u32(smem + kGuBarOff);
-  if (threadIdx.x < kTmaWarps * kGuStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
+  if (threadIdx.x < kGuWarps * kGuStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
   mbar_init_fence();
   pdl_trigger();
   build_lut_dyn(p.gate_code, p.up_code);
@@ -916,7 +933,7 @@ static int setup_kernels(const DeviceInfo& d, KernelSetup** out) {
     if (!st) st = setup_one(down_kernel<false, true>, kDownSmemStaged, &s.dn[0][1]);
     if (!st) st = setup_one(down_kernel<true, false>, kSmemHead, &s.dn[1][0]);
     if (!st) st = setup_one(down_kernel<true, true>, kDownSmemStaged, &s.dn[1][1]);
-    if (!st) st = setup_one(gateup_tma_kernel, kGuTmaSmem, &s.gu_tma, kTmaThreads);
+    if (!st) st = setup_one(gateup_tma_kernel, kGuTmaSmem, &s.gu_tma, kGuThreads);
     if (!st) st = setup_one(down_tma_kernel, kDnTmaSmem, &s.dn_tma, kTmaThreads);
     if (!st) st = router_setup();
     if (st) return st;
@@ -1008,12 +1025,14 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   const bool gu_stage = m.H <= kStageXMaxHidden;
   const bool gu_aligned = ((uintptr_t)gp.gate | (uintptr_t)gp.up | (uintptr_t)gp.gate_am | (uintptr_t)gp.up_am) % 16 == 0 &&
                           gp.gstride % 16 == 0 && (gp.gastride * 4) % 16 == 0;
-  const bool gu_tma = gu_tiled && gu_stage && gu_aligned && ks->gu_tma > 0;
+  const bool gu_tma = gu_tiled && gu_stage && gu_aligned && ks->gu_tma > 0 && (m.H / 64) % kGuUnitTiles == 0;
   NSM_CHECK_CUDA(stage_event(m.events, 1, stream));
   cudaError_t e;
+  gp.unit_tiles = 1;
   if (gu_tma) {
-    gp.total_warps = dev.sm_count * kTmaWarps;
-    e = launch_pdl(gateup_tma_kernel, dev.sm_count, kTmaThreads, kGuTmaSmem, stream, gp);
+    gp.unit_tiles = kGuUnitTiles;
+    gp.total_warps = dev.sm_count * kGuWarps;
+    e = launch_pdl(gateup_tma_kernel, dev.sm_count, kGuThreads, kGuTmaSmem, stream, gp);
   } else {
   const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
   gp.total_warps = gu_ctas * (kMlpThreads / 32);
