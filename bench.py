@@ -243,7 +243,9 @@ def run_ours(args) -> None:
             "config": {"workload": "BASELINE config 2: 126-layer 405B-shaped sparse-MLP decode step",
                        "hidden": HIDDEN, "intermediate": INTERMEDIATE, "blocks": NB, "top_k": TOP_K, "rank": RANK,
                        "layers": LAYERS, "unique_layers_resident": unique, "layer_cycling": unique < LAYERS,
-                       "parallelism": f"block-shard x{world}, router replicated, NCCL all-reduce bf16 [16384]",
+                       "parallelism": (f"block-shard x{world}, router replicated, fp32 partial sums exchanged over "
+                                       "CUDA-IPC NVLink buffers inside the next router kernel" if world > 1
+                                       else "single GPU, all blocks resident"),
                        "l2": "inputs larger than L2 (each layer >= 184 MB per rank)",
                        "cuda_graph": True, "synthetic_gen_s": round(gen_s, 1)},
             "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
@@ -550,7 +552,7 @@ def run_union(args) -> None:
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / pk["hbm_gbs"], 4), "algorithmic_bytes": bytes_union,
                      "tensor_tflops": round(flops / (ms_union * 1e-3) / 1e12, 2),
-                     "unit_of_launch": "router x32 + union decode launch group"},
+                     "unit_of_launch": "32-row router (3 launches) + union decode launch group"},
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)

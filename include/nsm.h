@@ -220,6 +220,17 @@ int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_w
               int32_t* idx_out, float* score_out, float* latent_out, void* ws, size_t ws_bytes,
               nsm_stream_t stream);
 
+/* Router for `rows` tokens at once: x [rows][hidden] row-major; idx_out
+ * [rows][top_k], score_out [rows][top_k] (may be NULL), latent_out
+ * [rows][rank] (may be NULL), each row as nsm_route would give it.  Replaces
+ * StreamingLlamaRuntime._route_sparse_mlp for rows > 1
+ * (streaming_llama_runtime.py:4311-4352): three launches for all rows.
+ * Workspace: nsm_route_workspace_bytes(hidden, num_blocks, top_k, rank, rows). */
+size_t nsm_route_workspace_bytes(int hidden, int num_blocks, int top_k, int rank, int rows);
+int nsm_route_rows(const void* x, int32_t x_dtype, int32_t rows, int32_t hidden, const nsm_router_weights* rw,
+                   int32_t* idx_out, float* score_out, float* latent_out, void* ws, size_t ws_bytes,
+                   nsm_stream_t stream);
+
 /* Whole decode MLP for one token: route, gather-GEMV gate/up, SiLU*up,
  * gather-GEMV down.  Replaces _mlp_forward_dispatch's decode branch
  * (streaming_llama_runtime.py:5906-5913) = _route_sparse_mlp +

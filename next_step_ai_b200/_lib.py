@@ -40,7 +40,8 @@ EXPORTED = (
     "nsm_sparse_input_linear_4bit", "nsm_sparse_output_linear_4bit", "nsm_cache_split", "nsm_cache_promote",
     "nsm_repack_tiled", "nsm_decode_gathered_static", "nsm_workspace_error", "nsm_cache_stage",
     "nsm_union_workspace_bytes", "nsm_union_decode", "nsm_residual_flush", "nsm_exchange_bytes",
-    "nsm_exchange_create", "nsm_exchange_connect", "nsm_exchange_destroy",
+    "nsm_exchange_create", "nsm_exchange_connect", "nsm_exchange_destroy", "nsm_route_workspace_bytes",
+    "nsm_route_rows",
 )
 
 
@@ -85,6 +86,9 @@ _SIGS = {
     "nsm_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "nsm_route": (c_int, [c_void_p, c_int32, c_int32, POINTER(RouterWeightsC), c_void_p, c_void_p, c_void_p,
                           c_void_p, c_size_t, c_void_p]),
+    "nsm_route_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "nsm_route_rows": (c_int, [c_void_p, c_int32, c_int32, c_int32, POINTER(RouterWeightsC), c_void_p, c_void_p,
+                               c_void_p, c_void_p, c_size_t, c_void_p]),
     "nsm_sparse_mlp_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, POINTER(LayerIoC),
                                       POINTER(RouterWeightsC), c_void_p, c_int32, POINTER(BlockMapC),
                                       POINTER(MlpWeightsC), c_void_p, c_int32, c_void_p, c_void_p, c_void_p,

@@ -4,6 +4,7 @@
 
 #include <cstdio>
 #include <mutex>
+#include <algorithm>
 #include <string>
 
 #include "nsm_internal.h"
@@ -56,7 +57,7 @@ int current_device(DeviceInfo* info) {
   return NSM_OK;
 }
 
-DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank) {
+DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank, int rows) {
   DecodeWs w{};
   char* b = reinterpret_cast<char*>(base);
   size_t off = 0;
@@ -75,15 +76,17 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   // the down partials sit at a fixed offset too: a layer's pending output is
   // read by the next call, whose router may have a different k or rank
   w.ypart = reinterpret_cast<float*>(take((size_t)kMaxSlotGroups * hidden * sizeof(float)));
-  w.latent_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * rank * sizeof(float)));
-  w.sumsq_part = reinterpret_cast<float*>(take((size_t)kRouterMaxCtas * sizeof(float)));
-  w.latent = reinterpret_cast<float*>(take((size_t)rank * sizeof(float)));
+  // router scratch: one copy per routed row (multi-row routing)
+  const size_t R = (size_t)std::max(1, rows);
+  w.latent_part = reinterpret_cast<float*>(take(R * kRouterMaxCtas * rank * sizeof(float)));
+  w.sumsq_part = reinterpret_cast<float*>(take(R * kRouterMaxCtas * sizeof(float)));
+  w.latent = reinterpret_cast<float*>(take(R * rank * sizeof(float)));
   w.norm_scale = reinterpret_cast<float*>(take(sizeof(float)));
-  w.scores = reinterpret_cast<float*>(take((size_t)nb * sizeof(float)));
+  w.scores = reinterpret_cast<float*>(take(R * nb * sizeof(float)));
   w.x16 = reinterpret_cast<__half*>(take((size_t)hidden * sizeof(__half)));
   w.xscale = reinterpret_cast<float*>(take((size_t)(hidden / 64) * sizeof(float)));
   w.rows = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
-  w.sel_idx = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
+  w.sel_idx = reinterpret_cast<int*>(take(R * top_k * sizeof(int)));
   w.row_block = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
   w.gu_part = reinterpret_cast<float*>(take((size_t)top_k * kMaxUnitsPerSlot * 64 * sizeof(float)));
   w.act16 = reinterpret_cast<__half*>(take((size_t)top_k * 32 * sizeof(__half)));
@@ -138,6 +141,11 @@ int nsm_workspace_error(void* ws, size_t ws_bytes, int32_t* code_out, nsm_stream
 size_t nsm_decode_workspace_bytes(int hidden, int intermediate, int top_k, int rank) {
   if (hidden <= 0 || intermediate <= 0 || top_k <= 0 || rank <= 0) return 0;
   return decode_ws_layout(nullptr, hidden, intermediate, top_k, rank).bytes;
+}
+
+size_t nsm_route_workspace_bytes(int hidden, int num_blocks, int top_k, int rank, int rows) {
+  if (hidden <= 0 || num_blocks <= 0 || top_k <= 0 || rank <= 0 || rows <= 0) return 0;
+  return decode_ws_layout(nullptr, hidden, num_blocks * 32, top_k, rank, rows).bytes;
 }
 
 }  // extern "C"

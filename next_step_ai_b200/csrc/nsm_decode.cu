@@ -1219,6 +1219,33 @@ int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_w
                             router_b_params(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w), s);
 }
 
+int nsm_route_rows(const void* x, int32_t x_dtype, int32_t rows, int32_t hidden, const nsm_router_weights* rw,
+                   int32_t* idx_out, float* score_out, float* latent_out, void* ws, size_t ws_bytes,
+                   nsm_stream_t stream) {
+  DeviceInfo dev;
+  int st = current_device(&dev);
+  if (st) return st;
+  st = validate_router(rw, hidden);
+  if (st) return st;
+  NSM_REQUIRE(x != nullptr && dtype_ok(x_dtype), NSM_ERR_INVALID_ARG, "x is NULL or has a bad dtype");
+  NSM_REQUIRE(rows > 0 && rows <= 65535, NSM_ERR_UNSUPPORTED, "rows must be in [1, 65535]");
+  NSM_REQUIRE(hidden > 0 && hidden % 64 == 0 && hidden <= kMaxHidden, NSM_ERR_UNSUPPORTED,
+              "hidden must be a positive multiple of 64, at most 65536");
+  NSM_REQUIRE(idx_out != nullptr, NSM_ERR_INVALID_ARG, "idx_out is NULL");
+  const int k = std::max(1, std::min(rw->top_k, rw->num_blocks));
+  NSM_REQUIRE(k <= kMaxTopK, NSM_ERR_UNSUPPORTED, "top_k too large");
+  const int I = rw->num_blocks * 32;
+  const size_t need = decode_ws_layout(nullptr, hidden, I, k, rw->rank, rows).bytes;
+  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_route_rows");
+  DecodeWs w = decode_ws_layout(ws, hidden, I, k, rw->rank, rows);
+  KernelSetup* ks;
+  st = setup_kernels(dev, &ks);
+  if (st) return st;
+  return router_rows_launch(router_a_params(x, x_dtype, nullptr, rw, hidden, w),
+                            router_b_params(rw, k, idx_out, score_out, latent_out, nullptr, rw->num_blocks, w), rows,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
 int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_t intermediate,
                           const nsm_layer_io* io, const nsm_router_weights* rw, const int32_t* idx_in, int32_t k_in,
                           const nsm_block_map* map, const nsm_mlp_weights* w, void* y, int32_t y_dtype,

@@ -98,7 +98,7 @@ struct DecodeWs {
 
 // Counters sit at fixed offsets at the head of every workspace, whatever the
 // shape, so a zeroed workspace stays valid across calls with different shapes.
-DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank);
+DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, int rank, int rows = 1);
 
 // Cached occupancy-derived persistent grid sizes.
 struct LaunchShape {

@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
       sumsq += v * v;
       if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
     } else {
-      v = load_as_f32(p.x, p.x_dtype, c);
+      v = load_as_f32(p.x, p.x_dtype, (int64_t)blockIdx.y * p.H + c);
     }
     xs[i] = v;
   }
@@ -193,9 +193,9 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
   if (tid == 0) {
     float t = 0.f;
     for (int w = 0; w < 8; ++w) t += red[w];
-    p.ws.sumsq_part[blockIdx.x] = t;
+    p.ws.sumsq_part[blockIdx.y * kRouterMaxCtas + blockIdx.x] = t;
   }
-  const int ntiles = n >> 6;
+  const int ntiles = p.multi_rows ? 0 : (n >> 6);
   for (int tl = warp; tl < ntiles; tl += 8) {
     const float a = xs[tl * 64 + lane], b = xs[tl * 64 + 32 + lane];
     const float m = warp_max(fmaxf(fabsf(a), fabsf(b)));
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
     }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-    if (q == 0 && r < p.rank) p.ws.latent_part[blockIdx.x * p.rank + r] = acc;
+    if (q == 0 && r < p.rank) p.ws.latent_part[((int64_t)blockIdx.y * kRouterMaxCtas + blockIdx.x) * p.rank + r] = acc;
   } else if (enc != nullptr) {
     // thread (row r, quarter q): columns [q*n/4, (q+1)*n/4) of this slice
     for (int r0 = 0; r0 < p.rank; r0 += 64) {
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
       }
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      if (q == 0 && r < p.rank) p.ws.latent_part[blockIdx.x * p.rank + r] = acc;
+      if (q == 0 && r < p.rank) p.ws.latent_part[((int64_t)blockIdx.y * kRouterMaxCtas + blockIdx.x) * p.rank + r] = acc;
     }
   }
   if (p.reduce_in_scores) return;  // the scores kernel reduces the partials (and advances the epoch)
@@ -431,10 +431,11 @@ __device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat
   __shared__ float half[2][kMaxRank];
   __shared__ float s_norm;
   const int tid = threadIdx.x, lane = tid & 31;
+  const float* lpart = p.ws.latent_part + (int64_t)blockIdx.y * kRouterMaxCtas * p.rank;  // row blockIdx.y
   if (tid < 32) {
     float t = 0.f;
     if (p.use_norm)
-      for (int b = lane; b < p.nparts; b += 32) t += ldcg_f32(&p.ws.sumsq_part[b]);
+      for (int b = lane; b < p.nparts; b += 32) t += ldcg_f32(&p.ws.sumsq_part[blockIdx.y * kRouterMaxCtas + b]);
     t = warp_sum(t);
     if (lane == 0) s_norm = p.use_norm ? 1.f / sqrtf(t / (float)p.H + p.eps) : 1.f;
   }
@@ -445,11 +446,11 @@ __device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat
     for (; b + 14 < p.nparts; b += 16) {
       float v[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = ldcg_f32(&p.ws.latent_part[(b + 2 * u) * p.rank + r]);
+      for (int u = 0; u < 8; ++u) v[u] = ldcg_f32(&lpart[(b + 2 * u) * p.rank + r]);
 #pragma unroll
       for (int u = 0; u < 8; ++u) acc += v[u];
     }
-    for (; b < p.nparts; b += 2) acc += ldcg_f32(&p.ws.latent_part[b * p.rank + r]);
+    for (; b < p.nparts; b += 2) acc += ldcg_f32(&lpart[b * p.rank + r]);
     half[h][r] = acc;
   }
   __syncthreads();
@@ -476,8 +477,8 @@ __device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat
     __syncthreads();
   }
   if (blockIdx.x == 0) {
-    for (int r = tid; r < p.rank; r += blockDim.x) p.ws.latent[r] = lat[r];
-    if (tid == 0) {
+    for (int r = tid; r < p.rank; r += blockDim.x) p.ws.latent[blockIdx.y * p.rank + r] = lat[r];
+    if (tid == 0 && !p.multi_rows) {
       *p.ws.norm_scale = s_norm;
       if (p.epoch_counter) *p.epoch_counter = *p.epoch_counter + 1u;  // this rank finished its exchange
     }
@@ -496,7 +497,7 @@ __global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
     __syncthreads();
   }
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b < p.NB) p.ws.scores[b] = score_row<WT>(p, lat, b);
+  if (b < p.NB) p.ws.scores[(int64_t)blockIdx.y * p.NB + b] = score_row<WT>(p, lat, b);
 }
 
 // Top-k of the block scores in one CTA of 1024 threads: radix select of the
@@ -515,7 +516,11 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   const int tid = threadIdx.x;
   const int NB = p.NB, k = p.top_k;
   const bool want_order = p.idx_out != nullptr || p.score_out != nullptr;
-  for (int i = tid; i < NB; i += blockDim.x) keys[i] = orderable(ldcg_f32(&p.ws.scores[i]));
+  const int row = p.multi_rows ? blockIdx.x : 0;
+  int32_t* idx_out = p.idx_out ? p.idx_out + (int64_t)row * k : nullptr;
+  float* score_out = p.score_out ? p.score_out + (int64_t)row * k : nullptr;
+  int* sel_idx = p.ws.sel_idx + (int64_t)row * k;
+  for (int i = tid; i < NB; i += blockDim.x) keys[i] = orderable(ldcg_f32(&p.ws.scores[(int64_t)row * NB + i]));
   if (tid == 0) {
     s_prefix = 0u;
     s_mask = 0u;
@@ -618,14 +623,15 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
         ++e;
       }
       if (s) {
-        p.ws.sel_idx[out] = i;
+        sel_idx[out] = i;
         if (ordered && out < 1024) sorted[out] = ((unsigned long long)key << 32) | (0xffffffffu - (uint32_t)i);
         ++out;
       }
     }
   }
   if (p.latent_out)
-    for (int r = tid; r < p.rank; r += blockDim.x) p.latent_out[r] = ldcg_f32(&p.ws.latent[r]);
+    for (int r = tid; r < p.rank; r += blockDim.x)
+      p.latent_out[(int64_t)row * p.rank + r] = ldcg_f32(&p.ws.latent[(int64_t)row * p.rank + r]);
   __threadfence_block();
   __syncthreads();
   if (ordered) {
@@ -653,8 +659,8 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
       for (int j = tid; j < k; j += blockDim.x) {
         const unsigned long long key = sorted[j];
         const int id = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
-        if (p.idx_out) p.idx_out[j] = id;
-        if (p.score_out) p.score_out[j] = from_orderable((uint32_t)(key >> 32));
+        if (idx_out) idx_out[j] = id;
+        if (score_out) score_out[j] = from_orderable((uint32_t)(key >> 32));
       }
     } else {
       // large k: rank of every block among all blocks (exact, slower)
@@ -666,13 +672,14 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
           pos += (kq > ki) || (kq == ki && q < i);
         }
         if (pos < k) {
-          if (p.idx_out) p.idx_out[pos] = i;
-          if (p.score_out) p.score_out[pos] = from_orderable(ki);
+          if (idx_out) idx_out[pos] = i;
+          if (score_out) score_out[pos] = from_orderable(ki);
         }
       }
     }
   }
-  compact_selection(p, p.ws.sel_idx, k);
+  if (p.multi_rows) return;  // routing only: no pool rows
+  compact_selection(p, sel_idx, k);
 }
 
 __global__ void __launch_bounds__(512) select_given_kernel(RouterBParams p, const int32_t* idx_in, int k) {
@@ -739,6 +746,41 @@ int router_b_launch(const RouterBParams& b, cudaStream_t stream) {
   }
   NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(launch_pdl(router_topk_kernel, 1, 1024, (size_t)b.NB * 4, stream, b));
+  return NSM_OK;
+}
+
+int router_rows_launch(const RouterAParams& a_in, RouterBParams b, int rows, cudaStream_t stream) {
+  int st = router_setup();
+  if (st) return st;
+  RouterAParams a = a_in;
+  int cpc;
+  const int ctas = router_a_ctas(a.H, &cpc);
+  a.cols_per_cta = cpc;
+  a.reduce_in_scores = 1;
+  a.multi_rows = rows;
+  b.multi_rows = rows;
+  b.reduce_latent = 1;
+  b.nparts = ctas;
+  b.use_norm = 0;
+  b.H = a.H;
+  b.enc_b = a.enc_b;
+  b.basis_top_k = a.basis_top_k;
+  const size_t smem = 2 * (size_t)cpc * sizeof(float);
+  const dim3 ga(ctas, rows), gb((b.NB + 127) / 128, rows);
+  cudaError_t e;
+  switch (a.wdtype) {
+    case NSM_F32: e = launch_pdl(router_latent_kernel<float>, ga, 256, smem, stream, a); break;
+    case NSM_F16: e = launch_pdl(router_latent_kernel<__half>, ga, 256, smem, stream, a); break;
+    default: e = launch_pdl(router_latent_kernel<__nv_bfloat16>, ga, 256, smem, stream, a); break;
+  }
+  NSM_CHECK_CUDA(e);
+  switch (b.wdtype) {
+    case NSM_F32: e = launch_pdl(router_scores_kernel<float>, gb, 128, 0, stream, b); break;
+    case NSM_F16: e = launch_pdl(router_scores_kernel<__half>, gb, 128, 0, stream, b); break;
+    default: e = launch_pdl(router_scores_kernel<__nv_bfloat16>, gb, 128, 0, stream, b); break;
+  }
+  NSM_CHECK_CUDA(e);
+  NSM_CHECK_CUDA(launch_pdl(router_topk_kernel, rows, 1024, (size_t)b.NB * 4, stream, b));
   return NSM_OK;
 }
 

@@ -32,6 +32,7 @@ struct RouterAParams {
   // 1: the scores kernel that follows reduces the partial latents (no last-CTA
   // reduction here); 0: the last CTA reduces them (x-prep-only launches)
   int reduce_in_scores;
+  int multi_rows;  // > 0: routing only for rows = gridDim.y (row r reads x + r*H; per-row partials; no x16)
   DecodeWs ws;
 };
 
@@ -60,6 +61,7 @@ struct RouterBParams {
   const void* enc_b;
   int basis_top_k;
   uint32_t* epoch_counter;  // exchange epoch to advance (NULL without an exchange)
+  int multi_rows;           // > 0: routing only, one row per grid y (scores) / per CTA (top-k)
   DecodeWs ws;
 };
 // CTAs of the router kernel for hidden size H (kRouterMaxCtas at most).
@@ -68,6 +70,8 @@ int router_a_ctas(int H, int* cols_per_cta);
 int router_setup();
 int router_a_launch(const RouterAParams& a, cudaStream_t stream);
 int router_b_launch(const RouterBParams& b, cudaStream_t stream);
+// Routing only for `rows` rows of x (row-major [rows][H]) into idx_out [rows][k].
+int router_rows_launch(const RouterAParams& a, RouterBParams b, int rows, cudaStream_t stream);
 int select_given_launch(const RouterBParams& b, const int32_t* idx_in, int k, cudaStream_t stream);
 
 }  // namespace nsm

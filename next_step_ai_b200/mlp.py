@@ -35,15 +35,21 @@ def route_sparse_mlp(hidden: torch.Tensor, router: RouterWeights, *, top_k: int 
     rc = router.to_c()
     router.top_k = saved_k
     dev = hidden.device
-    ws_bytes = lib.nsm_decode_workspace_bytes(H, router.num_blocks * 32, k, router.rank)
-    ws = WORKSPACES.get(ws_bytes, dev)
-    idx = torch.empty((flat.shape[0], k), dtype=torch.int32, device=dev)
-    scores = torch.empty((flat.shape[0], k), dtype=torch.float32, device=dev) if return_scores else None
+    rows = int(flat.shape[0])
+    idx = torch.empty((rows, k), dtype=torch.int32, device=dev)
+    scores = torch.empty((rows, k), dtype=torch.float32, device=dev) if return_scores else None
     st = stream_handle(dev)
-    for r in range(flat.shape[0]):
-        _lib.check(lib.nsm_route(flat[r].data_ptr(), dtype_code(flat.dtype), H, ctypes.byref(rc),
-                                 idx[r].data_ptr(), scores[r].data_ptr() if scores is not None else None, None,
-                                 ws.data_ptr(), ws.numel(), st), "nsm_route")
+    if rows == 1:
+        ws = WORKSPACES.get(lib.nsm_decode_workspace_bytes(H, router.num_blocks * 32, k, router.rank), dev)
+        _lib.check(lib.nsm_route(flat.data_ptr(), dtype_code(flat.dtype), H, ctypes.byref(rc), idx.data_ptr(),
+                                 scores.data_ptr() if scores is not None else None, None, ws.data_ptr(), ws.numel(),
+                                 st), "nsm_route")
+    elif rows > 1:
+        # all rows in three launches (latent, scores, one top-k CTA per row)
+        ws = WORKSPACES.get(lib.nsm_route_workspace_bytes(H, router.num_blocks, k, router.rank, rows), dev)
+        _lib.check(lib.nsm_route_rows(flat.data_ptr(), dtype_code(flat.dtype), rows, H, ctypes.byref(rc),
+                                      idx.data_ptr(), scores.data_ptr() if scores is not None else None, None,
+                                      ws.data_ptr(), ws.numel(), st), "nsm_route_rows")
     out = idx.long()
     return (out, scores) if return_scores else out
 

@@ -101,6 +101,37 @@ def test_router_bit_exact(dev, name, rows):
         assert np.allclose(scores.cpu().numpy(), s_ref_sel, rtol=1e-4, atol=1e-5)
 
 
+def test_router_rows_match_single_row_calls(dev):
+    """nsm_route_rows (all rows in three launches) gives, per row, the bits of
+    nsm_route on that row alone, and the oracle's indices."""
+    from next_step_ai_b200 import route_sparse_mlp
+
+    shape = syn.SHAPES["cfg1"]
+    R = syn.make_router(shape, 9)
+    rows = 37
+    x = syn.make_x(shape, 9, rows, shared=0.6)
+    rw = router_for(shape, R, dev)
+    xd = T(x, dev, torch.bfloat16)
+    got, scores = route_sparse_mlp(xd, rw, return_scores=True)
+    for r in range(rows):
+        one, s_one = route_sparse_mlp(xd[r:r + 1], rw, return_scores=True)
+        assert torch.equal(one, got[r:r + 1]), r
+        assert torch.equal(s_one, scores[r:r + 1]), r
+    ref = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)
+    assert np.array_equal(got.cpu().numpy(), ref)
+    # ties across several rows resolve to the lower block id in every row
+    H, r_, NB = 128, 8, 40
+    sb = np.zeros(NB, np.float32)
+    sb[[3, 7, 11, 30]] = 1.0
+    sb[[5, 9]] = 2.0
+    from next_step_ai_b200 import RouterWeights
+
+    tw = RouterWeights(enc_w=T(np.zeros((r_, H), np.float32), dev), score_w=T(np.zeros((NB, r_), np.float32), dev),
+                       score_b=T(sb, dev), top_k=8, basis_top_k=r_)
+    tie = route_sparse_mlp(torch.ones(5, H, device=dev), tw).cpu().numpy()
+    assert all(row.tolist() == [5, 9, 3, 7, 11, 30, 0, 1] for row in tie)
+
+
 def test_router_golden_cfg1(dev, golden):
     """Indices pinned by the reference's own _route_sparse_mlp (fp32)."""
     from next_step_ai_b200 import route_sparse_mlp
