@@ -2,24 +2,30 @@
 //
 // Pipeline of one decode step (one decoder layer, one token), all on one stream,
 // chained with programmatic dependent launch:
-//   1. router_latent_kernel   x prep (optional residual add + RMSNorm), fp16 x
-//                             with per-64-column power-of-two scales, split-H
-//                             partial latent x . enc_w^T; the last CTA reduces,
-//                             applies the norm scale, bias and basis top-k.
-//   2. router_scores_kernel   block scores clamp0(latent . score_w^T + b)
-//                             (* down_block_norm).
+//   1. router_latent_kernel   x prep (optional residual add of the previous
+//                             layer's pending output + RMSNorm), fp16 x with
+//                             per-64-column power-of-two scales, split-H
+//                             partial latents x . enc_w^T.
+//   2. router_scores_kernel   every CTA reduces the partial latents (norm scale,
+//                             bias, basis top-k), then block scores
+//                             clamp0(latent . score_w^T + b) (* down_block_norm).
 //   3. router_topk_kernel     top-k (score desc, index asc) by radix select;
 //                             compacts the selection into pool rows through
 //                             the block map (resident table or shard range).
-//   4. gateup_kernel          warps stream equal ranges of the (block, 64-column
-//                             tile) pairs: NF4 gather-GEMV of gate and up, fp32
-//                             partials per block segment.
-//   5. gateup_finalize_kernel fixed-order segment sums, SiLU(g)*u as fp16 with a
-//                             per-block power-of-two scale.
-//   6. down_kernel            warps stream equal ranges of the (32-row tile,
-//                             block) pairs: NF4 column gather-GEMV, fp32
-//                             partials per row-tile segment.
-//   7. down_finalize_kernel   fixed-order segment sums (+ bias) -> y.
+//   4. gateup_tma_kernel /    warps stream equal ranges of the (block, 64-column
+//      gateup_kernel          tile) pairs: NF4 gather-GEMV of gate and up, fp32
+//                             partials per block segment.  In the bulk-copy
+//                             variant the warp that flushes a block's last
+//                             segment sums the segments and writes SiLU(g)*u.
+//   5. gateup_finalize_kernel (register variant only) the same finalize as a
+//                             kernel: fixed-order segment sums, SiLU(g)*u as
+//                             fp16 with a per-block power-of-two scale.
+//   6. down_tma_kernel /      warps stream equal ranges of the (row group,
+//      down_kernel            block) pairs: NF4 column gather-GEMV, fp32
+//                             partials per row-group segment.
+//   7. down_finalize_kernel   fixed-order segment sums (+ bias) -> y; or, when
+//                             the output is deferred, the next layer's router
+//                             kernel sums the segments into the residual.
 // Reference semantics: streaming_llama_runtime.py:4209-4238 (latent),
 // :4311-4352 (scores/top-k), :5433-5492 (MLP math).
 #include <cuda_fp16.h>
@@ -85,6 +91,7 @@ struct GateUpParams {
   float* act_out;  // optional fp32 [k][32]
   int total_warps;
   int unit_tiles;  // tiles per stream unit (the partial segments follow the units)
+  int* gu_ticket;  // non-NULL: the warp that flushes a block's last segment finalizes it
 };
 
 // One 64-column tile of one block, both projections: w[proj][rg] holds the
@@ -253,6 +260,90 @@ __device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, 
   }
 }
 
+// RMSNorm scale, biases, mask and SiLU(gate)*up of neuron `lane` of pool row
+// s from its summed gate/up dot products; fp16 with a per-block power-of-two
+// scale (the whole warp calls this for one block).
+__device__ __forceinline__ void gu_finalize_apply(const GateUpParams& p, int s, int lane, float gsum, float usum) {
+  const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
+  gsum *= ns;
+  usum *= ns;
+  if (p.gate_bias != nullptr || p.up_bias != nullptr) {
+    const int bi = (p.bias_by_block ? __ldcg(p.row_block + s) : s) * 32 + lane;
+    if (p.gate_bias) gsum += load_as_f32(p.gate_bias, p.bias_dtype, bi);
+    if (p.up_bias) usum += load_as_f32(p.up_bias, p.bias_dtype, bi);
+  }
+  if (p.act_mask != nullptr) {
+    const float m = load_as_f32(p.act_mask, p.mask_dtype, (int64_t)s * 32 + lane);
+    gsum *= m;
+    usum *= m;
+  }
+  const float act = silu_f32(gsum) * usum;
+  if (p.act_out) p.act_out[(int64_t)s * 32 + lane] = act;
+  const float m = warp_max(fabsf(act));
+  const float sc = pow2_scale_for(m);
+  p.act16[(int64_t)s * 32 + lane] = __float2half_rn(act * (1.f / sc));
+  if (lane == 0) p.act_scale[s] = sc;
+}
+
+// Gate/up partial segments of pool row s (ups of them) summed by one warp in
+// the finalize kernel's order: segments q = q0, q0+8, ... for q0 = 0..7, then
+// the eight sums in order.
+__device__ __forceinline__ void gu_finalize_warp(const GateUpParams& p, int s, int ups, int lane) {
+  const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
+  float gsum = 0.f, usum = 0.f;
+  if (ups <= 16) {
+    float vg[16], vu[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      vg[q] = q < ups ? ldcg_f32(base + q * 64 + lane) : 0.f;
+      vu[q] = q < ups ? ldcg_f32(base + q * 64 + 32 + lane) : 0.f;
+    }
+#pragma unroll
+    for (int q0 = 0; q0 < 8; ++q0) {
+      float g8 = 0.f, u8 = 0.f;
+      if (q0 < ups) {
+        g8 += vg[q0];
+        u8 += vu[q0];
+      }
+      if (q0 + 8 < ups) {
+        g8 += vg[q0 + 8];
+        u8 += vu[q0 + 8];
+      }
+      gsum += g8;
+      usum += u8;
+    }
+  } else {
+    for (int q0 = 0; q0 < 8; ++q0) {
+      float g8 = 0.f, u8 = 0.f;
+      for (int q = q0; q < ups; q += 8) {
+        g8 += ldcg_f32(base + q * 64 + lane);
+        u8 += ldcg_f32(base + q * 64 + 32 + lane);
+      }
+      gsum += g8;
+      usum += u8;
+    }
+  }
+  gu_finalize_apply(p, s, lane, gsum, usum);
+}
+
+// After a warp flushed its segment of pool row s: count the flush; the warp
+// that completes the row's `ups` segments finalizes it (no waiting: the other
+// segments are already written) and resets the count for the next call.
+__device__ __forceinline__ void gu_ticket_after_flush(const GateUpParams& p, int s, int ups, int lane) {
+  __threadfence();  // this lane's partial stores before the count
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    last = atomicAdd(p.gu_ticket + s, 1) == ups - 1;
+    if (last) {
+      p.gu_ticket[s] = 0;
+      __threadfence();  // the other warps' partials after their counts
+    }
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) gu_finalize_warp(p, s, ups, lane);
+}
+
 // One CTA (256 threads) per block: thread (q, lane) sums the column-range
 // partials q, q+8, ... of neuron `lane` (gate and up), the 8 sums combine in
 // fixed order, then RMSNorm scale, biases, mask and SiLU(gate)*up are applied
@@ -286,25 +377,7 @@ __global__ void __launch_bounds__(256) gateup_finalize_kernel(GateUpParams p) {
     gsum += red[0][q][lane];
     usum += red[1][q][lane];
   }
-  const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
-  gsum *= ns;
-  usum *= ns;
-  if (p.gate_bias != nullptr || p.up_bias != nullptr) {
-    const int bi = (p.bias_by_block ? p.row_block[s] : s) * 32 + lane;
-    if (p.gate_bias) gsum += load_as_f32(p.gate_bias, p.bias_dtype, bi);
-    if (p.up_bias) usum += load_as_f32(p.up_bias, p.bias_dtype, bi);
-  }
-  if (p.act_mask != nullptr) {
-    const float m = load_as_f32(p.act_mask, p.mask_dtype, (int64_t)s * 32 + lane);
-    gsum *= m;
-    usum *= m;
-  }
-  const float act = silu_f32(gsum) * usum;
-  if (p.act_out) p.act_out[(int64_t)s * 32 + lane] = act;
-  const float m = warp_max(fabsf(act));
-  const float sc = pow2_scale_for(m);
-  p.act16[(int64_t)s * 32 + lane] = __float2half_rn(act * (1.f / sc));
-  if (lane == 0) p.act_scale[s] = sc;
+  gu_finalize_apply(p, s, lane, gsum, usum);
 }
 
 constexpr int kStageXMaxHidden = 16384;
@@ -701,6 +774,10 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
           xsa += UT * 4;
           if (++j == cps || q == q1) {
             gu_flush(p, s, seg, g, t, acc);
+            if (p.gu_ticket != nullptr) {
+              const int ups = stream_owner(total, nw, s * cps + cps - 1) - stream_owner(total, nw, s * cps) + 1;
+              gu_ticket_after_flush(p, s, ups, lane);
+            }
             seg = 0;  // this warp holds the first unit of the next block
             if (j == cps) {
               j = 0;
@@ -1031,6 +1108,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.unit_tiles = 1;
   if (gu_tma) {
     gp.unit_tiles = kGuUnitTiles;
+    gp.gu_ticket = ws.gu_ticket;
     gp.total_warps = dev.sm_count * kGuWarps;
     e = launch_pdl(gateup_tma_kernel, dev.sm_count, kGuThreads, kGuTmaSmem, stream, gp);
   } else {
@@ -1047,7 +1125,8 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   }
   NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(stage_event(m.events, 2, stream));
-  NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
+  // the bulk-copy kernel finalizes each block itself (its last segment's warp)
+  if (!gu_tma) NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
   NSM_CHECK_CUDA(stage_event(m.events, 3, stream));
 
   DownParams dp{};

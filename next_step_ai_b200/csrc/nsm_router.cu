@@ -422,40 +422,77 @@ __device__ __forceinline__ float score_row(const RouterBParams& p, const float* 
   return acc;
 }
 
-// Block scores, one thread per block (grid-wide; waits for the latent).
 // The router kernel's partial latents reduced in fixed order -- every scores
-// CTA computes the same values: thread (row r, half h) sums partials h, h+2,
-// ...; the halves combine, then the RMSNorm scale, enc_b and the basis top-k
-// mask apply (streaming_llama_runtime.py:4220-4238).
+// CTA computes the same values, then the RMSNorm scale, enc_b and the basis
+// top-k mask apply (streaming_llama_runtime.py:4220-4238).  Rank 64 with a
+// multiple of 8 partials (the decode shapes): thread (column quad c4, group g)
+// sums partials g, g+8, ... with all of its 16-byte loads in flight, and the 8
+// group sums combine in order; other shapes: thread (row r, half h) sums
+// partials h, h+2, ... and the halves combine.
 __device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat) {
-  __shared__ float half[2][kMaxRank];
+  __shared__ float grp[8][kMaxRank];
   __shared__ float s_norm;
   const int tid = threadIdx.x, lane = tid & 31;
   const float* lpart = p.ws.latent_part + (int64_t)blockIdx.y * kRouterMaxCtas * p.rank;  // row blockIdx.y
   if (tid < 32) {
+    const float* sp = p.ws.sumsq_part + blockIdx.y * kRouterMaxCtas;
+    float v[kRouterMaxCtas / 32];
+#pragma unroll
+    for (int u = 0; u < kRouterMaxCtas / 32; ++u) {
+      const int b = lane + 32 * u;
+      v[u] = (p.use_norm && b < p.nparts) ? ldcg_f32(sp + b) : 0.f;
+    }
     float t = 0.f;
-    if (p.use_norm)
-      for (int b = lane; b < p.nparts; b += 32) t += ldcg_f32(&p.ws.sumsq_part[blockIdx.y * kRouterMaxCtas + b]);
+#pragma unroll
+    for (int u = 0; u < kRouterMaxCtas / 32; ++u) t += v[u];
     t = warp_sum(t);
     if (lane == 0) s_norm = p.use_norm ? 1.f / sqrtf(t / (float)p.H + p.eps) : 1.f;
   }
-  for (int e = tid; e < 2 * p.rank; e += blockDim.x) {
-    const int r = e % p.rank, h = e / p.rank;
-    float acc = 0.f;
-    int b = h;
-    for (; b + 14 < p.nparts; b += 16) {
-      float v[8];
+  int ngroups;
+  if (p.rank == 64 && (p.nparts & 7) == 0 && p.nparts <= 128 && blockDim.x == 128) {
+    ngroups = 8;
+    const int c4 = tid & 15, g = tid >> 4;
+    const float4* base = reinterpret_cast<const float4*>(lpart) + c4;
+    float4 v[16];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = ldcg_f32(&lpart[(b + 2 * u) * p.rank + r]);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) acc += v[u];
+    for (int u = 0; u < 16; ++u) {
+      const int b = g + 8 * u;
+      v[u] = b < p.nparts ? __ldcg(base + b * 16) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    for (; b < p.nparts; b += 2) acc += ldcg_f32(&lpart[b * p.rank + r]);
-    half[h][r] = acc;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      a.x += v[u].x;
+      a.y += v[u].y;
+      a.z += v[u].z;
+      a.w += v[u].w;
+    }
+    grp[g][4 * c4 + 0] = a.x;
+    grp[g][4 * c4 + 1] = a.y;
+    grp[g][4 * c4 + 2] = a.z;
+    grp[g][4 * c4 + 3] = a.w;
+  } else {
+    ngroups = 2;
+    for (int e = tid; e < 2 * p.rank; e += blockDim.x) {
+      const int r = e % p.rank, h = e / p.rank;
+      float acc = 0.f;
+      int b = h;
+      for (; b + 14 < p.nparts; b += 16) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = ldcg_f32(&lpart[(b + 2 * u) * p.rank + r]);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc += v[u];
+      }
+      for (; b < p.nparts; b += 2) acc += ldcg_f32(&lpart[b * p.rank + r]);
+      grp[h][r] = acc;
+    }
   }
   __syncthreads();
   for (int r = tid; r < p.rank; r += blockDim.x) {
-    float acc = (half[0][r] + half[1][r]) * s_norm;
+    float acc = 0.f;
+    for (int g = 0; g < ngroups; ++g) acc += grp[g][r];
+    acc *= s_norm;
     if (p.enc_b != nullptr) acc += load_as_f32(p.enc_b, p.wdtype, r);
     lat[r] = acc;
   }
@@ -485,18 +522,57 @@ __device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat
   }
 }
 
+// Block scores, one thread per block (grid-wide; waits for the latent).  At
+// rank 64 with 2-byte weights the thread's score-head row is loaded before the
+// wait on the upstream kernels (weights are not written upstream).
 template <typename WT>
 __global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
   __shared__ float lat[kMaxRank];
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool pre = sizeof(WT) == 2 && p.rank == 64 && b < p.NB;
+  uint4 wrow[8];
+  if (pre) {
+    const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const WT*>(p.score_w) + (int64_t)b * 64);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wrow[i] = __ldg(row + i);
+  }
   pdl_trigger();
   pdl_wait();
   if (p.reduce_latent) {
     reduce_latent(p, lat);
   } else {
-    for (int r = threadIdx.x; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r]);
+    for (int r = threadIdx.x; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r + blockIdx.y * p.rank]);
     __syncthreads();
   }
-  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (pre) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t w4[4] = {wrow[i].x, wrow[i].y, wrow[i].z, wrow[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float lo, hi;
+        if (std::is_same<WT, __half>::value) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+          lo = f.x;
+          hi = f.y;
+        } else {
+          lo = __uint_as_float(w4[e] << 16);
+          hi = __uint_as_float(w4[e] & 0xffff0000u);
+        }
+        const int r = i * 8 + 2 * e;
+        acc = fmaf(p.legacy ? fabsf(lat[r]) : lat[r], lo, acc);
+        acc = fmaf(p.legacy ? fabsf(lat[r + 1]) : lat[r + 1], hi, acc);
+      }
+    }
+    if (!p.legacy) {
+      if (p.score_b != nullptr) acc += to_f32(reinterpret_cast<const WT*>(p.score_b)[b]);
+      acc = fmaxf(acc, 0.f);
+    }
+    if (p.dbn != nullptr) acc *= p.dbn[b];
+    p.ws.scores[(int64_t)blockIdx.y * p.NB + b] = acc;
+    return;
+  }
   if (b < p.NB) p.ws.scores[(int64_t)blockIdx.y * p.NB + b] = score_row<WT>(p, lat, b);
 }
 
@@ -509,7 +585,8 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   extern __shared__ uint32_t keys[];  // [NB]
   __shared__ int hist[256];
   __shared__ uint32_t s_prefix, s_mask;
-  __shared__ int s_need, s_bin_count;
+  __shared__ int s_need, s_bin_count, s_start;
+  __shared__ uint32_t s_or[32], s_and[32];
   __shared__ unsigned long long sorted[1024];
   pdl_trigger();
   pdl_wait();
@@ -520,15 +597,39 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   int32_t* idx_out = p.idx_out ? p.idx_out + (int64_t)row * k : nullptr;
   float* score_out = p.score_out ? p.score_out + (int64_t)row * k : nullptr;
   int* sel_idx = p.ws.sel_idx + (int64_t)row * k;
-  for (int i = tid; i < NB; i += blockDim.x) keys[i] = orderable(ldcg_f32(&p.ws.scores[(int64_t)row * NB + i]));
-  if (tid == 0) {
-    s_prefix = 0u;
-    s_mask = 0u;
-    s_need = k;
-    s_bin_count = -1;
+  // the keys' common leading bits need no pass: digits start below them
+  uint32_t kor = 0u, kand = 0xffffffffu;
+  for (int i = tid; i < NB; i += blockDim.x) {
+    const uint32_t key = orderable(ldcg_f32(&p.ws.scores[(int64_t)row * NB + i]));
+    keys[i] = key;
+    kor |= key;
+    kand &= key;
+  }
+  kor = __reduce_or_sync(0xffffffffu, kor);
+  kand = __reduce_and_sync(0xffffffffu, kand);
+  if ((tid & 31) == 0) {
+    s_or[tid >> 5] = kor;
+    s_and[tid >> 5] = kand;
   }
   __syncthreads();
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  if (tid < 32) {
+    const int nwarps = (int)(blockDim.x >> 5);
+    const uint32_t o = __reduce_or_sync(0xffffffffu, tid < nwarps ? s_or[tid] : 0u);
+    const uint32_t a = __reduce_and_sync(0xffffffffu, tid < nwarps ? s_and[tid] : 0xffffffffu);
+    if (tid == 0) {
+      const int start = 32 - __clz(o ^ a);  // low bits that differ somewhere; 0: all keys equal
+      const uint32_t hi = start >= 32 ? 0u : (0xffffffffu << start);
+      s_prefix = a & hi;
+      s_mask = hi;
+      s_need = k;
+      s_bin_count = start == 0 ? NB : -1;
+      s_start = start;
+    }
+  }
+  __syncthreads();
+  const int start = s_start;
+  for (int shift = start - 8; start > 0; shift -= 8) {
+    const int sh = max(shift, 0);  // a last digit narrower than 8 bits overlaps fixed bits (constant)
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t pre = s_prefix, msk = s_mask;
@@ -536,7 +637,7 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
       const int i = i0 + tid;
       const uint32_t key = i < NB ? keys[i] : 0u;
       const bool on = i < NB && (key & msk) == pre;
-      const uint32_t bin = on ? ((key >> shift) & 255u) : 256u;
+      const uint32_t bin = on ? ((key >> sh) & 255u) : 256u;
       const unsigned grp = __match_any_sync(0xffffffffu, bin);
       if (on && (threadIdx.x & 31) == (__ffs(grp) - 1)) atomicAdd(&hist[bin], __popc(grp));
     }
@@ -564,8 +665,8 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
         for (int e = 0; e < 8; ++e) {
           if (run < need && need <= run + c[e]) {
             const uint32_t bin = 255u - 8u * tid - e;
-            s_prefix = pre | (bin << shift);
-            s_mask = msk | (255u << shift);
+            s_prefix = (pre & ~(255u << sh)) | (bin << sh);
+            s_mask = msk | (255u << sh);
             s_need = need - run;
             s_bin_count = c[e];  // after the last pass: keys equal to the threshold
           }
@@ -574,9 +675,10 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
       }
     }
     __syncthreads();
-    // unordered selection: once the whole threshold bin is needed, every key
-    // with this prefix is selected and the lower bits do not matter
-    if (!want_order && s_need == s_bin_count) break;
+    // once the whole threshold bin is needed, every key with this prefix is
+    // selected and the lower bits do not matter (the order, when asked for,
+    // comes from the full keys)
+    if (sh == 0 || s_need == s_bin_count) break;
   }
   const uint32_t thr = s_prefix;
   const int take_eq = s_need;

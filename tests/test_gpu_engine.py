@@ -118,5 +118,5 @@ def test_engine_stage_timing(dev):
     dec.residual.copy_(_t(np.ones(shape.hidden, np.float32), dev))
     t = dec.time_stages()
     assert list(t) == list(SparseMlpDecoder.STAGES)
-    assert all(t[s] > 0 for s in ("router", "gateup", "gateup_finalize", "down")), t
-    assert t["down_finalize"] >= 0
+    assert all(t[s] > 0 for s in ("router", "gateup", "down")), t
+    assert t["gateup_finalize"] >= 0 and t["down_finalize"] >= 0  # folded into gate/up / the next layer
