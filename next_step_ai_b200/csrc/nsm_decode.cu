@@ -326,22 +326,27 @@ __device__ __forceinline__ void gu_finalize_warp(const GateUpParams& p, int s, i
   gu_finalize_apply(p, s, lane, gsum, usum);
 }
 
-// After a warp flushed its segment of pool row s: count the flush; the warp
-// that completes the row's `ups` segments finalizes it (no waiting: the other
-// segments are already written) and resets the count for the next call.
-__device__ __forceinline__ void gu_ticket_after_flush(const GateUpParams& p, int s, int ups, int lane) {
-  __threadfence();  // this lane's partial stores before the count
+// After a warp flushed its segments of pool rows [s_first, s_last]: count
+// them; the warp that completes a row's segments finalizes it (no waiting:
+// the other segments are already written) and resets the count for the next
+// call.  `ups` of a row = the warps whose ranges touch it.
+__device__ __forceinline__ void gu_tickets_after_range(const GateUpParams& p, int s_first, int s_last, int cps,
+                                                       int total, int nw, int lane) {
+  __threadfence();  // this lane's partial stores before the counts
   __syncwarp();
-  int last = 0;
-  if (lane == 0) {
-    last = atomicAdd(p.gu_ticket + s, 1) == ups - 1;
-    if (last) {
-      p.gu_ticket[s] = 0;
-      __threadfence();  // the other warps' partials after their counts
+  for (int s = s_first; s <= s_last; ++s) {
+    const int ups = stream_owner(total, nw, s * cps + cps - 1) - stream_owner(total, nw, s * cps) + 1;
+    int last = 0;
+    if (lane == 0) {
+      last = atomicAdd(p.gu_ticket + s, 1) == ups - 1;
+      if (last) {
+        p.gu_ticket[s] = 0;
+        __threadfence();  // the other warps' partials after their counts
+      }
     }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) gu_finalize_warp(p, s, ups, lane);
   }
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) gu_finalize_warp(p, s, ups, lane);
 }
 
 // One CTA (256 threads) per block: thread (q, lane) sums the column-range
@@ -774,10 +779,6 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
           xsa += UT * 4;
           if (++j == cps || q == q1) {
             gu_flush(p, s, seg, g, t, acc);
-            if (p.gu_ticket != nullptr) {
-              const int ups = stream_owner(total, nw, s * cps + cps - 1) - stream_owner(total, nw, s * cps) + 1;
-              gu_ticket_after_flush(p, s, ups, lane);
-            }
             seg = 0;  // this warp holds the first unit of the next block
             if (j == cps) {
               j = 0;
@@ -794,6 +795,11 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
   if (!ok) {
     record_error(p.err, NSM_ERR_TIMEOUT);
     drain_ring<kGuStages>(wbar, q - q0, issued);
+  } else if (p.gu_ticket != nullptr) {
+    // count this warp's flushed segments once its whole range is done (one
+    // fence for all of them, off the streaming loop); the warp completing a
+    // block's segments finalizes it
+    gu_tickets_after_range(p, q0 / cps, (q1 - 1) / cps, cps, total, nw, lane);
   }
 }
 
