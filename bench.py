@@ -52,7 +52,7 @@ def gateup_bytes_per_launch(k: int = TOP_K, H: int = HIDDEN) -> int:
 
 # DRAM bytes (read + write) of one gateup_tma_kernel launch at this workload, from one
 # ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; profiles/gateup_tma_kernel_cfg1.txt)
-GATEUP_DRAM_BYTES_PER_LAUNCH = 122_789_888 + 3_802_112
+GATEUP_DRAM_BYTES_PER_LAUNCH = 122_787_840 + 5_259_776
 
 
 def peaks() -> dict:
