@@ -73,8 +73,6 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   w.err = tick ? tick + 2 : nullptr;
   w.down_meta = tick ? tick + 3 : nullptr;
   w.count = tick ? tick + 5 : nullptr;
-  w.gu_ticket = tick ? tick + 8 : nullptr;
-  static_assert(8 + kMaxTopK <= kCounterInts, "gate/up tickets must fit in the counter head");
   // the down partials sit at a fixed offset too: a layer's pending output is
   // read by the next call, whose router may have a different k or rank
   w.ypart = reinterpret_cast<float*>(take((size_t)kMaxSlotGroups * hidden * sizeof(float)));

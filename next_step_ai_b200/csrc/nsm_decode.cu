@@ -14,12 +14,9 @@
 //                             the block map (resident table or shard range).
 //   4. gateup_tma_kernel /    warps stream equal ranges of the (block, 64-column
 //      gateup_kernel          tile) pairs: NF4 gather-GEMV of gate and up, fp32
-//                             partials per block segment.  In the bulk-copy
-//                             variant the warp that flushes a block's last
-//                             segment sums the segments and writes SiLU(g)*u.
-//   5. gateup_finalize_kernel (register variant only) the same finalize as a
-//                             kernel: fixed-order segment sums, SiLU(g)*u as
-//                             fp16 with a per-block power-of-two scale.
+//                             partials per block segment.
+//   5. gateup_finalize_kernel fixed-order segment sums, SiLU(g)*u as fp16 with a
+//                             per-block power-of-two scale.
 //   6. down_tma_kernel /      warps stream equal ranges of the (row group,
 //      down_kernel            block) pairs: NF4 column gather-GEMV, fp32
 //                             partials per row-group segment.
@@ -91,7 +88,6 @@ struct GateUpParams {
   float* act_out;  // optional fp32 [k][32]
   int total_warps;
   int unit_tiles;  // tiles per stream unit (the partial segments follow the units)
-  int* gu_ticket;  // non-NULL: the warp that flushes a block's last segment finalizes it
 };
 
 // One 64-column tile of one block, both projections: w[proj][rg] holds the
@@ -283,70 +279,6 @@ __device__ __forceinline__ void gu_finalize_apply(const GateUpParams& p, int s, 
   const float sc = pow2_scale_for(m);
   p.act16[(int64_t)s * 32 + lane] = __float2half_rn(act * (1.f / sc));
   if (lane == 0) p.act_scale[s] = sc;
-}
-
-// Gate/up partial segments of pool row s (ups of them) summed by one warp in
-// the finalize kernel's order: segments q = q0, q0+8, ... for q0 = 0..7, then
-// the eight sums in order.
-__device__ __forceinline__ void gu_finalize_warp(const GateUpParams& p, int s, int ups, int lane) {
-  const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
-  float gsum = 0.f, usum = 0.f;
-  if (ups <= 16) {
-    float vg[16], vu[16];
-#pragma unroll
-    for (int q = 0; q < 16; ++q) {
-      vg[q] = q < ups ? ldcg_f32(base + q * 64 + lane) : 0.f;
-      vu[q] = q < ups ? ldcg_f32(base + q * 64 + 32 + lane) : 0.f;
-    }
-#pragma unroll
-    for (int q0 = 0; q0 < 8; ++q0) {
-      float g8 = 0.f, u8 = 0.f;
-      if (q0 < ups) {
-        g8 += vg[q0];
-        u8 += vu[q0];
-      }
-      if (q0 + 8 < ups) {
-        g8 += vg[q0 + 8];
-        u8 += vu[q0 + 8];
-      }
-      gsum += g8;
-      usum += u8;
-    }
-  } else {
-    for (int q0 = 0; q0 < 8; ++q0) {
-      float g8 = 0.f, u8 = 0.f;
-      for (int q = q0; q < ups; q += 8) {
-        g8 += ldcg_f32(base + q * 64 + lane);
-        u8 += ldcg_f32(base + q * 64 + 32 + lane);
-      }
-      gsum += g8;
-      usum += u8;
-    }
-  }
-  gu_finalize_apply(p, s, lane, gsum, usum);
-}
-
-// After a warp flushed its segments of pool rows [s_first, s_last]: count
-// them; the warp that completes a row's segments finalizes it (no waiting:
-// the other segments are already written) and resets the count for the next
-// call.  `ups` of a row = the warps whose ranges touch it.
-__device__ __forceinline__ void gu_tickets_after_range(const GateUpParams& p, int s_first, int s_last, int cps,
-                                                       int total, int nw, int lane) {
-  __threadfence();  // this lane's partial stores before the counts
-  __syncwarp();
-  for (int s = s_first; s <= s_last; ++s) {
-    const int ups = stream_owner(total, nw, s * cps + cps - 1) - stream_owner(total, nw, s * cps) + 1;
-    int last = 0;
-    if (lane == 0) {
-      last = atomicAdd(p.gu_ticket + s, 1) == ups - 1;
-      if (last) {
-        p.gu_ticket[s] = 0;
-        __threadfence();  // the other warps' partials after their counts
-      }
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) gu_finalize_warp(p, s, ups, lane);
-  }
 }
 
 // One CTA (256 threads) per block: thread (q, lane) sums the column-range
@@ -795,11 +727,6 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
   if (!ok) {
     record_error(p.err, NSM_ERR_TIMEOUT);
     drain_ring<kGuStages>(wbar, q - q0, issued);
-  } else if (p.gu_ticket != nullptr) {
-    // count this warp's flushed segments once its whole range is done (one
-    // fence for all of them, off the streaming loop); the warp completing a
-    // block's segments finalizes it
-    gu_tickets_after_range(p, q0 / cps, (q1 - 1) / cps, cps, total, nw, lane);
   }
 }
 
@@ -1114,7 +1041,6 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.unit_tiles = 1;
   if (gu_tma) {
     gp.unit_tiles = kGuUnitTiles;
-    gp.gu_ticket = ws.gu_ticket;
     gp.total_warps = dev.sm_count * kGuWarps;
     e = launch_pdl(gateup_tma_kernel, dev.sm_count, kGuThreads, kGuTmaSmem, stream, gp);
   } else {
@@ -1131,8 +1057,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   }
   NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(stage_event(m.events, 2, stream));
-  // the bulk-copy kernel finalizes each block itself (its last segment's warp)
-  if (!gu_tma) NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
+  NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
   NSM_CHECK_CUDA(stage_event(m.events, 3, stream));
 
   DownParams dp{};

@@ -75,7 +75,6 @@ struct DecodeWs {
   int* ticket_router_b;          // [1]
   int* err;                      // [1] device-side error code (0 = none), sticky
   int* down_meta;                // [2] last down launch: total warps, log2 rows per reduction group
-  int* gu_ticket;                // [kMaxTopK] gate/up segments flushed per pool row (back to 0 after use)
   // (count below and ypart live at fixed offsets after the counter head)
   // router
   float* latent_part;            // [kRouterMaxCtas][rank]

@@ -127,21 +127,14 @@ class SparseMlpDecoder:
                    "nsm_residual_flush")
 
     # kernels per layer: router latent (+ previous layer's output), block scores,
-    # top-k, gate/up, gate/up reduction, down; plus one output kernel per token.
-    # The bulk-copy gate/up kernel (tiled pools, H <= 16384, H/64 even) does the
-    # gate/up reduction itself: one kernel fewer.
+    # top-k, gate/up, gate/up reduction, down; plus one output kernel per token
     KERNELS_PER_LAYER = 6
-
-    def _kernels_for(self, li: int) -> int:
-        w = self.layers[li].weights
-        bulk = (w.layout & _lib.NSM_LAYOUT_GATEUP_TILED) and self.H <= 16384 and (self.H // 64) % 2 == 0
-        return self.KERNELS_PER_LAYER - (1 if bulk else 0)
 
     @property
     def kernels_per_step(self) -> int:
         """This library's kernel launches per token (the final copy to ``out``
         is not counted)."""
-        return sum(self._kernels_for(i % len(self.layers)) for i in range(self.num_layers)) + 1
+        return self.KERNELS_PER_LAYER * self.num_layers + 1
 
     def step_eager(self) -> None:
         """One token through all layers (no graph).  Input: ``residual``;
