@@ -136,6 +136,8 @@ __device__ __forceinline__ void exchange_chunk(const RouterAParams& p, int c0, i
   __syncthreads();
 }
 
+constexpr int kLatentRowsPerCta = 32;
+
 template <typename WT>
 __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) {
   extern __shared__ float xs[];  // [cols_per_cta] x slice | [cols_per_cta] pending output
@@ -171,87 +173,113 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
       exchange_chunk(p, c0, n, ybuf, epoch);
     }
   }
-  float sumsq = 0.f;
-  for (int i = tid; i < n; i += blockDim.x) {
-    const int c = c0 + i;
-    float v;
-    if (p.residual != nullptr) {
-      v = p.residual[c];
-      if (p.pending) v += ybuf[i];
-      else if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
-      p.residual[c] = v;
-      sumsq += v * v;
-      if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
-    } else {
-      v = load_as_f32(p.x, p.x_dtype, (int64_t)blockIdx.y * p.H + c);
-    }
-    xs[i] = v;
-  }
-  sumsq = warp_sum(sumsq);
-  if (lane == 0) red[warp] = sumsq;
-  __syncthreads();
-  if (tid == 0) {
-    float t = 0.f;
-    for (int w = 0; w < 8; ++w) t += red[w];
-    p.ws.sumsq_part[blockIdx.y * kRouterMaxCtas + blockIdx.x] = t;
-  }
-  const int ntiles = p.multi_rows ? 0 : (n >> 6);
-  for (int tl = warp; tl < ntiles; tl += 8) {
-    const float a = xs[tl * 64 + lane], b = xs[tl * 64 + 32 + lane];
-    const float m = warp_max(fmaxf(fabsf(a), fabsf(b)));
-    const float s = pow2_scale_for(m);
-    const float inv = 1.f / s;
-    const int c = c0 + tl * 64;
-    p.ws.x16[c + lane] = __float2half_rn(a * inv);
-    p.ws.x16[c + 32 + lane] = __float2half_rn(b * inv);
-    if (lane == 0) p.ws.xscale[c >> 6] = s;
-  }
-  if (fast) {
-    const int r = tid >> 2, q = tid & 3;
-    float acc = 0.f;
-    if (r < p.rank) {
+  // rows of x this CTA handles: one, or (multi-row routing) up to
+  // kLatentRowsPerCta, whose slices are loaded together and then multiplied
+  // by the encoder slice held in registers, one row after the other
+  const int row0 = p.multi_rows ? blockIdx.y * kLatentRowsPerCta : 0;
+  const int row1 = p.multi_rows ? min(p.multi_rows, row0 + kLatentRowsPerCta) : 1;
+  if (p.multi_rows) {
+    const int total = (row1 - row0) * n;
+    for (int i0 = 0; i0 < total; i0 += 16 * (int)blockDim.x) {
+      float v[16];  // 16 loads in flight per thread
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t w4[4] = {pre[i].x, pre[i].y, pre[i].z, pre[i].w};
+      for (int u = 0; u < 16; ++u) {
+        const int i = i0 + u * (int)blockDim.x + tid, rr = i / n;
+        v[u] = i < total ? load_as_f32(p.x, p.x_dtype, (int64_t)(row0 + rr) * p.H + c0 + (i - rr * n)) : 0.f;
+      }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float lo, hi;
-          if (sizeof(WT) == 2 && std::is_same<WT, __half>::value) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
-            lo = f.x;
-            hi = f.y;
-          } else {
-            lo = __uint_as_float(w4[e] << 16);
-            hi = __uint_as_float(w4[e] & 0xffff0000u);
-          }
-          acc = fmaf(lo, xs[q * seg + i * 8 + 2 * e], acc);
-          acc = fmaf(hi, xs[q * seg + i * 8 + 2 * e + 1], acc);
-        }
+      for (int u = 0; u < 16; ++u) {
+        const int i = i0 + u * (int)blockDim.x + tid;
+        if (i < total) xs[i] = v[u];
       }
     }
-    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-    if (q == 0 && r < p.rank) p.ws.latent_part[((int64_t)blockIdx.y * kRouterMaxCtas + blockIdx.x) * p.rank + r] = acc;
-  } else if (enc != nullptr) {
-    // thread (row r, quarter q): columns [q*n/4, (q+1)*n/4) of this slice
-    for (int r0 = 0; r0 < p.rank; r0 += 64) {
-      const int r = r0 + (tid >> 2), q = tid & 3;
+    __syncthreads();
+  }
+  for (int row = row0; row < row1; ++row) {
+    const float* xr = xs + (row - row0) * n;  // this row's slice
+    if (!p.multi_rows) {
+      float sumsq = 0.f;
+      for (int i = tid; i < n; i += blockDim.x) {
+        const int c = c0 + i;
+        float v;
+        if (p.residual != nullptr) {
+          v = p.residual[c];
+          if (p.pending) v += ybuf[i];
+          else if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
+          p.residual[c] = v;
+          sumsq += v * v;
+          if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
+        } else {
+          v = load_as_f32(p.x, p.x_dtype, (int64_t)row * p.H + c);
+        }
+        xs[i] = v;
+      }
+      sumsq = warp_sum(sumsq);
+      if (lane == 0) red[warp] = sumsq;
+      __syncthreads();
+      if (tid == 0) {
+        float t = 0.f;
+        for (int w = 0; w < 8; ++w) t += red[w];
+        p.ws.sumsq_part[row * kRouterMaxCtas + blockIdx.x] = t;
+      }
+      for (int tl = warp; tl < (n >> 6); tl += 8) {
+        const float a = xs[tl * 64 + lane], b = xs[tl * 64 + 32 + lane];
+        const float m = warp_max(fmaxf(fabsf(a), fabsf(b)));
+        const float s = pow2_scale_for(m);
+        const float inv = 1.f / s;
+        const int c = c0 + tl * 64;
+        p.ws.x16[c + lane] = __float2half_rn(a * inv);
+        p.ws.x16[c + 32 + lane] = __float2half_rn(b * inv);
+        if (lane == 0) p.ws.xscale[c >> 6] = s;
+      }
+    }
+    if (fast) {
+      const int r = tid >> 2, q = tid & 3;
       float acc = 0.f;
       if (r < p.rank) {
-        const WT* row = enc + (int64_t)r * p.H + c0 + q * seg;
-        for (int i = 0; i < seg; i += 16) {
-          float a[8], b[8];
-          Vec8<WT>::load(row + i, a);
-          Vec8<WT>::load(row + i + 8, b);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(a[e], xs[q * seg + i + e], acc);
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t w4[4] = {pre[i].x, pre[i].y, pre[i].z, pre[i].w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(b[e], xs[q * seg + i + 8 + e], acc);
+          for (int e = 0; e < 4; ++e) {
+            float lo, hi;
+            if (sizeof(WT) == 2 && std::is_same<WT, __half>::value) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[e]));
+              lo = f.x;
+              hi = f.y;
+            } else {
+              lo = __uint_as_float(w4[e] << 16);
+              hi = __uint_as_float(w4[e] & 0xffff0000u);
+            }
+            acc = fmaf(lo, xr[q * seg + i * 8 + 2 * e], acc);
+            acc = fmaf(hi, xr[q * seg + i * 8 + 2 * e + 1], acc);
+          }
         }
       }
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      if (q == 0 && r < p.rank) p.ws.latent_part[((int64_t)blockIdx.y * kRouterMaxCtas + blockIdx.x) * p.rank + r] = acc;
+      if (q == 0 && r < p.rank) p.ws.latent_part[((int64_t)row * kRouterMaxCtas + blockIdx.x) * p.rank + r] = acc;
+    } else if (enc != nullptr) {
+      // thread (row r, quarter q): columns [q*n/4, (q+1)*n/4) of this slice
+      for (int r0 = 0; r0 < p.rank; r0 += 64) {
+        const int r = r0 + (tid >> 2), q = tid & 3;
+        float acc = 0.f;
+        if (r < p.rank) {
+          const WT* erow = enc + (int64_t)r * p.H + c0 + q * seg;
+          for (int i = 0; i < seg; i += 16) {
+            float a[8], b[8];
+            Vec8<WT>::load(erow + i, a);
+            Vec8<WT>::load(erow + i + 8, b);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc = fmaf(a[e], xr[q * seg + i + e], acc);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc = fmaf(b[e], xr[q * seg + i + 8 + e], acc);
+          }
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        if (q == 0 && r < p.rank) p.ws.latent_part[((int64_t)row * kRouterMaxCtas + blockIdx.x) * p.rank + r] = acc;
+      }
     }
   }
   if (p.reduce_in_scores) return;  // the scores kernel reduces the partials (and advances the epoch)
@@ -867,8 +895,8 @@ int router_rows_launch(const RouterAParams& a_in, RouterBParams b, int rows, cud
   b.H = a.H;
   b.enc_b = a.enc_b;
   b.basis_top_k = a.basis_top_k;
-  const size_t smem = 2 * (size_t)cpc * sizeof(float);
-  const dim3 ga(ctas, rows), gb((b.NB + 127) / 128, rows);
+  const size_t smem = (size_t)std::min(rows, kLatentRowsPerCta) * cpc * sizeof(float);
+  const dim3 ga(ctas, (rows + kLatentRowsPerCta - 1) / kLatentRowsPerCta), gb((b.NB + 127) / 128, rows);
   cudaError_t e;
   switch (a.wdtype) {
     case NSM_F32: e = launch_pdl(router_latent_kernel<float>, ga, 256, smem, stream, a); break;

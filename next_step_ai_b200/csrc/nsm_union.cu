@@ -132,9 +132,19 @@ __global__ void __launch_bounds__(1024) union_build_kernel(UnionBuildParams p) {
   pdl_wait();
   for (int b = threadIdx.x; b < p.NB; b += blockDim.x) rowbits[b] = 0u;
   __syncthreads();
-  for (int i = threadIdx.x; i < p.rows * p.k; i += blockDim.x) {
-    const int b = p.idx[i];
-    if (b >= 0 && b < p.NB) atomicOr(&rowbits[b], 1u << (i / p.k));
+  const int nidx = p.rows * p.k;
+  for (int i0 = 0; i0 < nidx; i0 += 8 * (int)blockDim.x) {
+    int bv[8];  // 8 loads in flight per thread
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * (int)blockDim.x + (int)threadIdx.x;
+      bv[u] = i < nidx ? p.idx[i] : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * (int)blockDim.x + (int)threadIdx.x;
+      if (bv[u] >= 0 && bv[u] < p.NB) atomicOr(&rowbits[bv[u]], 1u << (i / p.k));
+    }
   }
   __syncthreads();
   // ascending compaction of the selected blocks present in the pool
@@ -161,23 +171,47 @@ __global__ void __launch_bounds__(1024) union_build_kernel(UnionBuildParams p) {
 // ---------------------------------------------------------------------------
 // token prep
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) union_x_kernel(const void* x, int x_dtype, int rows, int H, UnionWs ws) {
-  __shared__ float red[8];
+// One CTA per token: the row's values stay in registers between the max and
+// the conversion (16 per thread at H <= 16384; longer rows are read twice).
+constexpr int kUxThreads = 1024, kUxPer = 16;
+__global__ void __launch_bounds__(kUxThreads) union_x_kernel(const void* x, int x_dtype, int rows, int H, UnionWs ws) {
+  __shared__ float red[kUxThreads / 32];
   pdl_trigger();
   pdl_wait();
   const int r = blockIdx.x;
+  const int64_t base = (int64_t)r * H;
+  float v[kUxPer];
   float m = 0.f;
-  if (r < rows)
-    for (int c = threadIdx.x; c < H; c += blockDim.x) m = fmaxf(m, fabsf(load_as_f32(x, x_dtype, (int64_t)r * H + c)));
+  for (int c0 = 0; c0 < H; c0 += kUxThreads * kUxPer) {
+#pragma unroll
+    for (int i = 0; i < kUxPer; ++i) {
+      const int c = c0 + i * kUxThreads + threadIdx.x;
+      v[i] = (r < rows && c < H) ? load_as_f32(x, x_dtype, base + c) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < kUxPer; ++i) m = fmaxf(m, fabsf(v[i]));
+  }
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   float mm = 0.f;
-  for (int w = 0; w < 8; ++w) mm = fmaxf(mm, red[w]);
+  for (int w = 0; w < kUxThreads / 32; ++w) mm = fmaxf(mm, red[w]);
   const float sc = pow2_scale_for(mm);
   const float inv = 1.f / sc;
-  for (int c = threadIdx.x; c < H; c += blockDim.x)
-    ws.x16[(int64_t)r * H + c] = __float2half_rn(r < rows ? load_as_f32(x, x_dtype, (int64_t)r * H + c) * inv : 0.f);
+  for (int c0 = 0; c0 < H; c0 += kUxThreads * kUxPer) {
+    if (H > kUxThreads * kUxPer) {  // reload (the registers hold the last chunk only)
+#pragma unroll
+      for (int i = 0; i < kUxPer; ++i) {
+        const int c = c0 + i * kUxThreads + threadIdx.x;
+        v[i] = (r < rows && c < H) ? load_as_f32(x, x_dtype, base + c) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kUxPer; ++i) {
+      const int c = c0 + i * kUxThreads + threadIdx.x;
+      if (c < H) ws.x16[base + c] = __float2half_rn(v[i] * inv);
+    }
+  }
   if (threadIdx.x == 0) ws.xscale[r] = r < rows ? sc : 1.f;
 }
 
@@ -278,9 +312,21 @@ __device__ __forceinline__ void union_gateup_body(const UnionMlpParams& p, uint3
       for (int c = 0; c < 4; ++c)
 #pragma unroll
         for (int d = 0; d < 4; ++d) acc[a][b][c][d] = 0.f;
+  // register double buffer: the next tile's weights and x fragments are in
+  // flight while this tile's MMAs run
   UTile cur, nxt;
+  uint4 xc[4][2], xn[4][2];
+  auto load_x = [&](int jj, uint4 (&xf)[4][2]) {
+#pragma unroll
+    for (int grp = 0; grp < 4; ++grp) {
+      const __half* xr = p.ws.x16 + (int64_t)(grp * 8 + g) * p.H + jj * 64 + t * 16;
+      xf[grp][0] = ldg_u4(xr);
+      xf[grp][1] = ldg_u4(xr + 8);
+    }
+  };
   int prow = __ldcg(p.ws.u_rows + s);
   union_tile_load(p, prow, j, lane, cur);
+  load_x(j, xc);
   for (int q = q0; q < q1; ++q) {
     int sn = s, jn = j + 1;
     if (jn == tpr) { jn = 0; ++sn; }
@@ -288,14 +334,13 @@ __device__ __forceinline__ void union_gateup_body(const UnionMlpParams& p, uint3
     if (q + 1 < q1) {
       if (sn != s) prow_n = __ldcg(p.ws.u_rows + sn);
       union_tile_load(p, prow_n, jn, lane, nxt);
+      load_x(jn, xn);
     }
     uint32_t xb[4][8];
 #pragma unroll
     for (int grp = 0; grp < 4; ++grp) {
-      const __half* xr = p.ws.x16 + (int64_t)(grp * 8 + g) * p.H + j * 64 + t * 16;
-      const uint4 a = ldg_u4(xr), b = ldg_u4(xr + 8);
-      xb[grp][0] = a.x; xb[grp][1] = a.y; xb[grp][2] = a.z; xb[grp][3] = a.w;
-      xb[grp][4] = b.x; xb[grp][5] = b.y; xb[grp][6] = b.z; xb[grp][7] = b.w;
+      xb[grp][0] = xc[grp][0].x; xb[grp][1] = xc[grp][0].y; xb[grp][2] = xc[grp][0].z; xb[grp][3] = xc[grp][0].w;
+      xb[grp][4] = xc[grp][1].x; xb[grp][5] = xc[grp][1].y; xb[grp][6] = xc[grp][1].z; xb[grp][7] = xc[grp][1].w;
     }
     union_tile_mma<kBase>(cur, xb, lb, acc);
     if (q + 1 == q1 || sn != s) {
@@ -319,6 +364,11 @@ __device__ __forceinline__ void union_gateup_body(const UnionMlpParams& p, uint3
     j = jn;
     prow = prow_n;
     cur = nxt;
+#pragma unroll
+    for (int grp = 0; grp < 4; ++grp) {
+      xc[grp][0] = xn[grp][0];
+      xc[grp][1] = xn[grp][1];
+    }
   }
 }
 
@@ -348,10 +398,18 @@ __global__ void __launch_bounds__(1024) union_act_kernel(UnionMlpParams p) {
   const int nseg = stream_owner(total, nw, s * tpr + tpr - 1) - stream_owner(total, nw, s * tpr) + 1;
   const float* base = p.ws.gu_part + (int64_t)s * kUnionGuMaxSeg * (2 * kUnionRows * 32);
   float g = 0.f, u = 0.f;
-  for (int q = 0; q < nseg; ++q) {
-    g += __ldcg(base + ((int64_t)q * 2 * kUnionRows + tok) * 32 + row);
-    u += __ldcg(base + ((int64_t)q * 2 * kUnionRows + kUnionRows + tok) * 32 + row);
+  float vg[kUnionGuMaxSeg], vu[kUnionGuMaxSeg];  // all segment loads in flight, summed in order
+#pragma unroll
+  for (int q = 0; q < kUnionGuMaxSeg; ++q) {
+    vg[q] = q < nseg ? __ldcg(base + ((int64_t)q * 2 * kUnionRows + tok) * 32 + row) : 0.f;
+    vu[q] = q < nseg ? __ldcg(base + ((int64_t)q * 2 * kUnionRows + kUnionRows + tok) * 32 + row) : 0.f;
   }
+#pragma unroll
+  for (int q = 0; q < kUnionGuMaxSeg; ++q)
+    if (q < nseg) {
+      g += vg[q];
+      u += vu[q];
+    }
   const float xs = __ldcg(p.ws.xscale + tok);
   g *= xs;
   u *= xs;
@@ -459,7 +517,13 @@ __global__ void __launch_bounds__(256) union_y_kernel(UnionMlpParams p) {
     const int RT = p.H >> 5, rt = h >> 5, total = RT * count;
     const int nw = stream_warps(RT, count, kUnionDnMaxSeg, p.total_warps);
     const int nseg = stream_owner(total, nw, rt * count + count - 1) - stream_owner(total, nw, rt * count) + 1;
-    for (int q = 0; q < nseg; ++q) y += __ldcg(p.ws.ypart + ((int64_t)q * p.H + h) * kUnionRows + tok);
+    float v[kUnionDnMaxSeg];  // all segment loads in flight, summed in order
+#pragma unroll
+    for (int q = 0; q < kUnionDnMaxSeg; ++q)
+      v[q] = q < nseg ? __ldcg(p.ws.ypart + ((int64_t)q * p.H + h) * kUnionRows + tok) : 0.f;
+#pragma unroll
+    for (int q = 0; q < kUnionDnMaxSeg; ++q)
+      if (q < nseg) y += v[q];
   }
   if (tok < p.rows) store_from_f32(p.y, p.y_dtype, (int64_t)tok * p.H + h, y);
 }
@@ -545,7 +609,8 @@ int nsm_union_decode(const void* x, int32_t x_dtype, int32_t rows, int32_t hidde
   bp.ws = wsl;
   bp.union_out = union_out;
   NSM_CHECK_CUDA(launch_pdl(union_build_kernel, 1, 1024, (size_t)NB * 4, s, bp));
-  NSM_CHECK_CUDA(launch_pdl(union_x_kernel, kUnionRows, 256, 0, s, x, (int)x_dtype, (int)rows, (int)hidden, wsl));
+  NSM_CHECK_CUDA(
+      launch_pdl(union_x_kernel, kUnionRows, kUxThreads, 0, s, x, (int)x_dtype, (int)rows, (int)hidden, wsl));
 
   UnionMlpParams p{};
   p.gate = w->gate_packed;
