@@ -73,6 +73,31 @@ struct Vec8<float> {
 // down kernel's segments (the down launch records its warp count and row-group
 // size in ws.down_meta; the segment arithmetic mirrors the down kernels').
 __device__ __forceinline__ void pending_output(const RouterAParams& p, int c0, int n, float* ybuf) {
+  if (n <= (int)blockDim.x) {
+    // one column per thread: every segment's word is requested together with
+    // the selection count and the down launch's shape (one round trip); the
+    // segments past this group's count are ignored
+    const int i = threadIdx.x, c = c0 + i;
+    const int count = ldcg_i32(p.ws.count);
+    const int nw_down = ldcg_i32(p.ws.down_meta), glog = ldcg_i32(p.ws.down_meta + 1);
+    float v[kMaxSlotGroups];
+#pragma unroll
+    for (int q = 0; q < kMaxSlotGroups; ++q) v[q] = i < n ? ldcg_f32(p.ws.ypart + (int64_t)q * p.H + c) : 0.f;
+    if (i < n) {
+      float y = 0.f;
+      if (count > 0 && nw_down > 0) {
+        const int G = p.H >> glog, g = c >> glog, total = G * count;
+        const int nw = stream_warps(G, count, kMaxSlotGroups, nw_down);
+        const int nseg = stream_owner(total, nw, g * count + count - 1) - stream_owner(total, nw, g * count) + 1;
+#pragma unroll
+        for (int q = 0; q < kMaxSlotGroups; ++q)
+          if (q < nseg) y += v[q];
+      }
+      ybuf[i] = y;
+    }
+    __syncthreads();
+    return;
+  }
   const int count = ldcg_i32(p.ws.count);
   const int nw_down = ldcg_i32(p.ws.down_meta), glog = ldcg_i32(p.ws.down_meta + 1);
   const int G = p.H >> glog;
@@ -162,8 +187,16 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
       for (int i = 0; i < 4; ++i) pre[i] = __ldg(row + i);
     }
   }
+  // this thread's RMSNorm weight (a layer weight, not written upstream)
+  const bool one_col = !p.multi_rows && n <= (int)blockDim.x;  // one column per thread (always, H <= 65536)
+  float nwv = 1.f;
+  if (one_col && tid < n && p.residual != nullptr && p.norm_w != nullptr)
+    nwv = load_as_f32(p.norm_w, p.norm_w_dtype, c0 + tid);
   pdl_trigger();
   pdl_wait();  // residual / x / y_prev come from earlier kernels
+  // the residual load goes out together with the pending-output loads
+  float res = 0.f;
+  if (one_col && tid < n && p.residual != nullptr) res = p.residual[c0 + tid];
   float* ybuf = xs + p.cols_per_cta;  // [cols_per_cta]: the pending output of the previous layer
   uint32_t epoch = 0;
   if (p.pending) {
@@ -203,12 +236,12 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
         const int c = c0 + i;
         float v;
         if (p.residual != nullptr) {
-          v = p.residual[c];
+          v = one_col ? res : p.residual[c];
           if (p.pending) v += ybuf[i];
           else if (p.y_prev != nullptr) v += load_as_f32(p.y_prev, p.y_prev_dtype, c);
           p.residual[c] = v;
           sumsq += v * v;
-          if (p.norm_w != nullptr) v *= load_as_f32(p.norm_w, p.norm_w_dtype, c);
+          if (p.norm_w != nullptr) v *= one_col ? nwv : load_as_f32(p.norm_w, p.norm_w_dtype, c);
         } else {
           v = load_as_f32(p.x, p.x_dtype, (int64_t)row * p.H + c);
         }
@@ -457,7 +490,7 @@ __device__ __forceinline__ float score_row(const RouterBParams& p, const float* 
 // sums partials g, g+8, ... with all of its 16-byte loads in flight, and the 8
 // group sums combine in order; other shapes: thread (row r, half h) sums
 // partials h, h+2, ... and the halves combine.
-__device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat) {
+__device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat, float enc_b_own = 0.f) {
   __shared__ float grp[8][kMaxRank];
   __shared__ float s_norm;
   const int tid = threadIdx.x, lane = tid & 31;
@@ -521,7 +554,8 @@ __device__ __forceinline__ void reduce_latent(const RouterBParams& p, float* lat
     float acc = 0.f;
     for (int g = 0; g < ngroups; ++g) acc += grp[g][r];
     acc *= s_norm;
-    if (p.enc_b != nullptr) acc += load_as_f32(p.enc_b, p.wdtype, r);
+    // enc_b_own: enc_b[tid], loaded by the caller before its upstream wait
+    if (p.enc_b != nullptr) acc += r == tid ? enc_b_own : load_as_f32(p.enc_b, p.wdtype, r);
     lat[r] = acc;
   }
   __syncthreads();
@@ -559,15 +593,21 @@ __global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   const bool pre = sizeof(WT) == 2 && p.rank == 64 && b < p.NB;
   uint4 wrow[8];
+  float sbias = 0.f, dbn = 1.f;
   if (pre) {
     const uint4* row = reinterpret_cast<const uint4*>(reinterpret_cast<const WT*>(p.score_w) + (int64_t)b * 64);
 #pragma unroll
     for (int i = 0; i < 8; ++i) wrow[i] = __ldg(row + i);
+    if (p.score_b != nullptr) sbias = to_f32(reinterpret_cast<const WT*>(p.score_b)[b]);
+    if (p.dbn != nullptr) dbn = p.dbn[b];
   }
+  const float enc_b_own =
+      (p.reduce_latent && p.enc_b != nullptr && (int)threadIdx.x < p.rank) ? load_as_f32(p.enc_b, p.wdtype, threadIdx.x)
+                                                                           : 0.f;
   pdl_trigger();
   pdl_wait();
   if (p.reduce_latent) {
-    reduce_latent(p, lat);
+    reduce_latent(p, lat, enc_b_own);
   } else {
     for (int r = threadIdx.x; r < p.rank; r += blockDim.x) lat[r] = ldcg_f32(&p.ws.latent[r + blockIdx.y * p.rank]);
     __syncthreads();
@@ -594,10 +634,10 @@ __global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
       }
     }
     if (!p.legacy) {
-      if (p.score_b != nullptr) acc += to_f32(reinterpret_cast<const WT*>(p.score_b)[b]);
+      if (p.score_b != nullptr) acc += sbias;
       acc = fmaxf(acc, 0.f);
     }
-    if (p.dbn != nullptr) acc *= p.dbn[b];
+    if (p.dbn != nullptr) acc *= dbn;
     p.ws.scores[(int64_t)blockIdx.y * p.NB + b] = acc;
     return;
   }
@@ -611,7 +651,7 @@ __global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
 // also ordered score-descending (ties: lower id first) by a bitonic sort.
 __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   extern __shared__ uint32_t keys[];  // [NB]
-  __shared__ int hist[256];
+  __shared__ int hists[2][256];  // digit histograms, alternating by pass
   __shared__ uint32_t s_prefix, s_mask;
   __shared__ int s_need, s_bin_count, s_start;
   __shared__ uint32_t s_or[32], s_and[32];
@@ -627,12 +667,26 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   int* sel_idx = p.ws.sel_idx + (int64_t)row * k;
   // the keys' common leading bits need no pass: digits start below them
   uint32_t kor = 0u, kand = 0xffffffffu;
-  for (int i = tid; i < NB; i += blockDim.x) {
-    const uint32_t key = orderable(ldcg_f32(&p.ws.scores[(int64_t)row * NB + i]));
-    keys[i] = key;
-    kor |= key;
-    kand &= key;
+  {
+    constexpr int kPer = kMaxNumBlocks / 1024;  // all of this thread's score loads in flight
+    float v[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = u * (int)blockDim.x + tid;
+      v[u] = i < NB ? ldcg_f32(&p.ws.scores[(int64_t)row * NB + i]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int i = u * (int)blockDim.x + tid;
+      if (i < NB) {
+        const uint32_t key = orderable(v[u]);
+        keys[i] = key;
+        kor |= key;
+        kand &= key;
+      }
+    }
   }
+  for (int i = tid; i < 512; i += blockDim.x) (&hists[0][0])[i] = 0;
   kor = __reduce_or_sync(0xffffffffu, kor);
   kand = __reduce_and_sync(0xffffffffu, kand);
   if ((tid & 31) == 0) {
@@ -656,10 +710,10 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   }
   __syncthreads();
   const int start = s_start;
-  for (int shift = start - 8; start > 0; shift -= 8) {
+  int pass = 0;
+  for (int shift = start - 8; start > 0; shift -= 8, ++pass) {
     const int sh = max(shift, 0);  // a last digit narrower than 8 bits overlaps fixed bits (constant)
-    for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-    __syncthreads();
+    int* hist = hists[pass & 1];  // zero: cleared in the prologue / during the previous pass's scan
     const uint32_t pre = s_prefix, msk = s_mask;
     for (int i0 = 0; i0 < NB; i0 += blockDim.x) {
       const int i = i0 + tid;
@@ -701,6 +755,9 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
           run += c[e];
         }
       }
+    } else {
+      // the next pass's histogram is cleared while warp 0 scans this one
+      for (int i = tid - 32; i < 256; i += (int)blockDim.x - 32) hists[(pass + 1) & 1][i] = 0;
     }
     __syncthreads();
     // once the whole threshold bin is needed, every key with this prefix is
