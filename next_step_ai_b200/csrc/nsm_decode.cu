@@ -88,6 +88,7 @@ struct GateUpParams {
   float* act_out;  // optional fp32 [k][32]
   int total_warps;
   int unit_tiles;  // tiles per stream unit (the partial segments follow the units)
+  int max_rows;    // capacity of rows / partials (>= *count_ptr): prologues load this much without waiting for the count
 };
 
 // One 64-column tile of one block, both projections: w[proj][rg] holds the
@@ -259,8 +260,8 @@ __device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, 
 // RMSNorm scale, biases, mask and SiLU(gate)*up of neuron `lane` of pool row
 // s from its summed gate/up dot products; fp16 with a per-block power-of-two
 // scale (the whole warp calls this for one block).
-__device__ __forceinline__ void gu_finalize_apply(const GateUpParams& p, int s, int lane, float gsum, float usum) {
-  const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
+__device__ __forceinline__ void gu_finalize_apply(const GateUpParams& p, int s, int lane, float gsum, float usum,
+                                                  float ns) {
   gsum *= ns;
   usum *= ns;
   if (p.gate_bias != nullptr || p.up_bias != nullptr) {
@@ -291,15 +292,29 @@ __global__ void __launch_bounds__(256) gateup_finalize_kernel(GateUpParams p) {
   pdl_wait();
   const int lane = threadIdx.x & 31, q0 = threadIdx.x >> 5;
   const int s = blockIdx.x;
+  // segments q0, q0+8, q0+16, q0+24 go out with the count (one round trip;
+  // the ones past this block's segment count are ignored)
   const int count = *p.count_ptr;
+  const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
+  float vg[4], vu[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    vg[u] = ldcg_f32(base + (q0 + 8 * u) * 64 + lane);
+    vu[u] = ldcg_f32(base + (q0 + 8 * u) * 64 + 32 + lane);
+  }
+  const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
   if (s >= count) return;
   const int cps = (p.H >> 6) / p.unit_tiles;
   const int nw = stream_warps(count, cps, kMaxUnitsPerSlot, p.total_warps);
   const int ups = stream_owner(count * cps, nw, s * cps + cps - 1) - stream_owner(count * cps, nw, s * cps) + 1;
-  const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
   float gsum = 0.f, usum = 0.f;
-#pragma unroll 8
-  for (int q = q0; q < ups; q += 8) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+    if (q0 + 8 * u < ups) {
+      gsum += vg[u];
+      usum += vu[u];
+    }
+  for (int q = q0 + 32; q < ups; q += 8) {
     gsum += ldcg_f32(base + q * 64 + lane);
     usum += ldcg_f32(base + q * 64 + 32 + lane);
   }
@@ -314,7 +329,7 @@ __global__ void __launch_bounds__(256) gateup_finalize_kernel(GateUpParams p) {
     gsum += red[0][q][lane];
     usum += red[1][q][lane];
   }
-  gu_finalize_apply(p, s, lane, gsum, usum);
+  gu_finalize_apply(p, s, lane, gsum, usum, ns);
 }
 
 constexpr int kStageXMaxHidden = 16384;
@@ -370,6 +385,7 @@ struct DownParams {
   void* y;
   int y_dtype;
   int total_warps;
+  int max_rows;  // capacity of rows / act16 (>= *count_ptr): the prologue loads this much without waiting for the count
 };
 
 __device__ __forceinline__ void record_down_meta(const DownParams& p) {
@@ -748,9 +764,11 @@ __global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams 
     for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = __ldcg(src + i);
     for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
   }
-  const bool stage_rows = count <= kStageRowsMax;
+  // the pool rows go out with the count (up to the capacity; rows past the
+  // count are never read)
+  const bool stage_rows = p.max_rows <= kStageRowsMax;
   if (stage_rows)
-    for (int i = threadIdx.x; i < count; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
+    for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
   __syncthreads();
   const int* rows = stage_rows ? srows : p.rows;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
@@ -889,10 +907,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1) down_tma_kernel(DownParams p) 
   float* sscale = reinterpret_cast<float*>(smem + kDnScaleOff);
   int* srows = reinterpret_cast<int*>(smem + kDnRowsOff);
   {
+    // staged up to the capacity, with the count (entries past it are never read)
     const uint4* src = reinterpret_cast<const uint4*>(p.act16);
     uint4* dst = reinterpret_cast<uint4*>(sact);
-    for (int i = threadIdx.x; i < count * 4; i += blockDim.x) dst[i] = __ldcg(src + i);
-    for (int i = threadIdx.x; i < count; i += blockDim.x) {
+    for (int i = threadIdx.x; i < p.max_rows * 4; i += blockDim.x) dst[i] = __ldcg(src + i);
+    for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) {
       sscale[i] = __ldcg(p.act_scale + i);
       srows[i] = __ldcg(p.rows + i);
     }
@@ -1020,6 +1039,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.H = m.H;
   gp.rows = m.rows;
   gp.count_ptr = m.count;
+  gp.max_rows = m.k;
   gp.row_block = m.row_block;
   gp.x16 = ws.x16;
   gp.xscale = ws.xscale;
@@ -1075,6 +1095,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   dp.H = m.H;
   dp.rows = m.rows;
   dp.count_ptr = m.count;
+  dp.max_rows = m.k;
   dp.act16 = ws.act16;
   dp.act_scale = ws.act_scale;
   dp.ypart = ws.ypart;
