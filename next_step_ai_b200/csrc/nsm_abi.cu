@@ -69,7 +69,6 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   const int nb = intermediate / 32;
   int* tick = reinterpret_cast<int*>(take((size_t)kCounterInts * sizeof(int)));
   w.ticket_router_a = tick;
-  w.ticket_router_b = tick ? tick + 1 : nullptr;
   w.err = tick ? tick + 2 : nullptr;
   w.down_meta = tick ? tick + 3 : nullptr;
   w.count = tick ? tick + 5 : nullptr;

@@ -71,8 +71,7 @@ const ExchangeDev* exchange_dev(const nsm_exchange* ex);
 
 struct DecodeWs {
   // counters (must be zero between calls)
-  int* ticket_router_a;          // [1]
-  int* ticket_router_b;          // [1]
+  int* ticket_router_a;          // [1] (head int 1 is unused)
   int* err;                      // [1] device-side error code (0 = none), sticky
   int* down_meta;                // [2] last down launch: total warps, log2 rows per reduction group
   // (count below and ypart live at fixed offsets after the counter head)

@@ -1,21 +1,26 @@
-// nsm_router.cu -- learned-basis router for one token on sm_100a.
+// nsm_router.cu -- learned-basis router on sm_100a (one token, or many rows).
 //
 // router_latent_kernel (split-H, ~128 columns per CTA):
-//   * x preparation: optional residual += y_prev, RMSNorm sum of squares,
-//     fp16 copy of the MLP input with one power-of-two scale per 64 columns
-//     (consumed by the gate/up kernel);
+//   * x preparation: the residual += the previous layer's output (its pending
+//     down partials summed here, and with several GPUs exchanged over NVLink),
+//     RMSNorm sum of squares, fp16 copy of the MLP input with one power-of-two
+//     scale per 64 columns (consumed by the gate/up kernel);
 //   * partial latent = enc_w[:, slice] . x[slice] with 16-byte loads of enc_w
-//     issued before x is ready;
-//   * the last CTA (atomic ticket) reduces the partials in fixed CTA order,
-//     applies the RMSNorm scale and enc_b, and the optional basis top-k mask
-//     (streaming_llama_runtime.py:4220-4238).
-// router_scores_kernel / router_topk_kernel:
+//     issued before x is ready (multi-row routing: up to 32 rows per CTA);
+//   * x-prep-only launches (the final residual flush): the last CTA (atomic
+//     ticket) reduces the partials.
+// router_scores_kernel:
+//   * every CTA reduces the partial latents in fixed order, applies the
+//     RMSNorm scale, enc_b and the optional basis top-k mask
+//     (streaming_llama_runtime.py:4220-4238);
 //   * one thread per block: score = clamp0(latent . score_w[b] + score_b[b])
-//     (or |latent| . dec_norm_t[:, b] in legacy mode), times down_block_norm;
-//   * one 1024-thread CTA selects the top-k with an 8-bit-digit radix select on
-//     order-preserving score bits, resolves ties at the threshold by lower
-//     block id, orders the k winners (score desc, block id asc) and compacts
-//     them into pool rows through the block map (:4324-4352).
+//     (or |latent| . dec_norm_t[:, b] in legacy mode), times down_block_norm.
+// router_topk_kernel:
+//   * one 1024-thread CTA per row selects the top-k with an 8-bit-digit radix
+//     select on order-preserving score bits (the keys' common leading bits
+//     skipped), resolves ties at the threshold by lower block id, orders the
+//     k winners (score desc, block id asc) when asked, and compacts them into
+//     pool rows through the block map (:4324-4352).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
