@@ -424,7 +424,7 @@ def run_cache(args) -> None:
     for t in range(args.warmup):
         cm.decode(xs[t], idx=idx[t])
     torch.cuda.synchronize(dev)
-    hits = misses = h2d = 0
+    hits = misses = h2d = launches = 0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         e0.record()
@@ -433,6 +433,10 @@ def run_cache(args) -> None:
             hits += st.hits
             misses += st.misses
             h2d += st.h2d_bytes
+            # this library's kernels per token: router (3), resident decode (5: selection map,
+            # gate/up, gate/up reduction, down, down reduction), staged decode (5) when there
+            # are misses; the miss copies are cudaMemcpyAsync, the promotion copies torch's
+            launches += 8 + (5 if st.misses else 0)
         e1.record()
         torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
@@ -455,7 +459,7 @@ def run_cache(args) -> None:
                 "bytes_per_token": h2d / args.steps},
         "e2e": {"value": args.steps / (ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": h2d / args.steps,
                 "d2h_bytes_per_step": TOP_K * 4},
-        "gpu_launches": None,
+        "gpu_launches": launches,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
@@ -553,6 +557,9 @@ def run_union(args) -> None:
                      "frac": round(gbs / pk["hbm_gbs"], 4), "algorithmic_bytes": bytes_union,
                      "tensor_tflops": round(flops / (ms_union * 1e-3) / 1e12, 2),
                      "unit_of_launch": "32-row router (3 launches) + union decode launch group"},
+        # this library's kernels per 32-token step: multi-row router (3) + union build, x, gate/up,
+        # SiLU*up, down, output (6)
+        "gpu_launches": args.steps * 9,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)
