@@ -254,7 +254,8 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(gu_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(gu_gbs / pk["hbm_gbs"], 4),
                          "traffic": GATEUP_DRAM_BYTES_PER_LAUNCH if world == 1 else None,
-                         "kernel": "gateup_tma_kernel (NF4 gate+up gather-GEMV, one launch per layer)",
+                         "kernel": "gateup_tma_kernel (block selection from the router's scores + NF4 gate+up "
+                                   "gather-GEMV, one launch per layer)",
                          "algorithmic_bytes": int(gu_bytes), "us_per_launch": round(stage_us["gateup"], 3),
                          "peak_source": pk["source"], "peak_note": "of measured (MEASURED_PEAKS.json hbm_gbs)",
                          "stage_us": {k: round(v, 3) for k, v in stage_us.items()},

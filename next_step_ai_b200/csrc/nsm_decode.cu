@@ -36,6 +36,7 @@
 #include "nsm_internal.h"
 #include "nsm_nf4.cuh"
 #include "nsm_router.h"
+#include "nsm_select.cuh"
 
 namespace nsm {
 
@@ -89,6 +90,17 @@ struct GateUpParams {
   int total_warps;
   int unit_tiles;  // tiles per stream unit (the partial segments follow the units)
   int max_rows;    // capacity of rows / partials (>= *count_ptr): prologues load this much without waiting for the count
+  // select != 0 (bulk-copy kernel only): the kernel selects the blocks itself
+  // from the router's scores -- top `top_k` of NB, through the block map --
+  // and CTA 0 writes rows_out / row_block_out / count_out for the later kernels
+  int select;
+  const float* scores;
+  int NB, top_k;
+  const int* slot_of_block;
+  int block_begin, block_end, pool_rows;
+  int* rows_out;
+  int* row_block_out;
+  int* count_out;
 };
 
 // One 64-column tile of one block, both projections: w[proj][rg] holds the
@@ -746,6 +758,78 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
   }
 }
 
+// Block map of the fused selection (the router kernels' map_block).
+__device__ __forceinline__ int gu_map_block(const GateUpParams& p, int b) {
+  int r;
+  if (p.slot_of_block != nullptr) r = __ldg(p.slot_of_block + b);
+  else r = (b >= p.block_begin && b < p.block_end) ? b - p.block_begin : -1;
+  return (r >= 0 && r < p.pool_rows) ? r : -1;
+}
+
+// The decode path's block selection inside the gate/up kernel (every CTA, the
+// same result): the router's scores -> order-preserving keys in `keys`, exact
+// top-k (ties at the threshold to the lower block id), the selected blocks
+// present in this pool compacted in block-id order into srows.  CTA 0 also
+// writes the rows, their block ids and the count for the later kernels.
+// Returns the count.  Everything lives in dynamic shared memory.
+__device__ __forceinline__ int gu_select_blocks(const GateUpParams& p, uint32_t* keys, RadixSelectSmem& S, int* srows) {
+  const int tid = threadIdx.x, NB = p.NB;
+  uint32_t kor = 0u, kand = 0xffffffffu;
+  for (int i0 = 0; i0 < NB; i0 += 8 * (int)blockDim.x) {
+    float v[8];  // 8 score loads in flight per thread
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * (int)blockDim.x + tid;
+      v[u] = i < NB ? ldcg_f32(p.scores + i) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * (int)blockDim.x + tid;
+      if (i < NB) {
+        const uint32_t key = orderable(v[u]);
+        keys[i] = key;
+        kor |= key;
+        kand &= key;
+      }
+    }
+  }
+  block_radix_select(keys, NB, p.top_k, kor, kand, S);
+  const uint32_t thr = S.prefix;
+  const int take_eq = S.need;
+  const bool split = take_eq != S.bin_count;  // a tie at the threshold is split: rank the equal keys
+  const int per = (NB + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int lo = min(NB, tid * per), hi = min(NB, lo + per);  // contiguous chunk: block-id order
+  int tot, eq_before = 0;
+  if (split) {
+    int n_eq = 0;
+    for (int i = lo; i < hi; ++i) n_eq += keys[i] == thr;
+    eq_before = block_exclusive_scan_s(n_eq, &tot, S.wsum);
+  }
+  int m = 0;
+  for (int i = lo, e = eq_before; i < hi; ++i) {
+    const uint32_t key = keys[i];
+    const bool sel = key > thr || (key == thr && (!split || e++ < take_eq));
+    m += sel && gu_map_block(p, i) >= 0;
+  }
+  int pos = block_exclusive_scan_s(m, &tot, S.wsum);
+  for (int i = lo, e = eq_before; i < hi; ++i) {
+    const uint32_t key = keys[i];
+    const bool sel = key > thr || (key == thr && (!split || e++ < take_eq));
+    const int r = sel ? gu_map_block(p, i) : -1;
+    if (r < 0) continue;
+    srows[pos] = r;
+    if (blockIdx.x == 0) {
+      p.rows_out[pos] = r;
+      p.row_block_out[pos] = i;
+    }
+    ++pos;
+  }
+  if (blockIdx.x == 0 && tid == 0) *p.count_out = tot;
+  return tot;
+}
+static_assert(kGuWarps * kGuStages * kGuStageBytes >= kMaxNumBlocks * 4 + (int)sizeof(RadixSelectSmem),
+              "the fused selection's keys must fit in the gate/up ring");
+
 __global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams p) {
   char* smem = reinterpret_cast<char*>(g_lut_smem);
   const uint32_t bar0 = smem_u32(smem + kGuBarOff);
@@ -757,18 +841,27 @@ __global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams 
   __half* xs16 = reinterpret_cast<__half*>(smem + kGuX16Off);
   float* xss = reinterpret_cast<float*>(smem + kGuXsOff);
   int* srows = reinterpret_cast<int*>(smem + kGuRowsOff);
-  const int count = *p.count_ptr;
   {
     const uint4* src = reinterpret_cast<const uint4*>(p.x16);
     uint4* dst = reinterpret_cast<uint4*>(xs16);
     for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = __ldcg(src + i);
     for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
   }
-  // the pool rows go out with the count (up to the capacity; rows past the
-  // count are never read)
   const bool stage_rows = p.max_rows <= kStageRowsMax;
-  if (stage_rows)
-    for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
+  int count;
+  if (p.select) {
+    // keys and selection scratch in the ring, which no copy has touched yet
+    uint32_t* keys = reinterpret_cast<uint32_t*>(smem + kGuRingOff);
+    RadixSelectSmem* sel =
+        reinterpret_cast<RadixSelectSmem*>(smem + kGuRingOff + (((size_t)p.NB * 4 + 127) & ~(size_t)127));
+    count = gu_select_blocks(p, keys, *sel, srows);
+  } else {
+    // the pool rows go out with the count (up to the capacity; rows past the
+    // count are never read)
+    count = *p.count_ptr;
+    if (stage_rows)
+      for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
+  }
   __syncthreads();
   const int* rows = stage_rows ? srows : p.rows;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
@@ -989,6 +1082,10 @@ struct MlpPlan {
   const float* norm_scale;
   void* const* events;  // optional NSM_STAGE_EVENTS stage events (index 1..5 recorded here)
   bool defer_y;         // leave the output as down partials in the workspace
+  // select: the gate/up kernel selects the blocks from ws.scores (no top-k kernel)
+  bool select;
+  int NB;
+  const nsm_block_map* map;
 };
 
 static cudaError_t stage_event(void* const* ev, int i, cudaStream_t s) {
@@ -1013,6 +1110,18 @@ static int validate_weights(const nsm_mlp_weights* w, int H) {
   const int64_t dbs = w->down_block_stride ? w->down_block_stride : (int64_t)16 * H;
   NSM_REQUIRE(drs % 4 == 0 && dbs % 4 == 0, NSM_ERR_INVALID_ARG, "down strides must be multiples of 4 bytes");
   return NSM_OK;
+}
+
+// The bulk-copy gate/up kernel applies: tiled pools, the x vector staged in
+// shared memory, 16-byte aligned pools and strides, whole two-tile units.
+static bool gateup_tma_ok(const nsm_mlp_weights* w, int H, const KernelSetup* ks) {
+  const int64_t gstride = w->gateup_block_stride ? w->gateup_block_stride : (int64_t)16 * H;
+  const int64_t gastride = w->gateup_absmax_block_stride ? w->gateup_absmax_block_stride : (int64_t)H / 2;
+  const bool aligned = ((uintptr_t)w->gate_packed | (uintptr_t)w->up_packed | (uintptr_t)w->gate_absmax |
+                        (uintptr_t)w->up_absmax) % 16 == 0 &&
+                       gstride % 16 == 0 && (gastride * 4) % 16 == 0;
+  return (w->layout & NSM_LAYOUT_GATEUP_TILED) != 0 && H <= kStageXMaxHidden && aligned && ks->gu_tma > 0 &&
+         (H / 64) % kGuUnitTiles == 0;
 }
 
 static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream) {
@@ -1053,9 +1162,21 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.act_out = m.act_out;
   const bool gu_tiled = (w->layout & NSM_LAYOUT_GATEUP_TILED) != 0;
   const bool gu_stage = m.H <= kStageXMaxHidden;
-  const bool gu_aligned = ((uintptr_t)gp.gate | (uintptr_t)gp.up | (uintptr_t)gp.gate_am | (uintptr_t)gp.up_am) % 16 == 0 &&
-                          gp.gstride % 16 == 0 && (gp.gastride * 4) % 16 == 0;
-  const bool gu_tma = gu_tiled && gu_stage && gu_aligned && ks->gu_tma > 0 && (m.H / 64) % kGuUnitTiles == 0;
+  const bool gu_tma = gateup_tma_ok(w, m.H, ks);
+  if (m.select) {
+    NSM_REQUIRE(gu_tma, NSM_ERR_INVALID_ARG, "the fused block selection needs the bulk-copy gate/up kernel");
+    gp.select = 1;
+    gp.scores = ws.scores;
+    gp.NB = m.NB;
+    gp.top_k = m.k;
+    gp.slot_of_block = m.map ? m.map->slot_of_block : nullptr;
+    gp.block_begin = m.map ? m.map->block_begin : 0;
+    gp.block_end = m.map ? m.map->block_end : m.NB;
+    gp.pool_rows = w->pool_rows;
+    gp.rows_out = ws.rows;
+    gp.row_block_out = ws.row_block;
+    gp.count_out = ws.count;
+  }
   NSM_CHECK_CUDA(stage_event(m.events, 1, stream));
   cudaError_t e;
   gp.unit_tiles = 1;
@@ -1167,7 +1288,7 @@ static int router_a_prepare(const void* x, int x_dtype, const nsm_layer_io* io, 
 
 // Router kernel + scores/top-k kernels; the scores kernel reduces the router
 // kernel's partial latents (and advances the exchange epoch).
-static int router_launch_pair(const RouterAParams& a_in, RouterBParams b, cudaStream_t stream) {
+static int router_launch_pair(const RouterAParams& a_in, RouterBParams b, cudaStream_t stream, bool topk = true) {
   RouterAParams a = a_in;
   a.reduce_in_scores = 1;
   int cpc;
@@ -1181,7 +1302,7 @@ static int router_launch_pair(const RouterAParams& a_in, RouterBParams b, cudaSt
   b.epoch_counter = (a.pending && a.ex.world > 1) ? a.ex.counter : nullptr;
   int st = router_a_launch(a, stream);
   if (st) return st;
-  return router_b_launch(b, stream);
+  return router_b_launch(b, stream, topk);
 }
 
 static int validate_router(const nsm_router_weights* rw, int H) {
@@ -1325,9 +1446,14 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
 
   void* const* events = io != nullptr ? io->stage_events : nullptr;
   NSM_CHECK_CUDA(stage_event(events, 0, s));
+  // the gate/up kernel selects the blocks itself (no top-k kernel) when nobody
+  // asks for the ordered indices and the bulk-copy kernel applies
+  const bool fuse_select = idx_in == nullptr && idx_out == nullptr && score_out == nullptr && k <= kStageRowsMax &&
+                           NB <= kMaxNumBlocks && gateup_tma_ok(w, hidden, ks);
   if (idx_in == nullptr) {
     st = router_launch_pair(router_a_params(x, x_dtype, io, rw, hidden, wsl),
-                            router_b_params(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl), s);
+                            router_b_params(rw, k, idx_out, score_out, nullptr, map, w->pool_rows, wsl), s,
+                            !fuse_select);
     if (st) return st;
   } else {
     st = router_a_prepare(x, x_dtype, io, nullptr, hidden, wsl, s);
@@ -1356,6 +1482,9 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   m.norm_scale = wsl.norm_scale;
   m.events = events;
   m.defer_y = defer;
+  m.select = fuse_select;
+  m.NB = NB;
+  m.map = map;
   return launch_mlp(m, wsl, s);
 }
 

@@ -31,6 +31,7 @@
 #include "nsm_common.cuh"
 #include "nsm_internal.h"
 #include "nsm_router.h"
+#include "nsm_select.cuh"
 
 namespace nsm {
 
@@ -386,14 +387,6 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
 // ---------------------------------------------------------------------------
 // router B
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t orderable(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float from_orderable(uint32_t u) {
-  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
-}
-
 __device__ __forceinline__ int map_block(const RouterBParams& p, int b) {
   if (b < 0 || b >= p.NB) return -1;
   int r;
@@ -408,29 +401,7 @@ __device__ __forceinline__ int map_block(const RouterBParams& p, int b) {
 // Block-wide exclusive scan of one int per thread (blockDim <= 1024).
 __device__ __forceinline__ int block_exclusive_scan(int v, int* total) {
   __shared__ int wsum[32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) wsum[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    int s = lane < nw ? wsum[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += y;
-    }
-    if (lane < nw) wsum[lane] = s;  // inclusive
-  }
-  __syncthreads();
-  const int before = (warp > 0 ? wsum[warp - 1] : 0) + x - v;
-  *total = wsum[nw - 1];
-  __syncthreads();
-  return before;
+  return block_exclusive_scan_s(v, total, wsum);
 }
 
 // Compacts sel[0..k) through the block map into ws.rows / ws.row_block / ws.count.
@@ -656,10 +627,7 @@ __global__ void __launch_bounds__(128) router_scores_kernel(RouterBParams p) {
 // also ordered score-descending (ties: lower id first) by a bitonic sort.
 __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
   extern __shared__ uint32_t keys[];  // [NB]
-  __shared__ int hists[2][256];  // digit histograms, alternating by pass
-  __shared__ uint32_t s_prefix, s_mask;
-  __shared__ int s_need, s_bin_count, s_start;
-  __shared__ uint32_t s_or[32], s_and[32];
+  __shared__ RadixSelectSmem S;
   __shared__ unsigned long long sorted[1024];
   pdl_trigger();
   pdl_wait();
@@ -691,92 +659,14 @@ __global__ void __launch_bounds__(1024) router_topk_kernel(RouterBParams p) {
       }
     }
   }
-  for (int i = tid; i < 512; i += blockDim.x) (&hists[0][0])[i] = 0;
-  kor = __reduce_or_sync(0xffffffffu, kor);
-  kand = __reduce_and_sync(0xffffffffu, kand);
-  if ((tid & 31) == 0) {
-    s_or[tid >> 5] = kor;
-    s_and[tid >> 5] = kand;
-  }
-  __syncthreads();
-  if (tid < 32) {
-    const int nwarps = (int)(blockDim.x >> 5);
-    const uint32_t o = __reduce_or_sync(0xffffffffu, tid < nwarps ? s_or[tid] : 0u);
-    const uint32_t a = __reduce_and_sync(0xffffffffu, tid < nwarps ? s_and[tid] : 0xffffffffu);
-    if (tid == 0) {
-      const int start = 32 - __clz(o ^ a);  // low bits that differ somewhere; 0: all keys equal
-      const uint32_t hi = start >= 32 ? 0u : (0xffffffffu << start);
-      s_prefix = a & hi;
-      s_mask = hi;
-      s_need = k;
-      s_bin_count = start == 0 ? NB : -1;
-      s_start = start;
-    }
-  }
-  __syncthreads();
-  const int start = s_start;
-  int pass = 0;
-  for (int shift = start - 8; start > 0; shift -= 8, ++pass) {
-    const int sh = max(shift, 0);  // a last digit narrower than 8 bits overlaps fixed bits (constant)
-    int* hist = hists[pass & 1];  // zero: cleared in the prologue / during the previous pass's scan
-    const uint32_t pre = s_prefix, msk = s_mask;
-    for (int i0 = 0; i0 < NB; i0 += blockDim.x) {
-      const int i = i0 + tid;
-      const uint32_t key = i < NB ? keys[i] : 0u;
-      const bool on = i < NB && (key & msk) == pre;
-      const uint32_t bin = on ? ((key >> sh) & 255u) : 256u;
-      const unsigned grp = __match_any_sync(0xffffffffu, bin);
-      if (on && (threadIdx.x & 31) == (__ffs(grp) - 1)) atomicAdd(&hist[bin], __popc(grp));
-    }
-    __syncthreads();
-    if (tid < 32) {
-      // lane l owns bins [255-8l-7, 255-8l] (descending)
-      int c[8];
-      int loc = 0;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        c[e] = hist[255 - 8 * tid - e];
-        loc += c[e];
-      }
-      int incl = loc;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (tid >= o) incl += y;
-      }
-      const int excl = incl - loc;
-      const int need = s_need;
-      if (excl < need && need <= incl) {
-        int run = excl;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (run < need && need <= run + c[e]) {
-            const uint32_t bin = 255u - 8u * tid - e;
-            s_prefix = (pre & ~(255u << sh)) | (bin << sh);
-            s_mask = msk | (255u << sh);
-            s_need = need - run;
-            s_bin_count = c[e];  // after the last pass: keys equal to the threshold
-          }
-          run += c[e];
-        }
-      }
-    } else {
-      // the next pass's histogram is cleared while warp 0 scans this one
-      for (int i = tid - 32; i < 256; i += (int)blockDim.x - 32) hists[(pass + 1) & 1][i] = 0;
-    }
-    __syncthreads();
-    // once the whole threshold bin is needed, every key with this prefix is
-    // selected and the lower bits do not matter (the order, when asked for,
-    // comes from the full keys)
-    if (sh == 0 || s_need == s_bin_count) break;
-  }
-  const uint32_t thr = s_prefix;
-  const int take_eq = s_need;
+  block_radix_select(keys, NB, k, kor, kand, S);
+  const uint32_t thr = S.prefix;
+  const int take_eq = S.need;
   // winners in block-id order (contiguous chunk per thread)
   const int per = (NB + blockDim.x - 1) / blockDim.x;
   const int lo = min(NB, tid * per), hi = min(NB, lo + per);
   const bool ordered = want_order;
-  if (!ordered && take_eq == s_bin_count) {
+  if (!ordered && take_eq == S.bin_count) {
     // no tie is split at the threshold: the selection is key >= thr; one scan
     // compacts the selected blocks present here into pool rows (block-id order)
     int m = 0;
@@ -926,7 +816,7 @@ int router_a_launch(const RouterAParams& a_in, cudaStream_t stream) {
   return NSM_OK;
 }
 
-int router_b_launch(const RouterBParams& b, cudaStream_t stream) {
+int router_b_launch(const RouterBParams& b, cudaStream_t stream, bool topk) {
   int st = router_setup();
   if (st) return st;
   const int ctas = (b.NB + 127) / 128;
@@ -937,7 +827,7 @@ int router_b_launch(const RouterBParams& b, cudaStream_t stream) {
     default: e = launch_pdl(router_scores_kernel<__nv_bfloat16>, ctas, 128, 0, stream, b); break;
   }
   NSM_CHECK_CUDA(e);
-  NSM_CHECK_CUDA(launch_pdl(router_topk_kernel, 1, 1024, (size_t)b.NB * 4, stream, b));
+  if (topk) NSM_CHECK_CUDA(launch_pdl(router_topk_kernel, 1, 1024, (size_t)b.NB * 4, stream, b));
   return NSM_OK;
 }
 

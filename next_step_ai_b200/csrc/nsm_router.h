@@ -69,7 +69,8 @@ int router_a_ctas(int H, int* cols_per_cta);
 
 int router_setup();
 int router_a_launch(const RouterAParams& a, cudaStream_t stream);
-int router_b_launch(const RouterBParams& b, cudaStream_t stream);
+// Scores kernel, then (topk) the top-k kernel.
+int router_b_launch(const RouterBParams& b, cudaStream_t stream, bool topk = true);
 // Routing only for `rows` rows of x (row-major [rows][H]) into idx_out [rows][k].
 int router_rows_launch(const RouterAParams& a, RouterBParams b, int rows, cudaStream_t stream);
 int select_given_launch(const RouterBParams& b, const int32_t* idx_in, int k, cudaStream_t stream);

@@ -127,14 +127,23 @@ class SparseMlpDecoder:
                    "nsm_residual_flush")
 
     # kernels per layer: router latent (+ previous layer's output), block scores,
-    # top-k, gate/up, gate/up reduction, down; plus one output kernel per token
+    # top-k, gate/up, gate/up reduction, down; plus one output kernel per token.
+    # With the bulk-copy gate/up kernel (tiled pools, H <= 16384, H / 64 even,
+    # k <= 1024) the gate/up kernel selects the blocks itself: no top-k kernel.
     KERNELS_PER_LAYER = 6
+
+    def _kernels_for(self, li: int) -> int:
+        layer = self.layers[li]
+        k = min(layer.router.top_k, layer.router.num_blocks)
+        fused = (bool(layer.weights.layout & _lib.NSM_LAYOUT_GATEUP_TILED) and self.H <= 16384
+                 and (self.H // 64) % 2 == 0 and k <= 1024)
+        return self.KERNELS_PER_LAYER - (1 if fused else 0)
 
     @property
     def kernels_per_step(self) -> int:
         """This library's kernel launches per token (the final copy to ``out``
         is not counted)."""
-        return self.KERNELS_PER_LAYER * self.num_layers + 1
+        return sum(self._kernels_for(i % len(self.layers)) for i in range(self.num_layers)) + 1
 
     def step_eager(self) -> None:
         """One token through all layers (no graph).  Input: ``residual``;

@@ -206,6 +206,52 @@ def test_router_tie_break_lower_index(dev):
     assert got.tolist() == [5, 9, 3, 7, 11, 30, 0, 1]
 
 
+@pytest.mark.parametrize("name,seed", [("small", 31), ("cfg0", 32)])
+def test_decode_fused_selection_matches_topk_kernel(dev, name, seed):
+    """Without idx_out the gate/up kernel selects the blocks itself (no top-k
+    kernel); asking for idx_out runs the top-k kernel.  Same blocks, same
+    block-id order of the pool rows: the outputs must be bit-identical."""
+    from next_step_ai_b200 import sparse_mlp_decode
+
+    shape = syn.SHAPES[name]
+    w = weights_for(shape, full_layer(name, seed), dev)
+    rw = router_for(shape, syn.make_router(shape, seed), dev)
+    x = T(syn.make_x(shape, seed, 1)[0], dev, torch.bfloat16)
+    y_fused = sparse_mlp_decode(x, rw, w, out_dtype=torch.float32)
+    idx = torch.empty(shape.top_k, dtype=torch.int32, device=dev)
+    y_topk = sparse_mlp_decode(x, rw, w, out_dtype=torch.float32, idx_out=idx)
+    assert torch.equal(y_fused, y_topk)
+
+
+def test_decode_fused_selection_splits_ties_by_block_id(dev):
+    """Tied scores at the threshold (all-zero score head, biases 2, 2, 1, 1, 1,
+    1 and zeros): the fused selection keeps the lower block ids among the tied
+    zeros, like the top-k kernel, and the MLP matches the oracle on that set."""
+    from next_step_ai_b200 import RouterWeights, sparse_mlp_decode
+
+    shape = syn.SHAPES["tiny"]
+    full = full_layer("tiny", 33)
+    w = weights_for(shape, full, dev)
+    H, r, NB, k = shape.hidden, 8, shape.num_blocks, 8
+    sb = np.zeros(NB, np.float32)
+    sb[[3, 7, 11, 20]] = 1.0
+    sb[[5, 9]] = 2.0
+    rw = RouterWeights(enc_w=T(np.zeros((r, H), np.float32), dev), score_w=T(np.zeros((NB, r), np.float32), dev),
+                       score_b=T(sb, dev), top_k=k, basis_top_k=r)
+    xh = syn.make_x(shape, 34, 1)[0]
+    x = T(xh, dev, torch.bfloat16)
+    y_fused = sparse_mlp_decode(x, rw, w, out_dtype=torch.float32)
+    idx = torch.empty(k, dtype=torch.int32, device=dev)
+    y_topk = sparse_mlp_decode(x, rw, w, out_dtype=torch.float32, idx_out=idx)
+    assert idx.cpu().numpy().tolist() == [5, 9, 3, 7, 11, 20, 0, 1]
+    assert torch.equal(y_fused, y_topk)
+    blocks = np.array([0, 1, 3, 5, 7, 9, 11, 20], np.int64)
+    ref = om.sparse_mlp_full(bf16_round(xh), blocks, full["gate_packed"], full["gate_absmax"], full["up_packed"],
+                             full["up_absmax"], full["down_packed"], full["down_absmax"], full["code"],
+                             hidden=shape.hidden, intermediate=shape.intermediate)[0]
+    assert_close(y_fused.cpu().numpy(), ref)
+
+
 # --------------------------------------------------------------------------- decode, resident weights
 @pytest.mark.parametrize("name,seed", [("tiny", 11), ("small", 12), ("cfg0", 0)])
 def test_decode_resident_matches_oracle(dev, name, seed):
