@@ -215,6 +215,14 @@ def target_hot_blocks(*, layer_idx: int, runtime_top_k: int, count_slots: int, p
     return max(1, min(max(fallback, per_layer // max(1, int(bytes_per_block))), int(count_slots)))
 
 
+def hot_cache_bytes_per_block(hidden: int, block_size: int = 32) -> int:
+    """VRAM bytes of one hot block: gate and up packed rows with fp32 absmax,
+    plus the down column slice and its absmax
+    (``_estimate_mlp_hot_cache_bytes_per_block``, ``streaming_llama_runtime.py:2245-2273``)."""
+    per_proj = (int(hidden) // 2) * int(block_size) + (int(hidden) // 64) * int(block_size) * 4
+    return 2 * per_proj + int(hidden) * max(1, int(block_size) // 2) + int(hidden) * 4
+
+
 # --------------------------------------------------------------------------- cached decode
 @dataclass
 class CacheStats:

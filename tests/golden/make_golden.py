@@ -13,13 +13,18 @@ code and records its outputs on seeded synthetic inputs:
 * the reference's Triton kernels ``_sparse_mlp_decode_4bit_single_kernel_sm75``,
   ``_sparse_output_linear_4bit_kernel``, ``_sparse_input_linear_4bit_tiled_kernel``
   and ``_sparse_input_linear_4bit_atomic_kernel`` executed by Triton's CPU
-  interpreter (``TRITON_INTERPRET=1``).
+  interpreter (``TRITON_INTERPRET=1``);
+* ``checkpoint.json`` (argument ``checkpoint`` regenerates only this file):
+  ``ShardedSafetensorLoader`` (weight map, quant-state grouping,
+  ``load_nf4_packed_blocks``, ``_load_raw_for_param``) on a seeded
+  bitsandbytes-format snapshot written by ``oracle.bnb_checkpoint``, and
+  ``_derive_hot_blocks_for_layer`` on a ``__new__``-built runtime.
 
 Inputs come from ``oracle.synthetic`` (seeded).  Small inputs are stored in the
 fixtures; large ones are stored as seeds plus a SHA-256 of the regenerated
 bytes, so the tests can rebuild them and prove they are the same bytes.
 
-Usage: ``NSM_REFERENCE_ROOT=/path/to/next_step_ai python tests/golden/make_golden.py``
+Usage: ``NSM_REFERENCE_ROOT=/path/to/next_step_ai python tests/golden/make_golden.py [checkpoint]``
 """
 from __future__ import annotations
 
@@ -373,8 +378,148 @@ def gen_linear4bit(tsm, out: dict) -> None:
     out["lin4/cases.json"] = np.frombuffer(json.dumps(cases).encode(), dtype=np.uint8)
 
 
+# --------------------------------------------------------------------------- artifacts and checkpoints
+CHECKPOINT_SHAPE = "tiny"
+CHECKPOINT_SEED = 41
+
+
+def write_checkpoint_snapshot(directory, index: bool) -> dict:
+    """The seeded bitsandbytes-format snapshot the checkpoint fixtures use
+    (layer 0 and 1 of the tiny shape, plus a dense bf16 norm weight)."""
+    from oracle import bnb_checkpoint as bc
+    shape = syn.SHAPES[CHECKPOINT_SHAPE]
+    params = {}
+    for layer in (0, 1):
+        full = syn.make_layer_full(shape, CHECKPOINT_SEED, layer)
+        params.update(bc.layer_params(full, shape.hidden, shape.intermediate, layer))
+    extra = {"model.layers.0.post_attention_layernorm.weight":
+             np.linspace(0.5, 1.5, shape.hidden, dtype=np.float32)}
+    return bc.write_snapshot(directory, params, shards=2, index=index, extra=extra)
+
+
+def gen_checkpoint(rt) -> None:
+    import tempfile
+    import types as _types
+
+    import torch
+    from llama3_neuroplastic.experiments.runtime import safetensor_loader as sl
+
+    shape = syn.SHAPES[CHECKPOINT_SHAPE]
+    H, NB = shape.hidden, shape.num_blocks
+    loader_cases = []
+    rng = np.random.default_rng(43)
+    for index in (True, False):
+        with tempfile.TemporaryDirectory() as tmp:
+            write_checkpoint_snapshot(tmp, index)
+            try:
+                ld = sl.ShardedSafetensorLoader(Path(tmp), pin_ram_cache=False)
+            except TypeError as e:
+                # without an index the reference iterates a safe_open handle,
+                # which safetensors 0.7 does not support
+                loader_cases.append({"index": index, "error": f"TypeError: {e}"})
+                continue
+            case = {"index": index, "weight_map": dict(sorted(ld.weight_map.items())),
+                    "aux": {k: sorted(v) for k, v in sorted(ld._quant_aux_by_base.items())}, "blocks": []}
+            for name in sorted(ld._quant_aux_by_base):
+                if name not in ld.weight_map:
+                    continue
+                is_down = "down_proj" in name
+                bpb = (shape.intermediate // 2) * 32 if is_down else (H // 2) * 32
+                nblk = (H if is_down else shape.intermediate) // 32
+                idx = rng.choice(nblk, size=min(5, nblk), replace=False)
+                got = ld.load_nf4_packed_blocks(name, torch.from_numpy(idx), bytes_per_block=bpb)
+                w, aux = ld._load_raw_for_param(name, store_in_ram_cache=False)
+                case["blocks"].append({"name": name, "bytes_per_block": bpb, "idx": idx.tolist(),
+                                       "shape": list(got.shape), "sha": sha(got.numpy()),
+                                       "raw_shape": list(w.shape), "aux_keys": sorted(aux)})
+            loader_cases.append(case)
+
+    R = rt.StreamingLlamaRuntime
+    hot_cases = []
+    g = np.random.default_rng(47)
+
+    def runtime_for(limit, used, routing_layers, rtk):
+        r = new_runtime(rt)
+        r._hot_block_threshold = 0.8
+        r._sparse_runtime_top_k = rtk
+        r._sparse_top_k = max(1, rtk)
+        r._vram_hot_cache_limit_bytes = limit
+        r._vram_hot_cache_used_bytes = used
+        r._sparse_routing = {i: {} for i in range(routing_layers)}
+        r.num_layers = 126
+        r._sparse_param_cache = {}
+        r._sparse_block_size = 32
+        r.config = _types.SimpleNamespace(hidden_size=H, intermediate_size=shape.intermediate)
+        return r
+
+    def vec(kind, n):
+        if kind == "rand":
+            return g.random(n).astype(np.float32)
+        if kind == "peaky":   # a few blocks near the max, the rest well below the threshold
+            v = (g.random(n) * 0.5).astype(np.float32)
+            v[g.choice(n, size=4, replace=False)] = (0.85 + 0.15 * g.random(4)).astype(np.float32)
+            return v
+        return np.zeros(n, np.float32)
+
+    specs = [
+        ("state.block_importance", "rand", NB, None, 0.8),
+        ("state.block_importance_probs", "rand", NB - 7, None, 0.8),
+        ("state._block_importance_probs", "peaky", NB, None, 0.8),
+        ("stats.scores", "rand", NB + 5, None, 0.8),
+        ("stats.map", "rand", NB, None, 0.8),
+        ("importance", "rand", NB, None, 0.8),
+        ("state.block_importance", "zero", NB, None, 0.8),
+        ("decoder_bias", "rand", NB, None, 0.8),
+        ("none", "rand", NB, None, 0.8),
+        ("state.block_importance", "peaky", NB, 150_000, 0.8),
+        ("state.block_importance", "rand", NB, 260_000, 0.5),
+        ("state.block_importance", "rand", NB, None, 0.0),
+        ("state.block_importance", "rand", NB, None, 1.0),
+        ("stats.map", "peaky", NB, 400_000, 0.9),
+    ]
+    for t, (where, kind, n, limit, thr) in enumerate(specs):
+        v = vec(kind, n)
+        state, stats, imp = {"layer_idx": int(t % 5)}, {"explained_variance_ratio": 0.9}, None
+        if t % 3 == 0:
+            state["top_k"] = int(3 + t)
+        if where.startswith("state."):
+            state[where.split(".", 1)[1]] = torch.from_numpy(v) if t % 2 == 0 else v.tolist()
+        elif where == "stats.scores":
+            stats = {"scores": torch.from_numpy(v)}
+        elif where == "stats.map":
+            nz = g.choice(n, size=n // 3, replace=False)
+            stats = {str(int(i)): float(v[i]) for i in nz}
+            stats["not_a_block"] = 3.0
+            stats[str(n + 9)] = 99.0
+        elif where == "importance":
+            imp = torch.from_numpy(v)
+        elif where == "decoder_bias":
+            state["decoder_bias"] = torch.from_numpy(g.standard_normal((NB, 8)).astype(np.float32))
+        rtk = int(g.integers(1, 12))
+        routing_layers = int(g.integers(1, 4))
+        r = runtime_for(limit, 0, routing_layers, rtk)
+        r._hot_block_threshold = float(thr)
+        got = R._derive_hot_blocks_for_layer(r, layer_state=state, layer_stats=stats,
+                                             block_importance_by_layer=imp, layer_num_blocks=NB)
+        def enc(x):
+            if torch.is_tensor(x):
+                return {"tensor": x.tolist()}
+            if isinstance(x, dict):
+                return {"dict": {k: enc(v) for k, v in x.items()}}
+            return x
+        hot_cases.append({"state": enc(state), "stats": enc(stats), "importance": enc(imp), "num_blocks": NB,
+                          "hidden": H, "limit": limit, "routing_layers": routing_layers, "runtime_top_k": rtk,
+                          "threshold": float(thr), "hot": None if got is None else got.tolist()})
+    blob = {"shape": CHECKPOINT_SHAPE, "seed": CHECKPOINT_SEED, "loader": loader_cases, "hot_blocks": hot_cases}
+    (HERE / "checkpoint.json").write_text(json.dumps(blob, indent=0))
+
+
 def main() -> None:
     rt, tsm = load_reference()
+    if sys.argv[1:] == ["checkpoint"]:
+        gen_checkpoint(rt)
+        print("wrote", HERE / "checkpoint.json")
+        return
     out: dict = {}
     gen_router(rt, out)
     print("router done", flush=True)
