@@ -223,13 +223,91 @@ def hot_cache_bytes_per_block(hidden: int, block_size: int = 32) -> int:
     return 2 * per_proj + int(hidden) * max(1, int(block_size) // 2) + int(hidden) * 4
 
 
+def top_count_blocks(counts: np.ndarray, k: int) -> np.ndarray:
+    """The ``k`` blocks with the highest counts, count-descending, ties to the
+    lower block id (``torch.topk`` in the reference leaves tie order open)."""
+    c = np.asarray(counts, np.float32).reshape(-1)
+    k = max(0, min(int(k), c.size))
+    return np.argsort(-c, kind="stable")[:k].astype(np.int64)
+
+
+def assign_staging_rows(misses: np.ndarray, prefetched: dict[int, int], staging: int) -> tuple[np.ndarray, np.ndarray]:
+    """Staging row of every miss -- a prefetched block keeps its row, the
+    others take the remaining rows in ascending order -- and the mask of the
+    misses whose records still have to be copied."""
+    misses = np.asarray(misses, np.int64).reshape(-1)
+    if misses.size > int(staging):
+        raise RuntimeError(f"{misses.size} misses exceed the {int(staging)} staging rows")
+    rows = np.full(misses.size, -1, np.int32)
+    copy = np.ones(misses.size, bool)
+    taken = np.zeros(int(staging), bool)
+    for i, blk in enumerate(misses.tolist()):
+        r = prefetched.get(int(blk))
+        if r is not None:
+            rows[i], copy[i], taken[r] = r, False, True
+    free = np.nonzero(~taken)[0]
+    rows[copy] = free[: int(copy.sum())]
+    return rows, copy
+
+
+class HotCacheCalibration:
+    """Live calibration of the layers' hot sets from decode routes
+    (``calibrate_vram_hot_cache``, ``streaming_llama_runtime.py:2374-2500``):
+    while active, every decode selection adds recency-weighted hits
+    (``record_calibration_hits``); ``hot_sets`` then gives each layer with hits
+    its capacity (``target_hot_blocks``, at least the previous hot count) of
+    top-count blocks, and ``rebuild`` pre-warms the caches with them."""
+
+    def __init__(self, recency_power: float = 0.0):
+        self.recency_power = float(recency_power)
+        self.hits: dict[int, np.ndarray] = {}
+        self.active = True
+
+    def record(self, layer_idx: int, active_blocks, num_blocks: int) -> None:
+        if self.active:
+            self.hits[int(layer_idx)] = record_calibration_hits(self.hits.get(int(layer_idx)), active_blocks,
+                                                                num_blocks, self.recency_power)
+
+    def hot_sets(self, *, runtime_top_k, previous_hot: dict[int, int] | None = None, limit_bytes: int | None = None,
+                 used_bytes: int = 0, sparse_layers: int | None = None,
+                 bytes_per_block: int = 1_048_576) -> dict[int, np.ndarray]:
+        """``runtime_top_k``: one k, or a dict layer -> k (the routing's top-k)."""
+        out = {}
+        n_layers = int(sparse_layers) if sparse_layers is not None else max(1, len(self.hits))
+        for li, counts in sorted(self.hits.items()):
+            if float(counts.sum()) <= 0.0:
+                continue
+            rtk = runtime_top_k[li] if isinstance(runtime_top_k, dict) else runtime_top_k
+            cap = target_hot_blocks(layer_idx=li, runtime_top_k=int(rtk), count_slots=counts.size,
+                                    previous_hot_count=int((previous_hot or {}).get(li, 0)), limit_bytes=limit_bytes,
+                                    used_bytes=used_bytes, sparse_layers=n_layers, bytes_per_block=bytes_per_block)
+            out[li] = top_count_blocks(counts, cap)
+        return out
+
+    def rebuild(self, caches: dict[int, "CachedSparseMlp"], **kw) -> dict:
+        """Pre-warm each calibrated layer's cache with its new hot set (the
+        first ``capacity`` blocks of it: the banks here do not grow)."""
+        kw.setdefault("runtime_top_k", {li: c.router.top_k for li, c in caches.items()})
+        kw.setdefault("previous_hot", {li: c.bank.active for li, c in caches.items()})
+        kw.setdefault("bytes_per_block", hot_cache_bytes_per_block(next(iter(caches.values())).H) if caches else 1)
+        sets = self.hot_sets(**kw)
+        cached = 0
+        for li, blocks in sets.items():
+            if li in caches:
+                caches[li].pre_warm(blocks)
+                cached += min(blocks.size, caches[li].capacity)
+        return {"updated_layers": len(sets), "hits": float(sum(float(self.hits[li].sum()) for li in sets)),
+                "cached_blocks": cached}
+
+
 # --------------------------------------------------------------------------- cached decode
 @dataclass
 class CacheStats:
     hits: int
     misses: int
-    h2d_bytes: int
+    h2d_bytes: int        # bytes copied host -> device for this token (prefetched misses excluded)
     promoted: int
+    prefetched: int = 0   # misses whose records a lookahead prefetch had already staged
 
 
 class CachedSparseMlp:
@@ -260,6 +338,7 @@ class CachedSparseMlp:
         self.idx_dev = torch.empty(self.router.top_k, dtype=torch.int32, device=self.dev)
         self.idx_host = torch.empty(self.router.top_k, dtype=torch.int32, pin_memory=True)
         self.side = torch.cuda.Stream(device=self.dev)
+        self.prefetched: dict[int, int] = {}  # block -> staging row, staged ahead by prefetch()
         self._lib = _lib.load()
 
     # ---- bank contents
@@ -280,10 +359,34 @@ class CachedSparseMlp:
         self._upload_table(main)
         torch.cuda.synchronize(self.dev)
 
+    # ---- lookahead
+    def prefetch(self, blocks) -> int:
+        """Start copying the records of ``blocks`` that are not resident into
+        the staging rows on the side stream, ahead of this layer's next
+        ``decode`` (the reference's decode lookahead,
+        ``streaming_llama_runtime.py:7780-7795``, ``:4910-5102``).  A block the
+        next selection also lists is then served from its staged row without a
+        copy; rows of blocks it does not list are reused.  Returns the number
+        of records copied."""
+        b = np.asarray(blocks, np.int64).reshape(-1)
+        b = b[(b >= 0) & (b < self.NB)]
+        b = b[self.slot_host[b] < 0]
+        b = np.unique(b)[: self.staging] if b.size else b
+        self.prefetched = {int(blk): i for i, blk in enumerate(b.tolist())}
+        if b.size:
+            # staging rows are free once the work queued so far (this layer's
+            # previous token included) has run
+            self.side.wait_stream(torch.cuda.current_stream(self.dev))
+            self._stage(b, np.arange(b.size, dtype=np.int32), self.pool[self.capacity:], self.staging, self.side)
+        return int(b.size)
+
     # ---- one token
-    def decode(self, x: torch.Tensor, idx: torch.Tensor | None = None, out_dtype=torch.float32):
+    def decode(self, x: torch.Tensor, idx: torch.Tensor | None = None, out_dtype=torch.float32, *,
+               calibration: "HotCacheCalibration | None" = None, layer_idx: int = 0):
         """MLP output for one token ``x [H]``.  The router always runs; ``idx``
-        (int32 block ids on the device) replaces its selection when given."""
+        (int32 block ids on the device) replaces its selection when given.
+        With ``calibration`` the selection is recorded as layer ``layer_idx``'s
+        live route."""
         from .mlp import sparse_mlp_decode
 
         main = torch.cuda.current_stream(self.dev)
@@ -303,19 +406,23 @@ class CachedSparseMlp:
             raise RuntimeError("selected block id out of range")
         if np.unique(blocks).size != blocks.size:
             raise RuntimeError("the selection lists a block twice")
+        if calibration is not None:
+            calibration.record(layer_idx, blocks[None, :], self.NB)
         slots = self.slot_host[blocks]
         hit_mask = slots >= 0
         misses = blocks[~hit_mask]
         if misses.size > self.staging:
             raise RuntimeError(f"{misses.size} misses exceed the {self.staging} staging rows")
-        # misses: pinned host -> staging rows on the side stream
+        # misses: pinned host -> staging rows on the side stream (prefetched
+        # records are already there or on their way, queued on the same stream)
+        rows, copy = assign_staging_rows(misses, self.prefetched, self.staging)
         smap = self.stage_map_host.numpy()
         smap[:] = -1
-        smap[misses] = np.arange(misses.size, dtype=np.int32)
+        smap[misses] = rows
         self.side.wait_stream(main)  # staging rows are free once the previous token is done
-        if misses.size:
-            self._stage(misses, np.arange(misses.size, dtype=np.int32), self.pool[self.capacity:], self.staging,
-                        self.side)
+        if copy.any():
+            self._stage(misses[copy], rows[copy], self.pool[self.capacity:], self.staging, self.side)
+        self.prefetched = {}
         with torch.cuda.stream(self.side):
             self.stage_map_dev.copy_(self.stage_map_host, non_blocking=True)
         staged = torch.cuda.Event()
@@ -331,9 +438,10 @@ class CachedSparseMlp:
         if hit_mask.any():
             self.bank.add_hits(slots[hit_mask])
         if self.promote and misses.size:
-            promoted = self._promote(misses, main)
-        stats = CacheStats(hits=int(hit_mask.sum()), misses=int(misses.size), h2d_bytes=int(misses.size) * self.rec,
-                           promoted=promoted)
+            promoted = self._promote(misses, rows, main)
+        n_copy = int(copy.sum())
+        stats = CacheStats(hits=int(hit_mask.sum()), misses=int(misses.size), h2d_bytes=n_copy * self.rec,
+                           promoted=promoted, prefetched=int(misses.size) - n_copy)
         return (y if out_dtype == torch.float32 else y.to(out_dtype)), stats
 
     def _stage(self, blocks: np.ndarray, rows: np.ndarray, pool: torch.Tensor, pool_rows: int,
@@ -346,7 +454,7 @@ class CachedSparseMlp:
                                              dst.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), int(pool_rows),
                                              stream.cuda_stream), "nsm_cache_stage")
 
-    def _promote(self, misses: np.ndarray, main: torch.cuda.Stream) -> int:
+    def _promote(self, misses: np.ndarray, rows: np.ndarray, main: torch.cuda.Stream) -> int:
         old = self.bank.block_ids.copy()
         active_before = self.bank.active
         slots = self.bank.plan_update(misses)
@@ -358,12 +466,62 @@ class CachedSparseMlp:
             if ob >= 0 and self.slot_host[ob] == slot:
                 self.slot_host[ob] = -1
             self.slot_host[misses[i]] = slot
-        # staged record i -> bank slot (device to device), after the staged compute
-        src = torch.from_numpy(np.arange(n, dtype=np.int64) + self.capacity).to(self.dev, non_blocking=True)
+        # staged record of miss i -> bank slot (device to device), after the staged compute
+        src = torch.from_numpy(rows[:n].astype(np.int64) + self.capacity).to(self.dev, non_blocking=True)
         dst = torch.from_numpy(slots.astype(np.int64)).to(self.dev, non_blocking=True)
         self.pool.index_copy_(0, dst, self.pool.index_select(0, src))
         self._upload_table(main)
         return int(n)
+
+
+class CachedLayerStack:
+    """A token through several cached layers with the residual carried
+    (``residual += MLP(rmsnorm(residual) * norm_weight)``; attention is
+    identity, as in the benchmark's layer stack).  With ``lookahead``, each
+    layer first routes the NEXT layer from its own pre-MLP residual and starts
+    that layer's predicted misses on the next layer's side stream, so the
+    copies overlap this layer's MLP (the reference predicts the next layer from
+    the residual before the next attention, ``:7780-7795``).  A prediction
+    only decides what is copied early: the selection is always the real
+    router's, so outputs do not depend on ``lookahead``."""
+
+    def __init__(self, caches: list[CachedSparseMlp], norm_weights: list[torch.Tensor | None] | None = None, *,
+                 eps: float = 1e-5, lookahead: bool = True):
+        self.caches = list(caches)
+        self.norm = list(norm_weights) if norm_weights is not None else [None] * len(self.caches)
+        self.eps = float(eps)
+        self.lookahead = bool(lookahead)
+        dev = self.caches[0].dev
+        self._pred = torch.empty(max(c.router.top_k for c in self.caches), dtype=torch.int32, device=dev)
+        self._pred_host = torch.empty(self._pred.numel(), dtype=torch.int32, pin_memory=True)
+
+    def _input(self, residual: torch.Tensor, li: int) -> torch.Tensor:
+        r = residual.float()
+        x = r * torch.rsqrt(r.square().mean() + self.eps)
+        if self.norm[li] is not None:
+            x = x * self.norm[li].float()
+        return x.to(torch.bfloat16)
+
+    def _predict(self, x: torch.Tensor, li: int) -> np.ndarray:
+        c = self.caches[li]
+        k = c.router.top_k
+        sparse_route_only(x, c.router, self._pred[:k])
+        self._pred_host[:k].copy_(self._pred[:k], non_blocking=True)
+        torch.cuda.current_stream(c.dev).synchronize()
+        return self._pred_host[:k].numpy().astype(np.int64)
+
+    def decode_token(self, residual: torch.Tensor, *, calibration: HotCacheCalibration | None = None):
+        """Run every layer on ``residual`` (fp32 ``[H]``, updated in place);
+        returns the per-layer ``CacheStats``."""
+        stats = []
+        for li, c in enumerate(self.caches):
+            x = self._input(residual, li)
+            if self.lookahead and li + 1 < len(self.caches):
+                self.caches[li + 1].prefetch(self._predict(self._input(residual, li + 1), li + 1))
+            y, st = c.decode(x, calibration=calibration, layer_idx=li)
+            residual.add_(y)
+            stats.append(st)
+        return stats
 
 
 def sparse_route_only(x: torch.Tensor, router: RouterWeights, idx_out: torch.Tensor) -> None:

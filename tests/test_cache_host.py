@@ -77,3 +77,46 @@ def test_record_layout(hidden):
     assert end == cache.record_bytes(hidden)
     # the per-block algorithmic bytes of the decode (gate+up packed+absmax, down packed+absmax)
     assert end == 2 * (16 * hidden + 2 * hidden) + 16 * hidden + 4 * hidden
+
+
+# --------------------------------------------------------------------------- lookahead rows and calibration
+def test_assign_staging_rows_keeps_prefetched_rows():
+    rows, copy = cache.assign_staging_rows(np.array([7, 3, 9, 4]), {9: 0, 5: 1, 3: 2}, 6)
+    assert rows.tolist() == [1, 2, 0, 3] and copy.tolist() == [True, False, False, True]
+    rows, copy = cache.assign_staging_rows(np.array([1, 2]), {}, 4)
+    assert rows.tolist() == [0, 1] and copy.all()
+    rows, copy = cache.assign_staging_rows(np.zeros(0, np.int64), {2: 0}, 4)
+    assert rows.size == 0
+    with pytest.raises(RuntimeError, match="staging rows"):
+        cache.assign_staging_rows(np.arange(5), {}, 4)
+
+
+def test_top_count_blocks_order_and_ties():
+    c = np.array([1.0, 3.0, 3.0, 0.0, 2.0, 3.0], np.float32)
+    assert cache.top_count_blocks(c, 4).tolist() == [1, 2, 5, 4]
+    assert cache.top_count_blocks(c, 10).tolist() == [1, 2, 5, 4, 0, 3]
+    assert cache.top_count_blocks(c, 0).size == 0
+
+
+def test_calibration_matches_reference_pieces():
+    rng = np.random.default_rng(4)
+    nb, k = 64, 6
+    cal = cache.HotCacheCalibration(recency_power=1.0)
+    ref = {}
+    for tok in range(12):
+        for li in (0, 2):
+            sel = rng.choice(nb, size=(1 if tok % 3 else 2, k), replace=True if tok % 5 == 0 else False)
+            cal.record(li, sel, nb)
+            ref[li] = cp.record_calibration_hits(ref.get(li), sel, nb, 1.0)
+    cal.record(5, np.zeros((1, 0), np.int64), nb)   # a layer without hits is skipped
+    for li in (0, 2):
+        assert np.array_equal(cal.hits[li], ref[li])
+    kw = dict(limit_bytes=3 * 917504 * 20, used_bytes=917504, sparse_layers=4, bytes_per_block=917504)
+    sets = cal.hot_sets(runtime_top_k={0: k, 2: k, 5: k}, previous_hot={2: 30}, **kw)
+    assert sorted(sets) == [0, 2]
+    for li, prev in ((0, 0), (2, 30)):
+        cap = cp.target_hot_blocks(layer_idx=li, runtime_top_k=k, count_slots=nb, previous_hot_count=prev, **kw)
+        assert sets[li].tolist() == np.argsort(-ref[li], kind="stable")[:cap].tolist()
+    cal.active = False
+    cal.record(0, np.arange(k)[None, :], nb)
+    assert np.array_equal(cal.hits[0], ref[0])

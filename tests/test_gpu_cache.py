@@ -132,3 +132,100 @@ def test_cache_rejects_bad_selections(dev):
         cm.decode(x, idx=torch.tensor([0, 0, 1, 2], dtype=torch.int32, device=dev))
     with pytest.raises(RuntimeError):
         cm.decode(x, idx=torch.tensor([0, 1, 2, shape.num_blocks], dtype=torch.int32, device=dev))
+
+
+def _twin_caches(shape, w, rw, capacity, hot):
+    from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore
+
+    store = HostBlockStore.from_weights(w)
+    a, b = CachedSparseMlp(rw, store, capacity), CachedSparseMlp(rw, store, capacity)
+    a.pre_warm(hot)
+    b.pre_warm(hot)
+    return a, b
+
+
+def test_prefetch_serves_misses_without_copies(dev):
+    from next_step_ai_b200 import sparse_mlp_decode
+    from next_step_ai_b200 import synthetic as dsyn
+
+    shape, w, rw = _layer("small", dev, seed=13)
+    nb, k, cap = shape.num_blocks, shape.top_k, 40
+    rng = np.random.default_rng(3)
+    a, b = _twin_caches(shape, w, rw, cap, rng.choice(nb, cap, replace=False))
+    for tok, frac in enumerate((1.0, 0.5, 0.0)):
+        res = set(a.bank.block_ids[: a.bank.active].tolist())
+        cold = sorted(set(range(nb)) - res)
+        sel = np.concatenate([rng.choice(sorted(res), 9, replace=False), rng.choice(cold, k - 9, replace=False)])
+        misses = sel[9:]
+        early = misses[: int(round(frac * misses.size))]
+        others = rng.choice(sorted(set(cold) - set(misses.tolist())), 3, replace=False)
+        assert a.prefetch(np.concatenate([early, others])) == early.size + 3
+        x = dsyn.make_x(shape, 40 + tok, 1, dev)[0]
+        idx = torch.from_numpy(sel.astype(np.int32)).to(dev)
+        ya, sa = a.decode(x, idx=idx)
+        yb, sb = b.decode(x, idx=idx)
+        assert torch.equal(ya, yb)
+        assert (sa.hits, sa.misses, sa.promoted) == (sb.hits, sb.misses, sb.promoted)
+        assert sa.prefetched == early.size and sa.h2d_bytes == (misses.size - early.size) * 56 * shape.hidden
+        assert np.array_equal(a.bank.block_ids, b.bank.block_ids) and np.array_equal(a.slot_host, b.slot_host)
+        _close(ya.cpu().numpy(), sparse_mlp_decode(x, None, w, idx=idx, out_dtype=torch.float32).cpu().numpy())
+    # promoted records came from the prefetched rows: the banks hold the same bytes
+    torch.cuda.synchronize()
+    assert torch.equal(a.pool[:cap], b.pool[:cap])
+
+
+def test_layer_stack_lookahead_is_exact(dev):
+    from next_step_ai_b200 import sparse_mlp_decode
+    from next_step_ai_b200 import synthetic as dsyn
+    from next_step_ai_b200.cache import CachedLayerStack, CachedSparseMlp, HostBlockStore
+
+    layers = [_layer("small", dev, seed=20 + i) for i in range(3)]
+    shape = layers[0][0]
+    rng = np.random.default_rng(8)
+    stacks = []
+    hots = [rng.choice(shape.num_blocks, 40, replace=False) for _ in layers]
+    for look in (True, False):
+        cs = []
+        for (_, w, rw), hot in zip(layers, hots):
+            c = CachedSparseMlp(rw, HostBlockStore.from_weights(w), 40)
+            c.pre_warm(hot)
+            cs.append(c)
+        stacks.append(CachedLayerStack(cs, lookahead=look))
+    prefetched = 0
+    for tok in range(3):
+        h0 = dsyn.make_x(shape, 70 + tok, 1, dev)[0].float() * 3.0
+        ra, rb, rr = h0.clone(), h0.clone(), h0.clone()
+        sta = stacks[0].decode_token(ra)
+        stb = stacks[1].decode_token(rb)
+        assert torch.equal(ra, rb)
+        assert [s.misses for s in sta] == [s.misses for s in stb]
+        prefetched += sum(s.prefetched for s in sta)
+        assert all(s.prefetched == 0 for s in stb)
+        for li, (_, w, rw) in enumerate(layers):   # all-resident replay of the same layers
+            rr.add_(sparse_mlp_decode(stacks[1]._input(rr, li), rw, w, out_dtype=torch.float32))
+        _close(ra.cpu().numpy(), rr.cpu().numpy())
+    assert prefetched > 0
+
+
+def test_calibration_rebuild_prewarms_top_counts(dev):
+    from next_step_ai_b200 import route_sparse_mlp, sparse_mlp_decode
+    from next_step_ai_b200 import synthetic as dsyn
+    from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore, HotCacheCalibration, top_count_blocks
+
+    shape, w, rw = _layer("small", dev, seed=31)
+    cm = CachedSparseMlp(rw, HostBlockStore.from_weights(w), 24)
+    cm.pre_warm(np.arange(24))
+    cal = HotCacheCalibration()
+    counts = np.zeros(shape.num_blocks, np.float32)
+    for tok in range(5):
+        x = dsyn.make_x(shape, 90 + tok, 1, dev)[0]
+        cm.decode(x, calibration=cal, layer_idx=3)
+        np.add.at(counts, route_sparse_mlp(x, rw)[0].cpu().numpy(), 1.0)
+    assert np.array_equal(cal.hits[3], counts)
+    out = cal.rebuild({3: cm})
+    assert out["updated_layers"] == 1 and out["hits"] == 5 * shape.top_k
+    assert cm.bank.block_ids[: cm.bank.active].tolist() == top_count_blocks(counts, 24).tolist()
+    x = dsyn.make_x(shape, 99, 1, dev)[0]
+    y, st = cm.decode(x)
+    sel = route_sparse_mlp(x, rw)[0].to(torch.int32)
+    _close(y.cpu().numpy(), sparse_mlp_decode(x, None, w, idx=sel, out_dtype=torch.float32).cpu().numpy())
