@@ -566,6 +566,109 @@ def run_union(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+LM_HEAD_VOCAB = 128256   # Llama-3.1 vocabulary (405B LM head: 128256 x 16384)
+
+
+def run_lm_head(args) -> None:
+    """NF4 LM head of the 405B shape (vocab 128256 x hidden 16384, NF4 blocksize
+    64): one decode token's logits per step through ``Nf4LmHead`` (prep, GEMV
+    and split-K finalize launches), the whole 1.18 GB weight streamed per step
+    (larger than L2, so no flush is needed).  Not a BASELINE config: the row of
+    the build's scope table that follows the MLP path."""
+    import numpy as np
+    import torch
+
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from next_step_ai_b200.lm_head import Nf4LmHead
+
+    V, H = LM_HEAD_VOCAB, HIDDEN
+    t0 = time.time()
+    gen = torch.Generator(device=dev).manual_seed(77)
+    w = torch.randn((V, H), generator=gen, device=dev, dtype=torch.bfloat16) * 0.02
+    head = Nf4LmHead.from_dense(w, dev)
+    del w
+    torch.cuda.empty_cache()
+    x = (torch.randn((1, H), generator=gen, device=dev)).to(torch.bfloat16)
+    out = torch.empty((1, V), dtype=torch.bfloat16, device=dev)
+    gen_s = time.time() - t0
+
+    def step():
+        out.copy_(head(x))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        # end to end: pinned host x -> device, logits -> pinned host, every step
+        xh = x.cpu().pin_memory()
+        oh = torch.empty((1, V), dtype=torch.bfloat16).pin_memory()
+        for _ in range(args.warmup):
+            oh.copy_(head(xh.to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(args.steps):
+            oh.copy_(head(xh.to(dev, non_blocking=True)), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms_e2e = e0.elapsed_time(e1) / args.steps
+    # parity spot check on 64 rows (fp64 dequant of the same bytes)
+    rows = torch.from_numpy(np.random.default_rng(3).choice(V, 64, replace=False)).to(dev)
+    pk = head.packed.view(V, H // 2)[rows]
+    nib = torch.stack([pk >> 4, pk & 15], dim=-1).reshape(64, H).long()
+    wd = head.code.double()[nib] * head.absmax.view(V, H // 64)[rows].double().repeat_interleave(64, dim=1)
+    ref = wd @ x.double().reshape(H)
+    got = head(x, out_dtype=torch.float32).reshape(V)[rows].double()
+    max_abs = float((got - ref).abs().max())
+    algo = V * H // 2 + V * (H // 64) * 4 + 2 * H + 2 * V
+    pk_ = peaks()
+    gbs = algo / (ms * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        # the reference's CPU head is F.linear on the dense weight: time it on
+        # a 2048-row slice with all host threads and scale to the vocabulary
+        torch.set_num_threads(os.cpu_count() or 1)
+        wc = torch.randn((2048, H), dtype=torch.float32) * 0.02
+        xc = torch.randn((1, H), dtype=torch.float32)
+        torch.nn.functional.linear(xc, wc)
+        c0 = time.time()
+        reps = 20
+        for _ in range(reps):
+            torch.nn.functional.linear(xc, wc)
+        per = (time.time() - c0) / reps * (V / 2048)
+        cpu = {"value": 1.0 / per, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": "F.linear fp32 [1,16384] x [2048,16384].T, 20 reps, scaled to 128256 rows"}
+    line = {
+        "metric": "NF4 LM head tok/s (405B shape: vocab 128256 x 16384, one decode token)",
+        "value": 1e3 / ms, "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+        "dtype": "nf4 weights, fp16 x fp16 -> fp32 MMA, bf16 io",
+        "data": "synthetic: N(0, 0.02) weight quantised to NF4 on the device, N(0,1) bf16 hidden",
+        "config": {"workload": "NF4 LM head, 405B shape", "vocab": V, "hidden": H, "quant_block_size": 64,
+                   "l2": "weight (1.18 GB) larger than L2", "synthetic_gen_s": round(gen_s, 1)},
+        "e2e": {"value": 1e3 / ms_e2e, "unit": "tok/s", "h2d_bytes_per_step": 2 * H, "d2h_bytes_per_step": 2 * V},
+        "gpu_launches": 3 * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk_["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / pk_["hbm_gbs"], 4), "algorithmic_bytes": algo,
+                     "kernel": "nsm_lm_head_nf4 (prep + GEMV + finalize launches, timed together)",
+                     "peak_source": pk_["source"]},
+        "parity_spot_check": {"rows": 64, "max_abs_vs_fp64": max_abs},
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -575,9 +678,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--unique-layers", type=int, default=0,
                     help="cap the resident layers (cycled over the 126); for small profiling captures")
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4],
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5],
                     help="2: the 126-layer headline step (default); 3: hot-block cache layer; "
-                         "4: 32-token union decode")
+                         "4: 32-token union decode; 5: NF4 LM head (405B vocab)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -586,6 +689,9 @@ def main() -> None:
         return
     if args.config == 4 and args.impl != "reference":
         run_union(args)
+        return
+    if args.config == 5 and args.impl != "reference":
+        run_lm_head(args)
         return
     if args.impl == "reference":
         run_reference(args)

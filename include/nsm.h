@@ -375,6 +375,26 @@ int nsm_cache_promote(const nsm_mlp_weights* w, int32_t hidden, const int32_t* s
 int nsm_cache_stage(const void* host_base, const int32_t* blocks, int32_t n, size_t record_bytes, void* pool_base,
                     const int32_t* dst_rows, int32_t pool_rows, nsm_stream_t stream);
 
+/* ---- NF4 LM head ---------------------------------------------------------
+ * logits[t][v] = sum_h code[nib(v*H+h)] * absmax[(v*H+h)/qbs] * x[t][h] (+ bias[v])
+ * for a bitsandbytes row-major NF4 weight W [V = out_features, H = in_features]
+ * (flat bytes, element e in byte e/2, high nibble = even element; fp32
+ * absmax; 16-entry fp32 code) and 1..nsm_lm_head_max_tokens(H) tokens x
+ * [tokens][H].  Replaces the GPU NF4 LM head of runtime/lm_head.py:267-468
+ * (_materialize_lm_head_nf4_on_gpu + _lm_head_forward's
+ * triton_sparse_input_linear_4bit call, :450-468) with the math of its dense
+ * head (F.linear on the dequantised weight, :472-480).  H a multiple of 64,
+ * quant_block_size a multiple of 64; packed 16-byte, absmax 4-byte and the
+ * workspace 256-byte aligned.  x, bias and out may be fp32 / fp16 / bf16;
+ * accumulation is fp32 (fp16 weights x power-of-two-scaled fp16 x on the
+ * tensor cores, the absmax applied per 64 columns in fp32). */
+size_t nsm_lm_head_workspace_bytes(int32_t tokens, int32_t out_features, int32_t in_features);
+int nsm_lm_head_max_tokens(int32_t in_features);
+int nsm_lm_head_nf4(const void* x, int32_t x_dtype, int32_t tokens, const uint8_t* packed, const float* absmax,
+                    const float* code, int32_t out_features, int32_t in_features, int32_t quant_block_size,
+                    const void* bias, int32_t bias_dtype, void* out, int32_t out_dtype, void* workspace,
+                    size_t workspace_bytes, nsm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,6 +41,7 @@ EXPORTED = (
     "nsm_repack_tiled", "nsm_decode_gathered_static", "nsm_workspace_error", "nsm_cache_stage",
     "nsm_union_workspace_bytes", "nsm_union_decode", "nsm_residual_flush", "nsm_exchange_bytes",
     "nsm_exchange_create", "nsm_exchange_connect", "nsm_exchange_destroy", "nsm_route_workspace_bytes",
+    "nsm_lm_head_workspace_bytes", "nsm_lm_head_max_tokens", "nsm_lm_head_nf4",
     "nsm_route_rows",
 )
 
@@ -87,6 +88,10 @@ _SIGS = {
     "nsm_route": (c_int, [c_void_p, c_int32, c_int32, POINTER(RouterWeightsC), c_void_p, c_void_p, c_void_p,
                           c_void_p, c_size_t, c_void_p]),
     "nsm_route_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "nsm_lm_head_workspace_bytes": (c_size_t, [c_int32, c_int32, c_int32]),
+    "nsm_lm_head_max_tokens": (c_int, [c_int32]),
+    "nsm_lm_head_nf4": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_size_t, c_void_p]),
     "nsm_route_rows": (c_int, [c_void_p, c_int32, c_int32, c_int32, POINTER(RouterWeightsC), c_void_p, c_void_p,
                                c_void_p, c_void_p, c_size_t, c_void_p]),
     "nsm_sparse_mlp_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, POINTER(LayerIoC),

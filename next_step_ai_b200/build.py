@@ -15,7 +15,8 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libnsm.so"
-SOURCES = ["nsm_abi.cu", "nsm_router.cu", "nsm_decode.cu", "nsm_aux.cu", "nsm_static.cu", "nsm_union.cu", "nsm_exchange.cu"]
+SOURCES = ["nsm_abi.cu", "nsm_router.cu", "nsm_decode.cu", "nsm_aux.cu", "nsm_static.cu", "nsm_union.cu", "nsm_exchange.cu",
+           "nsm_lmhead.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
