@@ -407,6 +407,16 @@ class Nf4Checkpoint:
                 self.aux_names.setdefault(n.split(".weight.", 1)[0] + ".weight", []).append(n)
         self._handles: dict[str, Any] = {}
 
+    def close(self) -> None:
+        """Release the open shard handles (reopened on the next read)."""
+        self._handles.clear()
+
+    def __enter__(self) -> "Nf4Checkpoint":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
     def _tensors(self, names) -> dict[str, torch.Tensor]:
         from safetensors import safe_open
         out = {}

@@ -132,6 +132,16 @@ def test_load_param_recovers_bytes_and_absmax(snapshot):
         assert m.bytes_per_block == 32 * dims[1] // 2 and m.absmax_per_block == 32 * dims[1] // 64
 
 
+def test_reader_context_releases_handles(snapshot):
+    d, _ = snapshot
+    with ck.Nf4Checkpoint(d) as r:
+        r.load_raw("model.layers.0.mlp.up_proj.weight")
+        assert r._handles
+    assert not r._handles
+    w, aux = r.load_raw("model.layers.0.mlp.up_proj.weight")   # reopens on demand
+    assert w.dtype == torch.uint8 and aux
+
+
 def test_load_param_plain_absmax_and_errors(tmp_path):
     shape = syn.SHAPES["tiny"]
     full = syn.make_layer_full(shape, 3, 0)
