@@ -112,7 +112,8 @@ def load_router_artifact(source, *, hidden: int, intermediate: int, num_layers: 
                          sparse_top_k: int | None = None, sparse_basis_top_k: int | None = None,
                          dtype: torch.dtype = torch.float16, device: torch.device | str = "cpu",
                          hot_blocks: bool = False, hot_block_threshold: float = DEFAULT_HOT_BLOCK_THRESHOLD,
-                         hot_cache_limit_bytes: int | None = None, hot_cache_used_bytes: int = 0) -> RouterArtifact:
+                         hot_cache_limit_bytes: int | None = None, hot_cache_used_bytes: int = 0,
+                         trusted: bool = False) -> RouterArtifact:
     """Read a router artifact (a path or an already-loaded payload dict).
 
     Mirrors the reference's constructor (``streaming_llama_runtime.py:779-991``):
@@ -128,11 +129,22 @@ def load_router_artifact(source, *, hidden: int, intermediate: int, num_layers: 
     hot cache is enabled (``:979-990``), counting the layers loaded so far as
     the sparse layers of the capacity formula, as the reference does while it
     fills its routing table.
+
+    A file is read with torch's restricted unpickler (tensors, containers and
+    numbers: everything the artifact schema holds); ``trusted=True`` allows
+    arbitrary pickled objects, as the reference's ``weights_only=False`` load
+    does, and should only be used for files from a trusted source.
     """
     if isinstance(source, dict):
         payload = source
     else:
-        payload = torch.load(str(source), map_location="cpu", weights_only=False)
+        try:
+            payload = torch.load(str(source), map_location="cpu", weights_only=not trusted)
+        except Exception as e:
+            if trusted:
+                raise
+            raise RuntimeError(f"{source}: not loadable with the restricted unpickler ({type(e).__name__}: {e}); "
+                               "pass trusted=True for an artifact from a trusted source") from e
     cfg = payload.get("config", {}) or {}
     raw_sel = payload.get("layer_selection", [])
     selection = {int(i) for i in raw_sel if 0 <= int(i) < num_layers} if isinstance(raw_sel, (list, tuple)) else set()

@@ -239,6 +239,24 @@ def test_router_artifact_fields_and_overrides(tmp_path):
     assert b.layers[0].basis_top_k == 2 and b.layers[1].basis_top_k == 2
 
 
+class _PickledNote:
+    """An arbitrary class: the restricted unpickler refuses to build it."""
+
+    def __init__(self, text: str):
+        self.text = text
+
+
+def test_router_artifact_restricted_unpickling(tmp_path):
+    shape = syn.SHAPES["tiny"]
+    payload = _artifact(shape, layers=(0,))
+    payload["stats"]["note"] = _PickledNote("fitted elsewhere")
+    torch.save(payload, tmp_path / "odd.pt")
+    kw = dict(hidden=shape.hidden, intermediate=shape.intermediate, num_layers=2)
+    with pytest.raises(RuntimeError, match="trusted=True"):
+        ck.load_router_artifact(tmp_path / "odd.pt", **kw)
+    assert sorted(ck.load_router_artifact(tmp_path / "odd.pt", trusted=True, **kw).layers) == [0]
+
+
 def test_router_artifact_errors_and_domains():
     shape = syn.SHAPES["tiny"]
     H, I = shape.hidden, shape.intermediate
