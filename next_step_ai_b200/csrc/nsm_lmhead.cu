@@ -15,9 +15,12 @@
 //     [2^14, 2^15), x/s as fp16 into the workspace (exact for bf16 / fp16
 //     inputs; the fp16 products below cannot overflow) and s;
 //  2. lmhead_gemv_kernel: persistent, one CTA of 16 warps per SM.  A work
-//     unit is 32 rows (two m16 tiles) x a run of 64-column chunks (split-K).
-//     Each warp streams its unit's chunks through its own 4-stage cp.async
-//     ring (per chunk and tile: 16 rows x 32 B + the 16 rows' absmax),
+//     unit is 16 rows (one m16 tile) x a run of 64-column chunks (split-K).
+//     Each warp streams its unit through its own 3-stage cp.async ring; a
+//     stage is 4 chunks: 16 rows x one 128-byte line (so every copy
+//     instruction moves whole lines: the copy cost scales with the lines
+//     touched) plus the rows' 4 absmax, with the 16-byte granules of a row
+//     XOR-swizzled by the row so the fragment reads are conflict-free.  It
 //     dequantises with the per-lane byte->half2 table (one prmt and one
 //     conflict-free shared load per byte) and accumulates with mma.sync
 //     m16n8k16 (f16 x f16 -> f32): A = 16 rows x 16 permuted columns of W,
@@ -38,11 +41,11 @@ namespace {
 
 constexpr int kLhWarps = 16;
 constexpr int kLhThreads = 32 * kLhWarps;
-constexpr int kLhTiles = 2;                           // m16 row tiles per unit
-constexpr int kLhRows = 16 * kLhTiles;
-constexpr int kLhStages = 4;
-constexpr int kLhTileBytes = 16 * 32 + 16 * 4;        // 16 rows x 32 B, 16 absmax
-constexpr int kLhStageBytes = kLhTiles * kLhTileBytes;
+constexpr int kLhRows = 16;                           // one m16 row tile per unit
+constexpr int kLhSc = 4;                              // 64-column chunks per ring stage
+constexpr int kLhRowBytes = 32 * kLhSc;               // one row's bytes per stage (a 128 B line)
+constexpr int kLhStages = 3;
+constexpr int kLhStageBytes = kLhRows * kLhRowBytes + kLhRows * kLhSc * 4;  // 16 x 128 B + absmax
 constexpr int kLhRingBytes = kLhWarps * kLhStages * kLhStageBytes;
 constexpr int kLhMaxTokens = 8;
 constexpr int kLhUnitsPerWarp = 8;                    // split-K target for load balance
@@ -120,25 +123,39 @@ __global__ void __launch_bounds__(kLhThreads, 1) lmhead_gemv_kernel(LmHeadParams
   const int ngroups = (p.V + kLhRows - 1) / kLhRows;
   const int units = ngroups * p.splits;
   const int nw = gridDim.x * kLhWarps;
+  const size_t hq = (size_t)(p.H / 64);  // 64-column chunks per row
   for (int u = blockIdx.x * kLhWarps + warp; u < units; u += nw) {
     const int grp = u / p.splits, sp = u - grp * p.splits;
     const int r0 = grp * kLhRows;
-    const int c0 = sp * p.cps;
-    const int n = min(p.nchunks, c0 + p.cps) - c0;
-    // chunk q of the unit -> stage q % kLhStages (an empty group past the end
-    // keeps the group count uniform)
+    const int c0 = sp * p.cps;                                   // a multiple of kLhSc
+    const int nst = (min(p.nchunks, c0 + p.cps) - c0) / kLhSc;   // stages of this unit
+    // stage q = chunks c0 + 4q .. +3.  Each copy instruction moves 4 rows x
+    // one 128-byte line; a row's 16-byte granule k is stored at k ^ (row & 7)
+    // so that the fragment reads below hit every bank pair once.  An empty
+    // group past the end keeps the group count uniform.
     auto issue = [&](int q) {
-      if (q < n) {
-        const uint32_t c = (uint32_t)(c0 + q);
+      if (q < nst) {
+        const uint32_t c = (uint32_t)(c0 + kLhSc * q);
         const uint32_t st = ring + (uint32_t)(q % kLhStages) * kLhStageBytes;
+        const int gi = lane & 7;
 #pragma unroll
-        for (int i = 0; i < kLhTiles; ++i) {
-          const int row = min(r0 + 16 * i + (lane >> 1), p.V - 1);
-          const uint8_t* src = p.packed + (((size_t)row * p.H + 64u * c) >> 1) + 16 * (lane & 1);
-          cp_async16(st + i * kLhTileBytes + (lane >> 1) * 32 + 16 * (lane & 1), src);
-          if (lane < 16) {
-            const int ra = min(r0 + 16 * i + lane, p.V - 1);
-            cp_async4(st + i * kLhTileBytes + 512 + 4 * lane, p.absmax + ((size_t)ra * p.H + 64u * c) / p.qbs);
+        for (int k = 0; k < 4; ++k) {
+          const int r = 4 * k + (lane >> 3);
+          const size_t row = (size_t)min(r0 + r, p.V - 1);
+          cp_async16(st + r * kLhRowBytes + 16 * (gi ^ (r & 7)), p.packed + ((row * p.H + 64u * c) >> 1) + 16 * gi);
+        }
+        if (p.qbs == 64) {
+          if (lane < kLhRows) {
+            const size_t row = (size_t)min(r0 + lane, p.V - 1);
+            cp_async16(st + kLhRows * kLhRowBytes + 16 * lane, p.absmax + row * hq + c);
+          }
+        } else {
+          const int r = lane & 15;
+          const size_t row = (size_t)min(r0 + r, p.V - 1);
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int j = 2 * (lane >> 4) + jj;
+            cp_async4(st + kLhRows * kLhRowBytes + 16 * r + 4 * j, p.absmax + (row * p.H + 64u * (c + j)) / p.qbs);
           }
         }
       }
@@ -146,28 +163,28 @@ __global__ void __launch_bounds__(kLhThreads, 1) lmhead_gemv_kernel(LmHeadParams
     };
 #pragma unroll
     for (int q = 0; q < kLhStages - 1; ++q) issue(q);
-    float acc[kLhTiles][4];
-#pragma unroll
-    for (int i = 0; i < kLhTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-    for (int q = 0; q < n; ++q) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int q = 0; q < nst; ++q) {
       cp_async_wait<kLhStages - 2>();
       __syncwarp();
       const uint32_t st = ring + (uint32_t)(q % kLhStages) * kLhStageBytes;
-      // x of token g, columns 64c + 16t .. +16 as 8 half2 (slots g >= T are zero)
-      uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
-      if (has_tok) {
-        const uint32_t xaddr = xrow + (uint32_t)(c0 + q) * 128u;
-        xa = lds_u4(xaddr);
-        xb = lds_u4(xaddr + 16);
-      }
 #pragma unroll
-      for (int i = 0; i < kLhTiles; ++i) {
-        const uint32_t tb = st + i * kLhTileBytes;
-        const uint2 wa = lds_u2(tb + g * 32 + 8 * t);        // row g, bytes 8t..8t+8 of the chunk
-        const uint2 wb = lds_u2(tb + (g + 8) * 32 + 8 * t);  // row g + 8
-        const float ama = lds_f32(tb + 512 + 4 * g), amb = lds_f32(tb + 512 + 4 * (g + 8));
+      for (int j = 0; j < kLhSc; ++j) {
+        // x of token g, columns 64c + 16t .. +16 as 8 half2 (slots g >= T are zero)
+        uint4 xa = make_uint4(0, 0, 0, 0), xb = make_uint4(0, 0, 0, 0);
+        if (has_tok) {
+          const uint32_t xaddr = xrow + (uint32_t)(c0 + kLhSc * q + j) * 128u;
+          xa = lds_u4(xaddr);
+          xb = lds_u4(xaddr + 16);
+        }
+        // row g (and g + 8): bytes 32j + 8t .. +8 of the stage's line, granule 2j + t/2
+        const uint32_t goff = 16u * (uint32_t)((2 * j + (t >> 1)) ^ g) + 8u * (uint32_t)(t & 1);
+        const uint2 wa = lds_u2(st + g * kLhRowBytes + goff);
+        const uint2 wb = lds_u2(st + (g + 8) * kLhRowBytes + goff);
+        const float ama = lds_f32(st + kLhRows * kLhRowBytes + 16 * g + 4 * j);
+        const float amb = lds_f32(st + kLhRows * kLhRowBytes + 16 * (g + 8) + 4 * j);
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        // MMA j: bytes 2j and 2j+1 of the lane's 8 (columns 16t + 4j .. +4)
+        // MMA m: bytes 2m and 2m+1 of the lane's 8 (columns 16t + 4m .. +4)
         mma_16816(d, lut_lookup<0, 0>(lut, wa.x, lanebase), lut_lookup<0, 0>(lut, wb.x, lanebase),
                   lut_lookup<1, 0>(lut, wa.x, lanebase), lut_lookup<1, 0>(lut, wb.x, lanebase), xa.x, xa.y);
         mma_16816(d, lut_lookup<2, 0>(lut, wa.x, lanebase), lut_lookup<2, 0>(lut, wb.x, lanebase),
@@ -176,10 +193,10 @@ __global__ void __launch_bounds__(kLhThreads, 1) lmhead_gemv_kernel(LmHeadParams
                   lut_lookup<1, 0>(lut, wa.y, lanebase), lut_lookup<1, 0>(lut, wb.y, lanebase), xb.x, xb.y);
         mma_16816(d, lut_lookup<2, 0>(lut, wa.y, lanebase), lut_lookup<2, 0>(lut, wb.y, lanebase),
                   lut_lookup<3, 0>(lut, wa.y, lanebase), lut_lookup<3, 0>(lut, wb.y, lanebase), xb.z, xb.w);
-        acc[i][0] = fmaf(ama, d[0], acc[i][0]);
-        acc[i][1] = fmaf(ama, d[1], acc[i][1]);
-        acc[i][2] = fmaf(amb, d[2], acc[i][2]);
-        acc[i][3] = fmaf(amb, d[3], acc[i][3]);
+        acc[0] = fmaf(ama, d[0], acc[0]);
+        acc[1] = fmaf(ama, d[1], acc[1]);
+        acc[2] = fmaf(amb, d[2], acc[2]);
+        acc[3] = fmaf(amb, d[3], acc[3]);
       }
       __syncwarp();  // every lane is done with stage q before it is refilled
       issue(q + kLhStages - 1);
@@ -187,17 +204,14 @@ __global__ void __launch_bounds__(kLhThreads, 1) lmhead_gemv_kernel(LmHeadParams
     cp_async_wait<0>();
     __syncwarp();
     // D fragment: lane (g, t) holds rows g, g+8 for token slots 2t, 2t+1
+    const int ra = r0 + g, rb = ra + 8;
 #pragma unroll
-    for (int i = 0; i < kLhTiles; ++i) {
-      const int ra = r0 + 16 * i + g, rb = ra + 8;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int tok = 2 * t + h;
-        if (tok < p.T) {
-          float* dst = p.part + ((size_t)sp * p.T + tok) * p.V;
-          if (ra < p.V) dst[ra] = acc[i][h];
-          if (rb < p.V) dst[rb] = acc[i][2 + h];
-        }
+    for (int h = 0; h < 2; ++h) {
+      const int tok = 2 * t + h;
+      if (tok < p.T) {
+        float* dst = p.part + ((size_t)sp * p.T + tok) * p.V;
+        if (ra < p.V) dst[ra] = acc[h];
+        if (rb < p.V) dst[rb] = acc[2 + h];
       }
     }
   }
@@ -226,9 +240,10 @@ LmHeadPlan lmhead_plan(int T, int V, int H, int sm_count) {
   pl.nchunks = H / 64;
   const int ngroups = (V + kLhRows - 1) / kLhRows;
   const long want = (long)kLhUnitsPerWarp * sm_count * kLhWarps;
-  int splits = (int)std::min<long>(pl.nchunks, std::max<long>(1, (want + ngroups - 1) / ngroups));
+  int splits = (int)std::min<long>(pl.nchunks / kLhSc, std::max<long>(1, (want + ngroups - 1) / ngroups));
   pl.cps = (pl.nchunks + splits - 1) / splits;
-  pl.splits = (pl.nchunks + pl.cps - 1) / pl.cps;  // every split has >= 1 chunk
+  pl.cps = (pl.cps + kLhSc - 1) / kLhSc * kLhSc;   // whole ring stages
+  pl.splits = (pl.nchunks + pl.cps - 1) / pl.cps;  // every split has >= 1 stage
   pl.xh_off = 0;
   pl.scale_off = align_up((size_t)T * H * 2, 256);
   pl.part_off = pl.scale_off + align_up((size_t)T * 4, 256);
@@ -246,7 +261,7 @@ using namespace nsm;
 extern "C" {
 
 size_t nsm_lm_head_workspace_bytes(int32_t tokens, int32_t out_features, int32_t in_features) {
-  if (tokens <= 0 || out_features <= 0 || in_features < 64) return 0;
+  if (tokens <= 0 || out_features <= 0 || in_features < 256 || in_features % 256) return 0;
   DeviceInfo di;
   if (current_device(&di) != NSM_OK) return 0;
   return lmhead_plan(tokens, out_features, in_features, di.sm_count).bytes;
@@ -254,7 +269,7 @@ size_t nsm_lm_head_workspace_bytes(int32_t tokens, int32_t out_features, int32_t
 
 int nsm_lm_head_max_tokens(int32_t in_features) {
   DeviceInfo di;
-  if (in_features < 64 || current_device(&di) != NSM_OK) return 0;
+  if (in_features < 256 || in_features % 256 || current_device(&di) != NSM_OK) return 0;
   const long room = (long)di.max_smem_optin - 4096 - kLutBytes - kLhRingBytes;  // 4 KB: static tables
   return (int)std::max<long>(0, std::min<long>(kLhMaxTokens, room / (2L * in_features)));
 }
@@ -268,8 +283,8 @@ int nsm_lm_head_nf4(const void* x, int32_t x_dtype, int32_t tokens, const uint8_
               NSM_ERR_INVALID_ARG, "bad dtype");
   NSM_REQUIRE(tokens >= 0 && out_features >= 0, NSM_ERR_INVALID_ARG, "negative size");
   if (tokens == 0 || out_features == 0) return NSM_OK;
-  NSM_REQUIRE(in_features >= 64 && in_features % 64 == 0, NSM_ERR_UNSUPPORTED,
-              "in_features must be a positive multiple of 64");
+  NSM_REQUIRE(in_features >= 256 && in_features % 256 == 0, NSM_ERR_UNSUPPORTED,
+              "in_features must be a positive multiple of 256");
   NSM_REQUIRE(quant_block_size >= 64 && quant_block_size % 64 == 0, NSM_ERR_UNSUPPORTED,
               "quant_block_size must be a multiple of 64");
   NSM_REQUIRE((int64_t)out_features * in_features < ((int64_t)1 << 40), NSM_ERR_UNSUPPORTED, "weight too large");

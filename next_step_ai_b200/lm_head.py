@@ -60,8 +60,8 @@ class Nf4LmHead:
             raise RuntimeError(f"packed has {packed.numel()} bytes for a [{V}, {H}] NF4 weight")
         if absmax.numel() * qbs != V * H:
             raise RuntimeError(f"absmax has {absmax.numel()} values for a [{V}, {H}] weight with blocksize {qbs}")
-        if H % 64 or qbs % 64:
-            raise RuntimeError(f"in_features ({H}) and quant_block_size ({qbs}) must be multiples of 64")
+        if H % 256 or qbs % 64:
+            raise RuntimeError(f"in_features ({H}) must be a multiple of 256 and quant_block_size ({qbs}) of 64")
         self.packed = packed.reshape(-1).contiguous()
         self.absmax = absmax.reshape(-1).to(torch.float32).contiguous()
         self.code = code.reshape(-1).to(device=packed.device, dtype=torch.float32).contiguous()
