@@ -384,8 +384,8 @@ int nsm_cache_stage(const void* host_base, const int32_t* blocks, int32_t n, siz
  * (_materialize_lm_head_nf4_on_gpu + _lm_head_forward's
  * triton_sparse_input_linear_4bit call, :450-468) with the math of its dense
  * head (F.linear on the dequantised weight, :472-480).  H a multiple of 256,
- * quant_block_size a multiple of 64; packed 16-byte, absmax 4-byte and the
- * workspace 256-byte aligned.  x, bias and out may be fp32 / fp16 / bf16;
+ * quant_block_size a multiple of 64; packed 16-byte, absmax 16-byte (4-byte
+ * when quant_block_size > 64) and the workspace 256-byte aligned.  x, bias and out may be fp32 / fp16 / bf16;
  * accumulation is fp32 (fp16 weights x power-of-two-scaled fp16 x on the
  * tensor cores, the absmax applied per 64 columns in fp32). */
 size_t nsm_lm_head_workspace_bytes(int32_t tokens, int32_t out_features, int32_t in_features);

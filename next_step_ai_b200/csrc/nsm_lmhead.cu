@@ -289,8 +289,11 @@ int nsm_lm_head_nf4(const void* x, int32_t x_dtype, int32_t tokens, const uint8_
               "quant_block_size must be a multiple of 64");
   NSM_REQUIRE((int64_t)out_features * in_features < ((int64_t)1 << 40), NSM_ERR_UNSUPPORTED, "weight too large");
   NSM_REQUIRE(x && packed && absmax && code && out && workspace, NSM_ERR_INVALID_ARG, "NULL pointer");
-  NSM_REQUIRE(((uintptr_t)packed & 15) == 0 && ((uintptr_t)absmax & 3) == 0 && ((uintptr_t)workspace & 255) == 0,
-              NSM_ERR_INVALID_ARG, "packed must be 16-byte, absmax 4-byte, workspace 256-byte aligned");
+  NSM_REQUIRE(((uintptr_t)packed & 15) == 0 && ((uintptr_t)absmax & (quant_block_size == 64 ? 15 : 3)) == 0 &&
+                  ((uintptr_t)workspace & 255) == 0,
+              NSM_ERR_INVALID_ARG,
+              "packed must be 16-byte, absmax 16-byte (4-byte unless quant_block_size is 64), workspace 256-byte "
+              "aligned");
   DeviceInfo di;
   int st = current_device(&di);
   if (st != NSM_OK) return st;

@@ -62,8 +62,13 @@ class Nf4LmHead:
             raise RuntimeError(f"absmax has {absmax.numel()} values for a [{V}, {H}] weight with blocksize {qbs}")
         if H % 256 or qbs % 64:
             raise RuntimeError(f"in_features ({H}) must be a multiple of 256 and quant_block_size ({qbs}) of 64")
+        # the kernel copies 16-byte pieces of the weight and 16-byte absmax runs
         self.packed = packed.reshape(-1).contiguous()
+        if self.packed.data_ptr() % 16:
+            self.packed = self.packed.clone()
         self.absmax = absmax.reshape(-1).to(torch.float32).contiguous()
+        if self.absmax.data_ptr() % 16:
+            self.absmax = self.absmax.clone()
         self.code = code.reshape(-1).to(device=packed.device, dtype=torch.float32).contiguous()
         self.bias = bias.reshape(-1).contiguous() if bias is not None else None
         self.out_features, self.in_features, self.quant_block_size = V, H, qbs
