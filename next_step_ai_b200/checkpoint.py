@@ -418,6 +418,7 @@ class Nf4Checkpoint:
             if ".weight." in n:
                 self.aux_names.setdefault(n.split(".weight.", 1)[0] + ".weight", []).append(n)
         self._handles: dict[str, Any] = {}
+        self._headers: dict[str, tuple[int, dict]] = {}
 
     def close(self) -> None:
         """Release the open shard handles (reopened on the next read)."""
@@ -474,12 +475,62 @@ class Nf4Checkpoint:
                         out_features=out_f, in_features=in_f, blocksize=bs, quant_type=str(qs["quant_type"]),
                         dtype=str(qs.get("dtype", "")))
 
+    def _tensor_extent(self, name: str) -> tuple[Path, int, int]:
+        """(shard path, absolute byte offset, byte length) of a tensor's data,
+        from the shard's safetensors header (8-byte little-endian header size,
+        JSON header, then the data block)."""
+        shard = self.weight_map.get(name)
+        if shard is None:
+            raise KeyError(f"Tensor '{name}' not found in safetensors index")
+        hdr = self._headers.get(shard)
+        if hdr is None:
+            path = self.snapshot_dir / shard
+            with open(path, "rb") as f:
+                n = int.from_bytes(f.read(8), "little")
+                hdr = self._headers[shard] = (8 + n, json.loads(f.read(n).decode("utf-8")))
+        base, meta = hdr
+        ent = meta.get(name)
+        if not isinstance(ent, dict):
+            raise KeyError(f"Tensor '{name}' metadata missing from safetensors header")
+        start, end = (int(v) for v in ent["data_offsets"])
+        return self.snapshot_dir / shard, base + start, end - start
+
     def load_nf4_packed_blocks(self, name: str, block_indices, *, bytes_per_block: int) -> torch.Tensor:
         """``[n, bytes_per_block]`` uint8 rows of the flat weight, in the order
-        given (``ShardedSafetensorLoader.load_nf4_packed_blocks``)."""
-        w, _ = self.load_raw(name)
+        given (``ShardedSafetensorLoader.load_nf4_packed_blocks``,
+        ``runtime/safetensor_loader.py:291-350``).  Only the listed blocks are
+        read: sorted block ids are read as runs of consecutive blocks with one
+        seek each (the reference's direct path), then put back in the given
+        order."""
+        bpb = int(bytes_per_block)
         idx = torch.as_tensor(block_indices, dtype=torch.long).reshape(-1)
-        return w.reshape(-1).view(torch.uint8).view(-1, int(bytes_per_block))[idx].contiguous()
+        path, off, nbytes = self._tensor_extent(name)
+        if bpb <= 0 or nbytes % bpb:
+            raise RuntimeError(f"{name}: {nbytes} bytes are not a whole number of {bpb}-byte blocks")
+        nblk = nbytes // bpb
+        if idx.numel() and (int(idx.min()) < 0 or int(idx.max()) >= nblk):
+            raise IndexError(f"block index out of range for '{name}' with {nblk} blocks")
+        out = torch.empty((idx.numel(), bpb), dtype=torch.uint8)
+        if idx.numel() == 0:
+            return out
+        order = torch.argsort(idx, stable=True)
+        srt = idx[order].tolist()
+        buf = out.numpy()
+        with open(path, "rb") as f:
+            i = 0
+            while i < len(srt):
+                j = i + 1
+                while j < len(srt) and srt[j] == srt[j - 1] + 1:
+                    j += 1
+                f.seek(off + srt[i] * bpb)
+                run = f.read((j - i) * bpb)
+                if len(run) != (j - i) * bpb:
+                    raise RuntimeError(f"{name}: short read at block {srt[i]}")
+                chunk = np.frombuffer(run, dtype=np.uint8).reshape(j - i, bpb)
+                for k in range(i, j):
+                    buf[int(order[k])] = chunk[k - i]
+                i = j
+        return out
 
     def mlp_params(self, layer_idx: int, prefix: str | None = None) -> dict[str, Nf4Param]:
         p = prefix if prefix is not None else f"model.layers.{int(layer_idx)}.mlp."

@@ -132,6 +132,23 @@ def test_load_param_recovers_bytes_and_absmax(snapshot):
         assert m.bytes_per_block == 32 * dims[1] // 2 and m.absmax_per_block == 32 * dims[1] // 64
 
 
+def test_packed_block_reads_match_whole_tensor(snapshot):
+    d, _ = snapshot
+    r = ck.Nf4Checkpoint(d)
+    name = "model.layers.1.mlp.gate_proj.weight"
+    w, _ = r.load_raw(name)
+    shape = syn.SHAPES[CHECKPOINT_SHAPE]
+    bpb = 16 * shape.hidden
+    whole = w.reshape(-1).view(-1, bpb)
+    for idx in ([5, 6, 7, 2, 3, 31, 0], [9], [], [4, 4, 1], list(range(32))[::-1]):
+        got = r.load_nf4_packed_blocks(name, idx, bytes_per_block=bpb)
+        assert got.shape == (len(idx), bpb) and torch.equal(got, whole[torch.tensor(idx, dtype=torch.long)])
+    with pytest.raises(IndexError):
+        r.load_nf4_packed_blocks(name, [32], bytes_per_block=bpb)
+    with pytest.raises(RuntimeError, match="whole number"):
+        r.load_nf4_packed_blocks(name, [0], bytes_per_block=bpb + 1)
+
+
 def test_reader_context_releases_handles(snapshot):
     d, _ = snapshot
     with ck.Nf4Checkpoint(d) as r:
