@@ -57,6 +57,45 @@ class RouterWeights:
         if self.down_block_norm is not None:
             self.down_block_norm = self.down_block_norm.to(torch.float32).contiguous()
 
+    @classmethod
+    def from_routing(cls, routing: dict, *, layer_idx: int = 0, sparse_runtime_top_k: int = 0, sparse_top_k: int = 1,
+                     basis_top_k_by_layer: dict | None = None, prefill_top_k: int | None = None,
+                     device: torch.device | str | None = None) -> "RouterWeights":
+        """From one layer of the reference runtime's ``_sparse_routing`` dict,
+        resolved as ``_route_sparse_mlp`` / ``_compute_sparse_basis_latent``
+        read it (``streaming_llama_runtime.py:4209-4250``, ``:4311-4352``):
+        the score head ``route_score_weight`` (+ ``route_score_bias``) when it
+        is a tensor, else the legacy ``|latent| @ dec_norm_t``; the optional
+        ``down_block_norm``; ``top_k`` else the runtime's k, a prefill
+        override, clamped to ``[1, NB]``; ``basis_top_k`` else the by-layer
+        table else 8, clamped to ``[1, rank]``.  Weights stay in ``enc_w``'s
+        dtype (the runtime computes the router in it)."""
+        def put(t):
+            return t if t is None or device is None else t.to(device)
+
+        enc_w = put(routing["enc_w"])
+        enc_b = put(routing.get("enc_b"))
+        sw = routing.get("route_score_weight")
+        legacy = not torch.is_tensor(sw)
+        if legacy:
+            score_w = put(routing["dec_norm_t"]).t().contiguous()  # [NB, rank]
+            score_b = None
+        else:
+            score_w = put(sw)
+            sb = routing.get("route_score_bias")
+            score_b = put(sb) if torch.is_tensor(sb) else None
+        dbn = routing.get("down_block_norm")
+        dbn = put(dbn.to(torch.float32).reshape(-1)) if torch.is_tensor(dbn) else None
+        nb, rank = int(score_w.shape[0]), int(enc_w.shape[0])
+        if dbn is not None and int(dbn.numel()) != nb:
+            dbn = None  # the runtime ignores a norm of the wrong length
+        k = int(routing.get("top_k", sparse_runtime_top_k if int(sparse_runtime_top_k) > 0 else sparse_top_k))
+        if prefill_top_k is not None:
+            k = int(prefill_top_k)
+        btk = int(routing.get("basis_top_k", (basis_top_k_by_layer or {}).get(int(layer_idx), 8)))
+        return cls(enc_w=enc_w, score_w=score_w, enc_b=enc_b, score_b=score_b, down_block_norm=dbn,
+                   top_k=max(1, min(k, nb)), basis_top_k=max(1, min(btk, rank)), legacy_abs_latent=legacy)
+
     @property
     def rank(self) -> int:
         return int(self.enc_w.shape[0])

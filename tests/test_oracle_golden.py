@@ -229,3 +229,51 @@ def test_block_generators_agree_with_full_layer():
     dc, da = om.gather_down_cols(full["down_packed"], full["down_absmax"], meta_d, blocks)
     assert np.array_equal(gp, G["gate_packed"]) and np.array_equal(ga, G["gate_absmax"])
     assert np.array_equal(dc, G["down_cols"]) and np.array_equal(da, G["down_absmax_cols"])
+
+
+@pytest.mark.parametrize("name", ["tiny_r4_basisk", "small_r3_dbn", "small_r2_legacy", "small_r1_prefill", "cfg0_r8"])
+def test_routing_dict_conversion_routes_like_reference(golden, name):
+    """The reference's in-memory routing dict -> RouterWeights.from_routing ->
+    the oracle router on the converted fields gives the reference's indices."""
+    torch = pytest.importorskip("torch")
+    from next_step_ai_b200.weights import RouterWeights
+
+    case = {c["name"]: c for c in cases(golden, "router/cases.json")}[name]
+    shape = syn.SHAPES[case["shape"]]
+    R = syn.make_router(shape, case["seed"])
+    x = syn.make_x(shape, case["seed"], case["rows"])
+    routing = {"enc_w": torch.from_numpy(R["enc_w"]), "enc_b": torch.from_numpy(R["enc_b"]),
+               "route_score_weight": torch.from_numpy(R["score_w"]),
+               "route_score_bias": torch.from_numpy(R["score_b"]),
+               "top_k": shape.top_k, "basis_top_k": case["basis_top_k"], "num_blocks": shape.num_blocks}
+    if case["variant"] == "down_block_norm":
+        routing["down_block_norm"] = torch.from_numpy(golden[f"router/{name}/down_block_norm"])
+    if case["variant"] == "legacy":
+        del routing["route_score_weight"], routing["route_score_bias"]
+        routing["dec_norm_t"] = torch.from_numpy(golden[f"router/{name}/dec_norm_t"])
+    prefill = case["prefill_top_k"] if case["prefill_top_k"] > 0 else None
+    rw = RouterWeights.from_routing(routing, prefill_top_k=prefill)
+    assert rw.legacy_abs_latent == (case["variant"] == "legacy")
+    kw = {"down_block_norm": rw.down_block_norm.numpy()} if rw.down_block_norm is not None else {}
+    if rw.legacy_abs_latent:
+        kw["dec_norm_t"] = rw.score_w.t().numpy()
+        sw, sb = None, None
+    else:
+        sw, sb = rw.score_w.numpy(), rw.score_b.numpy() if rw.score_b is not None else None
+    got = orr.route_sparse_mlp(x, rw.enc_w.numpy(), rw.enc_b.numpy(), sw, sb, rw.top_k, rw.basis_top_k, **kw)
+    assert np.array_equal(got, golden[f"router/{name}/idx"])
+
+
+def test_routing_dict_k_resolution():
+    torch = pytest.importorskip("torch")
+    from next_step_ai_b200.weights import RouterWeights
+
+    base = {"enc_w": torch.zeros(16, 64), "enc_b": torch.zeros(16), "route_score_weight": torch.zeros(40, 16)}
+    assert RouterWeights.from_routing(base, sparse_runtime_top_k=0, sparse_top_k=7).top_k == 7
+    assert RouterWeights.from_routing(base, sparse_runtime_top_k=9, sparse_top_k=7).top_k == 9
+    assert RouterWeights.from_routing(dict(base, top_k=500)).top_k == 40
+    assert RouterWeights.from_routing(dict(base, top_k=5), prefill_top_k=0).top_k == 1
+    assert RouterWeights.from_routing(base).basis_top_k == 8
+    assert RouterWeights.from_routing(base, layer_idx=3, basis_top_k_by_layer={3: 99}).basis_top_k == 16
+    rw = RouterWeights.from_routing(dict(base, down_block_norm=torch.ones(39)))
+    assert rw.down_block_norm is None and rw.score_b is None
