@@ -126,9 +126,10 @@ def load_router_artifact(source, *, hidden: int, intermediate: int, num_layers: 
     ``decoder_blocks`` artifacts) belong to a different execution mode and are
     listed in ``output_domain_layers`` without weights.  With ``hot_blocks``,
     each layer's initial hot set is derived as the reference does when its VRAM
-    hot cache is enabled (``:979-990``), counting the layers loaded so far as
-    the sparse layers of the capacity formula, as the reference does while it
-    fills its routing table.
+    hot cache is enabled (``:979-990``), counting the layers loaded so far
+    (output-domain ones included) as the sparse layers of the capacity
+    formula, as the reference does while it fills its routing table; output-
+    domain layers get no hot set here (their execution mode is not this path).
 
     A file is read with torch's restricted unpickler (tensors, containers and
     numbers: everything the artifact schema holds); ``trusted=True`` allows
@@ -231,7 +232,8 @@ def load_router_artifact(source, *, hidden: int, intermediate: int, num_layers: 
             hb = derive_hot_blocks(
                 state, lstats, importance_by_layer.get(str(lidx)), nb, runtime_top_k=default_top_k,
                 threshold=hot_block_threshold, limit_bytes=hot_cache_limit_bytes, used_bytes=hot_cache_used_bytes,
-                sparse_layers=len(out.layers), bytes_per_block=hot_cache_bytes_per_block(hidden, block_size))
+                sparse_layers=len(out.layers) + len(out.output_domain_layers),
+                bytes_per_block=hot_cache_bytes_per_block(hidden, block_size))
             if hb is not None and hb.size > 0:
                 out.hot_blocks[lidx] = hb
     return out

@@ -17,8 +17,10 @@ code and records its outputs on seeded synthetic inputs:
 * ``checkpoint.json`` (argument ``checkpoint`` regenerates only this file):
   ``ShardedSafetensorLoader`` (weight map, quant-state grouping,
   ``load_nf4_packed_blocks``, ``_load_raw_for_param``) on a seeded
-  bitsandbytes-format snapshot written by ``oracle.bnb_checkpoint``, and
-  ``_derive_hot_blocks_for_layer`` on a ``__new__``-built runtime.
+  bitsandbytes-format snapshot written by ``oracle.bnb_checkpoint``,
+  ``_derive_hot_blocks_for_layer`` on a ``__new__``-built runtime, and the
+  constructor's router-artifact block (taken from the reference source when
+  the fixture is made) run on seeded artifacts.
 
 Inputs come from ``oracle.synthetic`` (seeded).  Small inputs are stored in the
 fixtures; large ones are stored as seeds plus a SHA-256 of the regenerated
@@ -514,10 +516,115 @@ def gen_checkpoint(rt) -> None:
     (HERE / "checkpoint.json").write_text(json.dumps(blob, indent=0))
 
 
+ARTIFACT_SHAPE = "tiny"
+
+
+def artifact_payload(case: int):
+    """Seeded router artifacts in the fitting script's schema
+    (``{config, layer_selection, layer_states, stats}``), one per case."""
+    import torch
+    shape = syn.SHAPES[ARTIFACT_SHAPE]
+    NB, r = shape.num_blocks, shape.rank
+    g = np.random.default_rng(900 + case)
+    cfg = {"artifact_target": "intermediate_block_scores", "block_size": 32, "num_blocks": NB, "basis_rank": r}
+    layers = [0, 1, 2, 5]
+    if case == 1:
+        cfg.update({"top_k_by_layer": {"1": 3, 2: 99}, "basis_top_k_by_layer": {"0": 2, 5: 40}, "basis_top_k": 6})
+    if case == 2:
+        cfg.pop("num_blocks")
+        cfg["top_k_by_layer"] = {"0": 0}
+    states, stats = {}, {}
+    for li in layers:
+        R = syn.make_router(shape, 31 + case, li)
+        st = {"encoder_weight": torch.from_numpy(R["enc_w"]), "encoder_bias": torch.from_numpy(R["enc_b"]),
+              "score_weight": torch.from_numpy(R["score_w"]), "scale": torch.tensor(1.0 + li)}
+        if li != 1:
+            st["score_bias"] = torch.from_numpy(R["score_b"])
+        if li == 2:
+            st["down_block_norm"] = torch.from_numpy(g.uniform(0.5, 1.5, NB).astype(np.float32))
+        if li == 5:
+            st["rank_effective"] = torch.tensor(float(r - 5))
+            st["explained_variance_ratio"] = torch.tensor(0.2)
+        imp = g.random(NB).astype(np.float32)
+        if case == 1 and li == 0:
+            st["block_importance"] = torch.from_numpy(imp)
+        elif li == 1:
+            stats[str(li)] = {"scores": torch.from_numpy(imp), "rank_effective": float(r - 2)}
+        states[str(li)] = st
+    if case == 2:
+        states["9"] = states["0"]   # out of range for 8 layers: skipped
+        states["3"] = {"artifact_target": "output_reconstruction", "block_domain": "output",
+                       "decoder_blocks": torch.zeros(shape.hidden // 32, r, 32),
+                       "encoder_weight": torch.zeros(r, shape.hidden), "encoder_bias": torch.zeros(r),
+                       "scale": torch.tensor(1.0)}
+    return {"config": cfg, "layer_selection": layers + [77], "layer_states": states, "stats": stats}
+
+
+def gen_artifact(rt) -> None:
+    """The reference constructor's artifact block (``StreamingLlamaRuntime.__init__``,
+    from ``if sparse_basis_path ...`` up to its summary printout), taken from
+    the reference source at generation time and run on a ``__new__``-built
+    runtime for seeded artifacts; records what it loads."""
+    import inspect
+    import tempfile
+    import textwrap
+    import types as _types
+
+    import torch
+    shape = syn.SHAPES[ARTIFACT_SHAPE]
+    lines = inspect.getsource(rt.StreamingLlamaRuntime.__init__).splitlines()
+    a = next(i for i, ln in enumerate(lines) if ln.strip().startswith("if sparse_basis_path and str(sparse_basis_path)"))
+    b = next(i for i, ln in enumerate(lines) if i > a and ln.strip().startswith("_pct = int(round(self._sparse_top_k"))
+    code = compile(textwrap.dedent("\n".join(lines[a:b])), "<reference artifact block>", "exec")
+    out = []
+    for case, (top_k, basis_k, hot, limit) in enumerate([(None, None, False, None), (5, None, True, None),
+                                                          (None, 3, True, 60_000)]):
+        with tempfile.TemporaryDirectory() as tmp:
+            path = Path(tmp) / "router.pt"
+            torch.save(artifact_payload(case), path)
+            r = new_runtime(rt)
+            r.num_layers = 8
+            r.config = _types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate)
+            r.dtype = torch.float32
+            r._sparse_routing, r._sparse_top_k_by_layer, r._sparse_basis_top_k_by_layer = {}, {}, {}
+            r._mlp_hot_blocks_by_layer = {}
+            r._sparse_checkpoint_basis_rank = 64
+            r._sparse_explicit_layer_selection = set()
+            r._vram_hot_cache_enabled = hot
+            r._sparse_mlp_prefill_mode = "dense"
+            r._hot_block_threshold = 0.8
+            r._vram_hot_cache_limit_bytes = limit
+            r._vram_hot_cache_used_bytes = 0
+            r._sparse_param_cache = {}
+            env = dict(vars(rt))
+            env.update(self=r, sparse_basis_path=str(path), sparse_top_k=top_k, sparse_basis_top_k=basis_k)
+            exec(code, env)
+            layers, output_layers = {}, []
+            for li, d in sorted(r._sparse_routing.items()):
+                if d.get("block_domain") != "intermediate":
+                    output_layers.append(int(li))
+                    continue
+                layers[str(li)] = {"top_k": int(d["top_k"]), "basis_top_k": int(d["basis_top_k"]),
+                                   "rank_effective": int(d["rank_effective"]), "scale": float(d["scale"]),
+                                   "evr": float(d["explained_variance_ratio"]), "num_blocks": int(d["num_blocks"]),
+                                   "has_score_bias": d["route_score_bias"] is not None,
+                                   "has_down_block_norm": d["down_block_norm"] is not None,
+                                   "enc_w_sha": sha(d["enc_w"].numpy()), "score_w_sha": sha(d["route_score_weight"].numpy())}
+            out.append({"case": case, "sparse_top_k": top_k, "sparse_basis_top_k": basis_k, "hot": hot,
+                        "limit": limit, "default_top_k": int(r._sparse_top_k),
+                        "layer_selection": sorted(r._sparse_explicit_layer_selection), "layers": layers,
+                        "output_domain_layers": output_layers,
+                        "hot_blocks": {str(k): v.tolist() for k, v in sorted(r._mlp_hot_blocks_by_layer.items())}})
+    blob = json.loads((HERE / "checkpoint.json").read_text())
+    blob["artifact"] = {"shape": ARTIFACT_SHAPE, "cases": out}
+    (HERE / "checkpoint.json").write_text(json.dumps(blob, indent=0))
+
+
 def main() -> None:
     rt, tsm = load_reference()
     if sys.argv[1:] == ["checkpoint"]:
         gen_checkpoint(rt)
+        gen_artifact(rt)
         print("wrote", HERE / "checkpoint.json")
         return
     out: dict = {}

@@ -315,6 +315,38 @@ def test_router_artifact_errors_and_domains():
     assert a.layers[0].down_block_norm.dtype == torch.float32
 
 
+def test_router_artifact_matches_reference_constructor(golden_ck):
+    """The reference constructor's artifact block, run on the same seeded
+    artifacts when the fixture was made (``tests/golden/make_golden.py``)."""
+    from tests.golden.make_golden import ARTIFACT_SHAPE, artifact_payload
+
+    gold = golden_ck["artifact"]
+    assert gold["shape"] == ARTIFACT_SHAPE
+    shape = syn.SHAPES[ARTIFACT_SHAPE]
+    for c in gold["cases"]:
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")
+            a = ck.load_router_artifact(artifact_payload(c["case"]), hidden=shape.hidden,
+                                        intermediate=shape.intermediate, num_layers=8,
+                                        sparse_top_k=c["sparse_top_k"], sparse_basis_top_k=c["sparse_basis_top_k"],
+                                        dtype=torch.float32, hot_blocks=c["hot"], hot_cache_limit_bytes=c["limit"])
+        assert a.top_k == c["default_top_k"], c["case"]
+        assert sorted(a.layer_selection) == c["layer_selection"]
+        assert a.output_domain_layers == c["output_domain_layers"]
+        assert sorted(str(k) for k in a.layers) == sorted(c["layers"])
+        for k, ref in c["layers"].items():
+            rw, info = a.layers[int(k)], a.info[int(k)]
+            assert (rw.top_k, rw.basis_top_k, info.rank_effective) == (ref["top_k"], ref["basis_top_k"],
+                                                                      ref["rank_effective"]), (c["case"], k)
+            assert info.scale == ref["scale"] and info.explained_variance_ratio == pytest.approx(ref["evr"])
+            assert info.num_blocks == ref["num_blocks"]
+            assert (rw.score_b is not None) == ref["has_score_bias"]
+            assert (rw.down_block_norm is not None) == ref["has_down_block_norm"]
+            assert sha(rw.enc_w.numpy()) == ref["enc_w_sha"] and sha(rw.score_w.numpy()) == ref["score_w_sha"]
+        ref_hot = {k: v for k, v in c["hot_blocks"].items() if k in c["layers"]}  # intermediate layers
+        assert {str(k): v.tolist() for k, v in a.hot_blocks.items()} == ref_hot, c["case"]
+
+
 def test_router_artifact_hot_blocks():
     shape = syn.SHAPES["tiny"]
     p = _artifact(shape)
