@@ -19,8 +19,9 @@ code and records its outputs on seeded synthetic inputs:
   ``load_nf4_packed_blocks``, ``_load_raw_for_param``) on a seeded
   bitsandbytes-format snapshot written by ``oracle.bnb_checkpoint``,
   ``_derive_hot_blocks_for_layer`` on a ``__new__``-built runtime, and the
-  constructor's router-artifact block (taken from the reference source when
-  the fixture is made) run on seeded artifacts.
+  constructor's router-artifact block and the rebuild loop of
+  ``calibrate_vram_hot_cache`` (both taken from the reference source when the
+  fixture is made) run on seeded artifacts and hit counts.
 
 Inputs come from ``oracle.synthetic`` (seeded).  Small inputs are stored in the
 fixtures; large ones are stored as seeds plus a SHA-256 of the regenerated
@@ -620,11 +621,60 @@ def gen_artifact(rt) -> None:
     (HERE / "checkpoint.json").write_text(json.dumps(blob, indent=0))
 
 
+def calibration_hits(case: int) -> dict:
+    """Seeded per-layer hit counts (distinct floats: no ties for topk)."""
+    g = np.random.default_rng(700 + case)
+    nb = 48
+    hits = {li: (g.permutation(nb).astype(np.float32) + g.random(nb).astype(np.float32) * 0.5)
+            for li in (0, 2, 3, 6)}
+    hits[3][:] = 0.0   # a layer without hits is skipped
+    return hits
+
+
+def gen_calibration(rt) -> None:
+    """The rebuild loop of ``calibrate_vram_hot_cache`` (from ``updated_layers =
+    0`` up to its summary printout), taken from the reference source when the
+    fixture is made and run on seeded hit counts."""
+    import inspect
+    import textwrap
+    import types as _types
+
+    import torch
+    lines = inspect.getsource(rt.StreamingLlamaRuntime.calibrate_vram_hot_cache).splitlines()
+    a = next(i for i, ln in enumerate(lines) if ln.strip() == "updated_layers = 0")
+    b = next(i for i, ln in enumerate(lines) if i > a and ln.strip().startswith("print("))
+    code = compile(textwrap.dedent("\n".join(lines[a:b])), "<reference calibration rebuild>", "exec")
+    out = []
+    for case, (limit, prev, rtk) in enumerate([(None, {}, 0), (None, {2: 11}, 5), (900_000, {0: 3}, 0)]):
+        r = new_runtime(rt)
+        r.num_layers = 8
+        r.config = _types.SimpleNamespace(hidden_size=1024, intermediate_size=48 * 32)
+        r._sparse_routing = {li: ({"top_k": 4 + li} if li % 2 == 0 else {}) for li in range(8)}
+        r._sparse_runtime_top_k, r._sparse_top_k = rtk, 6
+        r._hot_cache_calibration_hits = {li: torch.from_numpy(v.copy()) for li, v in calibration_hits(case).items()}
+        r._mlp_hot_blocks_by_layer = {li: torch.arange(n) for li, n in prev.items()}
+        r._vram_hot_cache_limit_bytes = limit
+        r._vram_hot_cache_used_bytes = 0
+        r._sparse_param_cache = {}
+        r._sparse_block_size = 32
+        env = dict(vars(rt))
+        env.update(self=r)
+        exec(code, env)
+        out.append({"case": case, "limit": limit, "prev": {str(k): v for k, v in prev.items()},
+                    "sparse_runtime_top_k": rtk, "sparse_top_k": 6, "hidden": 1024,
+                    "updated_layers": int(env["updated_layers"]), "total_hits": float(env["total_hits"]),
+                    "hot": {str(k): v.tolist() for k, v in sorted(r._mlp_hot_blocks_by_layer.items())}})
+    blob = json.loads((HERE / "checkpoint.json").read_text())
+    blob["calibration"] = out
+    (HERE / "checkpoint.json").write_text(json.dumps(blob, indent=0))
+
+
 def main() -> None:
     rt, tsm = load_reference()
     if sys.argv[1:] == ["checkpoint"]:
         gen_checkpoint(rt)
         gen_artifact(rt)
+        gen_calibration(rt)
         print("wrote", HERE / "checkpoint.json")
         return
     out: dict = {}

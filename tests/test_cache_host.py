@@ -120,3 +120,25 @@ def test_calibration_matches_reference_pieces():
     cal.active = False
     cal.record(0, np.arange(k)[None, :], nb)
     assert np.array_equal(cal.hits[0], ref[0])
+
+
+def test_calibration_rebuild_matches_reference():
+    """The rebuild loop of the reference's calibrate_vram_hot_cache, run on the
+    same seeded hit counts when the fixture was made."""
+    import json
+    from pathlib import Path
+
+    from tests.golden.make_golden import calibration_hits
+
+    gold = json.loads((Path(__file__).parent / "golden" / "checkpoint.json").read_text())["calibration"]
+    for c in gold:
+        cal = cache.HotCacheCalibration()
+        cal.hits = {li: v.copy() for li, v in calibration_hits(c["case"]).items()}
+        rtk = {li: (4 + li if li % 2 == 0 else (c["sparse_runtime_top_k"] if c["sparse_runtime_top_k"] > 0
+                                                else c["sparse_top_k"])) for li in range(8)}
+        sets = cal.hot_sets(runtime_top_k=rtk, previous_hot={int(k): v for k, v in c["prev"].items()},
+                            limit_bytes=c["limit"], used_bytes=0, sparse_layers=8,
+                            bytes_per_block=cache.hot_cache_bytes_per_block(c["hidden"]))
+        assert {str(k): v.tolist() for k, v in sets.items()} == c["hot"], c["case"]
+        assert len(sets) == c["updated_layers"]
+        assert sum(float(cal.hits[li].sum()) for li in sets) == pytest.approx(c["total_hits"], rel=1e-6)
