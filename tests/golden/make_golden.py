@@ -21,7 +21,8 @@ code and records its outputs on seeded synthetic inputs:
   ``_derive_hot_blocks_for_layer`` on a ``__new__``-built runtime, and the
   constructor's router-artifact block and the rebuild loop of
   ``calibrate_vram_hot_cache`` (both taken from the reference source when the
-  fixture is made) run on seeded artifacts and hit counts.
+  fixture is made) run on seeded artifacts and hit counts, and the LM head's
+  quant block-size rule.
 
 Inputs come from ``oracle.synthetic`` (seeded).  Small inputs are stored in the
 fixtures; large ones are stored as seeds plus a SHA-256 of the regenerated
@@ -669,12 +670,36 @@ def gen_calibration(rt) -> None:
     (HERE / "checkpoint.json").write_text(json.dumps(blob, indent=0))
 
 
+LM_HEAD_QBS_CASES = [(16384, None), (4096 + 128, None), (96, None), (100, None), (16384, "256"), (16384, "96"),
+                     (16384, "x"), (8192, "128"), (64, "0")]
+
+
+def gen_lm_head(rt) -> None:
+    """``_resolve_lm_head_nf4_quant_block_size`` (a static method of the
+    runtime's LM-head mixin) with and without its environment override."""
+    R = rt.StreamingLlamaRuntime
+    out = []
+    for h, env in LM_HEAD_QBS_CASES:
+        os.environ.pop("STREAMING_GPU_LM_HEAD_NF4_BLOCK_SIZE", None)
+        if env is not None:
+            os.environ["STREAMING_GPU_LM_HEAD_NF4_BLOCK_SIZE"] = env
+        try:
+            out.append({"in_features": h, "env": env, "qbs": int(R._resolve_lm_head_nf4_quant_block_size(h))})
+        except RuntimeError as e:
+            out.append({"in_features": h, "env": env, "error": str(e)})
+    os.environ.pop("STREAMING_GPU_LM_HEAD_NF4_BLOCK_SIZE", None)
+    blob = json.loads((HERE / "checkpoint.json").read_text())
+    blob["lm_head_qbs"] = out
+    (HERE / "checkpoint.json").write_text(json.dumps(blob, indent=0))
+
+
 def main() -> None:
     rt, tsm = load_reference()
     if sys.argv[1:] == ["checkpoint"]:
         gen_checkpoint(rt)
         gen_artifact(rt)
         gen_calibration(rt)
+        gen_lm_head(rt)
         print("wrote", HERE / "checkpoint.json")
         return
     out: dict = {}
