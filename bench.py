@@ -4,11 +4,14 @@ Workload: per token, 126 decoder layers of hidden 16384,
 intermediate 53248 (1664 blocks of 32), learned-basis router rank 64, top-k
 208, NF4 gate/up/down weights (synthetic N(0, 0.02), seeded per layer); the
 residual is carried across layers with attention replaced by identity.
-Intermediate blocks are sharded across ranks (one process per GPU); the router
-is replicated and the bf16 [16384] partial outputs are summed with one NCCL
-all-reduce per layer.  On one GPU the 126 layers do not all fit in HBM
-(126 x 1.47 GB), so as many unique layers as fit are cycled; every layer is
-far larger than L2, so HBM traffic is unchanged.
+Intermediate blocks are sharded across ranks (one process per GPU); every rank
+routes the token, and each layer's fp32 [16384] partial outputs are summed
+across ranks inside the next layer's router kernel: every rank stores its
+partial into every rank's CUDA-IPC exchange buffer over NVLink and sums the
+ranks' words in rank order (no NCCL collective on the data path).  On one GPU
+the 126 layers do not all fit in HBM (126 x 1.47 GB), so as many unique
+layers as fit are cycled; every layer is far larger than L2, so HBM traffic is
+unchanged.
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 (N > 1 is launched with torch.distributed.run, one rank per GPU).
@@ -53,6 +56,17 @@ def gateup_bytes_per_launch(k: int = TOP_K, H: int = HIDDEN) -> int:
 # DRAM bytes (read + write) of one gateup_tma_kernel launch at this workload, from one
 # ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; profiles/gateup_tma_kernel_cfg1.txt)
 GATEUP_DRAM_BYTES_PER_LAUNCH = 122_787_840 + 5_259_776
+
+
+def headline_config(world: int) -> dict:
+    """The ``config`` both arms print for the headline workload at ``world`` GPUs."""
+    return {"workload": "BASELINE config 2: 126-layer 405B-shaped sparse-MLP decode step",
+            "hidden": HIDDEN, "intermediate": INTERMEDIATE, "blocks": NB, "top_k": TOP_K, "rank": RANK,
+            "layers": LAYERS, "tokens_per_step": 1,
+            "parallelism": (f"block-shard x{world}, router on every rank, fp32 partial sums exchanged over "
+                            "CUDA-IPC NVLink buffers inside the next router kernel" if world > 1
+                            else "single GPU, all blocks resident"),
+            "l2": "inputs larger than L2 (each layer >= 184 MB per rank)"}
 
 
 def peaks() -> dict:
@@ -240,14 +254,9 @@ def run_ours(args) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "nf4 weights, fp16 x fp16 -> fp32 MMA, bf16 io",
             "data": "synthetic: seeded N(0,0.02) NF4 weights, bf16 RMS-normalised N(0,1) input, random-init router",
-            "config": {"workload": "BASELINE config 2: 126-layer 405B-shaped sparse-MLP decode step",
-                       "hidden": HIDDEN, "intermediate": INTERMEDIATE, "blocks": NB, "top_k": TOP_K, "rank": RANK,
-                       "layers": LAYERS, "unique_layers_resident": unique, "layer_cycling": unique < LAYERS,
-                       "parallelism": (f"block-shard x{world}, router replicated, fp32 partial sums exchanged over "
-                                       "CUDA-IPC NVLink buffers inside the next router kernel" if world > 1
-                                       else "single GPU, all blocks resident"),
-                       "l2": "inputs larger than L2 (each layer >= 184 MB per rank)",
-                       "cuda_graph": True, "synthetic_gen_s": round(gen_s, 1)},
+            "config": headline_config(world),
+            "run": {"unique_layers_resident": unique, "layer_cycling": unique < LAYERS, "cuda_graph": True,
+                    "synthetic_gen_s": round(gen_s, 1)},
             "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
                     "d2h_bytes_per_step": HIDDEN * 4},
             "gpu_launches": args.steps * dec.kernels_per_step,
@@ -265,7 +274,7 @@ def run_ours(args) -> None:
             "clocks": clk.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(samples=2)
+            line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     dec.release()
     del g
@@ -276,9 +285,9 @@ def run_ours(args) -> None:
 # ---------------------------------------------------------------------------------------------------- CPU arms
 def cpu_layer_sample(seed: int, layer: int):
     """One layer of the workload, generated block by block on the host (only the
-    router and the selected blocks are materialised).  Returns the state the
-    timed CPU step needs."""
+    router and the selected blocks are materialised), as torch CPU tensors."""
     import numpy as np
+    import torch
 
     from oracle import synthetic as syn
     from oracle.router import route_sparse_mlp
@@ -288,41 +297,57 @@ def cpu_layer_sample(seed: int, layer: int):
     x = syn.make_x(shape, seed + layer, 1)
     blocks = route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)[0]
     G = syn.selected_blocks_gathered(shape, seed, layer, blocks)
-    return {"R": R, "x": x, "G": G, "np": np}
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    return {"R": {k: (None if v is None else t(v)) for k, v in R.items()}, "x": t(x),
+            "G": {k: t(v) for k, v in G.items()}}
 
 
 def cpu_step(state) -> None:
-    """The reference's CPU path for one layer, restated: route, then the
-    fp32 dequant + matmul of the selected NF4 blocks."""
-    from oracle import mlp as om
-    from oracle.router import route_sparse_mlp
+    """The reference's CPU torch path for one layer (router, then the fp32
+    dequant + matmul of the selected NF4 blocks), on all host threads."""
+    from oracle import cpu_torch as ct
 
     R, x, G = state["R"], state["x"], state["G"]
-    route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], TOP_K, RANK)
-    om.sparse_mlp_gathered(x, G["gate_packed"], G["gate_absmax"], G["code"], G["up_packed"], G["up_absmax"],
-                           G["code"], G["down_cols"], G["down_absmax_cols"], G["code"])
+    ct.route(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], TOP_K)
+    ct.mlp_gathered(x, G["gate_packed"], G["gate_absmax"], G["up_packed"], G["up_absmax"], G["down_cols"],
+                    G["down_absmax_cols"], G["code"])
 
 
-def cpu_baseline(samples: int = 2) -> dict:
-    import numpy as np  # noqa: F401
+def cpu_threads() -> int:
+    import torch
 
-    cores = os.cpu_count() or 1
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+CPU_SAMPLE_SECONDS = 12.0
+
+
+def cpu_baseline() -> dict:
+    """Layer-steps timed until ~12 s of CPU work (at least 3), tok/s scaled x126."""
+    cores = cpu_threads()
     state = cpu_layer_sample(7, 0)
     cpu_step(state)  # warm
-    t0 = time.perf_counter()
-    for _ in range(samples):
+    n, t0 = 0, time.perf_counter()
+    while n < 3 or time.perf_counter() - t0 < CPU_SAMPLE_SECONDS:
         cpu_step(state)
-    per_layer = (time.perf_counter() - t0) / samples
+        n += 1
+    per_layer = (time.perf_counter() - t0) / n
     return {"value": 1.0 / (per_layer * LAYERS), "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{samples} timed layer-steps of the 126-layer workload (router + 208-block NF4 MLP, numpy "
-                      f"fp32 with the host BLAS on {cores} threads); tok/s = 1 / (126 x mean layer time)"}
+            "sample": f"{n} timed layer-steps of the 126-layer workload (router + 208-block NF4 MLP, torch fp32 "
+                      f"on {cores} host threads: the reference's CPU torch path restated); "
+                      f"tok/s = 1 / (126 x mean layer time)"}
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's CPU torch path for this workload
+    (restated -- the reference's own module needs bitsandbytes and is not
+    present on the GPU box), one layer-step per step, on all host threads."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    cores = os.cpu_count() or 1
+    cores = cpu_threads()
     state = cpu_layer_sample(7, 0)
     for _ in range(args.warmup):
         cpu_step(state)
@@ -334,12 +359,12 @@ def run_reference(args) -> None:
     value = 1.0 / (per_layer * LAYERS)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic (same generator family)",
-        "config": {"workload": "BASELINE config 2: 126-layer 405B-shaped sparse-MLP decode step",
-                   "step": "one layer-step sample of the 126-layer token (value extrapolated x126)"},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_layer * 1e3 * LAYERS,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (same generator family)", "config": headline_config(world),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": "each step = one layer (router + 208-block NF4 MLP) in numpy fp32 on the host"},
+                         "sample": "each step = one layer-step (router + 208-block NF4 MLP) in torch fp32 on the "
+                                   "host; ms_per_step and tok/s scaled to the 126-layer token"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -208,8 +208,41 @@ size_t nsm_exchange_bytes(int world, int hidden);
 int nsm_exchange_create(int32_t world, int32_t rank, int32_t hidden, nsm_exchange** ex_out, void* ipc_handle_out);
 int nsm_exchange_connect(nsm_exchange* ex, const void* handles);
 int nsm_exchange_destroy(nsm_exchange* ex);
+/* Connects n exchanges created in ONE process (ranks 0..n-1 of one world,
+ * in rank order) to each other directly, without IPC handles: for one process
+ * driving several ranks whose buffers every rank's device can reach (the
+ * caller enables peer access between different devices).  Kernels of ranks
+ * that wait on each other must never run as separate launches on one GPU;
+ * a single-GPU caller only launches one rank (the tests use it to make a wait
+ * run out).  No counterpart in the reference. */
+int nsm_exchange_connect_local(nsm_exchange* const* exs, int32_t n);
+/* Polls of one peer word the router makes before it gives up on a rank that
+ * never delivered and records NSM_ERR_TIMEOUT in the workspace error word
+ * (nsm_workspace_error) -- the bounded wait of the fused exchange.  0 = the
+ * default (2^24 polls, seconds).  Applies to launches issued after the call
+ * (a captured graph keeps the value it was captured with).  No counterpart in
+ * the reference (its runtime is single-GPU). */
+int nsm_exchange_set_spin_limit(nsm_exchange* ex, int32_t spins);
 
 size_t nsm_decode_workspace_bytes(int hidden, int intermediate, int top_k, int rank);
+/* Process-wide bound on a warp's wait for its own bulk copies (mbarrier tries)
+ * in the gather-GEMV kernels; a wait that runs out records NSM_ERR_TIMEOUT in
+ * the workspace error word, drains the warp's copies in flight and stops the
+ * warp.  0 = the default (2^22 tries).  Returns the previous bound (or a
+ * negative status for a negative argument).  Applies to later launches.  No
+ * counterpart in the reference. */
+int nsm_set_copy_wait_limit(int32_t spins);
+/* The blocks the last nsm_sparse_mlp_decode on this workspace computed (the
+ * router's selection present in the pool, ascending block ids) and their
+ * count: copies the workspace's selection record to blocks_out [min(top_k,
+ * intermediate/32)] and count_out [1] (both device int32; stream-ordered).
+ * hidden, intermediate, top_k and rank are the values that call used.  The
+ * selection the decode path makes inside its gate/up kernel (no idx_out) is
+ * otherwise never returned; this exposes the rows the reference's
+ * _route_sparse_mlp result would give (streaming_llama_runtime.py:4311-4352,
+ * sorted by block id as _build_sparse_active_layout orders them, :4857-4908). */
+int nsm_workspace_selection(const void* ws, size_t ws_bytes, int32_t hidden, int32_t intermediate, int32_t top_k,
+                            int32_t rank, int32_t* blocks_out, int32_t* count_out, nsm_stream_t stream);
 
 /* Router only (latent GEMV + block scores + top-k), one token.
  * Replaces StreamingLlamaRuntime._route_sparse_mlp for rows == 1
@@ -284,6 +317,13 @@ int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32
 int nsm_decode_gathered_static(const void* x, int32_t x_dtype, int32_t hidden, int32_t num_blocks_gathered,
                                const nsm_mlp_weights* w, void* y, int32_t y_dtype, float* act_out,
                                nsm_stream_t stream);
+/* The device error word of nsm_decode_gathered_static's array on the current
+ * device: *code_out = NSM_ERR_TIMEOUT when a kernel of an earlier static call
+ * gave up on a bounded wait (its output is then incomplete), else 0; the word
+ * is cleared.  Synchronises `stream`; allocates nothing.  The calls do not
+ * clear the word themselves, so one check after several calls covers them
+ * all.  Like the entry point it serves, no counterpart in the reference. */
+int nsm_static_error(int32_t* code_out, nsm_stream_t stream);
 
 /* ---- multi-token decode over the union of the tokens' blocks ------------
  * Up to 32 tokens: x [rows][H] (x_dtype), idx [rows][k] int32 block ids (each

@@ -42,7 +42,8 @@ EXPORTED = (
     "nsm_union_workspace_bytes", "nsm_union_decode", "nsm_residual_flush", "nsm_exchange_bytes",
     "nsm_exchange_create", "nsm_exchange_connect", "nsm_exchange_destroy", "nsm_route_workspace_bytes",
     "nsm_lm_head_workspace_bytes", "nsm_lm_head_max_tokens", "nsm_lm_head_nf4",
-    "nsm_route_rows",
+    "nsm_route_rows", "nsm_workspace_selection", "nsm_exchange_connect_local", "nsm_exchange_set_spin_limit",
+    "nsm_set_copy_wait_limit", "nsm_static_error",
 )
 
 
@@ -85,6 +86,8 @@ _SIGS = {
     "nsm_last_error": (c_char_p, []),
     "nsm_workspace_init": (c_int, [c_void_p, c_size_t, c_void_p]),
     "nsm_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "nsm_workspace_selection": (c_int, [c_void_p, c_size_t, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p,
+                                        c_void_p]),
     "nsm_route": (c_int, [c_void_p, c_int32, c_int32, POINTER(RouterWeightsC), c_void_p, c_void_p, c_void_p,
                           c_void_p, c_size_t, c_void_p]),
     "nsm_route_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
@@ -122,6 +125,10 @@ _SIGS = {
     "nsm_exchange_create": (c_int, [c_int32, c_int32, c_int32, POINTER(c_void_p), c_void_p]),
     "nsm_exchange_connect": (c_int, [c_void_p, c_void_p]),
     "nsm_exchange_destroy": (c_int, [c_void_p]),
+    "nsm_exchange_connect_local": (c_int, [c_void_p, c_int32]),
+    "nsm_exchange_set_spin_limit": (c_int, [c_void_p, c_int32]),
+    "nsm_set_copy_wait_limit": (c_int, [c_int32]),
+    "nsm_static_error": (c_int, [POINTER(c_int32), c_void_p]),
     "nsm_union_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "nsm_union_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32,
                                  POINTER(BlockMapC), POINTER(MlpWeightsC), c_void_p, c_int32, c_void_p, c_void_p,

@@ -2,6 +2,7 @@
 // decode workspace layout.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <algorithm>
@@ -24,6 +25,9 @@ int cuda_fail(cudaError_t e, const char* what) {
   g_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
   return NSM_ERR_CUDA;
 }
+
+static std::atomic<int> g_copy_wait_spins{kDefaultCopyWaitSpins};
+int copy_wait_spins() { return g_copy_wait_spins.load(std::memory_order_relaxed); }
 
 static std::mutex g_dev_mu;
 static DeviceInfo g_dev_cache[64];
@@ -134,6 +138,29 @@ int nsm_workspace_error(void* ws, size_t ws_bytes, int32_t* code_out, nsm_stream
   NSM_CHECK_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), s));
   NSM_CHECK_CUDA(cudaStreamSynchronize(s));
   *code_out = v;
+  return NSM_OK;
+}
+
+int nsm_set_copy_wait_limit(int32_t spins) {
+  if (spins < 0) return fail(NSM_ERR_INVALID_ARG, "nsm_set_copy_wait_limit: spins must be >= 0 (0 = the default)");
+  const int prev = g_copy_wait_spins.exchange(spins > 0 ? spins : kDefaultCopyWaitSpins);
+  return prev;
+}
+
+int nsm_workspace_selection(const void* ws, size_t ws_bytes, int32_t hidden, int32_t intermediate, int32_t top_k,
+                            int32_t rank, int32_t* blocks_out, int32_t* count_out, nsm_stream_t stream) {
+  if (blocks_out == nullptr || count_out == nullptr)
+    return fail(NSM_ERR_INVALID_ARG, "nsm_workspace_selection: blocks_out / count_out is NULL");
+  if (hidden <= 0 || hidden % 64 != 0 || intermediate <= 0 || intermediate % 64 != 0 || top_k <= 0 || rank <= 0)
+    return fail(NSM_ERR_INVALID_ARG, "nsm_workspace_selection: bad shape");
+  const int k = std::min(top_k, intermediate / 32);
+  const DecodeWs need = decode_ws_layout(nullptr, hidden, intermediate, k, rank);
+  if (ws == nullptr || ws_bytes < need.bytes)
+    return fail(NSM_ERR_WORKSPACE, "nsm_workspace_selection: workspace missing or smaller than the decode layout");
+  const DecodeWs w = decode_ws_layout(const_cast<void*>(ws), hidden, intermediate, k, rank);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  NSM_CHECK_CUDA(cudaMemcpyAsync(blocks_out, w.row_block, (size_t)k * sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+  NSM_CHECK_CUDA(cudaMemcpyAsync(count_out, w.count, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
   return NSM_OK;
 }
 

@@ -123,10 +123,14 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 // Bounded wait for phase `parity` of mbarrier `bar`; false when the bound ran
-// out (the caller records an error instead of spinning forever).
+// out (the caller records an error instead of spinning forever).  The kernels
+// take the bound of their first waits from their launch parameters (the
+// process-wide setting of nsm_set_copy_wait_limit); waits that drain a ring
+// after a failure always use the default bound, so a warp never leaves
+// while copies into its shared memory are still in flight.
 constexpr int kMbarSpinLimit = 1 << 22;
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (int i = 0; i < kMbarSpinLimit; ++i) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int limit = kMbarSpinLimit) {
+  for (int i = 0; i < limit; ++i) {
     uint32_t ok;
     asm volatile(
         "{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}"

@@ -90,6 +90,7 @@ struct GateUpParams {
   int total_warps;
   int unit_tiles;  // tiles per stream unit (the partial segments follow the units)
   int max_rows;    // capacity of rows / partials (>= *count_ptr): prologues load this much without waiting for the count
+  int wait_spins;  // bound of a warp's wait for its bulk copies (nsm_set_copy_wait_limit)
   // select != 0 (bulk-copy kernel only): the kernel selects the blocks itself
   // from the router's scores -- top `top_k` of NB, through the block map --
   // and CTA 0 writes rows_out / row_block_out / count_out for the later kernels
@@ -398,6 +399,7 @@ struct DownParams {
   int y_dtype;
   int total_warps;
   int max_rows;  // capacity of rows / act16 (>= *count_ptr): the prologue loads this much without waiting for the count
+  int wait_spins;  // bound of a warp's wait for its bulk copies (nsm_set_copy_wait_limit)
 };
 
 __device__ __forceinline__ void record_down_meta(const DownParams& p) {
@@ -713,7 +715,7 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
     for (int st = 0; st < kGuStages; ++st) {
       if (q < q1 && ok) {
         const uint32_t bar = wbar + 8u * st;
-        if (!mbar_wait(bar, phase)) {
+        if (!mbar_wait(bar, phase, p.wait_spins)) {
           ok = false;
         } else {
           const uint32_t sb = wring + (uint32_t)(st * kGuStageBytes);
@@ -928,7 +930,7 @@ __device__ __forceinline__ void down_tma_body(const DownParams& p, uint32_t lb, 
 #pragma unroll
     for (int st = 0; st < kDnStages; ++st) {
       if (q < q1 && ok) {
-        if (!mbar_wait(wbar + 8u * st, phase)) {
+        if (!mbar_wait(wbar + 8u * st, phase, p.wait_spins)) {
           ok = false;
         } else {
           const uint32_t sb = wring + (uint32_t)(st * kDnStageBytes);
@@ -1160,6 +1162,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.act16 = ws.act16;
   gp.act_scale = ws.act_scale;
   gp.act_out = m.act_out;
+  gp.wait_spins = copy_wait_spins();
   const bool gu_tiled = (w->layout & NSM_LAYOUT_GATEUP_TILED) != 0;
   const bool gu_stage = m.H <= kStageXMaxHidden;
   const bool gu_tma = gateup_tma_ok(w, m.H, ks);
@@ -1223,6 +1226,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   dp.err = ws.err;
   dp.y = m.y;
   dp.y_dtype = m.y_dtype;
+  dp.wait_spins = copy_wait_spins();
   const bool dn_tiled = (w->layout & NSM_LAYOUT_DOWN_TILED) != 0;
   const bool dn_stage = m.k <= kStageActMaxSlots;
   const bool dn_aligned = ((uintptr_t)dp.down | (uintptr_t)dp.down_am) % 16 == 0 && dp.dbs % 16 == 0 &&

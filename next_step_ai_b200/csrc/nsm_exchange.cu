@@ -63,6 +63,7 @@ int nsm_exchange_create(int32_t world, int32_t rank, int32_t hidden, nsm_exchang
   h->dev.world = world;
   h->dev.rank = rank;
   h->dev.hidden = hidden;
+  h->dev.spin_limit = kDefaultExchangeSpins;
   h->dev.counter = reinterpret_cast<uint32_t*>(h->local);
   *ex_out = reinterpret_cast<nsm_exchange*>(h);
   return NSM_OK;
@@ -86,6 +87,32 @@ int nsm_exchange_connect(nsm_exchange* ex, const void* handles) {
     }
     h->dev.data[p] = reinterpret_cast<unsigned long long*>(base + exchange_data_off());
   }
+  return NSM_OK;
+}
+
+int nsm_exchange_connect_local(nsm_exchange* const* exs, int32_t n) {
+  NSM_REQUIRE(exs != nullptr && n >= 1 && n <= kMaxWorld, NSM_ERR_INVALID_ARG, "need 1..8 exchanges");
+  const ExchangeHost* first = reinterpret_cast<const ExchangeHost*>(exs[0]);
+  NSM_REQUIRE(first != nullptr && first->dev.world == n, NSM_ERR_INVALID_ARG, "exchange world != n");
+  for (int i = 0; i < n; ++i) {
+    const ExchangeHost* h = reinterpret_cast<const ExchangeHost*>(exs[i]);
+    NSM_REQUIRE(h != nullptr && h->dev.world == n && h->dev.rank == i && h->dev.hidden == first->dev.hidden,
+                NSM_ERR_INVALID_ARG, "exchanges must be ranks 0..n-1 of one world with one hidden size");
+  }
+  for (int i = 0; i < n; ++i) {
+    ExchangeHost* h = reinterpret_cast<ExchangeHost*>(exs[i]);
+    for (int p = 0; p < n; ++p) {
+      char* base = reinterpret_cast<char*>(reinterpret_cast<const ExchangeHost*>(exs[p])->local);
+      h->dev.data[p] = reinterpret_cast<unsigned long long*>(base + exchange_data_off());
+    }
+  }
+  return NSM_OK;
+}
+
+int nsm_exchange_set_spin_limit(nsm_exchange* ex, int32_t spins) {
+  NSM_REQUIRE(ex != nullptr, NSM_ERR_INVALID_ARG, "NULL exchange");
+  NSM_REQUIRE(spins >= 0, NSM_ERR_INVALID_ARG, "spins must be >= 0 (0 = the default)");
+  reinterpret_cast<ExchangeHost*>(ex)->dev.spin_limit = spins > 0 ? spins : kDefaultExchangeSpins;
   return NSM_OK;
 }
 

@@ -59,12 +59,19 @@ constexpr int kCounterInts = 2 + kMaxTopK + kMaxHidden / 32;
 // rank's buffer and sums the ranks' words in rank order once each carries the
 // current epoch.
 constexpr int kMaxWorld = 8;
+// Default bounds of the device waits: polls of a peer's exchange words, and
+// tries of a warp's bulk-copy mbarrier.  Both are runtime settings
+// (nsm_exchange_set_spin_limit, nsm_set_copy_wait_limit).
+constexpr int kDefaultExchangeSpins = 1 << 24;
+constexpr int kDefaultCopyWaitSpins = 1 << 22;
+int copy_wait_spins();
 struct ExchangeDev {
   unsigned long long* data[kMaxWorld];  // peer p's data region (mapped into this process)
   uint32_t* counter;                    // this rank's epoch counter
   int world;
   int rank;
   int hidden;
+  int spin_limit;                       // polls of one peer word before NSM_ERR_TIMEOUT
 };
 
 const ExchangeDev* exchange_dev(const nsm_exchange* ex);

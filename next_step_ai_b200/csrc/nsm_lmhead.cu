@@ -32,6 +32,7 @@
 // Streams HBM-bound: 0.5625 B of weight + absmax per (row, column) at qbs 64.
 // No waits other than cp.async.wait_group on the warp's own copies.
 #include <algorithm>
+#include <mutex>
 
 #include "nsm_common.cuh"
 #include "nsm_internal.h"
@@ -309,11 +310,17 @@ int nsm_lm_head_nf4(const void* x, int32_t x_dtype, int32_t tokens, const uint8_
   lmhead_prep_kernel<<<tokens, 1024, 0, s>>>(x, x_dtype, in_features, xh, scale);
   NSM_CHECK_CUDA(cudaGetLastError());
   const size_t smem = lmhead_smem_bytes(tokens, in_features);
-  static size_t smem_set[64] = {};  // per device; setting it twice is harmless
-  const int dslot = di.device & 63;
-  if (smem > smem_set[dslot]) {
-    NSM_CHECK_CUDA(cudaFuncSetAttribute(lmhead_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    smem_set[dslot] = smem;
+  {
+    // largest dynamic shared memory set so far per device; host threads that
+    // call concurrently serialise on the lock
+    static std::mutex smem_mu;
+    static size_t smem_set[64] = {};
+    std::lock_guard<std::mutex> lk(smem_mu);
+    const int dslot = di.device & 63;
+    if (smem > smem_set[dslot]) {
+      NSM_CHECK_CUDA(cudaFuncSetAttribute(lmhead_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      smem_set[dslot] = smem;
+    }
   }
   LmHeadParams p;
   p.xh = xh;

@@ -135,7 +135,6 @@ __device__ __forceinline__ void pending_output(const RouterAParams& p, int c0, i
 // chunk into every rank's buffer (slot epoch & 1, row r); each thread then
 // waits (bounded) until its columns carry the current epoch from every rank
 // and sums them in rank order -- identical bits on every rank.
-constexpr int kExchangeSpinLimit = 1 << 24;
 __device__ __forceinline__ void exchange_chunk(const RouterAParams& p, int c0, int n, float* ybuf, uint32_t epoch) {
   const ExchangeDev& ex = p.ex;
   const int slot = (int)(epoch & 1u);
@@ -153,7 +152,7 @@ __device__ __forceinline__ void exchange_chunk(const RouterAParams& p, int c0, i
       unsigned long long v = ld_relaxed_sys_u64(w);
       int it = 0;
       while ((uint32_t)(v >> 32) != epoch && !timed_out) {
-        if (++it >= kExchangeSpinLimit) {
+        if (++it >= ex.spin_limit) {
           timed_out = true;
           break;
         }

@@ -13,20 +13,25 @@
 //
 // Limits: hidden <= NSM_STATIC_MAX_HIDDEN (16384) and num_blocks_gathered <=
 // NSM_STATIC_MAX_BLOCKS (256); the scratch for the largest such call is
-// 6,374,400 bytes, so the array is 6.5 MiB.
+// 6,374,144 bytes (the decode workspace layout at those limits, checked by a
+// host test through nsm_decode_rows_workspace_bytes), so the array is 6.5 MiB.
 //
 // Every call on a device shares the one array and finds the previous call's
 // contents in it.  The parts that must start at zero (the reduction tickets at
 // the head of the workspace layout) are cleared with a stream-ordered memset at
-// the start of each call; everything else is written before it is read.
-// Calls whose GPU work overlaps (different streams, different host threads
-// without ordering between their streams) race on the array and give wrong
-// results.
+// the start of each call; everything else is written before it is read.  The
+// device error word in that head is NOT cleared by a call: a kernel that gave
+// up on a bounded wait records NSM_ERR_TIMEOUT there, and it stays until
+// nsm_static_error reads and clears it.  Calls whose GPU work overlaps
+// (different streams, different host threads without ordering between their
+// streams) race on the array and give wrong results.
 //
 // Set-up: the first call on a device, with that device current, looks up the
 // array's device address with cudaGetSymbolAddress (which also makes the
 // runtime load this module on that device) and caches it.  Make that first
-// call before any stream capture on the device.
+// call before any stream capture on the device.  The cached address does not
+// survive cudaDeviceReset (the module is loaded again, possibly elsewhere):
+// do not use this entry point on a device after resetting it.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -84,8 +89,32 @@ extern "C" int nsm_decode_gathered_static(const void* x, int32_t x_dtype, int32_
               "nsm_decode_gathered_static: shape needs more scratch than the static array holds");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // The tickets at the head of the layout must read zero when the kernels
-  // start; a call that failed part-way may have left them non-zero.
-  NSM_CHECK_CUDA(cudaMemsetAsync(scratch, 0, align_up((size_t)kCounterInts * sizeof(int), 256), s));
+  // start; a call that failed part-way may have left them non-zero.  The
+  // error word between them keeps a timeout of an earlier call for
+  // nsm_static_error.
+  char* head = reinterpret_cast<char*>(scratch);
+  const size_t err_off = (size_t)(reinterpret_cast<char*>(decode_ws_layout(scratch, 64, 64, 1, 1).err) - head);
+  NSM_CHECK_CUDA(cudaMemsetAsync(head, 0, err_off, s));
+  NSM_CHECK_CUDA(cudaMemsetAsync(head + err_off + sizeof(int), 0,
+                                 align_up((size_t)kCounterInts * sizeof(int), 256) - err_off - sizeof(int), s));
   return nsm_decode_gathered(x, x_dtype, hidden, num_blocks_gathered, w, y, y_dtype, act_out, scratch,
                              kStaticScratchBytes, s);
+}
+
+extern "C" int nsm_static_error(int32_t* code_out, nsm_stream_t stream) {
+  NSM_REQUIRE(code_out != nullptr, NSM_ERR_INVALID_ARG, "nsm_static_error: code_out is NULL");
+  int dev = -1;
+  NSM_CHECK_CUDA(cudaGetDevice(&dev));
+  NSM_REQUIRE(dev >= 0 && dev < kMaxDevices, NSM_ERR_DEVICE, "device index out of range");
+  void* scratch = nullptr;
+  int st = static_scratch_for(dev, &scratch);
+  if (st) return st;
+  int* err = decode_ws_layout(scratch, 64, 64, 1, 1).err;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  NSM_CHECK_CUDA(cudaMemcpyAsync(&v, err, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  NSM_CHECK_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), s));
+  NSM_CHECK_CUDA(cudaStreamSynchronize(s));
+  *code_out = v;
+  return NSM_OK;
 }

@@ -155,6 +155,36 @@ class SparseMlpDecoder:
         self._flush(ws, st)
         self.out.copy_(self.residual)
 
+    def trace_layers(self) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        """One eager token like :meth:`step_eager`, synchronising after every
+        layer to record what that layer saw and chose: ``(residual, blocks)``
+        per layer, where ``residual`` is the fp32 residual the layer's
+        RMSNorm read (the previous layers' outputs already added) and
+        ``blocks`` the selected blocks present in this rank's pool, ascending
+        -- the selection the gate/up kernel makes itself on this path.  The
+        launches are exactly those of :meth:`step_eager`; the records are
+        copies taken between layers.  ``out`` holds the final residual."""
+        ws = WORKSPACES.get(self._ws_bytes, self.dev)
+        st = stream_handle(self.dev)
+        k_max = max(min(l.router.top_k, l.router.num_blocks) for l in self.layers)
+        blocks = torch.empty(k_max, dtype=torch.int32, device=self.dev)
+        count = torch.empty(1, dtype=torch.int32, device=self.dev)
+        trace = []
+        for i in range(self.num_layers):
+            self._layer(i, ws, st)
+            r = self.layers[i % len(self.layers)].router
+            k = min(r.top_k, r.num_blocks)
+            _lib.check(self._lib.nsm_workspace_selection(ws.data_ptr(), ws.numel(), self.H, self.I, k, r.rank,
+                                                         blocks.data_ptr(), count.data_ptr(), st),
+                       "nsm_workspace_selection")
+            torch.cuda.current_stream(self.dev).synchronize()
+            n = int(count.item())
+            trace.append((self.residual.clone(), blocks[:n].clone()))
+        self._flush(ws, st)
+        self.out.copy_(self.residual)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return trace
+
     STAGES = ("router", "gateup", "gateup_finalize", "down", "down_finalize")
 
     def time_stages(self, num_layers: int | None = None) -> dict[str, float]:

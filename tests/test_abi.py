@@ -50,6 +50,15 @@ def test_status_strings_and_version(lib):
     assert lib.nsm_status_string(12345) == b"unknown status"
 
 
+def test_static_array_holds_its_largest_call(lib):
+    """nsm_decode_gathered_static keeps its scratch in a 6.5 MiB device array;
+    the decode workspace layout at its limits (hidden 16384, 256 gathered
+    blocks) must fit in it."""
+    need = lib.nsm_decode_rows_workspace_bytes(16384, 256, 1)
+    assert need == 6_374_144
+    assert need <= 13 << 19
+
+
 def test_workspace_size_queries(lib):
     b1 = lib.nsm_decode_workspace_bytes(16384, 53248, 208, 64)
     b0 = lib.nsm_decode_workspace_bytes(4096, 14336, 56, 64)

@@ -1,11 +1,12 @@
 """The VRAM hot-block cache on the GPU: resident blocks computed from the bank,
 misses staged from pinned host memory on a side stream, promotion after use.
 
-Each token's output must equal the all-resident decode of the same selection
-within the decode tolerances (the two passes only regroup the block sum), the
-device block table must mirror the host bank after every promotion, and the
-bank must evolve exactly like the reference policy (the oracle) on the same
-hit/miss sequence.
+Each token's output must match the oracle's fp32 dequant + matmul of the
+selected blocks (evaluated on the bitsandbytes bytes the layer was generated
+from) within the decode tolerances, whichever blocks were resident, staged or
+prefetched; the device block table must mirror the host bank after every
+promotion, and the bank must evolve exactly like the reference policy (the
+oracle) on the same hit/miss sequence.
 """
 from __future__ import annotations
 
@@ -18,6 +19,7 @@ pytestmark = pytest.mark.gpu
 
 from oracle import cache_policy as cp  # noqa: E402
 from oracle import synthetic as syn  # noqa: E402
+from tests.gpu_oracle import host_router, oracle_mlp, oracle_route  # noqa: E402
 
 MAX_ABS = 2e-2
 REL_L2 = 5e-3
@@ -42,19 +44,25 @@ def _close(got, ref):
 
 
 def _layer(shape_name, dev, seed=5):
+    """(shape, resident weights, router, bitsandbytes bytes kept for the oracle)."""
     from next_step_ai_b200 import synthetic as dsyn
 
     shape = dsyn.SHAPES[shape_name]
-    return shape, dsyn.make_layer_weights(shape, seed, 0, dev), dsyn.make_router(shape, seed, 0, dev)
+    w, bnb = dsyn.make_layer_weights(shape, seed, 0, dev, keep_bnb=True)
+    return shape, w, dsyn.make_router(shape, seed, 0, dev), bnb
 
 
-@pytest.mark.parametrize("shape_name,capacity", [("small", 40), ("cfg0", 112)])
-def test_cached_decode_matches_resident_and_policy(dev, shape_name, capacity):
-    from next_step_ai_b200 import sparse_mlp_decode
+def _oracle_y(shape, bnb, x, blocks):
+    return oracle_mlp(bnb, shape.hidden, shape.intermediate, x, np.asarray(blocks, np.int64))
+
+
+@pytest.mark.parametrize("shape_name,capacity,tokens", [("small", 40, 6), ("cfg0", 112, 6), ("cfg1", 416, 3)])
+def test_cached_decode_matches_oracle_and_policy(dev, shape_name, capacity, tokens):
+    """cfg1 with 416 of 1664 blocks resident is BASELINE config 3's bank."""
     from next_step_ai_b200 import synthetic as dsyn
     from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore
 
-    shape, w, rw = _layer(shape_name, dev)
+    shape, w, rw, bnb = _layer(shape_name, dev)
     store = HostBlockStore.from_weights(w)
     rng = np.random.default_rng(11)
     nb, k = shape.num_blocks, shape.top_k
@@ -65,7 +73,7 @@ def test_cached_decode_matches_resident_and_policy(dev, shape_name, capacity):
     ids = np.full(capacity, -1, np.int64)
     ids[: hot.size] = hot
     scores, active = cp.initial_bank_scores(hot.size, capacity), hot.size
-    for tok in range(6):
+    for tok in range(tokens):
         x = dsyn.make_x(shape, 100 + tok, 1, dev)[0]
         res = set(ids[:active].tolist())
         n_hit = int(0.7 * k)
@@ -74,8 +82,7 @@ def test_cached_decode_matches_resident_and_policy(dev, shape_name, capacity):
         rng.shuffle(sel)
         idx = torch.from_numpy(sel.astype(np.int32)).to(dev)
         y, st = cm.decode(x, idx=idx)
-        ref = sparse_mlp_decode(x, None, w, idx=idx, out_dtype=torch.float32)
-        _close(y.cpu().numpy(), ref.cpu().numpy())
+        _close(y.cpu().numpy(), _oracle_y(shape, bnb, x, sel))
         assert (st.hits, st.misses) == (n_hit, k - n_hit)
         assert st.h2d_bytes == (k - n_hit) * 56 * shape.hidden
         # the reference policy on the same token
@@ -94,19 +101,21 @@ def test_cached_decode_matches_resident_and_policy(dev, shape_name, capacity):
 
 
 def test_cached_decode_router_path_and_promoted_hits(dev):
-    from next_step_ai_b200 import route_sparse_mlp, sparse_mlp_decode
+    from next_step_ai_b200 import route_sparse_mlp
     from next_step_ai_b200 import synthetic as dsyn
     from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore
 
-    shape, w, rw = _layer("small", dev, seed=9)
+    shape, w, rw, bnb = _layer("small", dev, seed=9)
     store = HostBlockStore.from_weights(w)
     cm = CachedSparseMlp(rw, store, 24)
     cm.pre_warm(np.arange(24))
     x = dsyn.make_x(shape, 3, 1, dev)[0]
     y, st = cm.decode(x)  # router selection
     sel = route_sparse_mlp(x, rw)[0].to(torch.int32)
-    ref = sparse_mlp_decode(x, None, w, idx=sel, out_dtype=torch.float32)
-    _close(y.cpu().numpy(), ref.cpu().numpy())
+    ref_sel = oracle_route(host_router(rw), x.float().cpu().numpy(), shape.top_k, shape.rank)
+    assert np.array_equal(sel.cpu().numpy(), ref_sel)
+    ref = _oracle_y(shape, bnb, x, ref_sel)
+    _close(y.cpu().numpy(), ref)
     assert st.hits + st.misses == shape.top_k and st.promoted == st.misses
     # the same token again: every block promoted last time is now a hit; a
     # block the promotion evicted (lowest score, possibly one of this token's
@@ -117,14 +126,14 @@ def test_cached_decode_router_path_and_promoted_hits(dev):
     assert all(cm.slot_host[b] >= 0 for b in first_misses)
     y2, st2 = cm.decode(x)
     assert st2.misses == int((~resident).sum()) and st2.hits == int(resident.sum())
-    _close(y2.cpu().numpy(), ref.cpu().numpy())
+    _close(y2.cpu().numpy(), ref)
 
 
 def test_cache_rejects_bad_selections(dev):
     from next_step_ai_b200 import synthetic as dsyn
     from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore
 
-    shape, w, rw = _layer("tiny", dev, seed=2)
+    shape, w, rw, _ = _layer("tiny", dev, seed=2)
     cm = CachedSparseMlp(rw, HostBlockStore.from_weights(w), 8)
     cm.pre_warm(np.arange(8))
     x = dsyn.make_x(shape, 1, 1, dev)[0]
@@ -145,10 +154,9 @@ def _twin_caches(shape, w, rw, capacity, hot):
 
 
 def test_prefetch_serves_misses_without_copies(dev):
-    from next_step_ai_b200 import sparse_mlp_decode
     from next_step_ai_b200 import synthetic as dsyn
 
-    shape, w, rw = _layer("small", dev, seed=13)
+    shape, w, rw, bnb = _layer("small", dev, seed=13)
     nb, k, cap = shape.num_blocks, shape.top_k, 40
     rng = np.random.default_rng(3)
     a, b = _twin_caches(shape, w, rw, cap, rng.choice(nb, cap, replace=False))
@@ -168,14 +176,13 @@ def test_prefetch_serves_misses_without_copies(dev):
         assert (sa.hits, sa.misses, sa.promoted) == (sb.hits, sb.misses, sb.promoted)
         assert sa.prefetched == early.size and sa.h2d_bytes == (misses.size - early.size) * 56 * shape.hidden
         assert np.array_equal(a.bank.block_ids, b.bank.block_ids) and np.array_equal(a.slot_host, b.slot_host)
-        _close(ya.cpu().numpy(), sparse_mlp_decode(x, None, w, idx=idx, out_dtype=torch.float32).cpu().numpy())
+        _close(ya.cpu().numpy(), _oracle_y(shape, bnb, x, sel))
     # promoted records came from the prefetched rows: the banks hold the same bytes
     torch.cuda.synchronize()
     assert torch.equal(a.pool[:cap], b.pool[:cap])
 
 
 def test_layer_stack_lookahead_is_exact(dev):
-    from next_step_ai_b200 import sparse_mlp_decode
     from next_step_ai_b200 import synthetic as dsyn
     from next_step_ai_b200.cache import CachedLayerStack, CachedSparseMlp, HostBlockStore
 
@@ -186,7 +193,7 @@ def test_layer_stack_lookahead_is_exact(dev):
     hots = [rng.choice(shape.num_blocks, 40, replace=False) for _ in layers]
     for look in (True, False):
         cs = []
-        for (_, w, rw), hot in zip(layers, hots):
+        for (_, w, rw, _), hot in zip(layers, hots):
             c = CachedSparseMlp(rw, HostBlockStore.from_weights(w), 40)
             c.pre_warm(hot)
             cs.append(c)
@@ -201,18 +208,22 @@ def test_layer_stack_lookahead_is_exact(dev):
         assert [s.misses for s in sta] == [s.misses for s in stb]
         prefetched += sum(s.prefetched for s in sta)
         assert all(s.prefetched == 0 for s in stb)
-        for li, (_, w, rw) in enumerate(layers):   # all-resident replay of the same layers
-            rr.add_(sparse_mlp_decode(stacks[1]._input(rr, li), rw, w, out_dtype=torch.float32))
+        # the oracle chain: each layer's input from the stack's own RMSNorm of the
+        # oracle residual, routed and multiplied by the oracle
+        for li, (_, w, rw, bnb) in enumerate(layers):
+            xi = stacks[1]._input(rr, li)
+            sel = oracle_route(host_router(rw), xi.float().cpu().numpy(), shape.top_k, shape.rank)
+            rr.add_(torch.from_numpy(_oracle_y(shape, bnb, xi, sel)).to(dev))
         _close(ra.cpu().numpy(), rr.cpu().numpy())
     assert prefetched > 0
 
 
 def test_calibration_rebuild_prewarms_top_counts(dev):
-    from next_step_ai_b200 import route_sparse_mlp, sparse_mlp_decode
+    from next_step_ai_b200 import route_sparse_mlp
     from next_step_ai_b200 import synthetic as dsyn
     from next_step_ai_b200.cache import CachedSparseMlp, HostBlockStore, HotCacheCalibration, top_count_blocks
 
-    shape, w, rw = _layer("small", dev, seed=31)
+    shape, w, rw, bnb = _layer("small", dev, seed=31)
     cm = CachedSparseMlp(rw, HostBlockStore.from_weights(w), 24)
     cm.pre_warm(np.arange(24))
     cal = HotCacheCalibration()
@@ -227,5 +238,5 @@ def test_calibration_rebuild_prewarms_top_counts(dev):
     assert cm.bank.block_ids[: cm.bank.active].tolist() == top_count_blocks(counts, 24).tolist()
     x = dsyn.make_x(shape, 99, 1, dev)[0]
     y, st = cm.decode(x)
-    sel = route_sparse_mlp(x, rw)[0].to(torch.int32)
-    _close(y.cpu().numpy(), sparse_mlp_decode(x, None, w, idx=sel, out_dtype=torch.float32).cpu().numpy())
+    sel = route_sparse_mlp(x, rw)[0].cpu().numpy()
+    _close(y.cpu().numpy(), _oracle_y(shape, bnb, x, sel))

@@ -93,6 +93,35 @@ def test_union_decode_matches_per_row_oracle(dev, name, rows, shared):
         _close(y[r].cpu().numpy(), ref[r])
 
 
+def test_union_decode_cfg1_config4(dev):
+    """BASELINE config 4 as the benchmark runs it: a 405B-shaped layer (H =
+    16384, 1664 blocks, k = 208), 32 tokens rms(0.85 z + sqrt(1 - 0.85^2) e_t)
+    routed together on the GPU (bit-exact against the oracle router), the union
+    in ascending order, and every row against the oracle's fp32 dequant +
+    matmul over the union with the reference's per-row flat_mask."""
+    from next_step_ai_b200 import route_sparse_mlp, union_decode
+    from next_step_ai_b200 import synthetic as dsyn
+    from tests.gpu_oracle import host_router, oracle_mlp_rows
+
+    shape = dsyn.SHAPES["cfg1"]
+    w, bnb = dsyn.make_layer_weights(shape, 1234, 0, dev, keep_bnb=True)
+    rw = dsyn.make_router(shape, 1234, 0, dev)
+    x = dsyn.make_x(shape, 99, 32, dev, shared=0.85)
+    idx = route_sparse_mlp(x, rw).to(torch.int32)
+    xh = x.float().cpu().numpy()
+    R = host_router(rw)
+    ref_idx = orr.route_sparse_mlp(xh, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)
+    assert np.array_equal(idx.cpu().numpy(), ref_idx)
+    y, uni = union_decode(x, idx, w, out_dtype=torch.float32, return_union=True)
+    ordered, _, flat_mask, _ = lay.build_sparse_active_layout(ref_idx, 32, 32, shape.num_blocks)
+    assert np.array_equal(uni.cpu().numpy(), np.asarray(ordered))
+    assert 600 <= len(ordered) <= 1000, len(ordered)
+    ref = oracle_mlp_rows(bnb, shape.hidden, shape.intermediate, xh, np.asarray(ordered), flat_mask)
+    got = y.cpu().numpy()
+    for r in range(32):
+        _close(got[r], ref[r])
+
+
 def test_union_decode_ignores_invalid_ids_and_respects_shards(dev):
     from next_step_ai_b200 import union_decode
 

@@ -277,3 +277,30 @@ def test_routing_dict_k_resolution():
     assert RouterWeights.from_routing(base, layer_idx=3, basis_top_k_by_layer={3: 99}).basis_top_k == 16
     rw = RouterWeights.from_routing(dict(base, down_block_norm=torch.ones(39)))
     assert rw.down_block_norm is None and rw.score_b is None
+
+
+@pytest.mark.parametrize("name", ["small", "cfg0"])
+def test_cpu_torch_arm_matches_numpy_oracle(name):
+    """The torch restatement bench.py times as the CPU arm computes what the
+    numpy oracle computes: the same selected blocks, the same MLP output
+    (fp32, up to summation order)."""
+    import torch
+
+    from oracle import cpu_torch as ct
+    from oracle import mlp as om
+    from oracle import router as orr
+
+    shape = syn.SHAPES[name]
+    R = syn.make_router(shape, 3)
+    x = syn.make_x(shape, 4, 2)
+    ref_idx = orr.route_sparse_mlp(x, R["enc_w"], R["enc_b"], R["score_w"], R["score_b"], shape.top_k, shape.rank)
+    t = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in R.items() if v is not None}
+    got_idx = ct.route(torch.from_numpy(x), t["enc_w"], t.get("enc_b"), t["score_w"], t.get("score_b"), shape.top_k)
+    assert np.array_equal(got_idx.numpy(), ref_idx)
+    G = syn.selected_blocks_gathered(shape, 3, 0, ref_idx[0])
+    y_ref = om.sparse_mlp_gathered(x[:1], G["gate_packed"], G["gate_absmax"], G["code"], G["up_packed"],
+                                   G["up_absmax"], G["code"], G["down_cols"], G["down_absmax_cols"], G["code"])
+    g = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in G.items()}
+    y = ct.mlp_gathered(torch.from_numpy(x[:1]), g["gate_packed"], g["gate_absmax"], g["up_packed"],
+                        g["up_absmax"], g["down_cols"], g["down_absmax_cols"], g["code"]).numpy()
+    assert np.allclose(y, y_ref, rtol=1e-4, atol=1e-4), float(np.abs(y - y_ref).max())

@@ -114,7 +114,20 @@ def test_static_matches_workspace_entry_and_oracle(dev, name):
                                      G["up_packed"], G["up_absmax"], G["code"], G["down_cols"],
                                      G["down_absmax_cols"], G["code"])[0]
         _close(y.cpu().numpy(), ref)
+    _assert_no_static_timeout()
     del keep
+
+
+def _assert_no_static_timeout():
+    """Every bounded wait of the static calls so far completed: the array's
+    error word (kept across calls, cleared by this read) is zero."""
+    from next_step_ai_b200 import _lib
+    from next_step_ai_b200._torch import stream_handle
+
+    code = ctypes.c_int32(-99)
+    _lib.check(_lib.load().nsm_static_error(ctypes.byref(code), stream_handle(torch.device("cuda", 0))),
+               "nsm_static_error")
+    assert code.value == 0
 
 
 def test_static_at_its_size_limit(dev):
@@ -141,6 +154,7 @@ def test_static_at_its_size_limit(dev):
         y_ws = torch.empty(H, dtype=torch.float32, device=dev)
         _lib.check(_workspace_call(x, H, U, c, y_ws), "nsm_decode_gathered")
         _close(y.cpu().numpy(), y_ws.cpu().numpy())
+    _assert_no_static_timeout()
     del keep
 
 
