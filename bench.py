@@ -53,9 +53,17 @@ def gateup_bytes_per_launch(k: int = TOP_K, H: int = HIDDEN) -> int:
     return k * 2 * (16 * H + 2 * H)
 
 
-# DRAM bytes (read + write) of one gateup_tma_kernel launch at this workload, from one
-# ncu capture (dram__bytes_read.sum + dram__bytes_write.sum; profiles/gateup_tma_kernel_cfg1.txt)
-GATEUP_DRAM_BYTES_PER_LAUNCH = 122_787_840 + 5_259_776
+# DRAM bytes (read + write) per layer of the token kernel from one ncu capture of a
+# 2-layer token (dram__bytes_read.sum + dram__bytes_write.sum of the launch / 2),
+# scaled to the 126-layer token; None until a capture of the current kernel exists.
+TOKEN_DRAM_BYTES_PER_LAYER = None
+TOKEN_TRAFFIC_SOURCE = "profiles/token_kernel_cfg1.txt (ncu of a 2-layer token, per layer x 126)"
+
+
+def token_traffic(world: int):
+    if TOKEN_DRAM_BYTES_PER_LAYER is None or world != 1:
+        return None
+    return int(TOKEN_DRAM_BYTES_PER_LAYER * LAYERS)
 
 
 def headline_config(world: int) -> dict:
@@ -239,15 +247,28 @@ def run_ours(args) -> None:
     alg_layer = algorithmic_bytes_per_layer()
     pk = peaks()
     layer_us = ms_step * 1e3 / LAYERS
-    # whole layer group (router + gate/up + down kernels) inside the graph; at N > 1 each
-    # rank reads 1/N of the block bytes plus the whole router
+    # whole layer (router + gate/up + down) inside the timed region; at N > 1 each rank
+    # reads 1/N of the block bytes plus the whole router
     router_b = 2 * RANK * HIDDEN + 2 * RANK * NB + 2 * NB
-    group_gbs = ((alg_layer - router_b) / world + router_b) / (layer_us * 1e-6) / 1e9
-    # dominant kernel (gate/up gather-GEMV): device time per launch from CUDA events the
-    # library records around each stage, in an eager pass after the timed region
-    stage_us = dec.time_stages(min(LAYERS, 2 * unique))
-    gu_bytes = gateup_bytes_per_launch() / world  # expected share of the selected blocks per rank
-    gu_gbs = gu_bytes / (stage_us["gateup"] * 1e-6) / 1e9
+    rank_layer_bytes = (alg_layer - router_b) / world + router_b
+    group_gbs = rank_layer_bytes / (layer_us * 1e-6) / 1e9
+    if dec.use_token:
+        # the token kernel is the only kernel of a step: its device time per launch is
+        # the CUDA-event time of the timed region per step (one graph node per step)
+        kern_name = ("token_kernel (one persistent cooperative launch per token: all 126 layers' router, "
+                     "block selection, NF4 gate/up and down gather-GEMVs)")
+        kern_bytes = rank_layer_bytes * LAYERS
+        kern_us = ms_step * 1e3
+        stage_us = None
+    else:
+        # dominant kernel (gate/up gather-GEMV): device time per launch from CUDA events the
+        # library records around each stage, in an eager pass after the timed region
+        kern_name = ("gateup_tma_kernel (block selection from the router's scores + NF4 gate+up gather-GEMV, one "
+                     "launch per layer)")
+        stage_us = dec.time_stages(min(LAYERS, 2 * unique))
+        kern_bytes = gateup_bytes_per_launch() / world  # expected share of the selected blocks per rank
+        kern_us = stage_us["gateup"]
+    kern_gbs = kern_bytes / (kern_us * 1e-6) / 1e9
     if rank == 0:
         line = {
             "metric": METRIC, "value": args.steps / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
@@ -260,14 +281,14 @@ def run_ours(args) -> None:
             "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
                     "d2h_bytes_per_step": HIDDEN * 4},
             "gpu_launches": args.steps * dec.kernels_per_step,
-            "roofline": {"bound": "hbm", "achieved": round(gu_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": round(gu_gbs / pk["hbm_gbs"], 4),
-                         "traffic": GATEUP_DRAM_BYTES_PER_LAUNCH if world == 1 else None,
-                         "kernel": "gateup_tma_kernel (block selection from the router's scores + NF4 gate+up "
-                                   "gather-GEMV, one launch per layer)",
-                         "algorithmic_bytes": int(gu_bytes), "us_per_launch": round(stage_us["gateup"], 3),
+            "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(kern_gbs / pk["hbm_gbs"], 4),
+                         "traffic": token_traffic(world) if dec.use_token else None,
+                         "traffic_source": TOKEN_TRAFFIC_SOURCE if dec.use_token else None,
+                         "kernel": kern_name,
+                         "algorithmic_bytes": int(kern_bytes), "us_per_launch": round(kern_us, 3),
                          "peak_source": pk["source"], "peak_note": "of measured (MEASURED_PEAKS.json hbm_gbs)",
-                         "stage_us": {k: round(v, 3) for k, v in stage_us.items()},
+                         "stage_us": {k: round(v, 3) for k, v in stage_us.items()} if stage_us else None,
                          "layer_group": {"algorithmic_bytes": alg_layer, "us_per_layer": round(layer_us, 3),
                                          "achieved": round(group_gbs, 1),
                                          "frac": round(group_gbs / pk["hbm_gbs"], 4)}},

@@ -325,6 +325,60 @@ int nsm_decode_gathered_static(const void* x, int32_t x_dtype, int32_t hidden, i
  * all.  Like the entry point it serves, no counterpart in the reference. */
 int nsm_static_error(int32_t* code_out, nsm_stream_t stream);
 
+/* ---- one token through a whole layer stack, one kernel ------------------
+ * The per-token layer loop of the reference's decode
+ * (StreamingLlamaRuntime.forward_token, streaming_llama_runtime.py:7612-7775)
+ * restricted to the MLP path -- for every layer: residual += the previous
+ * layer's MLP output, x = rmsnorm(residual) * norm_weight, _route_sparse_mlp
+ * (:4311-4352), the exact blockwise-sparse MLP on the selected blocks
+ * (:5433-5492) -- with attention left out (identity), run as ONE persistent
+ * cooperative kernel: the phases of a layer are linked inside the kernel by
+ * bounded waits on arrival counters, so a token costs one launch.
+ * Requirements: router rank 64, bf16 or fp16 router weights, top_k <= 256,
+ * at most 4096 blocks, hidden a multiple of 128 and at most 16384, tiled pools
+ * (NSM_LAYOUT_GATEUP_TILED | NSM_LAYOUT_DOWN_TILED), no biases, 16-byte
+ * aligned pools and strides, and a down codebook equal (by value) to the gate
+ * or the up codebook (a kernel that finds otherwise records
+ * NSM_ERR_UNSUPPORTED in the workspace error word).
+ * Numerics: x and SiLU(gate)*up enter the tensor cores as fp16 hi + lo pairs,
+ * the codebooks as fp16(alpha * code) with a per-codebook alpha in [1, 2)
+ * that minimises their fp16 rounding (1/alpha applied in fp32 with the
+ * absmax); accumulation is fp32. */
+typedef struct nsm_token_layer {
+  nsm_router_weights router;
+  nsm_mlp_weights mlp;
+  nsm_block_map map;          /* the blocks this rank's pools hold */
+  const void* norm_weight;    /* [H] RMSNorm weight of the MLP input, or NULL */
+  int32_t norm_weight_dtype;
+  int32_t reserved;
+} nsm_token_layer;
+/* Workspace of nsm_decode_token for num_layers layers; zero-fill it once
+ * (nsm_workspace_init).  Its error word is read by nsm_workspace_error. */
+size_t nsm_token_workspace_bytes(int hidden, int intermediate, int num_layers);
+/* Validates the layers and copies their descriptors into the workspace
+ * (synchronises `stream`; not capturable).  The weights must stay valid while
+ * the workspace is used. */
+int nsm_token_set_layers(void* ws, size_t ws_bytes, int32_t hidden, int32_t intermediate,
+                         const nsm_token_layer* layers, int32_t num_layers, nsm_stream_t stream);
+/* One token through the num_layers layers set on the workspace: residual [H]
+ * fp32 (in/out) ends as residual + every layer's MLP output.  ex: the cross-GPU
+ * exchange when the blocks are sharded over ranks (NULL on one GPU).  Optional
+ * records for tests (NULL to skip): trace_blocks [num_layers][trace_k] the
+ * selected blocks present here, ascending; trace_counts [num_layers];
+ * trace_residual [num_layers][H] the residual each layer's RMSNorm read.
+ * Calls sharing a workspace must not overlap on the GPU. */
+int nsm_decode_token(float* residual, int32_t hidden, int32_t intermediate, int32_t num_layers, float eps,
+                     const nsm_exchange* ex, int32_t* trace_blocks, int32_t trace_k, int32_t* trace_counts,
+                     float* trace_residual, void* ws, size_t ws_bytes, nsm_stream_t stream);
+/* Profiling hook of nsm_decode_token: with stamps != NULL, later calls on this
+ * workspace write 8 globaltimer readings (ns) per CTA for each of the first
+ * stamp_layers layers -- stamps[(layer * ctas + cta) * 8 + i], i = phase A
+ * start, A done, B start, B done, selection done, gate/up done, activations
+ * ready, down done (ctas = the SM count) -- for reading where a token's time
+ * goes.  stamps == NULL switches it off.  Synchronises `stream`. */
+int nsm_token_profile(void* ws, size_t ws_bytes, int32_t hidden, int32_t intermediate, int32_t num_layers,
+                      unsigned long long* stamps, int32_t stamp_layers, nsm_stream_t stream);
+
 /* ---- multi-token decode over the union of the tokens' blocks ------------
  * Up to 32 tokens: x [rows][H] (x_dtype), idx [rows][k] int32 block ids (each
  * row's router selection; ids < 0 or >= NB are ignored), the resident pools

@@ -43,7 +43,8 @@ EXPORTED = (
     "nsm_exchange_create", "nsm_exchange_connect", "nsm_exchange_destroy", "nsm_route_workspace_bytes",
     "nsm_lm_head_workspace_bytes", "nsm_lm_head_max_tokens", "nsm_lm_head_nf4",
     "nsm_route_rows", "nsm_workspace_selection", "nsm_exchange_connect_local", "nsm_exchange_set_spin_limit",
-    "nsm_set_copy_wait_limit", "nsm_static_error",
+    "nsm_set_copy_wait_limit", "nsm_static_error", "nsm_token_workspace_bytes", "nsm_token_set_layers",
+    "nsm_decode_token", "nsm_token_profile",
 )
 
 
@@ -70,6 +71,11 @@ class MlpWeightsC(ctypes.Structure):
 
 class BlockMapC(ctypes.Structure):
     _fields_ = [("slot_of_block", c_void_p), ("block_begin", c_int32), ("block_end", c_int32)]
+
+
+class TokenLayerC(ctypes.Structure):
+    _fields_ = [("router", RouterWeightsC), ("mlp", MlpWeightsC), ("map", BlockMapC), ("norm_weight", c_void_p),
+                ("norm_weight_dtype", c_int32), ("reserved", c_int32)]
 
 
 class LayerIoC(ctypes.Structure):
@@ -129,6 +135,11 @@ _SIGS = {
     "nsm_exchange_set_spin_limit": (c_int, [c_void_p, c_int32]),
     "nsm_set_copy_wait_limit": (c_int, [c_int32]),
     "nsm_static_error": (c_int, [POINTER(c_int32), c_void_p]),
+    "nsm_token_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "nsm_token_set_layers": (c_int, [c_void_p, c_size_t, c_int32, c_int32, c_void_p, c_int32, c_void_p]),
+    "nsm_decode_token": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_float, c_void_p, c_void_p, c_int32, c_void_p,
+                                 c_void_p, c_void_p, c_size_t, c_void_p]),
+    "nsm_token_profile": (c_int, [c_void_p, c_size_t, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p]),
     "nsm_union_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "nsm_union_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32,
                                  POINTER(BlockMapC), POINTER(MlpWeightsC), c_void_p, c_int32, c_void_p, c_void_p,

@@ -16,7 +16,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libnsm.so"
 SOURCES = ["nsm_abi.cu", "nsm_router.cu", "nsm_decode.cu", "nsm_aux.cu", "nsm_static.cu", "nsm_union.cu", "nsm_exchange.cu",
-           "nsm_lmhead.cu"]
+           "nsm_lmhead.cu", "nsm_token.cu"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -42,16 +42,24 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     nvcc = nvcc_path()
     objdir = PKG / "_build"
     objdir.mkdir(exist_ok=True)
-    objs = []
     common = GENCODE + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
                         "-I", str(PKG.parent / "include")]
+    objs = []
+    cmds = []
     for src in SOURCES:
         obj = objdir / (Path(src).stem + ".o")
-        cmd = [nvcc, *common, "-c", str(CSRC / src), "-o", str(obj)]
-        if verbose:
-            print(" ".join(cmd), file=sys.stderr)
-        subprocess.run(cmd, check=True)
+        cmds.append([nvcc, *common, "-c", str(CSRC / src), "-o", str(obj)])
         objs.append(str(obj))
+    if verbose:
+        for cmd in cmds:
+            print(" ".join(cmd), file=sys.stderr)
+    # the translation units are independent: compile them in parallel
+    from concurrent.futures import ThreadPoolExecutor
+
+    with ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as pool:
+        for r in list(pool.map(lambda c: subprocess.run(c, capture_output=True, text=True), cmds)):
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed: {' '.join(r.args)}\n{r.stdout}{r.stderr}")
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc, *GENCODE, "-shared", "-cudart", "static", "-o", str(tmp), *objs]
     if verbose:

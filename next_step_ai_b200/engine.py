@@ -6,11 +6,21 @@ every decoder layer the residual is updated with the previous layer's MLP
 output, RMS-normalised, routed, and pushed through the sparse NF4 MLP.
 Attention is out of scope (identity), as in the benchmark configuration.
 
+Two execution paths compute the same thing:
+
+* the token kernel (``nsm_decode_token``, the default when every layer
+  qualifies): ONE persistent cooperative kernel runs the whole token, the
+  phases of each layer linked by bounded waits inside the kernel;
+* the per-layer path (``nsm_sparse_mlp_decode`` per layer, five kernels each
+  with programmatic dependent launch), for layers the token kernel does not
+  take (another router rank or dtype, row-major pools, biases, ...).
+
 Multi-GPU: every rank holds a contiguous range of each layer's intermediate
 blocks and a full copy of the router; all ranks select the same blocks, each
-computes the partial output of the blocks it owns, and the partials are
-summed with one NCCL all-reduce per layer (``torch.distributed``).  The whole
-token is captured once into a CUDA graph and replayed.
+computes the partial output of the blocks it owns, and the partials are summed
+over NVLink in rank order inside the next layer's first phase (CUDA-IPC
+exchange buffers).  The whole token is captured once into a CUDA graph and
+replayed.
 """
 from __future__ import annotations
 
@@ -59,7 +69,7 @@ class SparseMlpDecoder:
     """
 
     def __init__(self, layers: list[DecodeLayer], num_layers: int, *, block_range: tuple[int, int] | None = None,
-                 group=None, eps: float = 1e-5):
+                 group=None, eps: float = 1e-5, token_kernel: bool | None = None):
         if not layers:
             raise RuntimeError("no layers")
         self.layers = layers
@@ -83,6 +93,76 @@ class SparseMlpDecoder:
         self._ex = None
         if group is not None and torch.distributed.get_world_size(group) > 1:
             self._ex = self._connect_exchange(group)
+        ok = self.token_kernel_applies()
+        if token_kernel and not ok:
+            raise RuntimeError("the token kernel does not apply to these layers (see token_kernel_applies)")
+        self.use_token = ok if token_kernel is None else bool(token_kernel)
+        self._tk_ws = None
+        if self.use_token:
+            self._setup_token()
+
+    # ---- the token kernel
+    def token_kernel_applies(self) -> bool:
+        """Whether nsm_decode_token takes every layer: router rank 64 in bf16 or
+        fp16, k <= 256, at most 4096 blocks, hidden a multiple of 128 and at
+        most 16384, tiled pools without biases, a down codebook equal to the
+        gate or up codebook."""
+        if self.H % 128 or self.H > 16384 or self.I // 32 > 4096:
+            return False
+        for l in self.layers:
+            r, w = l.router, l.weights
+            if r.rank != 64 or r.enc_w.dtype not in (torch.bfloat16, torch.float16) or min(r.top_k, r.num_blocks) > 256:
+                return False
+            if r.num_blocks != self.I // 32:
+                return False
+            if (w.layout & 3) != 3 or any(getattr(w, b, None) is not None for b in ("gate_bias", "up_bias", "down_bias")):
+                return False
+            if not (torch.equal(w.down_code, w.gate_code) or torch.equal(w.down_code, w.up_code)):
+                return False
+        return True
+
+    def _setup_token(self) -> None:
+        L = self.num_layers
+        nbytes = self._lib.nsm_token_workspace_bytes(self.H, self.I, L)
+        self._tk_ws = torch.empty(nbytes, dtype=torch.uint8, device=self.dev)
+        st = stream_handle(self.dev)
+        _lib.check(self._lib.nsm_workspace_init(self._tk_ws.data_ptr(), nbytes, st), "nsm_workspace_init")
+        arr = (_lib.TokenLayerC * L)()
+        for i in range(L):
+            li = i % len(self.layers)
+            rc, wc = self._c[li]
+            arr[i].router = rc
+            arr[i].mlp = wc
+            arr[i].map = self._bm
+            nw = self.layers[li].norm_weight
+            arr[i].norm_weight = ptr(nw) if nw is not None else None
+            arr[i].norm_weight_dtype = dtype_code(nw.dtype) if nw is not None else 0
+        _lib.check(self._lib.nsm_token_set_layers(self._tk_ws.data_ptr(), nbytes, self.H, self.I, ctypes.byref(arr), L,
+                                                  st), "nsm_token_set_layers")
+
+    def _token(self, st: int, trace=None) -> None:
+        tb, tk, tc, tr = (None, 0, None, None) if trace is None else trace
+        _lib.check(self._lib.nsm_decode_token(self.residual.data_ptr(), self.H, self.I, self.num_layers, self.eps,
+                                              self._ex, tb, tk, tc, tr, self._tk_ws.data_ptr(), self._tk_ws.numel(),
+                                              st), "nsm_decode_token")
+
+    def token_error(self) -> int:
+        """Reads and clears the token workspace's device error word (0: every
+        bounded wait of the token kernel completed).  Synchronises."""
+        if self._tk_ws is None:
+            return 0
+        code = ctypes.c_int32(0)
+        _lib.check(self._lib.nsm_workspace_error(self._tk_ws.data_ptr(), self._tk_ws.numel(), ctypes.byref(code),
+                                                 stream_handle(self.dev)), "nsm_workspace_error")
+        return int(code.value)
+
+    def token_profile(self, stamps: torch.Tensor | None) -> None:
+        """Switches the token kernel's phase timestamps on (``stamps``: int64
+        ``[layers][SMs][8]`` on the device) or off (None)."""
+        n = int(stamps.shape[0]) if stamps is not None else 0
+        _lib.check(self._lib.nsm_token_profile(self._tk_ws.data_ptr(), self._tk_ws.numel(), self.H, self.I,
+                                               self.num_layers, stamps.data_ptr() if stamps is not None else None, n,
+                                               stream_handle(self.dev)), "nsm_token_profile")
 
     def _connect_exchange(self, group) -> ctypes.c_void_p:
         world = torch.distributed.get_world_size(group)
@@ -143,16 +223,21 @@ class SparseMlpDecoder:
     def kernels_per_step(self) -> int:
         """This library's kernel launches per token (the final copy to ``out``
         is not counted)."""
+        if self.use_token:
+            return 1
         return sum(self._kernels_for(i % len(self.layers)) for i in range(self.num_layers)) + 1
 
     def step_eager(self) -> None:
         """One token through all layers (no graph).  Input: ``residual``;
         output: ``out`` = final residual (residual + every layer's MLP output)."""
-        ws = WORKSPACES.get(self._ws_bytes, self.dev)
         st = stream_handle(self.dev)
-        for i in range(self.num_layers):
-            self._layer(i, ws, st)
-        self._flush(ws, st)
+        if self.use_token:
+            self._token(st)
+        else:
+            ws = WORKSPACES.get(self._ws_bytes, self.dev)
+            for i in range(self.num_layers):
+                self._layer(i, ws, st)
+            self._flush(ws, st)
         self.out.copy_(self.residual)
 
     def trace_layers(self) -> list[tuple[torch.Tensor, torch.Tensor]]:
@@ -163,9 +248,21 @@ class SparseMlpDecoder:
         ``blocks`` the selected blocks present in this rank's pool, ascending
         -- the selection the gate/up kernel makes itself on this path.  The
         launches are exactly those of :meth:`step_eager`; the records are
-        copies taken between layers.  ``out`` holds the final residual."""
-        ws = WORKSPACES.get(self._ws_bytes, self.dev)
+        copies taken between layers (the token kernel writes them itself while
+        it runs).  ``out`` holds the final residual."""
         st = stream_handle(self.dev)
+        if self.use_token:
+            L = self.num_layers
+            k_max = max(min(l.router.top_k, l.router.num_blocks) for l in self.layers)
+            tb = torch.full((L, k_max), -1, dtype=torch.int32, device=self.dev)
+            tc = torch.zeros(L, dtype=torch.int32, device=self.dev)
+            tr = torch.empty((L, self.H), dtype=torch.float32, device=self.dev)
+            self._token(st, (tb.data_ptr(), k_max, tc.data_ptr(), tr.data_ptr()))
+            self.out.copy_(self.residual)
+            torch.cuda.current_stream(self.dev).synchronize()
+            counts = tc.cpu().tolist()
+            return [(tr[i].clone(), tb[i, :counts[i]].clone()) for i in range(L)]
+        ws = WORKSPACES.get(self._ws_bytes, self.dev)
         k_max = max(min(l.router.top_k, l.router.num_blocks) for l in self.layers)
         blocks = torch.empty(k_max, dtype=torch.int32, device=self.dev)
         count = torch.empty(1, dtype=torch.int32, device=self.dev)
@@ -196,6 +293,8 @@ class SparseMlpDecoder:
         previous layer's output (and the cross-GPU exchange); "down_finalize"
         is empty because each layer's output stays pending for the next.  The
         pass advances ``residual``."""
+        if self.use_token:
+            raise RuntimeError("time_stages times the per-layer path; the token kernel runs a token in one launch")
         n = int(num_layers or self.num_layers)
         ws = WORKSPACES.get(self._ws_bytes, self.dev)
         st = stream_handle(self.dev)

@@ -156,19 +156,46 @@ def _host_refs(shape, host):
     return route_ref, mlp_ref
 
 
-@pytest.mark.parametrize("shape_name,n_unique,num_layers", [("tiny", 2, 5), ("small", 3, 4)])
-def test_engine_per_layer_selection_and_output(dev, shape_name, n_unique, num_layers):
+@pytest.mark.parametrize("shape_name,n_unique,num_layers,token", [("tiny", 2, 5, None), ("small", 3, 4, False),
+                                                                  ("small", 3, 4, True), ("cfg0", 2, 3, True)])
+def test_engine_per_layer_selection_and_output(dev, shape_name, n_unique, num_layers, token):
+    """token: True = the one-launch token kernel, False = the per-layer
+    kernels, None = whichever applies (tiny: rank 16, per-layer)."""
     from next_step_ai_b200.engine import SparseMlpDecoder
 
     shape, layers, host = _build(shape_name, n_unique, dev, seed=60)
     x0 = _t((np.random.default_rng(8).standard_normal(shape.hidden) * 2).astype(np.float32), dev)
-    dec = SparseMlpDecoder(layers, num_layers)
+    dec = SparseMlpDecoder(layers, num_layers, token_kernel=token)
+    if token is not None:
+        assert dec.use_token == token
     route_ref, mlp_ref = _host_refs(shape, host)
     gammas = [host[i % n_unique][2] for i in range(num_layers)]
     traced = _per_layer_check(dec, x0, route_ref, mlp_ref, gammas)
     dec.residual.copy_(x0)
     dec.step_eager()
     assert torch.equal(dec.out, traced)  # the per-layer records change nothing
+    assert dec.token_error() == 0
+
+
+def test_engine_token_kernel_and_per_layer_path_agree(dev):
+    """The token kernel and the per-layer kernels on the same layers and
+    input: the same selections in every layer (bit-exact) and outputs within
+    the decode tolerance of each other (their fp16 roundings differ: the
+    token kernel carries x and SiLU*up as hi + lo pairs and prescaled codes)."""
+    from next_step_ai_b200.engine import SparseMlpDecoder
+
+    shape, layers, _ = _build("small", 3, dev, seed=61)
+    x0 = _t((np.random.default_rng(9).standard_normal(shape.hidden) * 2).astype(np.float32), dev)
+    outs, sels = [], []
+    for token in (False, True):
+        dec = SparseMlpDecoder(layers, 6, token_kernel=token)
+        dec.residual.copy_(x0)
+        tr = dec.trace_layers()
+        sels.append([b.cpu().numpy() for _, b in tr])
+        outs.append(dec.out.cpu().numpy())
+    for i, (a, b) in enumerate(zip(*sels)):
+        assert np.array_equal(a, b), i
+    _close(outs[1], outs[0], "token vs per-layer")
 
 
 def test_engine_cfg1_headline_path(dev):
@@ -233,7 +260,7 @@ def test_engine_stage_timing(dev):
     from next_step_ai_b200.engine import SparseMlpDecoder
 
     shape, layers, _ = _build("small", 1, dev)
-    dec = SparseMlpDecoder(layers, 3)
+    dec = SparseMlpDecoder(layers, 3, token_kernel=False)
     dec.residual.copy_(_t(np.ones(shape.hidden, np.float32), dev))
     t = dec.time_stages()
     assert list(t) == list(SparseMlpDecoder.STAGES)

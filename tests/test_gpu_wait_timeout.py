@@ -44,7 +44,11 @@ def _local_world2(lib, hidden):
     return exs
 
 
-def test_exchange_wait_runs_out_and_the_context_survives(dev):
+@pytest.mark.parametrize("token_kernel", [False, True])
+def test_exchange_wait_runs_out_and_the_context_survives(dev, token_kernel):
+    """Both execution paths: the per-layer kernels (the router kernel waits)
+    and the one-launch token kernel (its first phase waits; the other CTAs
+    see the recorded error and leave too)."""
     from next_step_ai_b200 import _lib
     from next_step_ai_b200._torch import WORKSPACES
     from next_step_ai_b200.engine import SparseMlpDecoder
@@ -53,9 +57,13 @@ def test_exchange_wait_runs_out_and_the_context_survives(dev):
     lib = _lib.load()
     shape, layers, host = _build("small", 2, dev, seed=90)
     x0 = _t((np.random.default_rng(4).standard_normal(shape.hidden)).astype(np.float32), dev)
-    dec = SparseMlpDecoder(layers, 3)
+    dec = SparseMlpDecoder(layers, 3, token_kernel=token_kernel)
     torch.cuda.synchronize()
-    WORKSPACES.errors()  # start from clear error words
+
+    def errors():
+        return [dec.token_error()] if token_kernel else list(WORKSPACES.errors().values())
+
+    errors()  # start from clear error words
     exs = _local_world2(lib, shape.hidden)
     try:
         _lib.check(lib.nsm_exchange_set_spin_limit(exs[0], 2000), "nsm_exchange_set_spin_limit")
@@ -63,9 +71,9 @@ def test_exchange_wait_runs_out_and_the_context_survives(dev):
         dec.residual.copy_(x0)
         dec.step_eager()  # layers 1, 2 and the final flush each wait for rank 1 and give up
         torch.cuda.synchronize()
-        errs = WORKSPACES.errors()
-        assert _lib.NSM_ERR_TIMEOUT in errs.values(), errs
-        assert WORKSPACES.errors() and all(v == 0 for v in WORKSPACES.errors().values())  # read clears it
+        errs = errors()
+        assert _lib.NSM_ERR_TIMEOUT in errs, errs
+        assert all(v == 0 for v in errors())  # the read cleared it
     finally:
         dec._ex = None
         torch.cuda.synchronize()
@@ -74,7 +82,7 @@ def test_exchange_wait_runs_out_and_the_context_survives(dev):
     # the same context, the same workspace: a normal token matches the oracle
     route_ref, mlp_ref = _host_refs(shape, host)
     _per_layer_check(dec, x0, route_ref, mlp_ref, [host[i % 2][2] for i in range(3)])
-    assert all(v == 0 for v in WORKSPACES.errors().values())
+    assert all(v == 0 for v in errors())
 
 
 def test_wait_limit_settings_are_validated(dev):
