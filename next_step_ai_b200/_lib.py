@@ -183,7 +183,17 @@ def last_error() -> str:
     return msg.decode() if msg else ""
 
 
+class NsmError(RuntimeError):
+    """A non-zero status of a ``libnsm.so`` call: ``status`` (``NSM_ERR_*``)
+    and ``detail`` (``nsm_last_error()`` of the failing call)."""
+
+    def __init__(self, what: str, status: int, name: str, detail: str):
+        super().__init__(f"{what} failed: {name} ({status}): {detail}")
+        self.status = int(status)
+        self.detail = detail
+
+
 def check(status: int, what: str) -> None:
     if status != NSM_OK:
         lib = load()
-        raise RuntimeError(f"{what} failed: {lib.nsm_status_string(status).decode()} ({status}): {last_error()}")
+        raise NsmError(what, status, lib.nsm_status_string(status).decode(), last_error())

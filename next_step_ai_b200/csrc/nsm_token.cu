@@ -61,8 +61,9 @@
 
 namespace nsm {
 
-constexpr int kTkWarps = 16;
+constexpr int kTkWarps = 8;
 constexpr int kTkThreads = kTkWarps * 32;
+static_assert(kTkThreads >= 256 && kTkThreads % 128 == 0, "the phases assume 2 to 8 groups of 128 threads");
 constexpr int kTkCols = 128;          // phase-A columns per CTA
 constexpr int kTkRank = 64;           // router rank of this path
 constexpr int kTkMaxK = 256;          // selected blocks per layer
@@ -236,6 +237,7 @@ __device__ __forceinline__ void tk_fail(const TkParams& p, int code) {
   atomicCAS(&p.ws.sync->err, 0, code);
   tk_misc().abort = 1;
 }
+constexpr unsigned kTkPollSleepNs = 256;
 // CTA-wide wait until *ctr has reached `target` (wrap-safe).  Thread 0 polls
 // with acquire loads, at most p.wait_spins times; a wait that runs out, or an
 // error another CTA recorded, makes the CTA leave the token.  Returns false
@@ -243,16 +245,21 @@ __device__ __forceinline__ void tk_fail(const TkParams& p, int code) {
 __device__ bool tk_wait(const TkParams& p, const unsigned* ctr, unsigned target) {
   TkMisc& M = tk_misc();
   if (threadIdx.x == 0 && !M.abort) {
+    // polls back off (up to kTkPollSleepNs between reads) so that CTAs waiting on
+    // a counter do not hammer its L2 line while the others still stream
+    unsigned ns = 32;
     for (int it = 0;; ++it) {
       if ((int)(ld_acquire_u32(ctr) - target) >= 0) break;
       if (it >= p.wait_spins) {
         tk_fail(p, NSM_ERR_TIMEOUT);
         break;
       }
-      if ((it & 63) == 63 && ld_volatile_i32(&p.ws.sync->err) != 0) {
+      if ((it & 15) == 15 && ld_volatile_i32(&p.ws.sync->err) != 0) {
         M.abort = 1;
         break;
       }
+      __nanosleep(ns);
+      ns = min(ns * 2u, kTkPollSleepNs);
     }
   }
   __syncthreads();
@@ -278,8 +285,8 @@ __device__ __noinline__ void tk_build_lut(const TkParams& p, const TkLayer& L) {
   const int tid = threadIdx.x;
   if (tid < 48) M.code_cur[tid >> 4][tid & 15] = (tid < 16 ? L.gate_code : tid < 32 ? L.up_code : L.down_code)[tid & 15];
   __syncthreads();
-  {
-    const int t = tid >> 8, i = tid & 255;  // 512 threads: two tables x 256 candidates
+  for (int ti = tid; ti < 512; ti += blockDim.x) {  // two tables x 256 candidates
+    const int t = ti >> 8, i = ti & 255;
     const float a = 1.f + (float)i * (1.f / 256.f);
     float e = 0.f;
 #pragma unroll
@@ -435,13 +442,17 @@ __device__ __forceinline__ float tk_from16(uint16_t v, int wdtype) {
 // Result in M.xs (threads < 128 hold their column).  Returns false on abort.
 __device__ __noinline__ bool tk_pending_output(const TkParams& p, int c0, int cnt, uint32_t epoch) {
   TkMisc& M = tk_misc();
-  const int tid = threadIdx.x, col = tid & (kTkCols - 1), q = tid >> 7;
-  float y = 0.f;
+  const int tid = threadIdx.x, col = tid & (kTkCols - 1);
+  int nseg = 0;
   if (cnt > 0) {
     const int RP = p.H >> 6, total = RP * cnt;
     const int nwd = stream_warps(RP, cnt, kMaxSlotGroups, (int)gridDim.x * kTkWarps);
     const int rg = (c0 + col) >> 6;
-    const int nseg = stream_owner(total, nwd, rg * cnt + cnt - 1) - stream_owner(total, nwd, rg * cnt) + 1;
+    nseg = stream_owner(total, nwd, rg * cnt + cnt - 1) - stream_owner(total, nwd, rg * cnt) + 1;
+  }
+  // quarter q sums segments q, q + 4, q + 8, ... of the column
+  for (int q = tid / kTkCols; q < 4; q += kTkThreads / kTkCols) {
+    float y = 0.f;
     float v[kMaxSlotGroups / 4];
 #pragma unroll
     for (int u = 0; u < kMaxSlotGroups / 4; ++u) {
@@ -450,9 +461,10 @@ __device__ __noinline__ bool tk_pending_output(const TkParams& p, int c0, int cn
     }
 #pragma unroll
     for (int u = 0; u < kMaxSlotGroups / 4; ++u) y += v[u];
+    M.ysum[q][col] = y;
   }
-  M.ysum[q][col] = y;
   __syncthreads();
+  float y = 0.f;
   bool timed_out = false;
   if (tid < kTkCols) {
     y = (M.ysum[0][tid] + M.ysum[1][tid]) + (M.ysum[2][tid] + M.ysum[3][tid]);
@@ -532,8 +544,9 @@ __device__ __noinline__ void tk_phase_a(const TkParams& p, const TkLayer& L, int
     if (lane == 0) p.ws.xscale[c >> 6] = sc;
   }
   // partial latent: thread (rank r, eighth e) over 16 columns, reduced over e
-  {
-    const int r = tid >> 3, e = tid & 7;
+  // (a warp holds 4 whole ranks, so every lane of a warp takes the same turns)
+  for (int r = tid >> 3; r < kTkRank; r += kTkThreads / 8) {
+    const int e = tid & 7;
     const uint4* row = reinterpret_cast<const uint4*>(sm + kTkEncOff + r * kTkCols * 2 + e * 32);
     const uint4 w0 = row[0], w1 = row[1];
     const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
@@ -560,8 +573,8 @@ __device__ __noinline__ void tk_phase_b(const TkParams& p, const TkLayer& L) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nA = p.H / kTkCols;
   float* grp = reinterpret_cast<float*>(sm + kTkKeyOff);  // [32][64] (the keys region is free here)
-  {
-    const int c4 = tid & 15, g = tid >> 4;  // 32 groups of partials
+  for (int g = tid >> 4; g < 32; g += kTkThreads / 16) {  // 32 groups of partials
+    const int c4 = tid & 15;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     const float4* base = reinterpret_cast<const float4*>(p.ws.latent_part) + c4;
     float4 v[4];
@@ -662,11 +675,13 @@ __device__ bool tk_select_hist(const uint32_t* keys, int NB, int k, uint32_t* th
   __syncthreads();
   for (int i = tid; i < NB; i += blockDim.x) atomicAdd(&hist[keys[i] >> 20], 1);
   __syncthreads();
-  // thread t owns bins 4095 - 8t ... 4088 - 8t (descending); 512 threads cover 4096 bins
-  int c[8], loc = 0;
+  // thread t owns bins 4095 - kPer t ... 4096 - kPer (t + 1) (descending)
+  constexpr int kPer = (4096 + kTkThreads - 1) / kTkThreads;
+  int c[kPer], loc = 0;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    c[e] = hist[4095 - 8 * tid - e];
+  for (int e = 0; e < kPer; ++e) {
+    const int b = 4095 - kPer * tid - e;
+    c[e] = b >= 0 ? hist[b] : 0;
     loc += c[e];
   }
   int tot;
@@ -674,9 +689,9 @@ __device__ bool tk_select_hist(const uint32_t* keys, int NB, int k, uint32_t* th
   if (excl < k && k <= excl + loc) {
     int run = excl;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+    for (int e = 0; e < kPer; ++e) {
       if (run < k && k <= run + c[e]) {
-        S.start = 4095 - 8 * tid - e;  // the threshold bin
+        S.start = 4095 - kPer * tid - e;  // the threshold bin
         S.need = k - run;              // keys to take from it
         S.bin_count = c[e];
       }
@@ -828,8 +843,10 @@ __device__ __forceinline__ void tk_tile(const TkTile& tl, const uint32_t b[8], f
 // The block's gate/up segments (fixed order), RMSNorm scale, SiLU(gate)*up as
 // fp16 hi + lo with one power-of-two scale per block; then the block's ticket
 // is reset and the activation counter advanced.  Whole warp, lane = neuron.
-__device__ __noinline__ void tk_act(const TkParams& p, int s, int nseg) {
+// total / nw: the gate/up stream's pairs and warps, tpr its tiles per block.
+__device__ __noinline__ void tk_act(const TkParams& p, int s, int total, int nw, int tpr) {
   const int lane = threadIdx.x & 31;
+  const int nseg = stream_owner(total, nw, s * tpr + tpr - 1) - stream_owner(total, nw, s * tpr) + 1;
   __threadfence();
   const float* base = p.ws.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
   float gs = 0.f, us = 0.f;
@@ -866,11 +883,11 @@ __device__ __noinline__ void tk_act(const TkParams& p, int s, int nseg) {
   }
 }
 
-// Writes the warp's segment of block s, counts it on the block's ticket and
-// returns true when it was the block's last segment (the caller then owes the
-// block's activation, tk_act).
-__device__ __forceinline__ bool tk_flush_gu(float* gu_part, unsigned* ticket, int s, int seg, int nseg, int lane,
-                                            float acc[2][4]) {
+// Writes the warp's segment of block s (ntiles of its tpr tiles), counts the
+// tiles on the block's ticket and returns true when they completed the block
+// (the caller then owes the block's activation, tk_act).
+__device__ __forceinline__ bool tk_flush_gu(float* gu_part, unsigned* ticket, int s, int seg, int ntiles, int tpr,
+                                            int lane, float acc[2][4]) {
   const int g = lane >> 2, t = lane & 3;
   if (t == 0) {
     float* part = gu_part + ((int64_t)s * kMaxUnitsPerSlot + seg) * 64;
@@ -886,12 +903,12 @@ __device__ __forceinline__ bool tk_flush_gu(float* gu_part, unsigned* ticket, in
     for (int i = 0; i < 4; ++i) acc[pr][i] = 0.f;
   __syncwarp();
   unsigned old = 0u;
-  if (lane == 0) old = atomicAdd(ticket + s, 1u);
+  if (lane == 0) old = atomicAdd(ticket + s, (unsigned)ntiles);
   old = __shfl_sync(0xffffffffu, old, 0);
-  return old + 1u == (unsigned)nseg;
+  return old + (unsigned)ntiles == (unsigned)tpr;
 }
 
-__device__ __noinline__ void tk_gateup(const TkParams& p, const TkLayer& L, int count) {
+__device__ __forceinline__ void tk_gateup(const TkParams& p, const TkLayer& L, int count) {
   char* sm = tk_smem();
   const TkMisc& M = tk_misc();
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;
@@ -901,24 +918,26 @@ __device__ __noinline__ void tk_gateup(const TkParams& p, const TkLayer& L, int 
   const int nw = stream_warps(count, tpr, kMaxUnitsPerSlot, (int)gridDim.x * kTkWarps);
   if (count <= 0 || warp_global >= nw) return;
   const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
-  // the layer's pointers and strides in registers (the loop's stores could alias the descriptor)
-  const uint8_t* const gate = L.gate;
-  const uint8_t* const up = L.up;
-  const float* const gate_am = L.gate_am;
-  const float* const up_am = L.up_am;
-  const int64_t gstride = L.gstride, gastride = L.gastride;
-  float* const gu_part = p.ws.gu_part;
-  unsigned* const ticket = p.ws.ticket;
   const int* srows = reinterpret_cast<const int*>(sm + kTkRowsOff);
   const uint32_t lb = (uint32_t)lane * 4u;
   const uint32_t xb = smem_u32(sm + kTkXOff) + ((g & 1) ? (uint32_t)p.H * 2u : 0u) + (uint32_t)t * 32u;
   const float* xss = reinterpret_cast<const float*>(sm + kTkXOff + p.H * 4);
   const float ig = M.inv_alpha[0], iu = M.inv_alpha[1];
-  int ls = q0 / tpr, lj = q0 - ls * tpr;  // load cursor
-  const uint8_t* gb = gate + (int64_t)srows[ls] * gstride + (int64_t)lj * 1024 + lane * 16;
-  const uint8_t* ub = up + (int64_t)srows[ls] * gstride + (int64_t)lj * 1024 + lane * 16;
-  const float* ga = gate_am + (int64_t)srows[ls] * gastride + lj * 32 + g * 4;
-  const float* ua = up_am + (int64_t)srows[ls] * gastride + lj * 32 + g * 4;
+  // load cursor: the next tile's gate / up bytes and absmax; block bases are
+  // read from the descriptor only when the cursor moves to the next block
+  int ls = q0 / tpr, lj = q0 - ls * tpr;
+  const uint8_t* gb;
+  const uint8_t* ub;
+  const float* ga;
+  const float* ua;
+  auto seek = [&]() {
+    const int64_t row = srows[ls];
+    gb = L.gate + row * L.gstride + (int64_t)lj * 1024 + lane * 16;
+    ub = L.up + row * L.gstride + (int64_t)lj * 1024 + lane * 16;
+    ga = L.gate_am + row * L.gastride + lj * 32 + g * 4;
+    ua = L.up_am + row * L.gastride + lj * 32 + g * 4;
+  };
+  seek();
   auto load = [&](TkTile& tl) {
     tl.w[0][0] = ldg_stream_u4(gb);
     tl.w[0][1] = ldg_stream_u4(gb + 512);
@@ -932,13 +951,7 @@ __device__ __noinline__ void tk_gateup(const TkParams& p, const TkLayer& L, int 
     ua += 32;
     if (++lj == tpr) {
       lj = 0;
-      if (++ls < count) {
-        const int64_t row = srows[ls];
-        gb = gate + row * gstride + lane * 16;
-        ub = up + row * gstride + lane * 16;
-        ga = gate_am + row * gastride + g * 4;
-        ua = up_am + row * gastride + g * 4;
-      }
+      if (++ls < count) seek();
     }
   };
   TkTile buf[kTkDepthGU];
@@ -946,9 +959,8 @@ __device__ __noinline__ void tk_gateup(const TkParams& p, const TkLayer& L, int 
   for (int i = 0; i < kTkDepthGU; ++i)
     if (q0 + i < q1) load(buf[i]);
   const int s_first = q0 / tpr;
-  int s = s_first, j = q0 - s * tpr;
+  int s = s_first, j = q0 - s * tpr, j_seg = j;  // j_seg: the tile this segment started at
   int seg = warp_global - stream_owner(total, nw, s * tpr);
-  int nseg = stream_owner(total, nw, s * tpr + tpr - 1) - stream_owner(total, nw, s * tpr) + 1;
   unsigned long long owed = 0ull;  // bit s - s_first: this warp finalizes block s
   float acc[2][4] = {};
   for (int q = q0; q < q1; q += kTkDepthGU) {
@@ -964,24 +976,24 @@ __device__ __noinline__ void tk_gateup(const TkParams& p, const TkLayer& L, int 
         if (++j == tpr || q + i + 1 == q1) {
           // a warp's range spans at most 3 blocks when blocks are longer than 62
           // tiles, and its length is at most 2 tiles otherwise: s - s_first < 64
-          if (tk_flush_gu(gu_part, ticket, s, seg, nseg, lane, acc)) owed |= 1ull << ((s - s_first) & 63);
+          if (tk_flush_gu(p.ws.gu_part, p.ws.ticket, s, seg, j - j_seg, tpr, lane, acc))
+            owed |= 1ull << ((s - s_first) & 63);
           seg = 0;
+          j_seg = j;
           if (j == tpr) {
             j = 0;
+            j_seg = 0;
             ++s;
-            nseg = stream_owner(total, nw, s * tpr + tpr - 1) - stream_owner(total, nw, s * tpr) + 1;
           }
         }
       }
     }
   }
-  // the activations of the blocks whose last segment this warp flushed
+  // the activations of the blocks whose last tiles this warp flushed
   while (owed) {
     const int b = __ffsll((long long)owed) - 1;
     owed &= owed - 1ull;
-    const int sb = s_first + b;
-    const int ns = stream_owner(total, nw, sb * tpr + tpr - 1) - stream_owner(total, nw, sb * tpr) + 1;
-    tk_act(p, sb, ns);
+    tk_act(p, s_first + b, total, nw, tpr);
   }
 }
 
@@ -1005,7 +1017,7 @@ __device__ __forceinline__ void tk_down_mma(uint32_t lb, uint32_t w0, uint32_t w
 // router slices of the next layer are prefetched once the activations are
 // staged.  Returns false on abort.
 template <int kTable>
-__device__ __noinline__ bool tk_down(const TkParams& p, const TkLayer& L, int count, const TkLayer* next) {
+__device__ __forceinline__ bool tk_down(const TkParams& p, const TkLayer& L, int count, const TkLayer* next) {
   char* sm = tk_smem();
   TkMisc& M = tk_misc();
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;

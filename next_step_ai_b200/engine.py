@@ -66,10 +66,16 @@ class SparseMlpDecoder:
 
     ``block_range``: the intermediate blocks this rank's pools hold
     (``(0, NB)`` on one GPU).
+
+    ``token_kernel=True`` runs the whole token as one persistent cooperative
+    launch (``nsm_decode_token``) instead of five graph-captured kernels per
+    layer; it measures slower than the per-layer kernels at the 405B shape
+    (108 against 65 us per layer on a B200), so the per-layer path is the
+    default.
     """
 
     def __init__(self, layers: list[DecodeLayer], num_layers: int, *, block_range: tuple[int, int] | None = None,
-                 group=None, eps: float = 1e-5, token_kernel: bool | None = None):
+                 group=None, eps: float = 1e-5, token_kernel: bool = False):
         if not layers:
             raise RuntimeError("no layers")
         self.layers = layers
@@ -96,7 +102,7 @@ class SparseMlpDecoder:
         ok = self.token_kernel_applies()
         if token_kernel and not ok:
             raise RuntimeError("the token kernel does not apply to these layers (see token_kernel_applies)")
-        self.use_token = ok if token_kernel is None else bool(token_kernel)
+        self.use_token = bool(token_kernel)
         self._tk_ws = None
         if self.use_token:
             self._setup_token()
