@@ -76,6 +76,10 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   w.err = tick ? tick + 2 : nullptr;
   w.down_meta = tick ? tick + 3 : nullptr;
   w.count = tick ? tick + 5 : nullptr;
+  // the gate/up kernel's per-block tickets return to zero within a call, so
+  // they live in the head too, where every shape finds them zero
+  static_assert(8 + kMaxTopK <= kCounterInts, "gate/up tickets in the counter head");
+  w.gu_ticket = tick ? reinterpret_cast<unsigned*>(tick + 8) : nullptr;
   // the down partials sit at a fixed offset too: a layer's pending output is
   // read by the next call, whose router may have a different k or rank
   w.ypart = reinterpret_cast<float*>(take((size_t)kMaxSlotGroups * hidden * sizeof(float)));
@@ -87,12 +91,14 @@ DecodeWs decode_ws_layout(void* base, int hidden, int intermediate, int top_k, i
   w.norm_scale = reinterpret_cast<float*>(take(sizeof(float)));
   w.scores = reinterpret_cast<float*>(take(R * nb * sizeof(float)));
   w.x16 = reinterpret_cast<__half*>(take((size_t)hidden * sizeof(__half)));
+  w.x16lo = reinterpret_cast<__half*>(take((size_t)hidden * sizeof(__half)));
   w.xscale = reinterpret_cast<float*>(take((size_t)(hidden / 64) * sizeof(float)));
   w.rows = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
   w.sel_idx = reinterpret_cast<int*>(take(R * top_k * sizeof(int)));
   w.row_block = reinterpret_cast<int*>(take((size_t)top_k * sizeof(int)));
   w.gu_part = reinterpret_cast<float*>(take((size_t)top_k * kMaxUnitsPerSlot * 64 * sizeof(float)));
   w.act16 = reinterpret_cast<__half*>(take((size_t)top_k * 32 * sizeof(__half)));
+  w.act16lo = reinterpret_cast<__half*>(take((size_t)top_k * 32 * sizeof(__half)));
   w.act_scale = reinterpret_cast<float*>(take((size_t)top_k * sizeof(float)));
   w.bytes = off;
   return w;

@@ -78,6 +78,7 @@ struct GateUpParams {
   const int* count_ptr;
   const int* row_block;  // block id of compacted slot s
   const __half* x16;
+  const __half* x16lo;  // remainder of x16 (the B operand's column 1)
   const float* xscale;
   const float* norm_scale;
   const void* act_mask;  // optional [U*32] (one row of flat_mask)
@@ -85,8 +86,14 @@ struct GateUpParams {
   float* gu_part;
   int* err;
   __half* act16;
+  __half* act16lo;
   float* act_scale;
   float* act_out;  // optional fp32 [k][32]
+  // fused_finalize != 0 (bulk-copy kernel only): the warp that completes a
+  // block's units (counted on gu_ticket[s], zero between calls) applies
+  // SiLU(gate)*up itself; no gateup_finalize_kernel follows
+  int fused_finalize;
+  unsigned* gu_ticket;
   int total_warps;
   int unit_tiles;  // tiles per stream unit (the partial segments follow the units)
   int max_rows;    // capacity of rows / partials (>= *count_ptr): prologues load this much without waiting for the count
@@ -156,43 +163,43 @@ __device__ __forceinline__ void gu_mma_rowgroup(uint32_t lb, const uint4 w, cons
             lut_get<kBase>(w.y, lb, 3, kTable), lut_get<kBase>(w.w, lb, 3, kTable), b[6], b[7]);
 }
 
-// Both projections of one tile: acc[proj][i] += (W_rows . x_tile) * absmax * xscale.
+// Both projections of one tile: acc[proj][i] += (W_rows . x_tile) * absmax * xscale / alpha.
+// The B operand carries x16 in column 0 (lanes g == 0) and x16lo in column 1
+// (lanes g == 1), so D columns 0 + 1 (d[0] + d[1], d[2] + d[3] of lanes
+// t == 0) hold the dot product with the hi + lo pair; xsg / xsu fold the
+// tables' 1 / alpha into the tile's x scale.
 template <int kBase>
-__device__ __forceinline__ void gu_tile_mma(const GuTile& tile, const uint32_t b[8], float xs, uint32_t lb,
-                                            float acc[2][4]) {
+__device__ __forceinline__ void gu_tile_mma(const GuTile& tile, const uint32_t b[8], float xsg, float xsu,
+                                            uint32_t lb, float acc[2][4]) {
   float d[4];
 #pragma unroll
   for (int rg = 0; rg < 2; ++rg) {
     gu_mma_rowgroup<kBase, 0>(lb, tile.w[0][rg], b, d);
     const float g0 = rg ? tile.am[0].z : tile.am[0].x, g1 = rg ? tile.am[0].w : tile.am[0].y;
-    acc[0][rg * 2] = fmaf(d[0], g0 * xs, acc[0][rg * 2]);
-    acc[0][rg * 2 + 1] = fmaf(d[2], g1 * xs, acc[0][rg * 2 + 1]);
+    acc[0][rg * 2] = fmaf(d[0] + d[1], g0 * xsg, acc[0][rg * 2]);
+    acc[0][rg * 2 + 1] = fmaf(d[2] + d[3], g1 * xsg, acc[0][rg * 2 + 1]);
     gu_mma_rowgroup<kBase, 1>(lb, tile.w[1][rg], b, d);
     const float u0 = rg ? tile.am[1].z : tile.am[1].x, u1 = rg ? tile.am[1].w : tile.am[1].y;
-    acc[1][rg * 2] = fmaf(d[0], u0 * xs, acc[1][rg * 2]);
-    acc[1][rg * 2 + 1] = fmaf(d[2], u1 * xs, acc[1][rg * 2 + 1]);
+    acc[1][rg * 2] = fmaf(d[0] + d[1], u0 * xsu, acc[1][rg * 2]);
+    acc[1][rg * 2 + 1] = fmaf(d[2] + d[3], u1 * xsu, acc[1][rg * 2 + 1]);
   }
 }
 
+// xv: this lane's x vector -- x16 (or its shared-memory copy) for lanes
+// g != 1, x16lo for lanes g == 1 (column 1 of the B operand).
 template <int kBase, bool kStageX>
 __device__ __forceinline__ void gu_compute(const GateUpParams& p, const GuTile& tile, int j, int t, uint32_t lb,
-                                           const __half* xs16, const float* xss, float acc[2][4]) {
+                                           const __half* xv, const float* xss, float ia0, float ia1,
+                                           float acc[2][4]) {
   uint32_t b[8];
   float xs;
-  if (kStageX) {
-    const uint4 xa = *reinterpret_cast<const uint4*>(xs16 + j * 64 + t * 16);
-    const uint4 xb = *reinterpret_cast<const uint4*>(xs16 + j * 64 + t * 16 + 8);
-    b[0] = xa.x; b[1] = xa.y; b[2] = xa.z; b[3] = xa.w;
-    b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
-    xs = xss[j];
-  } else {
-    const uint4 xa = ldg_u4(p.x16 + j * 64 + t * 16);
-    const uint4 xb = ldg_u4(p.x16 + j * 64 + t * 16 + 8);
-    b[0] = xa.x; b[1] = xa.y; b[2] = xa.z; b[3] = xa.w;
-    b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
-    xs = ldg_f32(p.xscale + j);
-  }
-  gu_tile_mma<kBase>(tile, b, xs, lb, acc);
+  const uint4 xa = kStageX ? *reinterpret_cast<const uint4*>(xv + j * 64 + t * 16) : ldg_u4(xv + j * 64 + t * 16);
+  const uint4 xb =
+      kStageX ? *reinterpret_cast<const uint4*>(xv + j * 64 + t * 16 + 8) : ldg_u4(xv + j * 64 + t * 16 + 8);
+  b[0] = xa.x; b[1] = xa.y; b[2] = xa.z; b[3] = xa.w;
+  b[4] = xb.x; b[5] = xb.y; b[6] = xb.z; b[7] = xb.w;
+  xs = kStageX ? xss[j] : ldg_f32(p.xscale + j);
+  gu_tile_mma<kBase>(tile, b, xs * ia0, xs * ia1, lb, acc);
 }
 
 constexpr int kStageRowsMax = 1024;  // pool rows staged in shared memory up to this count
@@ -237,6 +244,9 @@ __device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, 
   const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
   int s = q0 / tpr, j = q0 - s * tpr;
   int seg = warp_global - stream_owner(total, nw, s * tpr);
+  // lanes g == 1 read x16lo (from global memory: only x16 is staged)
+  const __half* xv = g == 1 ? p.x16lo : (kStageX ? xs16 : p.x16);
+  const float ia0 = lut_inv_alpha(0), ia1 = lut_inv_alpha(1);
   GuPtrs cp = gu_ptrs(p, rows[s]);
   GuTile ta, tb;
   gu_load<kTiled>(p, cp.g, cp.u, cp.ga, cp.ua, j, lane, ta);
@@ -253,7 +263,7 @@ __device__ __forceinline__ void gateup_body(const GateUpParams& p, uint32_t lb, 
       if (sn != s) np = gu_ptrs(p, rows[sn]);
       gu_load<kTiled>(p, np.g, np.u, np.ga, np.ua, jn, lane, nx);
     }
-    gu_compute<kBase, kStageX>(p, cur, j, t, lb, xs16, xss, acc);
+    gu_compute<kBase, kStageX>(p, cur, j, t, lb, xv, xss, ia0, ia1, acc);
     if (!more || sn != s) {
       gu_flush(p, s, seg, g, t, acc);
       seg = 0;  // this warp holds the first pair of the next block
@@ -291,7 +301,10 @@ __device__ __forceinline__ void gu_finalize_apply(const GateUpParams& p, int s, 
   if (p.act_out) p.act_out[(int64_t)s * 32 + lane] = act;
   const float m = warp_max(fabsf(act));
   const float sc = pow2_scale_for(m);
-  p.act16[(int64_t)s * 32 + lane] = __float2half_rn(act * (1.f / sc));
+  const float v = act * (1.f / sc);
+  const __half h = __float2half_rn(v);
+  p.act16[(int64_t)s * 32 + lane] = h;
+  p.act16lo[(int64_t)s * 32 + lane] = __float2half_rn(v - __half2float(h));
   if (lane == 0) p.act_scale[s] = sc;
 }
 
@@ -350,7 +363,7 @@ constexpr int kStageXMaxHidden = 16384;
 template <bool kTiled, bool kStageX>
 __global__ void __launch_bounds__(kMlpThreads, 2) gateup_kernel(GateUpParams p) {
   pdl_trigger();
-  build_lut_dyn(p.gate_code, p.up_code);
+  build_lut_alpha(p.gate_code, p.up_code);
   pdl_wait();  // rows, count, x16 come from the router kernels
   __half* xs16 = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
   float* xss = reinterpret_cast<float*>(xs16 + (kStageX ? p.H : 0));
@@ -390,6 +403,7 @@ struct DownParams {
   const int* rows;
   const int* count_ptr;
   const __half* act16;
+  const __half* act16lo;  // remainder of act16 (the B operand's column 1)
   const float* act_scale;
   float* ypart;
   int* err;
@@ -451,11 +465,15 @@ __device__ __forceinline__ int down_stream_warps(int count, int RT, int total_wa
   return stream_warps(RT, count, kMaxSlotGroups, total_warps);
 }
 
+// The B operand carries act16 in column 0 (lanes g == 0) and act16lo in
+// column 1 (lanes g == 1); D columns 0 + 1 hold the dot product with the pair.
 template <bool kTiled, bool kStage, int kBase>
-__device__ __forceinline__ void down_body(const DownParams& p, uint32_t lb, const __half* sact, const float* sscale,
-                                          const int* rows, int count) {
+__device__ __forceinline__ void down_body(const DownParams& p, uint32_t lb, const __half* sact,
+                                          const __half* sactlo, const float* sscale, const int* rows, int count) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  const __half* av = g == 1 ? (kStage ? sactlo : p.act16lo) : (kStage ? sact : p.act16);
+  const float ia = lut_inv_alpha(0);
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int RT = p.H >> 5;
   const int total = RT * count;
@@ -484,19 +502,19 @@ __device__ __forceinline__ void down_body(const DownParams& p, uint32_t lb, cons
         uint4 bf;
         float as;
         if (kStage) {
-          bf = *reinterpret_cast<const uint4*>(sact + s * 32 + t * 8);
-          as = sscale[s];
+          bf = *reinterpret_cast<const uint4*>(av + s * 32 + t * 8);
+          as = sscale[s] * ia;
         } else {
-          bf = ldg_u4(p.act16 + (int64_t)s * 32 + t * 8);
-          as = ldg_f32(p.act_scale + s);
+          bf = ldg_u4(av + (int64_t)s * 32 + t * 8);
+          as = ldg_f32(p.act_scale + s) * ia;
         }
         float d[4];
         down_mma<kBase>(lb, b.w[i].x, b.w[i].y, bf, d);
-        acc[0] = fmaf(d[0], b.am[i].x * as, acc[0]);
-        acc[1] = fmaf(d[2], b.am[i].y * as, acc[1]);
+        acc[0] = fmaf(d[0] + d[1], b.am[i].x * as, acc[0]);
+        acc[1] = fmaf(d[2] + d[3], b.am[i].y * as, acc[1]);
         down_mma<kBase>(lb, b.w[i].z, b.w[i].w, bf, d);
-        acc[2] = fmaf(d[0], b.am[i].z * as, acc[2]);
-        acc[3] = fmaf(d[2], b.am[i].w * as, acc[3]);
+        acc[2] = fmaf(d[0] + d[1], b.am[i].z * as, acc[2]);
+        acc[3] = fmaf(d[2] + d[3], b.am[i].w * as, acc[3]);
         if (++s == count || q + 1 == q1) {
           if (t == 0) {
             float* yp = p.ypart + (int64_t)seg * p.H + rt * 32;
@@ -549,17 +567,23 @@ __global__ void __launch_bounds__(256) down_finalize_kernel(DownParams p) {
 template <bool kTiled, bool kStage>
 __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
   pdl_trigger();
-  build_lut_dyn(p.down_code, p.down_code);
+  build_lut_alpha(p.down_code, p.down_code);
   pdl_wait();  // act16 / act_scale come from the gate/up kernel
   record_down_meta(p);
   const int count = *p.count_ptr;
   __half* sact = reinterpret_cast<__half*>(reinterpret_cast<char*>(g_lut_smem) + kSmemHead);
   float* sscale = reinterpret_cast<float*>(sact + kStageActMaxSlots * 32);
   int* srows = reinterpret_cast<int*>(sscale + kStageActMaxSlots);
+  __half* sactlo = reinterpret_cast<__half*>(srows + kStageActMaxSlots);
   if (kStage) {
     const uint4* src = reinterpret_cast<const uint4*>(p.act16);
+    const uint4* srclo = reinterpret_cast<const uint4*>(p.act16lo);
     uint4* dst = reinterpret_cast<uint4*>(sact);
-    for (int i = threadIdx.x; i < count * 4; i += blockDim.x) dst[i] = __ldcg(src + i);
+    uint4* dstlo = reinterpret_cast<uint4*>(sactlo);
+    for (int i = threadIdx.x; i < count * 4; i += blockDim.x) {
+      dst[i] = __ldcg(src + i);
+      dstlo[i] = __ldcg(srclo + i);
+    }
     for (int i = threadIdx.x; i < count; i += blockDim.x) {
       sscale[i] = __ldcg(p.act_scale + i);
       srows[i] = __ldcg(p.rows + i);
@@ -570,9 +594,9 @@ __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
   const uint32_t lb = (threadIdx.x & 31) * 4u;
   const uint32_t base = lut_base_addr();
   if (base == 0x400u)
-    down_body<kTiled, kStage, 0x400>(p, lb, sact, sscale, rows, count);
+    down_body<kTiled, kStage, 0x400>(p, lb, sact, sactlo, sscale, rows, count);
   else
-    down_body<kTiled, kStage, -1>(p, lb, sact, sscale, rows, count);
+    down_body<kTiled, kStage, -1>(p, lb, sact, sactlo, sscale, rows, count);
 }
 
 // ============================================================================
@@ -601,7 +625,7 @@ __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
 constexpr int kTmaWarps = NSM_TMA_WARPS;
 constexpr int kTmaThreads = kTmaWarps * 32;
 #ifndef NSM_GU_WARPS
-#define NSM_GU_WARPS 12
+#define NSM_GU_WARPS 10
 #endif
 constexpr int kGuWarps = NSM_GU_WARPS;  // gate/up: fewer warps, two-tile stages
 constexpr int kGuThreads = kGuWarps * 32;
@@ -616,17 +640,19 @@ constexpr int kDnPairsPerStage = NSM_DN_PAIRS_PER_STAGE;
 constexpr int kDnStageBytes = kDnPairsPerStage * (1024 + 256);
 // shared-memory layout (bytes from the dynamic base)
 constexpr int kGuX16Off = kSmemHead;
-constexpr int kGuXsOff = kGuX16Off + kStageXMaxHidden * 2;
+constexpr int kGuX16LoOff = kGuX16Off + kStageXMaxHidden * 2;
+constexpr int kGuXsOff = kGuX16LoOff + kStageXMaxHidden * 2;
 constexpr int kGuRowsOff = kGuXsOff + (kStageXMaxHidden / 64) * 4;
 constexpr int kGuRingOff = kGuRowsOff + kStageRowsMax * 4;
 constexpr int kGuBarOff = kGuRingOff + kGuWarps * kGuStages * kGuStageBytes;
-constexpr int kGuTmaSmem = kGuBarOff + kGuWarps * kGuStages * 8;
+constexpr int kGuTmaSmem = kGuBarOff + (kGuWarps * kGuStages + 1) * 8;  // + the x staging barrier
 constexpr int kDnActOff = kSmemHead;
-constexpr int kDnScaleOff = kDnActOff + kStageActMaxSlots * 64;
+constexpr int kDnActLoOff = kDnActOff + kStageActMaxSlots * 64;
+constexpr int kDnScaleOff = kDnActLoOff + kStageActMaxSlots * 64;
 constexpr int kDnRowsOff = kDnScaleOff + kStageActMaxSlots * 4;
 constexpr int kDnRingOff = kDnRowsOff + kStageActMaxSlots * 4;
 constexpr int kDnBarOff = kDnRingOff + kTmaWarps * kDnStages * kDnStageBytes;
-constexpr int kDnTmaSmem = kDnBarOff + kTmaWarps * kDnStages * 8;
+constexpr int kDnTmaSmem = kDnBarOff + (kTmaWarps * kDnStages + 1) * 8;  // + the act staging barrier
 static_assert(kGuTmaSmem <= 227 * 1024, "gate/up ring does not fit in shared memory");
 static_assert(kDnTmaSmem <= 227 * 1024, "down ring does not fit in shared memory");
 static_assert(kGuRingOff % 128 == 0 && kDnRingOff % 128 == 0, "rings must be 128-byte aligned");
@@ -643,15 +669,67 @@ __device__ __forceinline__ void drain_ring(uint32_t wbar, int consumed, int issu
   for (int b = consumed; b < issued; ++b) mbar_wait(wbar + 8u * (uint32_t)(b % kStages), (uint32_t)((b / kStages) & 1));
 }
 
+// Counts a flushed segment of `units` units of block s on its ticket; true
+// for the warp whose segment completed the block (it then owes the block's
+// SiLU(gate)*up, gu_finalize_block).  The partial stores of lanes t == 0 are
+// made visible before the count.
+__device__ __forceinline__ bool gu_ticket_add(const GateUpParams& p, int s, int units, int cps, int lane) {
+  __threadfence();
+  __syncwarp();
+  unsigned old = 0u;
+  if (lane == 0) old = atomicAdd(p.gu_ticket + s, (unsigned)units);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  return old + (unsigned)units == (unsigned)cps;
+}
+
+// gateup_finalize_kernel's work for block s by one warp (lane = neuron), in the
+// same summation order: segment q goes to group q mod 8, each group sums its
+// segments in order, the 8 group sums combine in order.  Then the ticket is
+// reset for the next call.
+__device__ __forceinline__ void gu_finalize_block(const GateUpParams& p, int s, int cps, int total, int nw,
+                                                  int lane) {
+  __threadfence();
+  const int ups = stream_owner(total, nw, s * cps + cps - 1) - stream_owner(total, nw, s * cps) + 1;
+  const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
+  float vg[8], vu[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    vg[q] = q < ups ? ldcg_f32(base + q * 64 + lane) : 0.f;
+    vu[q] = q < ups ? ldcg_f32(base + q * 64 + 32 + lane) : 0.f;
+  }
+  for (int q0 = 8; q0 < ups; q0 += 8) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (q0 + u < ups) {
+        vg[u] += ldcg_f32(base + (q0 + u) * 64 + lane);
+        vu[u] += ldcg_f32(base + (q0 + u) * 64 + 32 + lane);
+      }
+  }
+  const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
+  float gsum = 0.f, usum = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    gsum += vg[q];
+    usum += vu[q];
+  }
+  gu_finalize_apply(p, s, lane, gsum, usum, ns);
+  __syncwarp();
+  if (lane == 0) p.gu_ticket[s] = 0u;
+}
+
 // A ring stage holds one *unit* of kGuUnitTiles adjacent tiles of one block
 // (gate kGuUnitTiles KB, up kGuUnitTiles KB, their absmax runs): four bulk
 // copies and one round of cursor bookkeeping per unit instead of per tile.
 template <int kBase>
-__device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t lb, uint32_t xs16_s, uint32_t xss_s,
-                                                const int* rows, int count, uint32_t ring, uint32_t bar0) {
+__device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t lb, uint32_t xhi_s, uint32_t xlo_s,
+                                                uint32_t xss_s, const int* rows, int count, uint32_t ring,
+                                                uint32_t bar0) {
   constexpr int UT = kGuUnitTiles;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  // B operand column 0 (lanes g == 0) is x16, column 1 (lanes g == 1) x16lo
+  const uint32_t xs16_s = g == 1 ? xlo_s : xhi_s;
+  const float ia0 = lut_inv_alpha(0), ia1 = lut_inv_alpha(1);
   const int warp = threadIdx.x >> 5;
   const int warp_global = blockIdx.x * kGuWarps + warp;
   const int cps = (p.H >> 6) / UT;  // units per block
@@ -704,6 +782,9 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
 
   int s = q0 / cps, j = q0 - s * cps;  // unit j of block s
   int seg = warp_global - stream_owner(total, nw, s * cps);
+  const int s_first = s;
+  int j_seg = j;                    // the unit the current segment started at
+  unsigned long long owed = 0ull;   // bit s - s_first: this warp finalizes block s
   uint32_t xa = xs16_s + (uint32_t)(j * UT * 128 + t * 32);  // this lane's x fragment of the unit's first tile
   uint32_t xsa = xss_s + (uint32_t)(j * UT * 4);
   float acc[2][4] = {};
@@ -732,7 +813,7 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
             const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
             float xs;
             asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xs) : "r"(xsa + tt * 4));
-            gu_tile_mma<kBase>(tile, bx, xs, lb, acc);
+            gu_tile_mma<kBase>(tile, bx, xs * ia0, xs * ia1, lb, acc);
           }
           __syncwarp();
           if (q + kGuStages < q1) issue_next(st);
@@ -741,9 +822,16 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
           xsa += UT * 4;
           if (++j == cps || q == q1) {
             gu_flush(p, s, seg, g, t, acc);
+            if (p.fused_finalize && gu_ticket_add(p, s, j - j_seg, cps, lane)) {
+              // a warp's range covers a few blocks; past 64 it finalizes at once
+              if (s - s_first < 64) owed |= 1ull << (s - s_first);
+              else gu_finalize_block(p, s, cps, total, nw, lane);
+            }
             seg = 0;  // this warp holds the first unit of the next block
+            j_seg = j;
             if (j == cps) {
               j = 0;
+              j_seg = 0;
               ++s;
               xa = xs16_s + (uint32_t)(t * 32);
               xsa = xss_s;
@@ -757,6 +845,13 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
   if (!ok) {
     record_error(p.err, NSM_ERR_TIMEOUT);
     drain_ring<kGuStages>(wbar, q - q0, issued);
+    return;
+  }
+  // SiLU(gate)*up of the blocks whose last units this warp counted
+  while (owed) {
+    const int b = __ffsll((long long)owed) - 1;
+    owed &= owed - 1ull;
+    gu_finalize_block(p, s_first + b, cps, total, nw, lane);
   }
 }
 
@@ -835,20 +930,26 @@ static_assert(kGuWarps * kGuStages * kGuStageBytes >= kMaxNumBlocks * 4 + (int)s
 __global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams p) {
   char* smem = reinterpret_cast<char*>(g_lut_smem);
   const uint32_t bar0 = smem_u32(smem + kGuBarOff);
-  if (threadIdx.x < kGuWarps * kGuStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
+  const uint32_t xbar = bar0 + 8u * (uint32_t)(kGuWarps * kGuStages);
+  if (threadIdx.x <= kGuWarps * kGuStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
   mbar_init_fence();
   pdl_trigger();
-  build_lut_dyn(p.gate_code, p.up_code);
+  build_lut_alpha(p.gate_code, p.up_code);
   pdl_wait();  // rows, count, x16 come from the router kernels
   __half* xs16 = reinterpret_cast<__half*>(smem + kGuX16Off);
+  __half* xs16lo = reinterpret_cast<__half*>(smem + kGuX16LoOff);
   float* xss = reinterpret_cast<float*>(smem + kGuXsOff);
   int* srows = reinterpret_cast<int*>(smem + kGuRowsOff);
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(p.x16);
-    uint4* dst = reinterpret_cast<uint4*>(xs16);
-    for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x) dst[i] = __ldcg(src + i);
-    for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
+  if (threadIdx.x == 0) {
+    // x16 and x16lo (written by the router kernel) arrive by bulk copy while
+    // the block selection runs
+    const uint64_t pol = l2_evict_last_policy();
+    fence_proxy_async_global();
+    mbar_arrive_expect_tx(xbar, (uint32_t)p.H * 4u);
+    bulk_g2s(smem_u32(xs16), p.x16, (uint32_t)p.H * 2u, xbar, pol);
+    bulk_g2s(smem_u32(xs16lo), p.x16lo, (uint32_t)p.H * 2u, xbar, pol);
   }
+  for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
   const bool stage_rows = p.max_rows <= kStageRowsMax;
   int count;
   if (p.select) {
@@ -864,24 +965,34 @@ __global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams 
     if (stage_rows)
       for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
   }
-  __syncthreads();
+  bool x_late = false;
+  if (threadIdx.x == 0 && !mbar_wait(xbar, 0, p.wait_spins)) {
+    record_error(p.err, NSM_ERR_TIMEOUT);
+    mbar_wait(xbar, 0);  // the copies land before the CTA leaves
+    x_late = true;
+  }
+  if (__syncthreads_or(x_late)) return;
   const int* rows = stage_rows ? srows : p.rows;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
   const uint32_t ring = smem_u32(smem + kGuRingOff);
   if (lut_base_addr() == 0x400u)
-    gateup_tma_body<0x400>(p, lb, smem_u32(xs16), smem_u32(xss), rows, count, ring, bar0);
+    gateup_tma_body<0x400>(p, lb, smem_u32(xs16), smem_u32(xs16lo), smem_u32(xss), rows, count, ring, bar0);
   else
-    gateup_tma_body<-1>(p, lb, smem_u32(xs16), smem_u32(xss), rows, count, ring, bar0);
+    gateup_tma_body<-1>(p, lb, smem_u32(xs16), smem_u32(xs16lo), smem_u32(xss), rows, count, ring, bar0);
 }
 
 // Down, bulk-copy variant: a pair is (64-row group rp, slot s) = two adjacent
 // 32-row tiles of one block (1 KB packed + 256 B absmax, contiguous in the
 // tiled layout); pairs are rp-major.  A stage holds kDnPairsPerStage pairs.
 template <int kBase>
-__device__ __forceinline__ void down_tma_body(const DownParams& p, uint32_t lb, uint32_t sact_s, uint32_t sscale_s,
-                                              const int* rows, int count, uint32_t ring, uint32_t bar0) {
+__device__ __forceinline__ void down_tma_body(const DownParams& p, uint32_t lb, uint32_t shi_s, uint32_t slo_s,
+                                              uint32_t sscale_s, const int* rows, int count, uint32_t ring,
+                                              uint32_t bar0) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  // B operand column 0 (lanes g == 0) is act16, column 1 (lanes g == 1) act16lo
+  const uint32_t sact_s = g == 1 ? slo_s : shi_s;
+  const float ia = lut_inv_alpha(0);
   const int warp = threadIdx.x >> 5;
   const int warp_global = blockIdx.x * kTmaWarps + warp;
   const int RP = p.H >> 6;
@@ -944,19 +1055,20 @@ __device__ __forceinline__ void down_tma_body(const DownParams& p, uint32_t lb, 
               const uint4 bf = lds_u4(sact_s + (uint32_t)(s * 64 + t * 16));
               float as;
               asm volatile("ld.shared.f32 %0, [%1];" : "=f"(as) : "r"(sscale_s + (uint32_t)(s * 4)));
+              as *= ia;
               float d[4];
               down_mma<kBase>(lb, w0.x, w0.y, bf, d);
-              acc[0][0] = fmaf(d[0], a0.x * as, acc[0][0]);
-              acc[0][1] = fmaf(d[2], a0.y * as, acc[0][1]);
+              acc[0][0] = fmaf(d[0] + d[1], a0.x * as, acc[0][0]);
+              acc[0][1] = fmaf(d[2] + d[3], a0.y * as, acc[0][1]);
               down_mma<kBase>(lb, w0.z, w0.w, bf, d);
-              acc[0][2] = fmaf(d[0], a0.z * as, acc[0][2]);
-              acc[0][3] = fmaf(d[2], a0.w * as, acc[0][3]);
+              acc[0][2] = fmaf(d[0] + d[1], a0.z * as, acc[0][2]);
+              acc[0][3] = fmaf(d[2] + d[3], a0.w * as, acc[0][3]);
               down_mma<kBase>(lb, w1.x, w1.y, bf, d);
-              acc[1][0] = fmaf(d[0], a1.x * as, acc[1][0]);
-              acc[1][1] = fmaf(d[2], a1.y * as, acc[1][1]);
+              acc[1][0] = fmaf(d[0] + d[1], a1.x * as, acc[1][0]);
+              acc[1][1] = fmaf(d[2] + d[3], a1.y * as, acc[1][1]);
               down_mma<kBase>(lb, w1.z, w1.w, bf, d);
-              acc[1][2] = fmaf(d[0], a1.z * as, acc[1][2]);
-              acc[1][3] = fmaf(d[2], a1.w * as, acc[1][3]);
+              acc[1][2] = fmaf(d[0] + d[1], a1.z * as, acc[1][2]);
+              acc[1][3] = fmaf(d[2] + d[3], a1.w * as, acc[1][3]);
               ++q;
               if (++s == count || q == q1) {
                 if (t == 0) {
@@ -991,33 +1103,44 @@ __device__ __forceinline__ void down_tma_body(const DownParams& p, uint32_t lb, 
 __global__ void __launch_bounds__(kTmaThreads, 1) down_tma_kernel(DownParams p) {
   char* smem = reinterpret_cast<char*>(g_lut_smem);
   const uint32_t bar0 = smem_u32(smem + kDnBarOff);
-  if (threadIdx.x < kTmaWarps * kDnStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
+  const uint32_t abar = bar0 + 8u * (uint32_t)(kTmaWarps * kDnStages);
+  if (threadIdx.x <= kTmaWarps * kDnStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
   mbar_init_fence();
   pdl_trigger();
-  build_lut_dyn(p.down_code, p.down_code);
+  build_lut_alpha(p.down_code, p.down_code);
   pdl_wait();  // act16 / act_scale come from the gate/up kernels
   record_down_meta(p);
   const int count = *p.count_ptr;
   __half* sact = reinterpret_cast<__half*>(smem + kDnActOff);
+  __half* sactlo = reinterpret_cast<__half*>(smem + kDnActLoOff);
   float* sscale = reinterpret_cast<float*>(smem + kDnScaleOff);
   int* srows = reinterpret_cast<int*>(smem + kDnRowsOff);
-  {
-    // staged up to the capacity, with the count (entries past it are never read)
-    const uint4* src = reinterpret_cast<const uint4*>(p.act16);
-    uint4* dst = reinterpret_cast<uint4*>(sact);
-    for (int i = threadIdx.x; i < p.max_rows * 4; i += blockDim.x) dst[i] = __ldcg(src + i);
-    for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) {
-      sscale[i] = __ldcg(p.act_scale + i);
-      srows[i] = __ldcg(p.rows + i);
-    }
+  // staged up to the capacity, with the count (entries past it are never
+  // read): act16 / act16lo by bulk copy, scales and rows by plain loads
+  if (threadIdx.x == 0) {
+    const uint64_t pol = l2_evict_last_policy();
+    fence_proxy_async_global();
+    mbar_arrive_expect_tx(abar, (uint32_t)p.max_rows * 128u);
+    bulk_g2s(smem_u32(sact), p.act16, (uint32_t)p.max_rows * 64u, abar, pol);
+    bulk_g2s(smem_u32(sactlo), p.act16lo, (uint32_t)p.max_rows * 64u, abar, pol);
   }
-  __syncthreads();
+  for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) {
+    sscale[i] = __ldcg(p.act_scale + i);
+    srows[i] = __ldcg(p.rows + i);
+  }
+  bool a_late = false;
+  if (threadIdx.x == 0 && !mbar_wait(abar, 0, p.wait_spins)) {
+    record_error(p.err, NSM_ERR_TIMEOUT);
+    mbar_wait(abar, 0);  // the copies land before the CTA leaves
+    a_late = true;
+  }
+  if (__syncthreads_or(a_late)) return;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
   const uint32_t ring = smem_u32(smem + kDnRingOff);
   if (lut_base_addr() == 0x400u)
-    down_tma_body<0x400>(p, lb, smem_u32(sact), smem_u32(sscale), srows, count, ring, bar0);
+    down_tma_body<0x400>(p, lb, smem_u32(sact), smem_u32(sactlo), smem_u32(sscale), srows, count, ring, bar0);
   else
-    down_tma_body<-1>(p, lb, smem_u32(sact), smem_u32(sscale), srows, count, ring, bar0);
+    down_tma_body<-1>(p, lb, smem_u32(sact), smem_u32(sactlo), smem_u32(sscale), srows, count, ring, bar0);
 }
 
 // ============================================================================
@@ -1027,7 +1150,7 @@ static int dtype_ok(int d) { return d == NSM_F32 || d == NSM_F16 || d == NSM_BF1
 
 constexpr int kGateupSmem = kSmemHead + kStageRowsMax * 4;
 constexpr int kGateupSmemStaged = kGateupSmem + kStageXMaxHidden * 2 + (kStageXMaxHidden / 64) * 4;
-constexpr int kDownSmemStaged = kSmemHead + kStageActMaxSlots * (64 + 4 + 4);
+constexpr int kDownSmemStaged = kSmemHead + kStageActMaxSlots * (64 + 4 + 4 + 64);
 
 struct KernelSetup {
   bool done = false;
@@ -1153,6 +1276,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.max_rows = m.k;
   gp.row_block = m.row_block;
   gp.x16 = ws.x16;
+  gp.x16lo = ws.x16lo;
   gp.xscale = ws.xscale;
   gp.norm_scale = m.norm_scale;
   gp.act_mask = m.act_mask;
@@ -1160,6 +1284,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   gp.gu_part = ws.gu_part;
   gp.err = ws.err;
   gp.act16 = ws.act16;
+  gp.act16lo = ws.act16lo;
   gp.act_scale = ws.act_scale;
   gp.act_out = m.act_out;
   gp.wait_spins = copy_wait_spins();
@@ -1186,6 +1311,8 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   if (gu_tma) {
     gp.unit_tiles = kGuUnitTiles;
     gp.total_warps = dev.sm_count * kGuWarps;
+    gp.fused_finalize = 1;
+    gp.gu_ticket = ws.gu_ticket;
     e = launch_pdl(gateup_tma_kernel, dev.sm_count, kGuThreads, kGuTmaSmem, stream, gp);
   } else {
   const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
@@ -1201,7 +1328,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   }
   NSM_CHECK_CUDA(e);
   NSM_CHECK_CUDA(stage_event(m.events, 2, stream));
-  NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
+  if (!gp.fused_finalize) NSM_CHECK_CUDA(launch_pdl(gateup_finalize_kernel, m.k, 256, 0, stream, gp));
   NSM_CHECK_CUDA(stage_event(m.events, 3, stream));
 
   DownParams dp{};
@@ -1221,6 +1348,7 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   dp.count_ptr = m.count;
   dp.max_rows = m.k;
   dp.act16 = ws.act16;
+  dp.act16lo = ws.act16lo;
   dp.act_scale = ws.act_scale;
   dp.ypart = ws.ypart;
   dp.err = ws.err;

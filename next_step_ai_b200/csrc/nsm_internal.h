@@ -89,14 +89,17 @@ struct DecodeWs {
   float* norm_scale;             // [1]
   float* scores;                 // [NB]
   // activations
-  __half* x16;                   // [H]
+  __half* x16;                   // [H] x / xscale rounded to fp16
+  __half* x16lo;                 // [H] x / xscale - x16 rounded to fp16 (the hi + lo pair carries 22 bits)
   float* xscale;                 // [H/64]
   int* rows;                     // [top_k]
   int* count;                    // [1]
   int* sel_idx;                  // [top_k] router selection (when no idx_out)
   int* row_block;                // [top_k] block id of each compacted pool row
   float* gu_part;                // [top_k][kMaxUnitsPerSlot][2][32]
-  __half* act16;                 // [top_k][32]
+  unsigned* gu_ticket;           // [kMaxTopK] units of each block counted so far (counter head; zero between calls)
+  __half* act16;                 // [top_k][32] SiLU(gate)*up / act_scale rounded to fp16
+  __half* act16lo;               // [top_k][32] its remainder rounded to fp16
   float* act_scale;              // [top_k]
   float* ypart;                  // [kMaxSlotGroups][H]
   size_t bytes;

@@ -266,8 +266,12 @@ __global__ void __launch_bounds__(256, 1) router_latent_kernel(RouterAParams p) 
         const float s = pow2_scale_for(m);
         const float inv = 1.f / s;
         const int c = c0 + tl * 64;
-        p.ws.x16[c + lane] = __float2half_rn(a * inv);
-        p.ws.x16[c + 32 + lane] = __float2half_rn(b * inv);
+        // fp16 hi + lo: the gate/up kernels feed both to the tensor cores
+        const __half ah = __float2half_rn(a * inv), bh = __float2half_rn(b * inv);
+        p.ws.x16[c + lane] = ah;
+        p.ws.x16[c + 32 + lane] = bh;
+        p.ws.x16lo[c + lane] = __float2half_rn(a * inv - __half2float(ah));
+        p.ws.x16lo[c + 32 + lane] = __float2half_rn(b * inv - __half2float(bh));
         if (lane == 0) p.ws.xscale[c >> 6] = s;
       }
     }

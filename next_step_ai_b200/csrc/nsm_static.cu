@@ -13,7 +13,7 @@
 //
 // Limits: hidden <= NSM_STATIC_MAX_HIDDEN (16384) and num_blocks_gathered <=
 // NSM_STATIC_MAX_BLOCKS (256); the scratch for the largest such call is
-// 6,374,144 bytes (the decode workspace layout at those limits, checked by a
+// 6,423,296 bytes (the decode workspace layout at those limits, checked by a
 // host test through nsm_decode_rows_workspace_bytes), so the array is 6.5 MiB.
 //
 // Every call on a device shares the one array and finds the previous call's

@@ -13,6 +13,8 @@ the reference value for bf16 outputs).
 """
 from __future__ import annotations
 
+import types
+
 import numpy as np
 import pytest
 
@@ -120,13 +122,14 @@ def test_dispatch_with_smc_reuse(dev):
     rt._enable_smc = True
     X = syn.make_x(shape, 41, 1)
     x = T(X, dev, torch.bfloat16).view(1, 1, shape.hidden)
-    y0 = rt._mlp_forward_dispatch(0, None, x)
+    layer = types.SimpleNamespace(mlp=None)  # the decoder layer; the resident path does not read its module
+    y0 = rt._mlp_forward_dispatch(0, layer, x)
     assert_close(y0.float().cpu().numpy().reshape(-1), _oracle_mlp(shape, full, X[0], _oracle_route(shape, R, X)[0]),
                  bf16_out=True)
     assert bool(rt._smc_valid[0].item())
-    y1 = rt._mlp_forward_dispatch(0, None, x)  # same input: the cached output
+    y1 = rt._mlp_forward_dispatch(0, layer, x)  # same input: the cached output
     assert torch.equal(y1, y0)
     X2 = syn.make_x(shape, 42, 1)
-    y2 = rt._mlp_forward_dispatch(0, None, T(X2, dev, torch.bfloat16).view(1, 1, -1))
+    y2 = rt._mlp_forward_dispatch(0, layer, T(X2, dev, torch.bfloat16).view(1, 1, -1))
     assert_close(y2.float().cpu().numpy().reshape(-1),
                  _oracle_mlp(shape, full, X2[0], _oracle_route(shape, R, X2)[0]), bf16_out=True)
