@@ -60,6 +60,13 @@ TOKEN_DRAM_BYTES_PER_LAYER = None
 TOKEN_TRAFFIC_SOURCE = "profiles/token_kernel_cfg1.txt (ncu of a 2-layer token, per layer x 126)"
 
 
+# DRAM bytes (read + write) of one gateup_tma_kernel launch from the ncu capture in
+# profiles/gateup_tma_kernel_cfg1.txt (dram__bytes_read.sum + dram__bytes_write.sum),
+# the same workload on one GPU.
+GATEUP_DRAM_BYTES_PER_LAUNCH = 122_836_224 + 3_521_536
+GATEUP_TRAFFIC_SOURCE = "profiles/gateup_tma_kernel_cfg1.txt (ncu --set full, one launch, 1 GPU)"
+
+
 def token_traffic(world: int):
     if TOKEN_DRAM_BYTES_PER_LAYER is None or world != 1:
         return None
@@ -273,7 +280,8 @@ def run_ours(args) -> None:
         line = {
             "metric": METRIC, "value": args.steps / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "nf4 weights, fp16 x fp16 -> fp32 MMA, bf16 io",
+            "scaling": "strong", "vs_baseline": None, "dtype": ("nf4 weights; x and SiLU*up as fp16 hi+lo pairs, prescaled fp16 codebook, fp16 x fp16 -> "
+                      "fp32 MMA; fp32 residual"),
             "data": "synthetic: seeded N(0,0.02) NF4 weights, bf16 RMS-normalised N(0,1) input, random-init router",
             "config": headline_config(world),
             "run": {"unique_layers_resident": unique, "layer_cycling": unique < LAYERS, "cuda_graph": True,
@@ -283,8 +291,10 @@ def run_ours(args) -> None:
             "gpu_launches": args.steps * dec.kernels_per_step,
             "roofline": {"bound": "hbm", "achieved": round(kern_gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(kern_gbs / pk["hbm_gbs"], 4),
-                         "traffic": token_traffic(world) if dec.use_token else None,
-                         "traffic_source": TOKEN_TRAFFIC_SOURCE if dec.use_token else None,
+                         "traffic": (token_traffic(world) if dec.use_token
+                                     else GATEUP_DRAM_BYTES_PER_LAUNCH if world == 1 else None),
+                         "traffic_source": (TOKEN_TRAFFIC_SOURCE if dec.use_token
+                                            else GATEUP_TRAFFIC_SOURCE if world == 1 else None),
                          "kernel": kern_name,
                          "algorithmic_bytes": int(kern_bytes), "us_per_launch": round(kern_us, 3),
                          "peak_source": pk["source"], "peak_note": "of measured (MEASURED_PEAKS.json hbm_gbs)",

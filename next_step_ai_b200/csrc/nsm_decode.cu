@@ -640,15 +640,19 @@ constexpr int kDnPairsPerStage = NSM_DN_PAIRS_PER_STAGE;
 constexpr int kDnStageBytes = kDnPairsPerStage * (1024 + 256);
 // shared-memory layout (bytes from the dynamic base)
 constexpr int kGuX16Off = kSmemHead;
-constexpr int kGuX16LoOff = kGuX16Off + kStageXMaxHidden * 2;
-constexpr int kGuXsOff = kGuX16LoOff + kStageXMaxHidden * 2;
+// x16lo sits 16 bytes past a bank-aligned start: the lanes reading it (g == 1)
+// then hit the four banks the x16 lanes of the same t leave free
+constexpr int kGuX16LoOff = kGuX16Off + kStageXMaxHidden * 2 + 16;
+constexpr int kGuXsOff = kGuX16Off + 2 * kStageXMaxHidden * 2 + 128;
 constexpr int kGuRowsOff = kGuXsOff + (kStageXMaxHidden / 64) * 4;
 constexpr int kGuRingOff = kGuRowsOff + kStageRowsMax * 4;
 constexpr int kGuBarOff = kGuRingOff + kGuWarps * kGuStages * kGuStageBytes;
 constexpr int kGuTmaSmem = kGuBarOff + (kGuWarps * kGuStages + 1) * 8;  // + the x staging barrier
 constexpr int kDnActOff = kSmemHead;
-constexpr int kDnActLoOff = kDnActOff + kStageActMaxSlots * 64;
-constexpr int kDnScaleOff = kDnActLoOff + kStageActMaxSlots * 64;
+// act16lo sits 64 bytes past a bank-aligned start: the lanes reading it (g == 1)
+// then hit the 16 banks the act16 lanes leave free
+constexpr int kDnActLoOff = kDnActOff + kStageActMaxSlots * 64 + 64;
+constexpr int kDnScaleOff = kDnActOff + 2 * kStageActMaxSlots * 64 + 128;
 constexpr int kDnRowsOff = kDnScaleOff + kStageActMaxSlots * 4;
 constexpr int kDnRingOff = kDnRowsOff + kStageActMaxSlots * 4;
 constexpr int kDnBarOff = kDnRingOff + kTmaWarps * kDnStages * kDnStageBytes;
