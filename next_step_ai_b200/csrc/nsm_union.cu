@@ -19,9 +19,11 @@
 //   union_act_kernel       per slot: fixed-order segment sums, token scale,
 //                          row mask, SiLU(g)*u -> fp16 with one power-of-two
 //                          scale per (slot, token).
-//   union_down_kernel      warps stream (32-row tile, slot) pairs; partials per
-//                          row-tile segment.
-//   union_y_kernel         fixed-order segment sums -> y[token][h].
+//   union_down_kernel      CTA = (slot range, range of 64-row groups): the slot
+//                          range's activations staged in shared memory, each
+//                          warp streams its 64-row groups over the slots with
+//                          register-prefetched weights; partials per slot range.
+//   union_y_kernel         fixed-order sums over the slot ranges -> y[token][h].
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -36,7 +38,10 @@ namespace nsm {
 
 constexpr int kUnionRows = 32;       // tokens per call (4 groups of 8)
 constexpr int kUnionGuMaxSeg = 6;    // gate/up partial segments per union slot
-constexpr int kUnionDnMaxSeg = 8;    // down partial segments per 32-row tile
+// down: slot ranges (= partial segments of y) and their size
+constexpr int kUdMinSlots = 32;      // slots per range at least (unions up to 32 x 24 slots: 24 ranges)
+constexpr int kUdMaxRanges = 24;     // ranges for unions up to kUdMaxRanges x kUdMaxSlots slots
+constexpr int kUdMaxSlots = 72;      // slots per range at most (their activations fill shared memory)
 constexpr int kUnionThreads = 256;
 
 struct UnionWs {
@@ -75,7 +80,8 @@ static UnionWs union_ws_layout(void* base, int H, int umax) {
   w.gu_part = reinterpret_cast<float*>(take((size_t)umax * kUnionGuMaxSeg * 2 * kUnionRows * 32 * sizeof(float)));
   w.act16 = reinterpret_cast<__half*>(take((size_t)umax * kUnionRows * 32 * sizeof(__half)));
   w.act_scale = reinterpret_cast<float*>(take((size_t)umax * kUnionRows * sizeof(float)));
-  w.ypart = reinterpret_cast<float*>(take((size_t)kUnionDnMaxSeg * H * kUnionRows * sizeof(float)));
+  const int nseg = std::max(kUdMaxRanges, (umax + kUdMaxSlots - 1) / kUdMaxSlots);
+  w.ypart = reinterpret_cast<float*>(take((size_t)nseg * H * kUnionRows * sizeof(float)));
   w.bytes = off;
   return w;
 }
@@ -424,36 +430,46 @@ __global__ void __launch_bounds__(1024) union_act_kernel(UnionMlpParams p) {
 // ---------------------------------------------------------------------------
 // down over the union
 // ---------------------------------------------------------------------------
+// y[h][tok] = sum over slots s and their 32 columns c of W_d[h][s, c] act[s][tok][c].
+// The slots split into nsr ranges (a function of the union's size only, so the
+// y kernel finds the same split); a CTA takes one (slot range, range of 64-row
+// groups) item, stages the range's activations (fp16 [tok][col] per slot, 2 KB)
+// and their scales in shared memory, and each warp streams its 64-row groups
+// over the range's slots: the weight pair (64 rows x 32 columns, 1 KB + the
+// rows' absmax) comes from global memory kUdDepth pairs ahead in registers,
+// the activation fragments from shared memory, 32 mma.sync per pair (2 row
+// tiles x 2 row groups x 4 token groups x 2 K steps).  A warp owns whole row
+// groups, so each (range, row group) partial is written once.
+constexpr int kUdThreads = 256;
+constexpr int kUdWarps = kUdThreads / 32;
+constexpr int kUdDepth = 3;  // weight pairs in flight per warp, beyond the one computed
+constexpr int kUdActOff = kSmemHead;                                      // [kUdMaxSlots][32 tok][32 col] fp16
+constexpr int kUdScaleOff = kUdActOff + kUdMaxSlots * kUnionRows * 64;   // [kUdMaxSlots][32 tok] fp32
+constexpr int kUdRowsOff = kUdScaleOff + kUdMaxSlots * kUnionRows * 4;   // [kUdMaxSlots] pool rows
+constexpr int kUdSmem = kUdRowsOff + kUdMaxSlots * 4;
+static_assert(kUdSmem <= 227 * 1024, "union down shared memory");
+
+// Slot ranges of a union of `count` slots: at least kUdMinSlots slots per
+// range, at most kUdMaxRanges ranges unless a range would pass kUdMaxSlots.
+__device__ __forceinline__ int union_down_ranges(int count) {
+  int n = (count + kUdMinSlots - 1) / kUdMinSlots;
+  n = n < 1 ? 1 : (n > kUdMaxRanges ? kUdMaxRanges : n);
+  const int need = (count + kUdMaxSlots - 1) / kUdMaxSlots;
+  return n > need ? n : need;
+}
+
+struct UdPair {
+  uint4 w0, w1;    // row tiles 0 and 1 of the 64-row group: rows g, g+8, 16+g, 24+g (.x .y .z .w), bytes 4t..4t+3
+  float4 a0, a1;   // their absmax
+};
+
 template <int kBase>
-__device__ __forceinline__ void union_down_body(const UnionMlpParams& p, uint32_t lb, int count) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int RT = p.H >> 5;
-  const int total = RT * count;
-  if (total == 0) return;
-  const int nw = stream_warps(RT, count, kUnionDnMaxSeg, p.total_warps);
-  if (warp_global >= nw) return;
-  const int q0 = stream_begin(total, nw, warp_global), q1 = stream_begin(total, nw, warp_global + 1);
-  int rt = q0 / count, s = q0 - rt * count;
-  int seg = warp_global - stream_owner(total, nw, rt * count);
-  float acc[2][4][4];
+__device__ __forceinline__ void union_down_pair(const UdPair& pr, uint32_t lb, const uint4 bf[4], const float2 as[4],
+                                                float (&acc)[2][2][4][4]) {
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
-#pragma unroll
-    for (int c = 0; c < 4; ++c)
-#pragma unroll
-      for (int d = 0; d < 4; ++d) acc[a][c][d] = 0.f;
-  for (int q = q0; q < q1; ++q) {
-    const int prow = __ldcg(p.ws.u_rows + s);
-    const uint4 w = ldg_stream_u4(p.down + (int64_t)prow * p.dbs + (int64_t)rt * 512 + lane * 16);
-    const float4 am = ldg_f4(p.down_am + (int64_t)prow * p.dabs + rt * 32 + g * 4);
-    uint4 bf[4];
-    float2 as[4];
-#pragma unroll
-    for (int grp = 0; grp < 4; ++grp) {
-      bf[grp] = ldg_u4(p.ws.act16 + ((int64_t)s * kUnionRows + grp * 8 + g) * 32 + t * 8);
-      as[grp] = __ldcg(reinterpret_cast<const float2*>(p.ws.act_scale + (int64_t)s * kUnionRows + grp * 8 + 2 * t));
-    }
+  for (int r = 0; r < 2; ++r) {
+    const uint4 w = r ? pr.w1 : pr.w0;
+    const float4 am = r ? pr.a1 : pr.a0;
 #pragma unroll
     for (int rg = 0; rg < 2; ++rg) {
       const uint32_t w0 = rg ? w.z : w.x, w1 = rg ? w.w : w.y;
@@ -467,31 +483,113 @@ __device__ __forceinline__ void union_down_body(const UnionMlpParams& p, uint32_
         float d[4];
         mma_16816_z(d, a00, a01, a02, a03, bf[grp].x, bf[grp].y);
         mma_16816(d, a10, a11, a12, a13, bf[grp].z, bf[grp].w);
-        acc[rg][grp][0] = fmaf(d[0], r0 * as[grp].x, acc[rg][grp][0]);
-        acc[rg][grp][1] = fmaf(d[1], r0 * as[grp].y, acc[rg][grp][1]);
-        acc[rg][grp][2] = fmaf(d[2], r1 * as[grp].x, acc[rg][grp][2]);
-        acc[rg][grp][3] = fmaf(d[3], r1 * as[grp].y, acc[rg][grp][3]);
+        acc[r][rg][grp][0] = fmaf(d[0], r0 * as[grp].x, acc[r][rg][grp][0]);
+        acc[r][rg][grp][1] = fmaf(d[1], r0 * as[grp].y, acc[r][rg][grp][1]);
+        acc[r][rg][grp][2] = fmaf(d[2], r1 * as[grp].x, acc[r][rg][grp][2]);
+        acc[r][rg][grp][3] = fmaf(d[3], r1 * as[grp].y, acc[r][rg][grp][3]);
       }
-    }
-    if (++s == count || q + 1 == q1) {
-      float* yp = p.ws.ypart + ((int64_t)seg * p.H + rt * 32) * kUnionRows;
-#pragma unroll
-      for (int rg = 0; rg < 2; ++rg)
-#pragma unroll
-        for (int grp = 0; grp < 4; ++grp)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int row = rg * 16 + g + (e >> 1) * 8, tok = grp * 8 + 2 * t + (e & 1);
-            yp[row * kUnionRows + tok] = acc[rg][grp][e];
-            acc[rg][grp][e] = 0.f;
-          }
-      seg = 0;
-      if (s == count) { s = 0; ++rt; }
     }
   }
 }
 
-__global__ void __launch_bounds__(kUnionThreads, 2) union_down_kernel(UnionMlpParams p) {
+template <int kBase>
+__device__ __forceinline__ void union_down_body(const UnionMlpParams& p, uint32_t lb, int count) {
+  char* smem = reinterpret_cast<char*>(g_lut_smem);
+  const __half* sact = reinterpret_cast<const __half*>(smem + kUdActOff);
+  const float* sscale = reinterpret_cast<const float*>(smem + kUdScaleOff);
+  int* srows = reinterpret_cast<int*>(smem + kUdRowsOff);
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3, warp = threadIdx.x >> 5;
+  const int RP = p.H >> 6;
+  const int nsr = union_down_ranges(count);
+  const int per = (count + nsr - 1) / nsr;
+  const int nrr = max(1, (int)gridDim.x / nsr);
+  for (int item = blockIdx.x; item < nsr * nrr; item += gridDim.x) {
+    const int sr = item / nrr, rr = item - sr * nrr;
+    const int s0 = sr * per, s1 = min(count, s0 + per), ns = s1 - s0;
+    const int rp0 = (int)((int64_t)RP * rr / nrr), rp1 = (int)((int64_t)RP * (rr + 1) / nrr);
+    __syncthreads();  // the previous item's readers are done with the staging buffers
+    if (ns > 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.ws.act16 + (int64_t)s0 * kUnionRows * 32);
+      uint4* dst = reinterpret_cast<uint4*>(smem + kUdActOff);
+      for (int i = threadIdx.x; i < ns * kUnionRows * 4; i += blockDim.x) dst[i] = __ldcg(src + i);
+      float* ssc = reinterpret_cast<float*>(smem + kUdScaleOff);
+      for (int i = threadIdx.x; i < ns * kUnionRows; i += blockDim.x)
+        ssc[i] = __ldcg(p.ws.act_scale + (int64_t)s0 * kUnionRows + i);
+      for (int i = threadIdx.x; i < ns; i += blockDim.x) srows[i] = __ldcg(p.ws.u_rows + s0 + i);
+    }
+    __syncthreads();
+    if (ns <= 0) continue;
+    // this warp's row groups: rp0 + warp, rp0 + warp + kUdWarps, ...
+    const int nmine = rp1 - rp0 > warp ? (rp1 - rp0 - warp + kUdWarps - 1) / kUdWarps : 0;
+    const int npairs = nmine * ns;
+    if (npairs == 0) continue;
+    int lrp = rp0 + warp, ls = 0;  // load cursor
+    auto load = [&](UdPair& pr) {
+      const int64_t prow = srows[ls];
+      const uint8_t* wb = p.down + prow * p.dbs + (int64_t)lrp * 1024 + lane * 16;
+      pr.w0 = ldg_stream_u4(wb);
+      pr.w1 = ldg_stream_u4(wb + 512);
+      const float* ab = p.down_am + prow * p.dabs + lrp * 64 + g * 4;
+      pr.a0 = ldg_f4(ab);
+      pr.a1 = ldg_f4(ab + 32);
+      if (++ls == ns) {
+        ls = 0;
+        lrp += kUdWarps;
+      }
+    };
+    UdPair buf[kUdDepth + 1];
+#pragma unroll
+    for (int i = 0; i < kUdDepth + 1; ++i)
+      if (i < npairs) load(buf[i]);
+    float acc[2][2][4][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a)
+#pragma unroll
+      for (int b2 = 0; b2 < 2; ++b2)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int d = 0; d < 4; ++d) acc[a][b2][c][d] = 0.f;
+    int rp = rp0 + warp, s = 0;
+    for (int q0 = 0; q0 < npairs; q0 += kUdDepth + 1) {
+#pragma unroll
+      for (int u = 0; u < kUdDepth + 1; ++u) {
+        const int q = q0 + u;
+        if (q >= npairs) break;
+        const UdPair cur = buf[u];
+        if (q + kUdDepth + 1 < npairs) load(buf[u]);
+        uint4 bf[4];
+        float2 as[4];
+#pragma unroll
+        for (int grp = 0; grp < 4; ++grp) {
+          bf[grp] = *reinterpret_cast<const uint4*>(sact + ((s * kUnionRows + grp * 8 + g) * 32 + t * 8));
+          as[grp] = *reinterpret_cast<const float2*>(sscale + s * kUnionRows + grp * 8 + 2 * t);
+        }
+        union_down_pair<kBase>(cur, lb, bf, as, acc);
+        if (++s == ns) {
+          // row group rp done: its partial for this slot range
+          float* yp = p.ws.ypart + ((int64_t)sr * p.H + (int64_t)rp * 64) * kUnionRows;
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+              for (int grp = 0; grp < 4; ++grp)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int row = r * 32 + rg * 16 + g + (e >> 1) * 8, tok = grp * 8 + 2 * t + (e & 1);
+                  yp[row * kUnionRows + tok] = acc[r][rg][grp][e];
+                  acc[r][rg][grp][e] = 0.f;
+                }
+          s = 0;
+          rp += kUdWarps;
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kUdThreads, 1) union_down_kernel(UnionMlpParams p) {
   pdl_trigger();
   build_lut_dyn(p.down_code, p.down_code);
   pdl_wait();
@@ -504,7 +602,7 @@ __global__ void __launch_bounds__(kUnionThreads, 2) union_down_kernel(UnionMlpPa
     union_down_body<-1>(p, lb, count);
 }
 
-// y[token][h] = fixed-order sum of the row-tile segments; one thread per (h, token).
+// y[token][h] = the slot ranges' partials summed in range order; one thread per (h, token).
 __global__ void __launch_bounds__(256) union_y_kernel(UnionMlpParams p) {
   pdl_trigger();
   pdl_wait();
@@ -514,16 +612,16 @@ __global__ void __launch_bounds__(256) union_y_kernel(UnionMlpParams p) {
   const int count = __ldcg(p.ws.u_count);
   float y = 0.f;
   if (count > 0) {
-    const int RT = p.H >> 5, rt = h >> 5, total = RT * count;
-    const int nw = stream_warps(RT, count, kUnionDnMaxSeg, p.total_warps);
-    const int nseg = stream_owner(total, nw, rt * count + count - 1) - stream_owner(total, nw, rt * count) + 1;
-    float v[kUnionDnMaxSeg];  // all segment loads in flight, summed in order
+    const int nseg = union_down_ranges(count);
+    for (int q0 = 0; q0 < nseg; q0 += 8) {
+      float v[8];  // eight segment loads in flight, summed in order
 #pragma unroll
-    for (int q = 0; q < kUnionDnMaxSeg; ++q)
-      v[q] = q < nseg ? __ldcg(p.ws.ypart + ((int64_t)q * p.H + h) * kUnionRows + tok) : 0.f;
+      for (int u = 0; u < 8; ++u)
+        v[u] = q0 + u < nseg ? __ldcg(p.ws.ypart + ((int64_t)(q0 + u) * p.H + h) * kUnionRows + tok) : 0.f;
 #pragma unroll
-    for (int q = 0; q < kUnionDnMaxSeg; ++q)
-      if (q < nseg) y += v[q];
+      for (int u = 0; u < 8; ++u)
+        if (q0 + u < nseg) y += v[u];
+    }
   }
   if (tok < p.rows) store_from_f32(p.y, p.y_dtype, (int64_t)tok * p.H + h, y);
 }
@@ -536,11 +634,11 @@ static int union_setup(int device, int* gu_ctas, int* dn_ctas) {
     NSM_CHECK_CUDA(cudaFuncSetAttribute(union_build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         kMaxNumBlocks * 4));
     NSM_CHECK_CUDA(cudaFuncSetAttribute(union_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemHead));
-    NSM_CHECK_CUDA(cudaFuncSetAttribute(union_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemHead));
+    NSM_CHECK_CUDA(cudaFuncSetAttribute(union_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kUdSmem));
     NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&cache[device][0], union_gateup_kernel,
                                                                  kUnionThreads, kSmemHead));
     NSM_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&cache[device][1], union_down_kernel,
-                                                                 kUnionThreads, kSmemHead));
+                                                                 kUdThreads, kUdSmem));
     if (cache[device][0] <= 0 || cache[device][1] <= 0) return fail(NSM_ERR_CUDA, "union kernel occupancy is zero");
     done[device] = true;
   }
@@ -638,8 +736,7 @@ int nsm_union_decode(const void* x, int32_t x_dtype, int32_t rows, int32_t hidde
   NSM_CHECK_CUDA(launch_pdl(union_gateup_kernel, gu_ctas, kUnionThreads, kSmemHead, s, p));
   NSM_CHECK_CUDA(launch_pdl(union_act_kernel, umax, 1024, 0, s, p));
   const int dn_ctas = dev.sm_count * dn_per_sm;
-  p.total_warps = dn_ctas * (kUnionThreads / 32);
-  NSM_CHECK_CUDA(launch_pdl(union_down_kernel, dn_ctas, kUnionThreads, kSmemHead, s, p));
+  NSM_CHECK_CUDA(launch_pdl(union_down_kernel, dn_ctas, kUdThreads, kUdSmem, s, p));
   NSM_CHECK_CUDA(launch_pdl(union_y_kernel, (hidden * kUnionRows + 255) / 256, 256, 0, s, p));
   if (union_count_out) NSM_CHECK_CUDA(cudaMemcpyAsync(union_count_out, wsl.u_count, sizeof(int32_t),
                                                       cudaMemcpyDeviceToDevice, s));
