@@ -490,10 +490,11 @@ def run_cache(args) -> None:
             hits += st.hits
             misses += st.misses
             h2d += st.h2d_bytes
-            # this library's kernels per token: router (3), resident decode (5: selection map,
-            # gate/up, gate/up reduction, down, down reduction), staged decode (5) when there
-            # are misses; the miss copies are cudaMemcpyAsync, the promotion copies torch's
-            launches += 8 + (5 if st.misses else 0)
+            # this library's kernels per token: router (3), resident decode (4: selection map,
+            # gate/up with SiLU*up, down, down reduction) and, when there are misses, the
+            # gather kernel that stages them and the staged decode (4); the promotion
+            # copies are torch's
+            launches += 7 + (5 if st.misses else 0)
         e1.record()
         torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)

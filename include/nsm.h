@@ -457,17 +457,21 @@ int nsm_cache_promote(const nsm_mlp_weights* w, int32_t hidden, const int32_t* s
                       const int32_t* block_ids, const int32_t* evicted_ids, int32_t n, int32_t* slot_of_block,
                       nsm_stream_t stream);
 
-/* Stages blocks from a host block store into device pool rows: block
- * blocks[i] (record host_base + blocks[i]*record_bytes) -> pool row
- * dst_rows[i] (pool_base + dst_rows[i]*record_bytes), one cudaMemcpyAsync per
- * block on `stream` (a side stream, so the copies overlap the resident-block
- * compute).  blocks and dst_rows are HOST arrays; host_base should be pinned
- * so the copies run asynchronously.  A record holds all of one block's bytes
- * (gate, up, down and their absmax) so a miss is one contiguous copy.
- * Replaces the pinned host-to-device copies of _copy_cpu_to_gpu and the cold
- * block loads (streaming_llama_runtime.py:3443-3493, :3885-4002). */
-int nsm_cache_stage(const void* host_base, const int32_t* blocks, int32_t n, size_t record_bytes, void* pool_base,
-                    const int32_t* dst_rows, int32_t pool_rows, nsm_stream_t stream);
+/* Stages blocks from a host block store of host_records records into device
+ * pool rows: block blocks[i] (record host_base + blocks[i]*record_bytes) ->
+ * pool row dst_rows[i] (pool_base + dst_rows[i]*record_bytes), on `stream` (a
+ * side stream, so the copies overlap the resident-block compute).  When
+ * host_base is pinned host memory the device can address (cudaHostAlloc /
+ * pinned torch tensors) and the records are 16-byte multiples, one gather
+ * kernel reads all records over the host link; otherwise one cudaMemcpyAsync
+ * per block.  blocks and dst_rows are HOST arrays, checked against
+ * host_records and pool_rows before anything is queued.  A record holds all
+ * of one block's bytes (gate, up, down and their absmax).  Replaces the
+ * pinned host-to-device copies of _copy_cpu_to_gpu and the cold block loads
+ * (streaming_llama_runtime.py:3443-3493, :3885-4002). */
+int nsm_cache_stage(const void* host_base, int32_t host_records, const int32_t* blocks, int32_t n,
+                    size_t record_bytes, void* pool_base, const int32_t* dst_rows, int32_t pool_rows,
+                    nsm_stream_t stream);
 
 /* ---- NF4 LM head ---------------------------------------------------------
  * logits[t][v] = sum_h code[nib(v*H+h)] * absmax[(v*H+h)/qbs] * x[t][h] (+ bias[v])

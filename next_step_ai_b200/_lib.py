@@ -30,7 +30,7 @@ NSM_LAYOUT_GATEUP_TILED, NSM_LAYOUT_DOWN_TILED = 1, 2
 NSM_STAGE_EVENTS = 6
 NSM_IO_PENDING_Y, NSM_IO_DEFER_Y = 1, 2
 NSM_IPC_HANDLE_BYTES = 64
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # every symbol include/nsm.h declares (checked by tests/test_abi.py)
 EXPORTED = (
@@ -144,7 +144,8 @@ _SIGS = {
     "nsm_union_decode": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32,
                                  POINTER(BlockMapC), POINTER(MlpWeightsC), c_void_p, c_int32, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p]),
-    "nsm_cache_stage": (c_int, [c_void_p, c_void_p, c_int32, c_size_t, c_void_p, c_void_p, c_int32, c_void_p]),
+    "nsm_cache_stage": (c_int, [c_void_p, c_int32, c_void_p, c_int32, c_size_t, c_void_p, c_void_p, c_int32,
+                                c_void_p]),
     "nsm_cache_promote": (c_int, [POINTER(MlpWeightsC), c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_int32,
                                   c_void_p, c_void_p]),
 }

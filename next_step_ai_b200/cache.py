@@ -448,7 +448,7 @@ class CachedSparseMlp:
                stream: torch.cuda.Stream) -> None:
         blk = np.ascontiguousarray(blocks, dtype=np.int32)
         dst = np.ascontiguousarray(rows, dtype=np.int32)
-        _lib.check(self._lib.nsm_cache_stage(self.store.records.data_ptr(),
+        _lib.check(self._lib.nsm_cache_stage(self.store.records.data_ptr(), int(self.store.num_blocks),
                                              blk.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), int(blk.size),
                                              self.rec, pool.data_ptr(),
                                              dst.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), int(pool_rows),

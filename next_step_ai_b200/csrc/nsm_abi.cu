@@ -110,7 +110,7 @@ using namespace nsm;
 
 extern "C" {
 
-int nsm_abi_version(void) { return 3; }
+int nsm_abi_version(void) { return 4; }
 
 const char* nsm_status_string(int status) {
   switch (status) {

@@ -10,6 +10,18 @@
 
 namespace nsm {
 
+constexpr int kStageMaxJobs = 256;  // records per gather launch (the pointers travel in the parameters)
+constexpr int kStageThreads = 256;
+constexpr int kStageVec = 8;        // 16-byte loads in flight per thread
+struct StageParams {
+  const uint4* src[kStageMaxJobs];  // device view of the host record
+  uint4* dst[kStageMaxJobs];        // pool row
+  int64_t vecs;                     // 16-byte vectors per record
+  int n;
+};
+const char* stage_device_view(const void* host);
+__global__ void cache_stage_gather_kernel(const __grid_constant__ StageParams p);
+
 // ---------------------------------------------------------------------------
 // down weight [H][I/2] (+ absmax [H][I/64]) -> block-major [n][H][16] + [n][H]
 // ---------------------------------------------------------------------------
@@ -254,6 +266,49 @@ __global__ void cache_table_update_kernel(const int32_t* block_ids, const int32_
 
 static int dtype_ok(int d) { return d == NSM_F32 || d == NSM_F16 || d == NSM_BF16; }
 
+// ---------------------------------------------------------------------------
+// hot-block cache: miss records gathered from pinned host memory
+// ---------------------------------------------------------------------------
+// The device view of a pinned, mapped host allocation (nullptr for anything
+// else: pageable memory must go through the copy engine).
+const char* stage_device_view(const void* host) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, host) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (a.type != cudaMemoryTypeHost || a.devicePointer == nullptr) return nullptr;
+  return reinterpret_cast<const char*>(a.devicePointer);
+}
+
+// Copies whole records: the grid walks (record, 64 KB chunk) items; each
+// thread keeps kStageVec 16-byte loads from host memory in flight (a few MB
+// over the grid, enough to fill the host link).  No shared memory and few
+// registers, so its CTAs fit beside the decode kernels' on the same SMs.
+__global__ void __launch_bounds__(kStageThreads) cache_stage_gather_kernel(const __grid_constant__ StageParams p) {
+  constexpr int64_t kChunk = (int64_t)kStageThreads * kStageVec * 4;  // 16-byte vectors per item
+  const int64_t chunks = (p.vecs + kChunk - 1) / kChunk;
+  for (int64_t item = blockIdx.x; item < (int64_t)p.n * chunks; item += gridDim.x) {
+    const int j = (int)(item / chunks);
+    const int64_t c0 = (item - (int64_t)j * chunks) * kChunk;
+    const uint4* src = p.src[j];
+    uint4* dst = p.dst[j];
+    for (int64_t v0 = c0; v0 < c0 + kChunk && v0 < p.vecs; v0 += (int64_t)kStageThreads * kStageVec) {
+      uint4 r[kStageVec];
+#pragma unroll
+      for (int u = 0; u < kStageVec; ++u) {
+        const int64_t v = v0 + (int64_t)u * kStageThreads + threadIdx.x;
+        if (v < p.vecs) r[u] = src[v];
+      }
+#pragma unroll
+      for (int u = 0; u < kStageVec; ++u) {
+        const int64_t v = v0 + (int64_t)u * kStageThreads + threadIdx.x;
+        if (v < p.vecs) dst[v] = r[u];
+      }
+    }
+  }
+}
+
 }  // namespace nsm
 
 using namespace nsm;
@@ -389,20 +444,43 @@ int nsm_cache_split(const int32_t* idx, int32_t k, const int32_t* slot_of_block,
   return NSM_OK;
 }
 
-int nsm_cache_stage(const void* host_base, const int32_t* blocks, int32_t n, size_t record_bytes, void* pool_base,
-                    const int32_t* dst_rows, int32_t pool_rows, nsm_stream_t stream) {
+int nsm_cache_stage(const void* host_base, int32_t host_records, const int32_t* blocks, int32_t n,
+                    size_t record_bytes, void* pool_base, const int32_t* dst_rows, int32_t pool_rows,
+                    nsm_stream_t stream) {
   if (n <= 0) return NSM_OK;
   NSM_REQUIRE(host_base && blocks && pool_base && dst_rows, NSM_ERR_INVALID_ARG, "NULL pointer");
   NSM_REQUIRE(record_bytes > 0, NSM_ERR_INVALID_ARG, "record_bytes must be > 0");
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const char* src = reinterpret_cast<const char*>(host_base);
-  char* dst = reinterpret_cast<char*>(pool_base);
   for (int i = 0; i < n; ++i) {
-    NSM_REQUIRE(blocks[i] >= 0, NSM_ERR_INVALID_ARG, "negative block id");
+    NSM_REQUIRE(blocks[i] >= 0 && blocks[i] < host_records, NSM_ERR_INVALID_ARG,
+                "block id outside the host store");
     NSM_REQUIRE(dst_rows[i] >= 0 && dst_rows[i] < pool_rows, NSM_ERR_INVALID_ARG, "destination row out of range");
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* dst = reinterpret_cast<char*>(pool_base);
+  // pinned host memory that the device can address: one gather kernel reads
+  // every record over the host link; anything else goes through the copy engine
+  const char* dsrc = stage_device_view(host_base);
+  if (dsrc != nullptr && record_bytes % 16 == 0 && ((uintptr_t)dsrc | (uintptr_t)dst) % 16 == 0) {
+    DeviceInfo dev;
+    const int st = current_device(&dev);
+    if (st) return st;
+    for (int i0 = 0; i0 < n; i0 += kStageMaxJobs) {
+      StageParams sp{};
+      sp.n = std::min(n - i0, kStageMaxJobs);
+      sp.vecs = (int64_t)(record_bytes / 16);
+      for (int i = 0; i < sp.n; ++i) {
+        sp.src[i] = reinterpret_cast<const uint4*>(dsrc + (size_t)blocks[i0 + i] * record_bytes);
+        sp.dst[i] = reinterpret_cast<uint4*>(dst + (size_t)dst_rows[i0 + i] * record_bytes);
+      }
+      cache_stage_gather_kernel<<<std::max(1, dev.sm_count / 2), kStageThreads, 0, s>>>(sp);
+      NSM_CHECK_CUDA(cudaGetLastError());
+    }
+    return NSM_OK;
+  }
+  const char* src = reinterpret_cast<const char*>(host_base);
+  for (int i = 0; i < n; ++i)
     NSM_CHECK_CUDA(cudaMemcpyAsync(dst + (size_t)dst_rows[i] * record_bytes, src + (size_t)blocks[i] * record_bytes,
                                    record_bytes, cudaMemcpyHostToDevice, s));
-  }
   return NSM_OK;
 }
 

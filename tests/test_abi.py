@@ -44,7 +44,7 @@ def test_library_exports_every_declared_symbol(lib):
 def test_status_strings_and_version(lib):
     from next_step_ai_b200 import _lib
 
-    assert lib.nsm_abi_version() == _lib.ABI_VERSION == 3
+    assert lib.nsm_abi_version() == _lib.ABI_VERSION == 4
     assert lib.nsm_status_string(0) == b"ok"
     assert lib.nsm_status_string(-5).startswith(b"workspace")
     assert lib.nsm_status_string(12345) == b"unknown status"

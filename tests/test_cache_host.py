@@ -142,3 +142,28 @@ def test_calibration_rebuild_matches_reference():
         assert {str(k): v.tolist() for k, v in sets.items()} == c["hot"], c["case"]
         assert len(sets) == c["updated_layers"]
         assert sum(float(cal.hits[li].sum()) for li in sets) == pytest.approx(c["total_hits"], rel=1e-6)
+
+
+def test_stage_rejects_ids_outside_the_store_before_any_copy():
+    """nsm_cache_stage checks every block id against the host store and every
+    destination row against the pool on the host, before queueing anything
+    (no device is touched, so this runs without a GPU)."""
+    import ctypes
+
+    from next_step_ai_b200 import _lib
+
+    lib = _lib.load()
+    host = (ctypes.c_uint8 * 64)()
+    pool = (ctypes.c_uint8 * 64)()
+
+    def stage(blocks, rows, host_records=4, pool_rows=4):
+        b = (ctypes.c_int32 * len(blocks))(*blocks)
+        r = (ctypes.c_int32 * len(rows))(*rows)
+        return lib.nsm_cache_stage(ctypes.addressof(host), host_records, b, len(blocks), 16,
+                                   ctypes.addressof(pool), r, pool_rows, None)
+
+    assert stage([4], [0]) == _lib.NSM_ERR_INVALID_ARG      # one past the store
+    assert stage([-1], [0]) == _lib.NSM_ERR_INVALID_ARG
+    assert stage([1, 2], [0, 4]) == _lib.NSM_ERR_INVALID_ARG  # one past the pool
+    assert "outside the host store" in _lib.last_error() or "destination row" in _lib.last_error()
+    assert stage([], []) == _lib.NSM_OK

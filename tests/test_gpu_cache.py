@@ -240,3 +240,35 @@ def test_calibration_rebuild_prewarms_top_counts(dev):
     y, st = cm.decode(x)
     sel = route_sparse_mlp(x, rw)[0].cpu().numpy()
     _close(y.cpu().numpy(), _oracle_y(shape, bnb, x, sel))
+
+
+@pytest.mark.parametrize("pinned", [True, False])
+def test_stage_places_exact_records(dev, pinned):
+    """The miss copy: pinned stores go through the gather kernel (device reads
+    of mapped host memory), pageable ones through the copy engine; both put
+    each record's bytes in its pool row, byte for byte, and leave the other
+    rows alone."""
+    import ctypes
+
+    from next_step_ai_b200 import _lib
+
+    lib = _lib.load()
+    rec, nrec, prow = 56 * 256, 12, 6
+    g = torch.Generator().manual_seed(3)
+    host = torch.randint(0, 256, (nrec, rec), dtype=torch.uint8, generator=g)
+    if pinned:
+        host = host.pin_memory()
+    pool = torch.full((prow, rec), 7, dtype=torch.uint8, device=dev)
+    blocks = np.array([9, 0, 11, 4], np.int32)
+    rows = np.array([5, 2, 0, 3], np.int32)
+    s = torch.cuda.Stream(device=dev)
+    _lib.check(lib.nsm_cache_stage(host.data_ptr(), nrec, blocks.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                   len(blocks), rec, pool.data_ptr(),
+                                   rows.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), prow, s.cuda_stream),
+               "nsm_cache_stage")
+    s.synchronize()
+    got = pool.cpu()
+    for b, r in zip(blocks, rows):
+        assert torch.equal(got[r], host[b])
+    for r in (1, 4):
+        assert bool((got[r] == 7).all())
