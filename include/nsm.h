@@ -141,6 +141,12 @@ typedef struct nsm_mlp_weights {
  * ignored for a tiled part. */
 #define NSM_LAYOUT_GATEUP_TILED 1
 #define NSM_LAYOUT_DOWN_TILED 2
+/* gate_code and up_code hold the same 16 values (the standard NF4 codebook
+ * does).  The tiled gate/up kernel then serves both projections from one
+ * lookup table and runs more warps in the shared memory that frees; it
+ * checks the claim and records NSM_ERR_INVALID_ARG in the workspace error
+ * word (computing nothing) when the codebooks differ. */
+#define NSM_LAYOUT_SHARED_CODE 4
 
 /* Block -> pool-row mapping applied to the router's selection.
  *   slot_of_block [NB] int32 (device): pool row, or <0 = not present here.

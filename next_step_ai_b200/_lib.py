@@ -26,7 +26,7 @@ NSM_ERR_WORKSPACE = -5
 NSM_ERR_DEVICE = -6
 
 NSM_F32, NSM_F16, NSM_BF16 = 0, 1, 2
-NSM_LAYOUT_GATEUP_TILED, NSM_LAYOUT_DOWN_TILED = 1, 2
+NSM_LAYOUT_GATEUP_TILED, NSM_LAYOUT_DOWN_TILED, NSM_LAYOUT_SHARED_CODE = 1, 2, 4
 NSM_STAGE_EVENTS = 6
 NSM_IO_PENDING_Y, NSM_IO_DEFER_Y = 1, 2
 NSM_IPC_HANDLE_BYTES = 64

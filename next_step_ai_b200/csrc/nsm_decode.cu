@@ -168,7 +168,7 @@ __device__ __forceinline__ void gu_mma_rowgroup(uint32_t lb, const uint4 w, cons
 // (lanes g == 1), so D columns 0 + 1 (d[0] + d[1], d[2] + d[3] of lanes
 // t == 0) hold the dot product with the hi + lo pair; xsg / xsu fold the
 // tables' 1 / alpha into the tile's x scale.
-template <int kBase>
+template <int kBase, int kUpTable = 1>
 __device__ __forceinline__ void gu_tile_mma(const GuTile& tile, const uint32_t b[8], float xsg, float xsu,
                                             uint32_t lb, float acc[2][4]) {
   float d[4];
@@ -178,7 +178,7 @@ __device__ __forceinline__ void gu_tile_mma(const GuTile& tile, const uint32_t b
     const float g0 = rg ? tile.am[0].z : tile.am[0].x, g1 = rg ? tile.am[0].w : tile.am[0].y;
     acc[0][rg * 2] = fmaf(d[0] + d[1], g0 * xsg, acc[0][rg * 2]);
     acc[0][rg * 2 + 1] = fmaf(d[2] + d[3], g1 * xsg, acc[0][rg * 2 + 1]);
-    gu_mma_rowgroup<kBase, 1>(lb, tile.w[1][rg], b, d);
+    gu_mma_rowgroup<kBase, kUpTable>(lb, tile.w[1][rg], b, d);
     const float u0 = rg ? tile.am[1].z : tile.am[1].x, u1 = rg ? tile.am[1].w : tile.am[1].y;
     acc[1][rg * 2] = fmaf(d[0] + d[1], u0 * xsu, acc[1][rg * 2]);
     acc[1][rg * 2 + 1] = fmaf(d[2] + d[3], u1 * xsu, acc[1][rg * 2 + 1]);
@@ -657,6 +657,32 @@ constexpr int kDnRowsOff = kDnScaleOff + kStageActMaxSlots * 4;
 constexpr int kDnRingOff = kDnRowsOff + kStageActMaxSlots * 4;
 constexpr int kDnBarOff = kDnRingOff + kTmaWarps * kDnStages * kDnStageBytes;
 constexpr int kDnTmaSmem = kDnBarOff + (kTmaWarps * kDnStages + 1) * 8;  // + the act staging barrier
+// Shared-codebook variant (gate and up codebooks equal, NSM_LAYOUT_SHARED_CODE):
+// one lookup table serves both projections, so the second table's half of
+// every 256-byte entry is free and holds x16lo (tile j's 128 bytes in entry
+// j, rotated by 16 bytes so its lanes use the banks the x16 lanes leave
+// free); the 32 KB saved go to two more warps.
+constexpr int kGu1Warps = 12;
+constexpr int kGu1Threads = kGu1Warps * 32;
+constexpr int kGu1XsOff = kGuX16Off + kStageXMaxHidden * 2;
+constexpr int kGu1RowsOff = kGu1XsOff + (kStageXMaxHidden / 64) * 4;
+constexpr int kGu1RingOff = kGu1RowsOff + kStageRowsMax * 4;
+constexpr int kGu1BarOff = kGu1RingOff + kGu1Warps * kGuStages * kGuStageBytes;
+constexpr int kGu1TmaSmem = kGu1BarOff + (kGu1Warps * kGuStages + 1) * 8;
+static_assert(kGu1TmaSmem <= 227 * 1024, "gate/up ring (shared codebook) does not fit in shared memory");
+static_assert(kGu1RingOff % 128 == 0, "rings must be 128-byte aligned");
+static_assert(kStageXMaxHidden / 64 <= 256, "x16lo needs one lookup entry per 64-column tile");
+template <bool kOne> struct GuCfg {
+  static constexpr int kWarps = kOne ? kGu1Warps : kGuWarps;
+  static constexpr int kXsOff = kOne ? kGu1XsOff : kGuXsOff;
+  static constexpr int kRowsOff = kOne ? kGu1RowsOff : kGuRowsOff;
+  static constexpr int kRingOff = kOne ? kGu1RingOff : kGuRingOff;
+  static constexpr int kBarOff = kOne ? kGu1BarOff : kGuBarOff;
+};
+// byte offset of x16lo's 16-byte chunk c (0..7) of tile j inside the lookup table
+__host__ __device__ constexpr uint32_t gu1_xlo_off(int j, int c) {
+  return (uint32_t)j * 256u + 128u + (uint32_t)((c * 16 + 16) & 127);
+}
 static_assert(kGuTmaSmem <= 227 * 1024, "gate/up ring does not fit in shared memory");
 static_assert(kDnTmaSmem <= 227 * 1024, "down ring does not fit in shared memory");
 static_assert(kGuRingOff % 128 == 0 && kDnRingOff % 128 == 0, "rings must be 128-byte aligned");
@@ -724,18 +750,24 @@ __device__ __forceinline__ void gu_finalize_block(const GateUpParams& p, int s, 
 // A ring stage holds one *unit* of kGuUnitTiles adjacent tiles of one block
 // (gate kGuUnitTiles KB, up kGuUnitTiles KB, their absmax runs): four bulk
 // copies and one round of cursor bookkeeping per unit instead of per tile.
-template <int kBase>
+template <int kBase, bool kOne>
 __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t lb, uint32_t xhi_s, uint32_t xlo_s,
                                                 uint32_t xss_s, const int* rows, int count, uint32_t ring,
                                                 uint32_t bar0) {
   constexpr int UT = kGuUnitTiles;
+  constexpr int kUpTable = kOne ? 0 : 1;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  // B operand column 0 (lanes g == 0) is x16, column 1 (lanes g == 1) x16lo
-  const uint32_t xs16_s = g == 1 ? xlo_s : xhi_s;
-  const float ia0 = lut_inv_alpha(0), ia1 = lut_inv_alpha(1);
+  // B operand column 0 (lanes g == 0) is x16, column 1 (lanes g == 1) x16lo:
+  // tile jj's fragment of this lane at xbase + jj * xstride + xoff0 / xoff1
+  const bool lo = g == 1;
+  const uint32_t xbase = lo ? xlo_s : xhi_s;
+  const uint32_t xstride = (kOne && lo) ? 256u : 128u;
+  const uint32_t xoff0 = (kOne && lo) ? gu1_xlo_off(0, 2 * t) : (uint32_t)(t * 32);
+  const uint32_t xoff1 = (kOne && lo) ? gu1_xlo_off(0, 2 * t + 1) : (uint32_t)(t * 32 + 16);
+  const float ia0 = lut_inv_alpha(0), ia1 = lut_inv_alpha(kUpTable);
   const int warp = threadIdx.x >> 5;
-  const int warp_global = blockIdx.x * kGuWarps + warp;
+  const int warp_global = blockIdx.x * GuCfg<kOne>::kWarps + warp;
   const int cps = (p.H >> 6) / UT;  // units per block
   const int total = count * cps;
   const int nw = stream_warps(count, cps, kMaxUnitsPerSlot, p.total_warps);
@@ -789,7 +821,7 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
   const int s_first = s;
   int j_seg = j;                    // the unit the current segment started at
   unsigned long long owed = 0ull;   // bit s - s_first: this warp finalizes block s
-  uint32_t xa = xs16_s + (uint32_t)(j * UT * 128 + t * 32);  // this lane's x fragment of the unit's first tile
+  uint32_t xa = xbase + (uint32_t)(j * UT) * xstride;  // the unit's first tile
   uint32_t xsa = xss_s + (uint32_t)(j * UT * 4);
   float acc[2][4] = {};
   uint32_t phase = 0;
@@ -813,16 +845,16 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
             tile.w[1][1] = lds_u4(sb + UT * 1024 + tt * 1024 + 512 + lane * 16);
             tile.am[0] = lds_f4(sb + UT * 2048 + tt * 128 + g * 16);
             tile.am[1] = lds_f4(sb + UT * 2048 + UT * 128 + tt * 128 + g * 16);
-            const uint4 x0 = lds_u4(xa + tt * 128), x1 = lds_u4(xa + tt * 128 + 16);
+            const uint4 x0 = lds_u4(xa + tt * xstride + xoff0), x1 = lds_u4(xa + tt * xstride + xoff1);
             const uint32_t bx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
             float xs;
             asm volatile("ld.shared.f32 %0, [%1];" : "=f"(xs) : "r"(xsa + tt * 4));
-            gu_tile_mma<kBase>(tile, bx, xs * ia0, xs * ia1, lb, acc);
+            gu_tile_mma<kBase, kUpTable>(tile, bx, xs * ia0, xs * ia1, lb, acc);
           }
           __syncwarp();
           if (q + kGuStages < q1) issue_next(st);
           ++q;
-          xa += UT * 128;
+          xa += UT * xstride;
           xsa += UT * 4;
           if (++j == cps || q == q1) {
             gu_flush(p, s, seg, g, t, acc);
@@ -837,7 +869,7 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
               j = 0;
               j_seg = 0;
               ++s;
-              xa = xs16_s + (uint32_t)(t * 32);
+              xa = xbase;
               xsa = xss_s;
             }
           }
@@ -930,37 +962,60 @@ __device__ __forceinline__ int gu_select_blocks(const GateUpParams& p, uint32_t*
 }
 static_assert(kGuWarps * kGuStages * kGuStageBytes >= kMaxNumBlocks * 4 + (int)sizeof(RadixSelectSmem),
               "the fused selection's keys must fit in the gate/up ring");
+static_assert(kGu1Warps * kGuStages * kGuStageBytes >= kMaxNumBlocks * 4 + (int)sizeof(RadixSelectSmem),
+              "the fused selection's keys must fit in the gate/up ring");
 
-__global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams p) {
+template <bool kOne>
+__global__ void __launch_bounds__(GuCfg<kOne>::kWarps * 32, 1) gateup_tma_kernel(GateUpParams p) {
+  using C = GuCfg<kOne>;
   char* smem = reinterpret_cast<char*>(g_lut_smem);
-  const uint32_t bar0 = smem_u32(smem + kGuBarOff);
-  const uint32_t xbar = bar0 + 8u * (uint32_t)(kGuWarps * kGuStages);
-  if (threadIdx.x <= kGuWarps * kGuStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
+  const uint32_t bar0 = smem_u32(smem + C::kBarOff);
+  const uint32_t xbar = bar0 + 8u * (uint32_t)(C::kWarps * kGuStages);
+  if (threadIdx.x <= C::kWarps * kGuStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
   mbar_init_fence();
   pdl_trigger();
-  build_lut_alpha(p.gate_code, p.up_code);
+  if (kOne) {
+    // the caller declared the codebooks equal: check it (a mismatch is an
+    // argument error, not a silently wrong up projection)
+    const int diff = threadIdx.x < 16 && __ldg(p.gate_code + threadIdx.x) != __ldg(p.up_code + threadIdx.x);
+    if (__syncthreads_or(diff)) {
+      if (threadIdx.x == 0) record_error(p.err, NSM_ERR_INVALID_ARG);
+      return;
+    }
+  }
+  build_lut_alpha(p.gate_code, kOne ? p.gate_code : p.up_code, !kOne);
   pdl_wait();  // rows, count, x16 come from the router kernels
   __half* xs16 = reinterpret_cast<__half*>(smem + kGuX16Off);
-  __half* xs16lo = reinterpret_cast<__half*>(smem + kGuX16LoOff);
-  float* xss = reinterpret_cast<float*>(smem + kGuXsOff);
-  int* srows = reinterpret_cast<int*>(smem + kGuRowsOff);
+  float* xss = reinterpret_cast<float*>(smem + C::kXsOff);
+  int* srows = reinterpret_cast<int*>(smem + C::kRowsOff);
+  const uint64_t xpol = l2_evict_last_policy();
   if (threadIdx.x == 0) {
-    // x16 and x16lo (written by the router kernel) arrive by bulk copy while
-    // the block selection runs
-    const uint64_t pol = l2_evict_last_policy();
+    // x16 (and x16lo, two tables) arrive by bulk copy while the block
+    // selection runs
     fence_proxy_async_global();
-    mbar_arrive_expect_tx(xbar, (uint32_t)p.H * 4u);
-    bulk_g2s(smem_u32(xs16), p.x16, (uint32_t)p.H * 2u, xbar, pol);
-    bulk_g2s(smem_u32(xs16lo), p.x16lo, (uint32_t)p.H * 2u, xbar, pol);
+    mbar_arrive_expect_tx(xbar, (uint32_t)p.H * (kOne ? 2u : 4u));
+    bulk_g2s(smem_u32(xs16), p.x16, (uint32_t)p.H * 2u, xbar, xpol);
+    if (!kOne) bulk_g2s(smem_u32(smem + kGuX16LoOff), p.x16lo, (uint32_t)p.H * 2u, xbar, xpol);
+  }
+  // shared codebook: x16lo goes to the free table halves by plain loads, all
+  // in flight before the selection and stored after it
+  constexpr int kLoPer = kOne ? (kStageXMaxHidden / 8 + C::kWarps * 32 - 1) / (C::kWarps * 32) : 1;
+  uint4 xlo[kLoPer];
+  if (kOne) {
+#pragma unroll
+    for (int u = 0; u < kLoPer; ++u) {
+      const int i = (int)threadIdx.x + u * (int)blockDim.x;
+      if (i < p.H / 8) xlo[u] = __ldcg(reinterpret_cast<const uint4*>(p.x16lo) + i);
+    }
   }
   for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
   const bool stage_rows = p.max_rows <= kStageRowsMax;
   int count;
   if (p.select) {
     // keys and selection scratch in the ring, which no copy has touched yet
-    uint32_t* keys = reinterpret_cast<uint32_t*>(smem + kGuRingOff);
+    uint32_t* keys = reinterpret_cast<uint32_t*>(smem + C::kRingOff);
     RadixSelectSmem* sel =
-        reinterpret_cast<RadixSelectSmem*>(smem + kGuRingOff + (((size_t)p.NB * 4 + 127) & ~(size_t)127));
+        reinterpret_cast<RadixSelectSmem*>(smem + C::kRingOff + (((size_t)p.NB * 4 + 127) & ~(size_t)127));
     count = gu_select_blocks(p, keys, *sel, srows);
   } else {
     // the pool rows go out with the count (up to the capacity; rows past the
@@ -968,6 +1023,13 @@ __global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams 
     count = *p.count_ptr;
     if (stage_rows)
       for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
+  }
+  if (kOne) {
+#pragma unroll
+    for (int u = 0; u < kLoPer; ++u) {
+      const int i = (int)threadIdx.x + u * (int)blockDim.x;
+      if (i < p.H / 8) *reinterpret_cast<uint4*>(smem + gu1_xlo_off(i >> 3, i & 7)) = xlo[u];
+    }
   }
   bool x_late = false;
   if (threadIdx.x == 0 && !mbar_wait(xbar, 0, p.wait_spins)) {
@@ -978,11 +1040,12 @@ __global__ void __launch_bounds__(kGuThreads, 1) gateup_tma_kernel(GateUpParams 
   if (__syncthreads_or(x_late)) return;
   const int* rows = stage_rows ? srows : p.rows;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
-  const uint32_t ring = smem_u32(smem + kGuRingOff);
+  const uint32_t ring = smem_u32(smem + C::kRingOff);
+  const uint32_t xlo_s = kOne ? smem_u32(smem) : smem_u32(smem + kGuX16LoOff);
   if (lut_base_addr() == 0x400u)
-    gateup_tma_body<0x400>(p, lb, smem_u32(xs16), smem_u32(xs16lo), smem_u32(xss), rows, count, ring, bar0);
+    gateup_tma_body<0x400, kOne>(p, lb, smem_u32(xs16), xlo_s, smem_u32(xss), rows, count, ring, bar0);
   else
-    gateup_tma_body<-1>(p, lb, smem_u32(xs16), smem_u32(xs16lo), smem_u32(xss), rows, count, ring, bar0);
+    gateup_tma_body<-1, kOne>(p, lb, smem_u32(xs16), xlo_s, smem_u32(xss), rows, count, ring, bar0);
 }
 
 // Down, bulk-copy variant: a pair is (64-row group rp, slot s) = two adjacent
@@ -1161,6 +1224,7 @@ struct KernelSetup {
   int gu[2][2] = {{0, 0}, {0, 0}};  // [tiled][staged] CTAs per SM
   int dn[2][2] = {{0, 0}, {0, 0}};
   int gu_tma = 0;  // CTAs per SM of the bulk-copy variants (1 when they fit)
+  int gu_tma1 = 0;  // ... of the shared-codebook gate/up variant
   int dn_tma = 0;
 };
 static KernelSetup g_setup[64];
@@ -1184,7 +1248,8 @@ static int setup_kernels(const DeviceInfo& d, KernelSetup** out) {
     if (!st) st = setup_one(down_kernel<false, true>, kDownSmemStaged, &s.dn[0][1]);
     if (!st) st = setup_one(down_kernel<true, false>, kSmemHead, &s.dn[1][0]);
     if (!st) st = setup_one(down_kernel<true, true>, kDownSmemStaged, &s.dn[1][1]);
-    if (!st) st = setup_one(gateup_tma_kernel, kGuTmaSmem, &s.gu_tma, kGuThreads);
+    if (!st) st = setup_one(gateup_tma_kernel<false>, kGuTmaSmem, &s.gu_tma, kGuThreads);
+    if (!st) st = setup_one(gateup_tma_kernel<true>, kGu1TmaSmem, &s.gu_tma1, kGu1Threads);
     if (!st) st = setup_one(down_tma_kernel, kDnTmaSmem, &s.dn_tma, kTmaThreads);
     if (!st) st = router_setup();
     if (st) return st;
@@ -1313,11 +1378,13 @@ static int launch_mlp(const MlpPlan& m, const DecodeWs& ws, cudaStream_t stream)
   cudaError_t e;
   gp.unit_tiles = 1;
   if (gu_tma) {
+    const bool one = (w->layout & NSM_LAYOUT_SHARED_CODE) != 0 && ks->gu_tma1 > 0;
     gp.unit_tiles = kGuUnitTiles;
-    gp.total_warps = dev.sm_count * kGuWarps;
+    gp.total_warps = dev.sm_count * (one ? kGu1Warps : kGuWarps);
     gp.fused_finalize = 1;
     gp.gu_ticket = ws.gu_ticket;
-    e = launch_pdl(gateup_tma_kernel, dev.sm_count, kGuThreads, kGuTmaSmem, stream, gp);
+    if (one) e = launch_pdl(gateup_tma_kernel<true>, dev.sm_count, kGu1Threads, kGu1TmaSmem, stream, gp);
+    else e = launch_pdl(gateup_tma_kernel<false>, dev.sm_count, kGuThreads, kGuTmaSmem, stream, gp);
   } else {
   const int gu_ctas = dev.sm_count * ks->gu[gu_tiled][gu_stage];
   gp.total_warps = gu_ctas * (kMlpThreads / 32);

@@ -67,7 +67,8 @@ __device__ __forceinline__ float lut_inv_alpha(int t) { return lut_alpha_smem()[
 // candidates i, i + blockDim.x, ... of the 512 (two tables x 256); the best of
 // each 32-candidate chunk goes to the pair scratch, then warps 0 and 1 reduce
 // the chunks of tables 0 and 1.  Every thread of the CTA (at least 64) takes part.
-__device__ __forceinline__ void build_lut_alpha(const float* code0, const float* code1) {
+// both = false: table 0 only (the second table's words are left untouched).
+__device__ __forceinline__ void build_lut_alpha(const float* code0, const float* code1, bool both = true) {
   float* al = lut_alpha_smem();
   float* werr = reinterpret_cast<float*>(g_lut_smem + kLutBytes / 4);  // [2][32] best error per chunk
   int* widx = reinterpret_cast<int*>(werr + 64);                      // [2][32] its candidate
@@ -140,6 +141,7 @@ __device__ __forceinline__ void build_lut_alpha(const float* code0, const float*
   __syncthreads();
   uint4* lut4 = reinterpret_cast<uint4*>(g_lut_smem);
   for (int i = threadIdx.x; i < 256 * kLutWordsPerEntry / 4; i += blockDim.x) {
+    if (!both && ((i >> 3) & 1)) continue;
     const uint32_t v = pairs[((i >> 3) & 1) * 256 + (i >> 4)];
     lut4[i] = make_uint4(v, v, v, v);
   }

@@ -675,7 +675,8 @@ int nsm_union_decode(const void* x, int32_t x_dtype, int32_t rows, int32_t hidde
   NSM_REQUIRE(k > 0, NSM_ERR_INVALID_ARG, "k must be > 0");
   NSM_REQUIRE(x && idx && w && y, NSM_ERR_INVALID_ARG, "NULL pointer");
   NSM_REQUIRE(dtype_ok(x_dtype) && dtype_ok(y_dtype), NSM_ERR_INVALID_ARG, "bad x or y dtype");
-  NSM_REQUIRE(w->layout == (NSM_LAYOUT_GATEUP_TILED | NSM_LAYOUT_DOWN_TILED), NSM_ERR_UNSUPPORTED,
+  const int tiled = NSM_LAYOUT_GATEUP_TILED | NSM_LAYOUT_DOWN_TILED;
+  NSM_REQUIRE((w->layout & tiled) == tiled, NSM_ERR_UNSUPPORTED,
               "the union decode reads tiled gate/up and down pools");
   NSM_REQUIRE(!w->gate_bias && !w->up_bias && !w->down_bias, NSM_ERR_UNSUPPORTED,
               "the union decode does not take biases");

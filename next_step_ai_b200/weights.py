@@ -144,6 +144,12 @@ class SparseMlpWeights:
     layout: int = 0
     _c: object = field(default=None, repr=False)
 
+    def __post_init__(self) -> None:
+        # equal gate and up codebooks (the standard NF4 one) let the tiled gate/up
+        # kernel use one lookup table and more warps; checked once here, on the host
+        self._shared_code = bool(self.gate_code.shape == self.up_code.shape
+                                 and torch.equal(self.gate_code, self.up_code))
+
     @property
     def pool_rows(self) -> int:
         return int(self.gate_packed.shape[0])
@@ -175,7 +181,7 @@ class SparseMlpWeights:
         c.down_row_stride = 16
         c.down_absmax_block_stride = int(self.down_absmax.stride(0))
         c.down_absmax_row_stride = 1
-        c.layout = int(self.layout)
+        c.layout = int(self.layout) | (_lib.NSM_LAYOUT_SHARED_CODE if self._shared_code else 0)
         self._c = c
         return c
 

@@ -630,3 +630,61 @@ def test_no_kernel_recorded_a_wait_timeout(dev):
     torch.cuda.synchronize()
     errs = WORKSPACES.errors()
     assert errs and all(v == 0 for v in errs.values()), errs
+
+
+# --------------------------------------------------------------------------- codebooks
+def _scaled_code_layer(name, seed, dev):
+    """A layer whose up projection uses a different 16-value codebook (the
+    stored nibbles are unchanged, so only the dequantised up values differ)."""
+    from next_step_ai_b200 import SparseMlpWeights
+
+    shape = syn.SHAPES[name]
+    full = full_layer(name, seed)
+    code = full["code"]
+    up_code = (code * np.float32(0.75)).astype(np.float32)
+    w = SparseMlpWeights.from_bnb_rowmajor(
+        hidden=shape.hidden, intermediate=shape.intermediate, gate_packed=T(full["gate_packed"], dev),
+        gate_absmax=T(full["gate_absmax"], dev), up_packed=T(full["up_packed"], dev),
+        up_absmax=T(full["up_absmax"], dev), down_packed=T(full["down_packed"], dev),
+        down_absmax=T(full["down_absmax"], dev), code=T(code, dev), up_code=T(up_code, dev))
+    return shape, full, code, up_code, w
+
+
+def test_distinct_up_codebook_uses_two_tables(dev):
+    """Gate and up codebooks that differ: the tiled gate/up kernel keeps two
+    lookup tables (the shared-codebook variant does not apply) and matches the
+    oracle evaluated with each projection's own codebook."""
+    from next_step_ai_b200 import sparse_mlp_decode
+
+    shape, full, code, up_code, w = _scaled_code_layer("small", 14, dev)
+    assert not w._shared_code
+    H, I = shape.hidden, shape.intermediate
+    gm, dm = om.Nf4ParamMeta(I, H), om.Nf4ParamMeta(H, I)
+    rng = np.random.default_rng(5)
+    for _ in range(2):
+        x = syn.make_x(shape, int(rng.integers(1 << 30)), 1)[0]
+        blocks = np.sort(rng.choice(shape.num_blocks, shape.top_k, replace=False)).astype(np.int64)
+        y = sparse_mlp_decode(T(x, dev, torch.bfloat16), None, w, idx=T(blocks.astype(np.int32), dev),
+                              out_dtype=torch.float32)
+        gp, ga = om.gather_row_blocks(full["gate_packed"], full["gate_absmax"], gm, blocks)
+        upk, ua = om.gather_row_blocks(full["up_packed"], full["up_absmax"], gm, blocks)
+        dc, da = om.gather_down_cols(full["down_packed"], full["down_absmax"], dm, blocks)
+        ref = om.sparse_mlp_gathered(np.asarray(x, np.float32).reshape(1, -1), gp, ga, code, upk, ua, up_code,
+                                     dc, da, code)[0]
+        assert_close(y.cpu().numpy(), ref)
+
+
+def test_false_shared_codebook_claim_is_rejected(dev):
+    """NSM_LAYOUT_SHARED_CODE on weights whose codebooks differ: the gate/up
+    kernel checks the claim, records NSM_ERR_INVALID_ARG and computes nothing."""
+    from next_step_ai_b200 import _lib, sparse_mlp_decode
+    from next_step_ai_b200._torch import WORKSPACES
+
+    shape, full, code, up_code, w = _scaled_code_layer("small", 15, dev)
+    WORKSPACES.errors()  # start clean
+    w._shared_code = True  # the false claim
+    x = syn.make_x(shape, 3, 1)[0]
+    blocks = np.arange(shape.top_k, dtype=np.int32)
+    sparse_mlp_decode(T(x, dev, torch.bfloat16), None, w, idx=T(blocks, dev), out_dtype=torch.float32)
+    errs = list(WORKSPACES.errors().values())
+    assert _lib.NSM_ERR_INVALID_ARG in errs, errs
