@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(256) down_finalize_kernel(DownParams p) {
 template <bool kTiled, bool kStage>
 __global__ void __launch_bounds__(kMlpThreads, 2) down_kernel(DownParams p) {
   pdl_trigger();
-  build_lut_alpha(p.down_code, p.down_code);
+  build_lut_alpha(p.down_code, p.down_code, false);  // the down loops read table 0 only
   pdl_wait();  // act16 / act_scale come from the gate/up kernel
   record_down_meta(p);
   const int count = *p.count_ptr;
@@ -1174,7 +1174,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) down_tma_kernel(DownParams p) 
   if (threadIdx.x <= kTmaWarps * kDnStages) mbar_init(bar0 + 8u * threadIdx.x, 1);
   mbar_init_fence();
   pdl_trigger();
-  build_lut_alpha(p.down_code, p.down_code);
+  build_lut_alpha(p.down_code, p.down_code, false);  // the down loops read table 0 only
   pdl_wait();  // act16 / act_scale come from the gate/up kernels
   record_down_meta(p);
   const int count = *p.count_ptr;

@@ -67,7 +67,8 @@ __device__ __forceinline__ float lut_inv_alpha(int t) { return lut_alpha_smem()[
 // candidates i, i + blockDim.x, ... of the 512 (two tables x 256); the best of
 // each 32-candidate chunk goes to the pair scratch, then warps 0 and 1 reduce
 // the chunks of tables 0 and 1.  Every thread of the CTA (at least 64) takes part.
-// both = false: table 0 only (the second table's words are left untouched).
+// both = false: table 0 only (code1 is ignored, the second table's words are
+// left untouched and lut_inv_alpha(1) reads table 0's).
 __device__ __forceinline__ void build_lut_alpha(const float* code0, const float* code1, bool both = true) {
   float* al = lut_alpha_smem();
   float* werr = reinterpret_cast<float*>(g_lut_smem + kLutBytes / 4);  // [2][32] best error per chunk
@@ -78,7 +79,8 @@ __device__ __forceinline__ void build_lut_alpha(const float* code0, const float*
     widx[i] = 256;
   }
   __syncthreads();
-  for (int i0 = 0; i0 < 512; i0 += (int)blockDim.x) {
+  const int ncand = both ? 512 : 256;
+  for (int i0 = 0; i0 < ncand; i0 += (int)blockDim.x) {
     const int i = i0 + (int)threadIdx.x;
     const int t = (i >> 8) & 1, ci = i & 255;
     const float* c = t == 0 ? code0 : code1;
@@ -91,7 +93,7 @@ __device__ __forceinline__ void build_lut_alpha(const float* code0, const float*
       const float d = __half2float(__float2half_rn(a * ck)) * ia - ck;
       e = fmaf(d, d, e);
     }
-    if (i >= 512) e = 3.0e38f;
+    if (i >= ncand) e = 3.0e38f;
     // best (smallest error, then smallest candidate) of the warp's 32; a warp
     // covers one table (32 divides 256)
     int bi = ci;
@@ -104,13 +106,13 @@ __device__ __forceinline__ void build_lut_alpha(const float* code0, const float*
         bi = oi;
       }
     }
-    if (lane == 0 && i < 512) {  // one slot per 32-candidate chunk of a table
+    if (lane == 0 && i < ncand) {  // one slot per 32-candidate chunk of a table
       werr[t * 32 + (ci >> 5)] = e;
       widx[t * 32 + (ci >> 5)] = bi;
     }
   }
   __syncthreads();
-  if (warp < 2) {
+  if (warp < (both ? 2 : 1)) {
     float e = werr[warp * 32 + lane];
     int bi = widx[warp * 32 + lane];
 #pragma unroll
@@ -126,11 +128,15 @@ __device__ __forceinline__ void build_lut_alpha(const float* code0, const float*
       const float a = 1.f + (float)bi * (1.f / 256.f);
       al[warp] = a;
       al[2 + warp] = 1.f / a;
+      if (!both) {
+        al[1] = a;
+        al[3] = 1.f / a;
+      }
     }
   }
   __syncthreads();
   uint32_t* pairs = g_lut_smem + kLutBytes / 4;  // scratch [2][256]
-  for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+  for (int i = threadIdx.x; i < ncand; i += blockDim.x) {
     const int t = i >> 8, e = i & 255;
     const float* c = t == 0 ? code0 : code1;
     const float a = al[t];
