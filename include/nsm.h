@@ -5,9 +5,10 @@
  * returns an int status (NSM_OK == 0, negative on error), never throws,
  * never allocates device memory, and is ordered on the given stream.  Scratch
  * memory is a caller-owned workspace whose size is returned by the matching
- * *_workspace_bytes() query.  A workspace must be zero-filled once before
- * its first use (nsm_workspace_init); every call leaves its counters zero
- * again.  Calls that share one workspace must not overlap on the GPU.
+ * *_workspace_bytes() query; its address must be 256-byte aligned (as every
+ * CUDA allocation is), else the call returns NSM_ERR_WORKSPACE.  A workspace
+ * must be zero-filled once before its first use (nsm_workspace_init); every
+ * call leaves its counters zero again.  Calls that share one workspace must not overlap on the GPU.
  *
  * The reference (andott28/next_step_ai) has no native code: its hot path is
  * Python + Triton.  Each declaration below names the reference interface it
@@ -37,7 +38,7 @@ typedef struct CUstream_st* nsm_stream_t; /* == cudaStream_t */
 #define NSM_ERR_UNSUPPORTED (-2)   /* shape outside the supported set     */
 #define NSM_ERR_CUDA (-3)          /* a CUDA runtime call failed          */
 #define NSM_ERR_TIMEOUT (-4)       /* a bounded device wait gave up       */
-#define NSM_ERR_WORKSPACE (-5)     /* workspace missing or too small      */
+#define NSM_ERR_WORKSPACE (-5)     /* workspace missing, misaligned or too small */
 #define NSM_ERR_DEVICE (-6)        /* device is not sm_100 / not present  */
 
 /* ---- element types --------------------------------------------------- */

@@ -119,7 +119,7 @@ const char* nsm_status_string(int status) {
     case NSM_ERR_UNSUPPORTED: return "unsupported shape";
     case NSM_ERR_CUDA: return "CUDA error";
     case NSM_ERR_TIMEOUT: return "device wait timed out";
-    case NSM_ERR_WORKSPACE: return "workspace missing or too small";
+    case NSM_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
     case NSM_ERR_DEVICE: return "unsupported device";
     default: return "unknown status";
   }

@@ -671,6 +671,10 @@ constexpr int kGu1BarOff = kGu1RingOff + kGu1Warps * kGuStages * kGuStageBytes;
 constexpr int kGu1TmaSmem = kGu1BarOff + (kGu1Warps * kGuStages + 1) * 8;
 static_assert(kGu1TmaSmem <= 227 * 1024, "gate/up ring (shared codebook) does not fit in shared memory");
 static_assert(kGu1RingOff % 128 == 0, "rings must be 128-byte aligned");
+// x16lo's staging in the ring (shared codebook), past the selection's scratch
+constexpr int kGu1XloStageOff = 40 * 1024;
+static_assert(kGu1XloStageOff + kStageXMaxHidden * 2 <= kGu1Warps * kGuStages * kGuStageBytes,
+              "x16lo staging must fit in the gate/up ring");
 static_assert(kStageXMaxHidden / 64 <= 256, "x16lo needs one lookup entry per 64-column tile");
 template <bool kOne> struct GuCfg {
   static constexpr int kWarps = kOne ? kGu1Warps : kGuWarps;
@@ -960,6 +964,96 @@ __device__ __forceinline__ int gu_select_blocks(const GateUpParams& p, uint32_t*
   if (blockIdx.x == 0 && tid == 0) *p.count_out = tot;
   return tot;
 }
+// The same selection with the keys in registers (NB <= kSelKeysPerThread *
+// blockDim), in two steps so that the score loads leave first:
+// gu_select_load issues them (coalesced: every CTA reads the same lines), and
+// gu_select_finish stores the keys, hands thread t the blocks [t * per,
+// t * per + per) through shared memory (so one scan of the per-thread counts
+// gives the block-id order), and selects with one barrier per radix pass and
+// one per scan (block_select_reg, block_exclusive_scan_1b).
+constexpr int kSelKeysPerThread = 8;
+struct GuSelectSmem {
+  RegSelectSmem sel;
+  uint32_t keys[kSelKeysPerThread * 32 * 32];  // blockDim <= 1024
+};
+__device__ __forceinline__ void gu_select_load(const GateUpParams& p, float (&v)[kSelKeysPerThread]) {
+#pragma unroll
+  for (int j = 0; j < kSelKeysPerThread; ++j) {
+    const int i = (int)threadIdx.x + j * (int)blockDim.x;
+    v[j] = i < p.NB ? ldcg_f32(p.scores + i) : 0.f;
+  }
+}
+__device__ __forceinline__ int gu_select_finish(const GateUpParams& p, const float (&v)[kSelKeysPerThread],
+                                                GuSelectSmem& G, int* srows) {
+  constexpr int KPT = kSelKeysPerThread;
+  RegSelectSmem& S = G.sel;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = (int)(blockDim.x >> 5), NB = p.NB;
+  uint32_t kor = 0u, kand = 0xffffffffu;
+#pragma unroll
+  for (int j = 0; j < KPT; ++j) {
+    const int i = tid + j * (int)blockDim.x;
+    if (i < NB) {
+      const uint32_t key = orderable(v[j]);
+      G.keys[i] = key;
+      kor |= key;
+      kand &= key;
+    }
+  }
+  kor = __reduce_or_sync(0xffffffffu, kor);
+  kand = __reduce_and_sync(0xffffffffu, kand);
+  if (lane == 0) {
+    S.s_or[warp] = kor;
+    S.s_and[warp] = kand;
+  }
+  for (int i = tid; i < 512; i += (int)blockDim.x) (&S.hists[0][0])[i] = 0;
+  __syncthreads();
+  const uint32_t o = __reduce_or_sync(0xffffffffu, lane < nw ? S.s_or[lane] : 0u);
+  const uint32_t a = __reduce_and_sync(0xffffffffu, lane < nw ? S.s_and[lane] : 0xffffffffu);
+  const int per = (NB + (int)blockDim.x - 1) / (int)blockDim.x;  // <= KPT (the caller checks)
+  const int lo = min(NB, tid * per), cnt = min(NB, lo + per) - lo;
+  uint32_t key[KPT];
+#pragma unroll
+  for (int u = 0; u < KPT; ++u) key[u] = u < cnt ? G.keys[lo + u] : 0u;
+  const RegSelection r = block_select_reg<KPT>(key, cnt, NB, p.top_k, o, a, S);
+  int tot, eq_before = 0;
+  if (r.split) {  // a tie at the threshold is split: rank the equal keys by block id
+    int n_eq = 0;
+#pragma unroll
+    for (int u = 0; u < KPT; ++u) n_eq += u < cnt && key[u] == r.thr;
+    eq_before = block_exclusive_scan_1b(n_eq, &tot, S.wtot[0]);
+  }
+  unsigned selmask = 0u;
+  int m = 0;
+#pragma unroll
+  for (int u = 0, e = eq_before; u < KPT; ++u) {
+    if (u < cnt) {
+      const bool sel = key[u] > r.thr || (key[u] == r.thr && (!r.split || e++ < r.take_eq));
+      if (sel && gu_map_block(p, lo + u) >= 0) {
+        selmask |= 1u << u;
+        ++m;
+      }
+    }
+  }
+  int pos = block_exclusive_scan_1b(m, &tot, S.wtot[1]);
+#pragma unroll
+  for (int u = 0; u < KPT; ++u) {
+    if ((selmask >> u) & 1u) {
+      const int row = gu_map_block(p, lo + u);
+      srows[pos] = row;
+      if (blockIdx.x == 0) {
+        p.rows_out[pos] = row;
+        p.row_block_out[pos] = lo + u;
+      }
+      ++pos;
+    }
+  }
+  if (blockIdx.x == 0 && tid == 0) *p.count_out = tot;
+  return tot;
+}
+static_assert(kGu1XloStageOff >= (int)sizeof(GuSelectSmem), "x16lo staging overlaps the selection scratch");
+static_assert(kGu1Warps * kGuStages * kGuStageBytes >= (int)sizeof(GuSelectSmem) &&
+                  kGuWarps * kGuStages * kGuStageBytes >= (int)sizeof(GuSelectSmem),
+              "the register selection's scratch must fit in the gate/up ring");
 static_assert(kGuWarps * kGuStages * kGuStageBytes >= kMaxNumBlocks * 4 + (int)sizeof(RadixSelectSmem),
               "the fused selection's keys must fit in the gate/up ring");
 static_assert(kGu1Warps * kGuStages * kGuStageBytes >= kMaxNumBlocks * 4 + (int)sizeof(RadixSelectSmem),
@@ -989,34 +1083,38 @@ __global__ void __launch_bounds__(GuCfg<kOne>::kWarps * 32, 1) gateup_tma_kernel
   float* xss = reinterpret_cast<float*>(smem + C::kXsOff);
   int* srows = reinterpret_cast<int*>(smem + C::kRowsOff);
   const uint64_t xpol = l2_evict_last_policy();
+  // the block selection's score loads leave before the x copies (they gate
+  // the selection; every CTA reads the same lines)
+  const bool reg_select = p.select && p.NB <= kSelKeysPerThread * (int)blockDim.x;
+  float sv[kSelKeysPerThread];
+  if (reg_select) gu_select_load(p, sv);
+  // x16, x16lo and the x scales arrive by bulk copy while the block selection
+  // runs (no thread waits on a global load before the selection); with a
+  // shared codebook x16lo lands in the ring past the selection's scratch and
+  // moves to the free table halves after it
+  const bool xs_bulk = (p.H & 255) == 0;  // the scales' bytes (H / 16) a multiple of 16
+  char* xlo_dst = kOne ? smem + C::kRingOff + kGu1XloStageOff : smem + kGuX16LoOff;
   if (threadIdx.x == 0) {
-    // x16 (and x16lo, two tables) arrive by bulk copy while the block
-    // selection runs
     fence_proxy_async_global();
-    mbar_arrive_expect_tx(xbar, (uint32_t)p.H * (kOne ? 2u : 4u));
+    mbar_arrive_expect_tx(xbar, (uint32_t)p.H * 4u + (xs_bulk ? (uint32_t)p.H / 16u : 0u));
     bulk_g2s(smem_u32(xs16), p.x16, (uint32_t)p.H * 2u, xbar, xpol);
-    if (!kOne) bulk_g2s(smem_u32(smem + kGuX16LoOff), p.x16lo, (uint32_t)p.H * 2u, xbar, xpol);
+    bulk_g2s(smem_u32(xlo_dst), p.x16lo, (uint32_t)p.H * 2u, xbar, xpol);
+    if (xs_bulk) bulk_g2s(smem_u32(xss), p.xscale, (uint32_t)p.H / 16u, xbar, xpol);
   }
-  // shared codebook: x16lo goes to the free table halves by plain loads, all
-  // in flight before the selection and stored after it
-  constexpr int kLoPer = kOne ? (kStageXMaxHidden / 8 + C::kWarps * 32 - 1) / (C::kWarps * 32) : 1;
-  uint4 xlo[kLoPer];
-  if (kOne) {
-#pragma unroll
-    for (int u = 0; u < kLoPer; ++u) {
-      const int i = (int)threadIdx.x + u * (int)blockDim.x;
-      if (i < p.H / 8) xlo[u] = __ldcg(reinterpret_cast<const uint4*>(p.x16lo) + i);
-    }
-  }
-  for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
+  if (!xs_bulk)
+    for (int i = threadIdx.x; i < p.H / 64; i += blockDim.x) xss[i] = __ldcg(p.xscale + i);
   const bool stage_rows = p.max_rows <= kStageRowsMax;
   int count;
   if (p.select) {
     // keys and selection scratch in the ring, which no copy has touched yet
-    uint32_t* keys = reinterpret_cast<uint32_t*>(smem + C::kRingOff);
-    RadixSelectSmem* sel =
-        reinterpret_cast<RadixSelectSmem*>(smem + C::kRingOff + (((size_t)p.NB * 4 + 127) & ~(size_t)127));
-    count = gu_select_blocks(p, keys, *sel, srows);
+    if (reg_select) {
+      count = gu_select_finish(p, sv, *reinterpret_cast<GuSelectSmem*>(smem + C::kRingOff), srows);
+    } else {
+      uint32_t* keys = reinterpret_cast<uint32_t*>(smem + C::kRingOff);
+      RadixSelectSmem* sel =
+          reinterpret_cast<RadixSelectSmem*>(smem + C::kRingOff + (((size_t)p.NB * 4 + 127) & ~(size_t)127));
+      count = gu_select_blocks(p, keys, *sel, srows);
+    }
   } else {
     // the pool rows go out with the count (up to the capacity; rows past the
     // count are never read)
@@ -1024,19 +1122,17 @@ __global__ void __launch_bounds__(GuCfg<kOne>::kWarps * 32, 1) gateup_tma_kernel
     if (stage_rows)
       for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) srows[i] = __ldcg(p.rows + i);
   }
-  if (kOne) {
-#pragma unroll
-    for (int u = 0; u < kLoPer; ++u) {
-      const int i = (int)threadIdx.x + u * (int)blockDim.x;
-      if (i < p.H / 8) *reinterpret_cast<uint4*>(smem + gu1_xlo_off(i >> 3, i & 7)) = xlo[u];
-    }
-  }
+  // shared codebook: every thread waits for the copies and moves its chunks
+  // of x16lo into the table holes (the ring is free until the next barrier)
   bool x_late = false;
-  if (threadIdx.x == 0 && !mbar_wait(xbar, 0, p.wait_spins)) {
+  if ((kOne || threadIdx.x == 0) && !mbar_wait(xbar, 0, p.wait_spins)) {
     record_error(p.err, NSM_ERR_TIMEOUT);
     mbar_wait(xbar, 0);  // the copies land before the CTA leaves
     x_late = true;
   }
+  if (kOne && !x_late)
+    for (int i = threadIdx.x; i < p.H / 8; i += blockDim.x)
+      *reinterpret_cast<uint4*>(smem + gu1_xlo_off(i >> 3, i & 7)) = reinterpret_cast<const uint4*>(xlo_dst)[i];
   if (__syncthreads_or(x_late)) return;
   const int* rows = stage_rows ? srows : p.rows;
   const uint32_t lb = (threadIdx.x & 31) * 4u;
@@ -1564,7 +1660,7 @@ int nsm_route(const void* x, int32_t x_dtype, int32_t hidden, const nsm_router_w
   NSM_REQUIRE(k <= kMaxTopK, NSM_ERR_UNSUPPORTED, "top_k too large");
   const int I = rw->num_blocks * 32;
   const size_t need = decode_ws_layout(nullptr, hidden, I, k, rw->rank).bytes;
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_route");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, NSM_ERR_WORKSPACE, "nsm_route: workspace missing, not 256-byte aligned or too small");
   DecodeWs w = decode_ws_layout(ws, hidden, I, k, rw->rank);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   KernelSetup* ks;
@@ -1591,7 +1687,7 @@ int nsm_route_rows(const void* x, int32_t x_dtype, int32_t rows, int32_t hidden,
   NSM_REQUIRE(k <= kMaxTopK, NSM_ERR_UNSUPPORTED, "top_k too large");
   const int I = rw->num_blocks * 32;
   const size_t need = decode_ws_layout(nullptr, hidden, I, k, rw->rank, rows).bytes;
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_route_rows");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, NSM_ERR_WORKSPACE, "nsm_route_rows: workspace missing, not 256-byte aligned or too small");
   DecodeWs w = decode_ws_layout(ws, hidden, I, k, rw->rank, rows);
   KernelSetup* ks;
   st = setup_kernels(dev, &ks);
@@ -1640,7 +1736,7 @@ int nsm_sparse_mlp_decode(const void* x, int32_t x_dtype, int32_t hidden, int32_
   if (rw) rank = std::max(rank, rw->rank);
   NSM_REQUIRE(k <= kMaxTopK, NSM_ERR_UNSUPPORTED, "top_k too large");
   const size_t need = decode_ws_layout(nullptr, hidden, intermediate, k, rank).bytes;
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_sparse_mlp_decode");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, NSM_ERR_WORKSPACE, "nsm_sparse_mlp_decode: workspace missing, not 256-byte aligned or too small");
   DecodeWs wsl = decode_ws_layout(ws, hidden, intermediate, k, rank);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   KernelSetup* ks;
@@ -1702,7 +1798,7 @@ int nsm_residual_flush(int32_t hidden, const nsm_layer_io* io, void* ws, size_t 
   if (io->exchange) NSM_REQUIRE(exchange_dev(io->exchange)->hidden == hidden && exchange_dev(io->exchange)->data[0],
                                 NSM_ERR_INVALID_ARG, "exchange not connected or built for another hidden size");
   const size_t need = decode_ws_layout(nullptr, hidden, 64, 1, 1).bytes;
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_residual_flush");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, NSM_ERR_WORKSPACE, "nsm_residual_flush: workspace missing, not 256-byte aligned or too small");
   DecodeWs wsl = decode_ws_layout(ws, hidden, 64, 1, 1);
   return router_a_prepare(nullptr, 0, io, nullptr, hidden, wsl, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -1725,7 +1821,7 @@ int nsm_decode_gathered(const void* x, int32_t x_dtype, int32_t hidden, int32_t 
   const int k = num_blocks_gathered;
   const int I = 64 * ((k * 32 + 63) / 64);
   const size_t need = decode_ws_layout(nullptr, hidden, I, k, 1).bytes;
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_decode_gathered");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, NSM_ERR_WORKSPACE, "nsm_decode_gathered: workspace missing, not 256-byte aligned or too small");
   DecodeWs wsl = decode_ws_layout(ws, hidden, I, k, 1);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   KernelSetup* ks;
@@ -1776,7 +1872,7 @@ int nsm_decode_gathered_rows(const void* x, int32_t x_dtype, int32_t rows, int32
   const int k = num_blocks_gathered;
   const int I = 64 * ((k * 32 + 63) / 64);
   const size_t need = decode_ws_layout(nullptr, hidden, I, k, 1).bytes;
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace missing, not 256-byte aligned or too small");
   DecodeWs wsl = decode_ws_layout(ws, hidden, I, k, 1);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   KernelSetup* ks;

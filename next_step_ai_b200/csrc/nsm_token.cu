@@ -1305,7 +1305,7 @@ int nsm_token_set_layers(void* ws, size_t ws_bytes, int32_t hidden, int32_t inte
   NSM_REQUIRE(layers != nullptr && num_layers > 0, NSM_ERR_INVALID_ARG, "nsm_token_set_layers: no layers");
   const int NB = intermediate / 32;
   const TkWs w = tk_ws_layout(ws, hidden, NB, num_layers);
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= w.bytes, NSM_ERR_WORKSPACE,
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= w.bytes, NSM_ERR_WORKSPACE,
               "nsm_token_set_layers: workspace smaller than nsm_token_workspace_bytes");
   std::vector<TkLayer> dl((size_t)num_layers);
   for (int i = 0; i < num_layers; ++i) {
@@ -1381,7 +1381,7 @@ int nsm_token_profile(void* ws, size_t ws_bytes, int32_t hidden, int32_t interme
                       unsigned long long* stamps, int32_t stamp_layers, nsm_stream_t stream) {
   NSM_REQUIRE(hidden > 0 && intermediate > 0 && num_layers > 0, NSM_ERR_INVALID_ARG, "nsm_token_profile: bad shape");
   const TkWs w = tk_ws_layout(ws, hidden, intermediate / 32, num_layers);
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= w.bytes, NSM_ERR_WORKSPACE, "nsm_token_profile: workspace too small");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= w.bytes, NSM_ERR_WORKSPACE, "nsm_token_profile: workspace missing, not 256-byte aligned or too small");
   NSM_REQUIRE(stamps == nullptr || stamp_layers > 0, NSM_ERR_INVALID_ARG, "nsm_token_profile: stamp_layers <= 0");
   unsigned long long* sp = stamps;
   int n = stamps ? stamp_layers : 0;
@@ -1405,7 +1405,7 @@ int nsm_decode_token(float* residual, int32_t hidden, int32_t intermediate, int3
   NSM_REQUIRE(trace_blocks == nullptr || trace_k > 0, NSM_ERR_INVALID_ARG, "nsm_decode_token: trace_k must be > 0");
   const int NB = intermediate / 32;
   const TkWs w = tk_ws_layout(ws, hidden, NB, num_layers);
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= w.bytes, NSM_ERR_WORKSPACE,
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= w.bytes, NSM_ERR_WORKSPACE,
               "nsm_decode_token: workspace smaller than nsm_token_workspace_bytes");
   st = tk_setup(dev);
   if (st) return st;

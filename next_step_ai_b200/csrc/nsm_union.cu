@@ -689,7 +689,7 @@ int nsm_union_decode(const void* x, int32_t x_dtype, int32_t rows, int32_t hidde
   const int NB = intermediate / 32;
   const int umax = std::min(NB, rows * k);
   const size_t need = union_ws_layout(nullptr, hidden, umax).bytes;
-  NSM_REQUIRE(ws != nullptr && ws_bytes >= need, NSM_ERR_WORKSPACE, "workspace too small for nsm_union_decode");
+  NSM_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, NSM_ERR_WORKSPACE, "nsm_union_decode: workspace missing, not 256-byte aligned or too small");
   UnionWs wsl = union_ws_layout(ws, hidden, umax);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   int gu_per_sm, dn_per_sm;

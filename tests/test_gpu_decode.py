@@ -464,6 +464,41 @@ def test_decode_edge_cases(dev):
         sparse_mlp_decode(xd[:100], None, w, idx=T(np.array([1]), dev))
 
 
+def test_misaligned_workspace_is_refused(dev):
+    """The kernels stage x by bulk copies that need 16-byte aligned
+    addresses; a workspace that is not 256-byte aligned is refused on the host
+    (NSM_ERR_WORKSPACE) before anything is launched."""
+    import ctypes
+
+    from next_step_ai_b200 import _lib
+    from next_step_ai_b200._torch import dtype_code, ptr, stream_handle
+
+    lib = _lib.load()
+    shape = syn.SHAPES["tiny"]
+    full = full_layer("tiny", 3)
+    w = weights_for(shape, full, dev)
+    xd = T(syn.make_x(shape, 3, 1)[0], dev, torch.bfloat16)
+    idx = T(np.array([1, 2]), dev).to(torch.int32)
+    y = torch.empty(shape.hidden, dtype=torch.float32, device=dev)
+    need = lib.nsm_decode_workspace_bytes(shape.hidden, shape.intermediate, 2, 1)
+    buf = torch.zeros(need + 512, dtype=torch.uint8, device=dev)
+    bm = _lib.BlockMapC()
+    bm.block_begin, bm.block_end = 0, shape.intermediate // 32
+    wc = w.to_c()
+
+    def call(off):
+        return lib.nsm_sparse_mlp_decode(ptr(xd), dtype_code(xd.dtype), shape.hidden, shape.intermediate, None, None,
+                                         ptr(idx), 2, ctypes.byref(bm), ctypes.byref(wc), ptr(y),
+                                         dtype_code(y.dtype), None, None, buf.data_ptr() + off, need,
+                                         stream_handle(dev))
+
+    for off in (8, 16, 128):
+        assert call(off) == _lib.NSM_ERR_WORKSPACE, off
+        assert b"256-byte aligned" in lib.nsm_last_error()
+    assert call(256) == 0
+    torch.cuda.synchronize()
+
+
 def test_decode_deterministic(dev):
     from next_step_ai_b200 import sparse_mlp_decode
 
