@@ -53,11 +53,11 @@ def gateup_bytes_per_launch(k: int = TOP_K, H: int = HIDDEN) -> int:
     return k * 2 * (16 * H + 2 * H)
 
 
-# DRAM bytes (read + write) per layer of the token kernel from one ncu capture of a
-# 2-layer token (dram__bytes_read.sum + dram__bytes_write.sum of the launch / 2),
-# scaled to the 126-layer token; None until a capture of the current kernel exists.
+# DRAM bytes (read + write) per layer of the token kernel (SparseMlpDecoder(token_kernel=True)) from
+# an ncu capture of a 2-layer token, scaled to the 126-layer token; the opt-in
+# token kernel has no capture of its current build, so its line reports none.
 TOKEN_DRAM_BYTES_PER_LAYER = None
-TOKEN_TRAFFIC_SOURCE = "profiles/token_kernel_cfg1.txt (ncu of a 2-layer token, per layer x 126)"
+TOKEN_TRAFFIC_SOURCE = None
 
 
 # DRAM bytes (read + write) of one gateup_tma_kernel launch from the ncu capture in

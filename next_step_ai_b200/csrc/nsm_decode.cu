@@ -1273,24 +1273,32 @@ __global__ void __launch_bounds__(kTmaThreads, 1) down_tma_kernel(DownParams p) 
   build_lut_alpha(p.down_code, p.down_code, false);  // the down loops read table 0 only
   pdl_wait();  // act16 / act_scale come from the gate/up kernels
   record_down_meta(p);
-  const int count = *p.count_ptr;
   __half* sact = reinterpret_cast<__half*>(smem + kDnActOff);
   __half* sactlo = reinterpret_cast<__half*>(smem + kDnActLoOff);
   float* sscale = reinterpret_cast<float*>(smem + kDnScaleOff);
   int* srows = reinterpret_cast<int*>(smem + kDnRowsOff);
   // staged up to the capacity, with the count (entries past it are never
-  // read): act16 / act16lo by bulk copy, scales and rows by plain loads
+  // read), all on one barrier: act16 / act16lo, and the scales and rows when
+  // their bytes are whole 16-byte runs (else plain loads); no thread waits on
+  // a global load before the staging is in flight
+  const bool sr_bulk = (p.max_rows & 3) == 0 && (((uintptr_t)p.act_scale | (uintptr_t)p.rows) & 15) == 0;
   if (threadIdx.x == 0) {
     const uint64_t pol = l2_evict_last_policy();
     fence_proxy_async_global();
-    mbar_arrive_expect_tx(abar, (uint32_t)p.max_rows * 128u);
+    mbar_arrive_expect_tx(abar, (uint32_t)p.max_rows * (sr_bulk ? 136u : 128u));
     bulk_g2s(smem_u32(sact), p.act16, (uint32_t)p.max_rows * 64u, abar, pol);
     bulk_g2s(smem_u32(sactlo), p.act16lo, (uint32_t)p.max_rows * 64u, abar, pol);
+    if (sr_bulk) {
+      bulk_g2s(smem_u32(sscale), p.act_scale, (uint32_t)p.max_rows * 4u, abar, pol);
+      bulk_g2s(smem_u32(srows), p.rows, (uint32_t)p.max_rows * 4u, abar, pol);
+    }
   }
-  for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) {
-    sscale[i] = __ldcg(p.act_scale + i);
-    srows[i] = __ldcg(p.rows + i);
-  }
+  const int count = __ldcg(p.count_ptr);
+  if (!sr_bulk)
+    for (int i = threadIdx.x; i < p.max_rows; i += blockDim.x) {
+      sscale[i] = __ldcg(p.act_scale + i);
+      srows[i] = __ldcg(p.rows + i);
+    }
   bool a_late = false;
   if (threadIdx.x == 0 && !mbar_wait(abar, 0, p.wait_spins)) {
     record_error(p.err, NSM_ERR_TIMEOUT);
