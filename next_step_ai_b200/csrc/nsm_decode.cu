@@ -719,13 +719,13 @@ __device__ __forceinline__ bool gu_ticket_add(const GateUpParams& p, int s, int 
 // gateup_finalize_kernel's work for block s by one warp (lane = neuron), in the
 // same summation order: segment q goes to group q mod 8, each group sums its
 // segments in order, the 8 group sums combine in order.  Then the ticket is
-// reset for the next call.
-__device__ __forceinline__ void gu_finalize_block(const GateUpParams& p, int s, int cps, int total, int nw,
-                                                  int lane) {
-  __threadfence();
+// reset for the next call.  Split in two so that a warp owing several blocks
+// has all their partial loads in flight at once (gu_finalize_load for each,
+// then gu_finalize_store for each).
+__device__ __forceinline__ void gu_finalize_load(const GateUpParams& p, int s, int cps, int total, int nw, int lane,
+                                                 float (&vg)[8], float (&vu)[8]) {
   const int ups = stream_owner(total, nw, s * cps + cps - 1) - stream_owner(total, nw, s * cps) + 1;
   const float* base = p.gu_part + (int64_t)s * kMaxUnitsPerSlot * 64;
-  float vg[8], vu[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     vg[q] = q < ups ? ldcg_f32(base + q * 64 + lane) : 0.f;
@@ -739,7 +739,9 @@ __device__ __forceinline__ void gu_finalize_block(const GateUpParams& p, int s, 
         vu[u] += ldcg_f32(base + (q0 + u) * 64 + 32 + lane);
       }
   }
-  const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
+}
+__device__ __forceinline__ void gu_finalize_store(const GateUpParams& p, int s, int lane, const float (&vg)[8],
+                                                  const float (&vu)[8], float ns) {
   float gsum = 0.f, usum = 0.f;
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
@@ -749,6 +751,13 @@ __device__ __forceinline__ void gu_finalize_block(const GateUpParams& p, int s, 
   gu_finalize_apply(p, s, lane, gsum, usum, ns);
   __syncwarp();
   if (lane == 0) p.gu_ticket[s] = 0u;
+}
+__device__ __forceinline__ void gu_finalize_block(const GateUpParams& p, int s, int cps, int total, int nw,
+                                                  int lane) {
+  __threadfence();
+  float vg[8], vu[8];
+  gu_finalize_load(p, s, cps, total, nw, lane, vg, vu);
+  gu_finalize_store(p, s, lane, vg, vu, p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f);
 }
 
 // A ring stage holds one *unit* of kGuUnitTiles adjacent tiles of one block
@@ -887,11 +896,22 @@ __device__ __forceinline__ void gateup_tma_body(const GateUpParams& p, uint32_t 
     drain_ring<kGuStages>(wbar, q - q0, issued);
     return;
   }
-  // SiLU(gate)*up of the blocks whose last units this warp counted
-  while (owed) {
-    const int b = __ffsll((long long)owed) - 1;
-    owed &= owed - 1ull;
-    gu_finalize_block(p, s_first + b, cps, total, nw, lane);
+  // SiLU(gate)*up of the blocks whose last units this warp counted, two at a
+  // time with both blocks' partial loads in flight together
+  if (owed) {
+    __threadfence();
+    const float ns = p.norm_scale ? ldcg_f32(p.norm_scale) : 1.f;
+    while (owed) {
+      const int b0 = __ffsll((long long)owed) - 1;
+      owed &= owed - 1ull;
+      const int b1 = owed ? __ffsll((long long)owed) - 1 : -1;
+      if (b1 >= 0) owed &= owed - 1ull;
+      float vg0[8], vu0[8], vg1[8], vu1[8];
+      gu_finalize_load(p, s_first + b0, cps, total, nw, lane, vg0, vu0);
+      if (b1 >= 0) gu_finalize_load(p, s_first + b1, cps, total, nw, lane, vg1, vu1);
+      gu_finalize_store(p, s_first + b0, lane, vg0, vu0, ns);
+      if (b1 >= 0) gu_finalize_store(p, s_first + b1, lane, vg1, vu1, ns);
+    }
   }
 }
 
