@@ -63,7 +63,7 @@ TOKEN_TRAFFIC_SOURCE = None
 # DRAM bytes (read + write) of one gateup_tma_kernel launch from the ncu capture in
 # profiles/gateup_tma_kernel_cfg1.txt (dram__bytes_read.sum + dram__bytes_write.sum),
 # the same workload on one GPU.
-GATEUP_DRAM_BYTES_PER_LAUNCH = 122_843_904 + 3_776_256
+GATEUP_DRAM_BYTES_PER_LAUNCH = 122_852_608 + 3_301_120
 GATEUP_TRAFFIC_SOURCE = "profiles/gateup_tma_kernel_cfg1.txt (ncu --set full, one launch, 1 GPU)"
 
 

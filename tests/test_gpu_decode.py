@@ -247,6 +247,30 @@ def test_decode_fused_selection_matches_topk_kernel_cfg1(dev):
         assert np.array_equal(idx.cpu().numpy(), ref), r
 
 
+def test_decode_fused_selection_many_blocks(dev):
+    """4096 blocks, more keys than the gate/up CTA holds in registers (8 per
+    thread), so the fused selection takes its shared-memory radix select: the
+    outputs equal the top-k kernel path's bit for bit and its indices equal
+    the oracle router's."""
+    from next_step_ai_b200 import sparse_mlp_decode
+    from next_step_ai_b200 import synthetic as dsyn
+
+    shape = dsyn.LayerShape(256, 4096 * 32, 300, 64)
+    w = dsyn.make_layer_weights(shape, 7, 0, dev)
+    rw = dsyn.make_router(shape, 7, 0, dev)
+    R = {k: v.float().cpu().numpy() for k, v in
+         (("enc_w", rw.enc_w), ("enc_b", rw.enc_b), ("score_w", rw.score_w), ("score_b", rw.score_b))}
+    xs = dsyn.make_x(shape, 9, 3, dev)
+    idx = torch.empty(shape.top_k, dtype=torch.int32, device=dev)
+    for r in range(xs.shape[0]):
+        y_fused = sparse_mlp_decode(xs[r], rw, w, out_dtype=torch.float32)
+        y_topk = sparse_mlp_decode(xs[r], rw, w, out_dtype=torch.float32, idx_out=idx)
+        assert torch.equal(y_fused, y_topk), r
+        ref = orr.route_sparse_mlp(xs[r].float().cpu().numpy(), R["enc_w"], R["enc_b"], R["score_w"], R["score_b"],
+                                   shape.top_k, shape.rank)[0]
+        assert np.array_equal(idx.cpu().numpy(), ref), r
+
+
 def test_decode_fused_selection_splits_ties_by_block_id(dev):
     """Tied scores at the threshold (all-zero score head, biases 2, 2, 1, 1, 1,
     1 and zeros): the fused selection keeps the lower block ids among the tied
