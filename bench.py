@@ -275,6 +275,15 @@ def run_ours(args) -> None:
         stage_us = dec.time_stages(min(LAYERS, 2 * unique))
         kern_bytes = gateup_bytes_per_launch() / world  # expected share of the selected blocks per rank
         kern_us = stage_us["gateup"]
+    # selected blocks each rank held per layer (one eager token with records
+    # between layers, every rank together): the ranks' shares of the 208
+    # blocks differ, and each layer's exchange waits for the rank with the most
+    counts = [int(b.numel()) for _, b in dec.trace_layers()]
+    mine = {"mean": round(statistics.mean(counts), 1), "min": min(counts), "max": max(counts)}
+    blocks_per_rank = [mine]
+    if group is not None:
+        blocks_per_rank = [None] * world
+        torch.distributed.all_gather_object(blocks_per_rank, mine)
     kern_gbs = kern_bytes / (kern_us * 1e-6) / 1e9
     if rank == 0:
         line = {
@@ -285,7 +294,7 @@ def run_ours(args) -> None:
             "data": "synthetic: seeded N(0,0.02) NF4 weights, bf16 RMS-normalised N(0,1) input, random-init router",
             "config": headline_config(world),
             "run": {"unique_layers_resident": unique, "layer_cycling": unique < LAYERS, "cuda_graph": True,
-                    "synthetic_gen_s": round(gen_s, 1)},
+                    "synthetic_gen_s": round(gen_s, 1), "blocks_per_rank_per_layer": blocks_per_rank},
             "e2e": {"value": args.steps / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": HIDDEN * 4,
                     "d2h_bytes_per_step": HIDDEN * 4},
             "gpu_launches": args.steps * dec.kernels_per_step,
